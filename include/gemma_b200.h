@@ -1,0 +1,129 @@
+/*
+ * gemma_b200.h -- C-ABI of libgemma_b200.so, the B200 (sm_100a) Gemma 3 Q8_0 token loop.
+ *
+ * This library replaces the WebGPU half of the reference's engine (svenflow/webgpu-gemma,
+ * src/engine.ts: GemmaEngineImpl, lines 124-949 and 1039-1077). The reference's public
+ * TypeScript surface (createGemmaEngine, GemmaEngine.addUserMessage/generate/
+ * resetConversation/dispose), its GGUF parser and its tokenizer stay on the host side and
+ * call these functions with plain pointers and sizes.
+ *
+ * Every function returns 0 on success and a negative GG_E_* code on failure;
+ * gg_last_error() returns the message of the engine's most recent failure.
+ * One engine is bound to one GPU and one CUDA stream and is not re-entrant: calls on the
+ * same engine must be serialised by the caller (the reference awaits each step too).
+ */
+#ifndef GEMMA_B200_H
+#define GEMMA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GG_OK 0
+#define GG_E_ARG -1      /* bad argument (null pointer, size, name, range) */
+#define GG_E_CUDA -2     /* a CUDA runtime call failed */
+#define GG_E_STATE -3    /* call out of order (e.g. step before gg_finalize) */
+#define GG_E_DEVICE -4   /* a kernel reported an error (bounded wait expired, bad input) */
+#define GG_E_NOMEM -5    /* device allocation failed */
+
+typedef struct gg_engine gg_engine;
+
+/* Field-for-field the reference's GemmaConfig (src/types.ts:2-17), plus the number of
+ * independent KV slots and option flags. */
+typedef struct {
+  int32_t hidden_size, q_dim, kv_dim, num_q_heads, num_kv_heads, head_dim, intermediate_size,
+      vocab_size, num_layers, context_length;
+  float rms_norm_eps, rope_theta_global, rope_theta_swa;
+  int32_t swa_period;
+  int32_t max_seqs; /* KV slots (sequences); 1 for the reference's single conversation */
+  int32_t flags;    /* reserved, 0 */
+} gg_config;
+
+/* Sampling options of one step: GenerateOptions (src/types.ts:65-78). */
+typedef struct {
+  float temperature; /* 0 = greedy */
+  float top_p;
+  float rep_penalty; /* 1.0 = none */
+  float pad_;
+} gg_sample;
+
+/* Replaces initWebGPU + createWorkBuffers (engine.ts:124-138, 402-448): binds the engine
+ * to CUDA device `device`, allocates the KV caches and work buffers. */
+int gg_create(const gg_config* cfg, int device, gg_engine** out);
+
+/* Replaces the per-tensor upload of uploadWeightsStreaming / uploadWeightsFromBuffer
+ * (engine.ts:219-400, with packQ8_0ForGPU gguf.ts:126-149 moved to the device). `bytes`
+ * are the tensor's raw GGUF bytes (Q8_0 34-byte blocks, F32 or F16); `dims` are GGUF
+ * dims (ne0 first). The caller keeps ownership of `bytes`. */
+int gg_upload_tensor(gg_engine* eng, const char* name, int ggml_type, const void* bytes, size_t nbytes,
+                     const uint64_t* dims, int n_dims);
+
+/* Checks that every tensor is present and builds the step program (createBindGroups,
+ * engine.ts:450-732). */
+int gg_finalize(gg_engine* eng);
+
+/* Replaces prefillBatched (engine.ts:923-928): runs the n tokens through all layers at
+ * positions start_pos..start_pos+n-1 of KV slot `seq`, writing the KV cache. The ids are
+ * also added to the slot's repetition-penalty set (allTokens, engine.ts:989). */
+int gg_prefill(gg_engine* eng, int seq, const int32_t* ids, int n, int start_pos);
+
+/* Replaces getFirstTokenAfterPrefill (engine.ts:941-949): LM head on the last prefilled
+ * token of `seq` plus sampling. `uniform` replaces Math.random() (ignored when greedy). */
+int gg_sample_last(gg_engine* eng, int seq, const gg_sample* s, double uniform, int32_t* out_token);
+
+/* Replaces forwardPassAndGetToken (engine.ts:904-915): feeds `token` at `pos`, runs the
+ * LM head and the sampler, returns the next token. */
+int gg_step(gg_engine* eng, int seq, int32_t token, int pos, const gg_sample* s, double uniform,
+            int32_t* out_token);
+
+/* n chained steps on the device (the token loop of engine.ts:1003-1025 without stop
+ * checks): step i feeds the token sampled by step i-1. uniforms may be NULL when greedy.
+ * out_tokens receives the n sampled tokens. */
+int gg_decode(gg_engine* eng, int seq, int32_t token, int pos, int n, const gg_sample* s,
+              const double* uniforms, int32_t* out_tokens);
+
+/* Logits of the last LM-head run (vocab_size floats): the reference's logits buffer
+ * (engine.ts:432), for parity checks and teacher forcing. */
+int gg_get_logits(gg_engine* eng, float* out);
+
+/* Final-normed hidden state of the last step (hidden_size floats), engine.ts:797-801. */
+int gg_get_hidden(gg_engine* eng, float* out);
+
+/* One row of the KV cache (kv_dim floats; which = 0 for K, 1 for V). */
+int gg_get_kv(gg_engine* eng, int seq, int layer, int pos, int which, float* out);
+
+/* Debug/parity aid: copy `n` floats of an internal buffer of the last launch.
+ * which: 0 fused QKV output, 1 attention output, 2 O projection, 3 GeGLU output,
+ * 4 down projection (layer outputs hold the last layer's values), 5 hidden state,
+ * 6 residual, 7 final-normed hidden, 8 logits. */
+int gg_debug_read(gg_engine* eng, int which, float* out, int n);
+
+/* Repetition-penalty set of `seq` (allTokens, engine.ts:989-994): reset / add ids. */
+int gg_seen_reset(gg_engine* eng, int seq);
+int gg_seen_add(gg_engine* eng, int seq, const int32_t* ids, int n);
+
+/* resetKVCaches (engine.ts:930-939) for one slot. */
+int gg_reset_kv(gg_engine* eng, int seq);
+
+/* Bounded-wait limit of the device spins, in nanoseconds (default 1e9). */
+int gg_set_timeout(gg_engine* eng, uint64_t ns);
+
+/* Device time of the last gg_step / gg_decode / gg_prefill call, in milliseconds. */
+int gg_last_device_ms(gg_engine* eng, float* ms);
+
+/* dispose (engine.ts:1039-1077). */
+int gg_destroy(gg_engine* eng);
+
+/* Message of the engine's last failure ("" if none). eng may be NULL for gg_create errors. */
+const char* gg_last_error(const gg_engine* eng);
+
+/* Library build identifier (sm_100a kernels, compiled-in limits). */
+const char* gg_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GEMMA_B200_H */

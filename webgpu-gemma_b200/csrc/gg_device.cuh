@@ -1,0 +1,181 @@
+// gg_device.cuh -- device-side building blocks for the sm_100a Gemma 3 token loop.
+//
+// mbarrier + cp.async.bulk (TMA bulk copy) helpers for the weight-streaming ring,
+// tagged 64-bit words ("value | epoch << 32") used to pass activations between CTAs,
+// bounded spins that raise an error word instead of hanging, and the exact int8 -> f32
+// conversion used by the Q8_0 dot products.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define GG_DEV __device__ __forceinline__
+
+// Error bits written to GGState::error by a kernel that gave up waiting.
+enum : uint32_t {
+  GG_ERR_WAIT_FLAG = 1u,   // a tagged activation word never arrived
+  GG_ERR_WAIT_MBAR = 2u,   // a shared-memory ring slot never filled / drained
+  GG_ERR_BAD_INPUT = 4u,   // token / position out of range at kernel start
+};
+
+GG_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+GG_DEV uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------- mbarrier / bulk copy
+
+GG_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+GG_DEV void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+GG_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+GG_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+GG_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// L2 eviction policy for data read exactly once per step (weights): evict first, so the
+// small activations and KV rows keep their L2 lines.
+GG_DEV uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// One bulk copy global -> this CTA's shared memory, completing on `bar` (complete_tx).
+// dst/src 16-byte aligned, bytes a multiple of 16. No multicast.
+GG_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- tagged words
+
+// A tagged word carries one f32 and the epoch of the phase that produced it. Readers spin
+// until the tag matches, so the data word is its own ready flag (no separate barrier).
+GG_DEV void tag_store(uint64_t* p, float v, uint32_t tag) {
+  uint64_t w = ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+GG_DEV uint64_t tag_load(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+struct SpinCtl {
+  uint32_t* err;        // global error word (GGState::error)
+  uint64_t timeout_ns;  // give up after this long
+};
+
+// Wait for a tagged word; on timeout (or an error raised elsewhere) return 0.0f and set err.
+GG_DEV float tag_wait(const uint64_t* p, uint32_t tag, const SpinCtl& sc) {
+  uint64_t w = tag_load(p);
+  if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
+  uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    w = tag_load(p);
+    if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
+    if ((it & 63u) == 0) {
+      if (*(volatile uint32_t*)sc.err) return 0.0f;
+      if (global_timer_ns() - t0 > sc.timeout_ns) {
+        atomicOr(sc.err, GG_ERR_WAIT_FLAG);
+        return 0.0f;
+      }
+    }
+  }
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and sets err) on timeout.
+GG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const SpinCtl& sc) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15u) == 0) {
+      if (*(volatile uint32_t*)sc.err) return false;
+      if (global_timer_ns() - t0 > sc.timeout_ns) {
+        atomicOr(sc.err, GG_ERR_WAIT_MBAR);
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- math helpers
+
+// Exact int8 -> f32 for byte `b` of word `wx` (wx = raw ^ 0x80808080): the byte is placed in
+// the mantissa of 2^23 (0x4B0000xx = 2^23 + u) and the bias 2^23 + 128 removed. Both steps
+// are exact in f32.
+template <int B>
+GG_DEV float q8_byte(uint32_t wx) {
+  return __int_as_float((int)__byte_perm(wx, 0x4B000000u, 0x7440u + B)) - 8388736.0f;
+}
+
+// Sum over the 16 int8 of `w` times x[0..15] (fp32 fused multiply-adds, in element order).
+GG_DEV float dot16(uint4 w, float4 a, float4 b, float4 c, float4 d) {
+  uint32_t w0 = w.x ^ 0x80808080u, w1 = w.y ^ 0x80808080u, w2 = w.z ^ 0x80808080u, w3 = w.w ^ 0x80808080u;
+  float s = q8_byte<0>(w0) * a.x;
+  s = fmaf(q8_byte<1>(w0), a.y, s);
+  s = fmaf(q8_byte<2>(w0), a.z, s);
+  s = fmaf(q8_byte<3>(w0), a.w, s);
+  s = fmaf(q8_byte<0>(w1), b.x, s);
+  s = fmaf(q8_byte<1>(w1), b.y, s);
+  s = fmaf(q8_byte<2>(w1), b.z, s);
+  s = fmaf(q8_byte<3>(w1), b.w, s);
+  s = fmaf(q8_byte<0>(w2), c.x, s);
+  s = fmaf(q8_byte<1>(w2), c.y, s);
+  s = fmaf(q8_byte<2>(w2), c.z, s);
+  s = fmaf(q8_byte<3>(w2), c.w, s);
+  s = fmaf(q8_byte<0>(w3), d.x, s);
+  s = fmaf(q8_byte<1>(w3), d.y, s);
+  s = fmaf(q8_byte<2>(w3), d.z, s);
+  s = fmaf(q8_byte<3>(w3), d.w, s);
+  return s;
+}
+
+GG_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+GG_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Order-preserving map f32 -> u32 (larger float => larger key); NaN is never produced here.
+GG_DEV uint32_t f32_order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+GG_DEV float f32_from_order_key(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// Swizzled float4 slot of logical x element chunk c (16 elements = 4 float4), sub-slot i.
+// Eight consecutive chunks read their i-th float4 from eight distinct 16-byte bank groups.
+GG_DEV int xswz(int c, int i) { return 4 * c + ((i + (c >> 1)) & 3); }

@@ -1,0 +1,699 @@
+// gg_engine.cu -- host engine behind the C-ABI of include/gemma_b200.h.
+//
+// Owns one GPU's copy of the model (repacked on the device from raw GGUF bytes), the KV
+// caches, the tagged activation buffers and the step state; launches the persistent decode
+// kernel (gg_decode.cu) cooperatively, one launch per token.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/gemma_b200.h"
+#include "gg_device.cuh"
+#include "gg_model.h"
+
+namespace gg {
+extern "C" __global__ void gg_decode_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
+}
+
+// ------------------------------------------------------------------------------ utility kernels
+
+// Raw GGUF Q8_0 blocks (34 B: f16 d, 32 x int8) of an M x K tensor -> row format rows
+// dst_row0 + r * dst_step. Replaces packQ8_0ForGPU (src/gguf.ts:126-149) on the device.
+__global__ void gg_repack_q8_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, long long nblocks,
+                                    int K, int rs, long long dst_row0, int dst_step) {
+  long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nblocks) return;
+  const int bpr = K / 32;
+  long long r = b / bpr;
+  int j = (int)(b % bpr);
+  const uint8_t* s = src + b * 34;
+  uint8_t* row = dst + (dst_row0 + r * dst_step) * (long long)rs;
+  for (int k = 0; k < 32; k++) row[32 * j + k] = s[2 + k];
+  row[K + 2 * j] = s[0];
+  row[K + 2 * j + 1] = s[1];
+}
+
+// F16 -> F32 (dequantizeF16, src/gguf.ts:151-158). IEEE binary16 conversion is exact.
+__global__ void gg_f16_to_f32_kernel(const uint16_t* __restrict__ src, float* __restrict__ dst, long long n) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = __half2float(__ushort_as_half(src[i]));
+}
+
+__global__ void gg_init_keys_kernel(unsigned long long* keys) {
+  int i = threadIdx.x;
+  if (i < 256) keys[i] = ((unsigned long long)f32_order_key(-1e30f) << 32) | 0xffffffffull;
+}
+
+__global__ void gg_seen_add_kernel(uint8_t* seen, const int32_t* ids, int n, int V, GGState* st) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    int t = ids[i];
+    if (t >= 0 && t < V) atomicOr(reinterpret_cast<unsigned int*>(seen) + (t >> 5), 1u << (t & 31));
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&st->seen_count, n);
+}
+
+// ------------------------------------------------------------------------------ engine
+
+struct gg_engine {
+  gg_config cfg{};
+  int device = 0;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  GGModelDev md{};
+  GGModelDev* d_md = nullptr;
+  GGState* d_st = nullptr;
+  GGState* h_st = nullptr;  // pinned
+  std::vector<void*> allocs;
+  // weights
+  std::vector<uint8_t*> wqkv, wo, wgu, wdown;
+  std::vector<float*> norms[6];  // attn_norm, ffn_norm, q_norm, k_norm, post_attn_norm, post_ffw_norm
+  uint8_t* embd = nullptr;
+  float* out_norm = nullptr;
+  std::vector<uint32_t> have;  // per layer bitmask of uploaded tensors
+  bool have_embd = false, have_out_norm = false;
+  bool finalized = false;
+  uint8_t* staging = nullptr;
+  size_t staging_cap = 0;
+  int32_t* d_ids = nullptr;
+  int ids_cap = 0;
+  double* d_unif = nullptr;
+  int unif_cap = 0;
+  int32_t* d_ring = nullptr;
+  int ring_cap = 0;
+  int32_t* h_ring = nullptr;  // pinned
+  int last_hidden_seq = -1;
+  uint64_t timeout_ns = 1000000000ull;
+  float last_ms = 0.f;
+  std::string err;
+};
+
+static std::string g_create_err;
+
+static int fail(gg_engine* e, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (e) e->err = buf;
+  else g_create_err = buf;
+  return code;
+}
+
+#define GG_CUDA(e, call)                                                                      \
+  do {                                                                                        \
+    cudaError_t _r = (call);                                                                  \
+    if (_r != cudaSuccess) return fail((e), GG_E_CUDA, "%s: %s", #call, cudaGetErrorString(_r)); \
+  } while (0)
+
+template <class T>
+static int dalloc(gg_engine* e, T** p, size_t bytes) {
+  void* q = nullptr;
+  cudaError_t r = cudaMalloc(&q, bytes ? bytes : 16);
+  if (r != cudaSuccess) return fail(e, GG_E_NOMEM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(r));
+  // Stream-ordered zeroing: the engine's stream does not synchronise with the legacy stream.
+  r = cudaMemsetAsync(q, 0, bytes ? bytes : 16, e->stream);
+  if (r == cudaSuccess) r = cudaStreamSynchronize(e->stream);
+  if (r != cudaSuccess) return fail(e, GG_E_CUDA, "cudaMemset: %s", cudaGetErrorString(r));
+  e->allocs.push_back(q);
+  *p = static_cast<T*>(q);
+  return GG_OK;
+}
+#define GG_TRY(x)          \
+  do {                     \
+    int _c = (x);          \
+    if (_c != GG_OK) return _c; \
+  } while (0)
+
+enum { T_Q = 0, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN, T_ATTN_NORM, T_FFN_NORM, T_Q_NORM, T_K_NORM, T_POST_ATTN, T_POST_FFW, T_COUNT };
+static const char* kLayerNames[T_COUNT] = {"attn_q",    "attn_k",   "attn_v",      "attn_output",  "ffn_gate",
+                                           "ffn_up",    "ffn_down", "attn_norm",   "ffn_norm",     "attn_q_norm",
+                                           "attn_k_norm", "post_attention_norm", "post_ffw_norm"};
+
+extern "C" int gg_create(const gg_config* cfg, int device, gg_engine** out) {
+  if (!cfg || !out) return fail(nullptr, GG_E_ARG, "null argument");
+  *out = nullptr;
+  const gg_config& c = *cfg;
+  if (c.hidden_size <= 0 || c.hidden_size % 32 || c.num_layers <= 0 || c.num_layers > GG_MAX_LAYERS ||
+      c.num_q_heads <= 0 || c.num_kv_heads <= 0 || c.num_q_heads % c.num_kv_heads || c.head_dim <= 0 ||
+      c.head_dim % 32 || c.head_dim > 1024 || c.q_dim != c.num_q_heads * c.head_dim ||
+      c.kv_dim != c.num_kv_heads * c.head_dim || c.intermediate_size <= 0 || c.intermediate_size % 32 ||
+      c.vocab_size < 256 || c.context_length <= 0 || c.max_seqs <= 0 || c.q_dim % 32)
+    return fail(nullptr, GG_E_ARG, "unsupported config (dims must be positive multiples of 32, q_dim = heads*head_dim)");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+    return fail(nullptr, GG_E_CUDA, "no CUDA device %d", device);
+  gg_engine* e = new gg_engine();
+  e->cfg = c;
+  e->device = device;
+  auto bail = [&](int code) {
+    g_create_err = e->err;
+    gg_destroy(e);
+    return code;
+  };
+  if (cudaSetDevice(device) != cudaSuccess) { fail(e, GG_E_CUDA, "cudaSetDevice"); return bail(GG_E_CUDA); }
+  cudaDeviceProp prop;
+  cudaGetDeviceProperties(&prop, device);
+  if (prop.major < 10) { fail(e, GG_E_CUDA, "device %d is sm_%d%d; this library is built for sm_100a", device, prop.major, prop.minor); return bail(GG_E_CUDA); }
+  e->sm_count = prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreate(&e->ev0) != cudaSuccess || cudaEventCreate(&e->ev1) != cudaSuccess) {
+    fail(e, GG_E_CUDA, "stream/event creation failed");
+    return bail(GG_E_CUDA);
+  }
+  const int H = c.hidden_size, Q = c.q_dim, KV = c.kv_dim, I = c.intermediate_size, V = c.vocab_size, L = c.num_layers;
+  GGModelDev& m = e->md;
+  m.H = H; m.Q = Q; m.KV = KV; m.NQH = c.num_q_heads; m.NKH = c.num_kv_heads; m.HD = c.head_dim;
+  m.I = I; m.V = V; m.L = L; m.CTX = c.context_length;
+  m.eps = c.rms_norm_eps;
+  m.attn_scale = (float)(1.0 / sqrt((double)c.head_dim));  // engine.ts:200
+  m.rs_h = gg_row_stride(H); m.rs_q = gg_row_stride(Q); m.rs_i = gg_row_stride(I);
+  m.max_seqs = c.max_seqs;
+  int rc = GG_OK;
+  e->wqkv.resize(L); e->wo.resize(L); e->wgu.resize(L); e->wdown.resize(L);
+  for (auto& v : e->norms) v.resize(L);
+  e->have.assign(L, 0u);
+  for (int l = 0; l < L && rc == GG_OK; l++) {
+    rc = dalloc(e, &e->wqkv[l], (size_t)(Q + 2 * KV) * m.rs_h);
+    if (rc == GG_OK) rc = dalloc(e, &e->wo[l], (size_t)H * m.rs_q);
+    if (rc == GG_OK) rc = dalloc(e, &e->wgu[l], (size_t)2 * I * m.rs_h);
+    if (rc == GG_OK) rc = dalloc(e, &e->wdown[l], (size_t)H * m.rs_i);
+    const int nlen[6] = {H, H, c.head_dim, c.head_dim, H, H};
+    for (int k = 0; k < 6 && rc == GG_OK; k++) rc = dalloc(e, &e->norms[k][l], (size_t)nlen[k] * 4);
+  }
+  if (rc == GG_OK) rc = dalloc(e, &e->embd, (size_t)V * m.rs_h);
+  if (rc == GG_OK) rc = dalloc(e, &e->out_norm, (size_t)H * 4);
+  m.kv_seq_stride = (size_t)L * m.CTX * KV;
+  if (rc == GG_OK) rc = dalloc(e, &m.kcache, m.kv_seq_stride * 4 * c.max_seqs);
+  if (rc == GG_OK) rc = dalloc(e, &m.vcache, m.kv_seq_stride * 4 * c.max_seqs);
+  if (rc != GG_OK) return bail(rc);
+  return (*out = e, GG_OK);
+}
+
+static int schedule(gg_engine* e) {
+  GGModelDev& m = e->md;
+  const gg_config& c = e->cfg;
+  m.grid = e->sm_count;
+  m.stage_bytes = 20480;
+  if (m.rs_i > m.stage_bytes || m.rs_q > m.stage_bytes || 2 * m.rs_h > m.stage_bytes)
+    return fail(e, GG_E_ARG, "rows too wide for a %d-byte ring stage", m.stage_bytes);
+  m.rps_h = m.stage_bytes / m.rs_h;
+  m.rps_q = m.stage_bytes / m.rs_q;
+  m.rps_i = m.stage_bytes / m.rs_i;
+  m.pps_gu = m.stage_bytes / (2 * m.rs_h);
+  m.pos_per_split = std::min(8, m.stage_bytes / (8 * m.KV));
+  if (m.pos_per_split < 1) return fail(e, GG_E_ARG, "kv_dim too large for a ring stage");
+  m.max_splits = (m.CTX + m.pos_per_split - 1) / m.pos_per_split;
+  m.dims_per_comb = 8;
+  if (m.HD % m.dims_per_comb) return fail(e, GG_E_ARG, "head_dim must be a multiple of 8");
+  m.ncomb = m.Q / m.dims_per_comb;
+  // K-splits: enough units for every consumer warp on the short O / down phases
+  auto pick_ks = [&](int K) {
+    int rows = (m.H + m.grid - 1) / m.grid;
+    int nch = K / 16, ks = 1;
+    while (ks < 8 && rows * ks < GG_NCW && nch % (ks * 2) == 0) ks *= 2;
+    while (rows * ks > 1024) ks /= 2;
+    return ks;
+  };
+  m.ks_o = pick_ks(m.Q);
+  m.ks_down = pick_ks(m.I);
+  m.xs_floats = (std::max(std::max(m.H, m.Q), m.I) + 15) / 16 * 16;
+  m.tmp_floats = std::max(m.Q + 2 * m.KV, m.H);
+  size_t other = 8 * 256 + 4 * (size_t)m.xs_floats + 8 * (size_t)m.H + 4 * (size_t)m.tmp_floats + 4 * (size_t)m.HD +
+                 4 * 1024 + 4 * (size_t)(m.NQH * m.pos_per_split + 32) + 4 * (size_t)(3 * m.max_splits) + 4 * 128 + 16;
+  cudaFuncAttributes fa;
+  GG_CUDA(e, cudaFuncGetAttributes(&fa, gg::gg_decode_kernel));
+  int optin = 0;
+  GG_CUDA(e, cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->device));
+  long avail = (long)optin - (long)fa.sharedSizeBytes - (long)other;
+  int ns = (int)std::min<long>(16, avail / (m.stage_bytes + 16));
+  if (ns < 2) return fail(e, GG_E_ARG, "not enough shared memory for the weight ring (%ld bytes left)", avail);
+  m.nstages = ns;
+  m.smem_bytes = (int)(other + (size_t)ns * (m.stage_bytes + 16));
+  GG_CUDA(e, cudaFuncSetAttribute(gg::gg_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, m.smem_bytes));
+  int nb = 0;
+  GG_CUDA(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gg::gg_decode_kernel, GG_NTHREADS, m.smem_bytes));
+  if (nb < 1) return fail(e, GG_E_CUDA, "decode kernel cannot be resident (smem %d)", m.smem_bytes);
+  (void)c;
+  return GG_OK;
+}
+
+extern "C" int gg_upload_tensor(gg_engine* e, const char* name, int type, const void* bytes, size_t nbytes,
+                                const uint64_t* dims, int n_dims) {
+  if (!e || !name || !bytes || !dims || n_dims < 1 || n_dims > 4) return fail(e, GG_E_ARG, "null or bad argument");
+  if (e->finalized) return fail(e, GG_E_STATE, "gg_upload_tensor after gg_finalize");
+  GG_CUDA(e, cudaSetDevice(e->device));
+  const gg_config& c = e->cfg;
+  const GGModelDev& m = e->md;
+  uint64_t nel = 1;
+  for (int i = 0; i < n_dims; i++) nel *= dims[i];
+  const uint64_t ne0 = dims[0], ne1 = n_dims > 1 ? nel / dims[0] : 1;
+  // classify
+  int layer = -1, kind = -1;
+  bool is_embd = !strcmp(name, "token_embd.weight"), is_out = !strcmp(name, "output_norm.weight");
+  if (!is_embd && !is_out) {
+    char key[64];
+    int il = -1;
+    if (sscanf(name, "blk.%d.%63[^.].weight", &il, key) != 2 || il < 0 || il >= c.num_layers)
+      return fail(e, GG_E_ARG, "unknown tensor '%s'", name);
+    for (int k = 0; k < T_COUNT; k++)
+      if (!strcmp(key, kLayerNames[k])) kind = k;
+    if (kind < 0) return fail(e, GG_E_ARG, "unknown tensor '%s'", name);
+    layer = il;
+  }
+  const bool q8 = is_embd || (kind >= 0 && kind <= T_DOWN);
+  if (q8) {
+    if (type != 8) return fail(e, GG_E_ARG, "%s: expected Q8_0 (type 8), got %d", name, type);
+    uint64_t expK, expM;
+    uint8_t* dst;
+    long long row0 = 0;
+    int step = 1, rs;
+    if (is_embd) { expK = c.hidden_size; expM = c.vocab_size; dst = e->embd; rs = m.rs_h; }
+    else switch (kind) {
+      case T_Q: expK = c.hidden_size; expM = c.q_dim; dst = e->wqkv[layer]; rs = m.rs_h; break;
+      case T_K: expK = c.hidden_size; expM = c.kv_dim; dst = e->wqkv[layer]; rs = m.rs_h; row0 = c.q_dim; break;
+      case T_V: expK = c.hidden_size; expM = c.kv_dim; dst = e->wqkv[layer]; rs = m.rs_h; row0 = c.q_dim + c.kv_dim; break;
+      case T_O: expK = c.q_dim; expM = c.hidden_size; dst = e->wo[layer]; rs = m.rs_q; break;
+      case T_GATE: expK = c.hidden_size; expM = c.intermediate_size; dst = e->wgu[layer]; rs = m.rs_h; step = 2; break;
+      case T_UP: expK = c.hidden_size; expM = c.intermediate_size; dst = e->wgu[layer]; rs = m.rs_h; step = 2; row0 = 1; break;
+      default: expK = c.intermediate_size; expM = c.hidden_size; dst = e->wdown[layer]; rs = m.rs_i; break;
+    }
+    if (ne0 != expK || ne1 != expM)
+      return fail(e, GG_E_ARG, "%s: dims [%llu, %llu], expected [%llu, %llu]", name, (unsigned long long)ne0,
+                  (unsigned long long)ne1, (unsigned long long)expK, (unsigned long long)expM);
+    const size_t need = (size_t)(nel / 32) * 34;  // tensorByteSize (gguf.ts:181-187)
+    if (nbytes != need) return fail(e, GG_E_ARG, "%s: %zu bytes, expected %zu", name, nbytes, need);
+    if (e->staging_cap < need) {
+      if (e->staging) cudaFree(e->staging);
+      e->staging = nullptr;
+      e->staging_cap = 0;
+      GG_CUDA(e, cudaMalloc(&e->staging, need));
+      e->staging_cap = need;
+    }
+    // A pageable cudaMemcpy may return before its DMA lands; order the copy on our stream.
+    GG_CUDA(e, cudaMemcpyAsync(e->staging, bytes, need, cudaMemcpyHostToDevice, e->stream));
+    long long nb = (long long)(nel / 32);
+    gg_repack_q8_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, e->stream>>>(e->staging, dst, nb, (int)expK, rs, row0, step);
+    GG_CUDA(e, cudaGetLastError());
+    GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  } else {
+    uint64_t expN = c.hidden_size;
+    float* dst = nullptr;
+    if (is_out) dst = e->out_norm;
+    else {
+      if (kind == T_Q_NORM || kind == T_K_NORM) expN = c.head_dim;
+      dst = e->norms[kind - T_ATTN_NORM][layer];
+    }
+    if (nel != expN) return fail(e, GG_E_ARG, "%s: %llu elements, expected %llu", name, (unsigned long long)nel, (unsigned long long)expN);
+    if (type == 0) {
+      if (nbytes != nel * 4) return fail(e, GG_E_ARG, "%s: %zu bytes, expected %llu", name, nbytes, (unsigned long long)(nel * 4));
+      GG_CUDA(e, cudaMemcpyAsync(dst, bytes, nel * 4, cudaMemcpyHostToDevice, e->stream));
+      GG_CUDA(e, cudaStreamSynchronize(e->stream));
+    } else if (type == 1) {
+      if (nbytes != nel * 2) return fail(e, GG_E_ARG, "%s: %zu bytes, expected %llu", name, nbytes, (unsigned long long)(nel * 2));
+      if (e->staging_cap < nbytes) {
+        if (e->staging) cudaFree(e->staging);
+        e->staging = nullptr;
+        e->staging_cap = 0;
+        GG_CUDA(e, cudaMalloc(&e->staging, nbytes));
+        e->staging_cap = nbytes;
+      }
+      GG_CUDA(e, cudaMemcpyAsync(e->staging, bytes, nbytes, cudaMemcpyHostToDevice, e->stream));
+      gg_f16_to_f32_kernel<<<(unsigned)((nel + 255) / 256), 256, 0, e->stream>>>((const uint16_t*)e->staging, dst, (long long)nel);
+      GG_CUDA(e, cudaGetLastError());
+      GG_CUDA(e, cudaStreamSynchronize(e->stream));
+    } else {
+      return fail(e, GG_E_ARG, "%s: unsupported type %d (F32 or F16 expected)", name, type);
+    }
+  }
+  if (is_embd) e->have_embd = true;
+  else if (is_out) e->have_out_norm = true;
+  else e->have[layer] |= 1u << kind;
+  return GG_OK;
+}
+
+extern "C" int gg_finalize(gg_engine* e) {
+  if (!e) return fail(e, GG_E_ARG, "null engine");
+  if (e->finalized) return GG_OK;
+  GG_CUDA(e, cudaSetDevice(e->device));
+  const gg_config& c = e->cfg;
+  if (!e->have_embd) return fail(e, GG_E_STATE, "missing token_embd.weight");
+  if (!e->have_out_norm) return fail(e, GG_E_STATE, "missing output_norm.weight");
+  for (int l = 0; l < c.num_layers; l++)
+    for (int k = 0; k < T_COUNT; k++)
+      if (!(e->have[l] & (1u << k))) return fail(e, GG_E_STATE, "missing blk.%d.%s.weight", l, kLayerNames[k]);
+  GGModelDev& m = e->md;
+  GG_TRY(schedule(e));
+  m.embd = e->embd;
+  m.out_norm = e->out_norm;
+  for (int l = 0; l < c.num_layers; l++) {
+    GGLayerW& w = m.layers[l];
+    w.wqkv = e->wqkv[l]; w.wo = e->wo[l]; w.wgu = e->wgu[l]; w.wdown = e->wdown[l];
+    w.attn_norm = e->norms[0][l]; w.ffn_norm = e->norms[1][l]; w.q_norm = e->norms[2][l];
+    w.k_norm = e->norms[3][l]; w.post_attn_norm = e->norms[4][l]; w.post_ffw_norm = e->norms[5][l];
+    // getRopeTheta (types.ts:38-44)
+    bool swa = (l % c.swa_period) < (c.swa_period - 1);
+    w.theta = swa ? c.rope_theta_swa : c.rope_theta_global;
+  }
+  GG_TRY(dalloc(e, &m.t_qkv, 8 * (size_t)(m.Q + 2 * m.KV)));
+  GG_TRY(dalloc(e, &m.t_ml, 8 * (size_t)m.max_splits * m.NQH * 2));
+  GG_TRY(dalloc(e, &m.t_o, 8 * (size_t)m.max_splits * m.Q));
+  GG_TRY(dalloc(e, &m.t_att, 8 * (size_t)m.Q));
+  GG_TRY(dalloc(e, &m.t_proj, 8 * (size_t)m.H));
+  GG_TRY(dalloc(e, &m.t_act, 8 * (size_t)m.I));
+  GG_TRY(dalloc(e, &m.t_down, 8 * (size_t)m.H));
+  GG_TRY(dalloc(e, &m.logits, 4 * (size_t)m.V));
+  GG_TRY(dalloc(e, &m.lane_keys, 8 * 256));
+  GG_TRY(dalloc(e, &m.dbg_hidden, 4 * (size_t)m.H));
+  GG_TRY(dalloc(e, &m.dbg_residual, 4 * (size_t)m.H));
+  GG_TRY(dalloc(e, &m.dbg_normed, 4 * (size_t)m.H));
+  m.seen_stride = ((m.V + 31) / 32) * 4;
+  GG_TRY(dalloc(e, &m.seen, (size_t)m.seen_stride * c.max_seqs));
+  GG_TRY(dalloc(e, &e->d_md, sizeof(GGModelDev)));
+  GG_TRY(dalloc(e, &e->d_st, sizeof(GGState)));
+  GG_CUDA(e, cudaMallocHost(&e->h_st, sizeof(GGState)));
+  memset(e->h_st, 0, sizeof(GGState));
+  GG_CUDA(e, cudaMemcpyAsync(e->d_md, &m, sizeof(GGModelDev), cudaMemcpyHostToDevice, e->stream));
+  GGState s0{};
+  s0.epoch = 1;
+  s0.timeout_ns = e->timeout_ns;
+  GG_CUDA(e, cudaMemcpyAsync(e->d_st, &s0, sizeof(GGState), cudaMemcpyHostToDevice, e->stream));
+  gg_init_keys_kernel<<<1, 256, 0, e->stream>>>(m.lane_keys);
+  GG_CUDA(e, cudaGetLastError());
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  if (e->staging) { cudaFree(e->staging); e->staging = nullptr; e->staging_cap = 0; }
+  e->finalized = true;
+  return GG_OK;
+}
+
+// ------------------------------------------------------------------------------ launches
+
+static int ready(gg_engine* e, int seq) {
+  if (!e) return fail(e, GG_E_ARG, "null engine");
+  if (!e->finalized) return fail(e, GG_E_STATE, "engine not finalized");
+  if (seq < 0 || seq >= e->cfg.max_seqs) return fail(e, GG_E_ARG, "seq %d out of range", seq);
+  cudaError_t r = cudaSetDevice(e->device);
+  if (r != cudaSuccess) return fail(e, GG_E_CUDA, "cudaSetDevice: %s", cudaGetErrorString(r));
+  return GG_OK;
+}
+
+// Write the host-owned prefix of the state (everything before `epoch`).
+static int put_inputs(gg_engine* e, const GGState& in) {
+  *e->h_st = in;
+  GG_CUDA(e, cudaMemcpyAsync(e->d_st, e->h_st, offsetof(GGState, epoch), cudaMemcpyHostToDevice, e->stream));
+  return GG_OK;
+}
+
+static int launch(gg_engine* e) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(e->md.grid);
+  lc.blockDim = dim3(GG_NTHREADS);
+  lc.dynamicSmemBytes = e->md.smem_bytes;
+  lc.stream = e->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  lc.attrs = at;
+  lc.numAttrs = 1;
+  GG_CUDA(e, cudaLaunchKernelEx(&lc, gg::gg_decode_kernel, (const GGModelDev*)e->d_md, e->d_st));
+  return GG_OK;
+}
+
+// Read back error/out_token, synchronise, and turn device error bits into a status.
+static int finish(gg_engine* e, int32_t* out_token) {
+  GG_CUDA(e, cudaMemcpyAsync(&e->h_st->epoch, &e->d_st->epoch, sizeof(GGState) - offsetof(GGState, epoch),
+                             cudaMemcpyDeviceToHost, e->stream));
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+  uint32_t err = e->h_st->error;
+  if (err) {
+    cudaMemsetAsync(&e->d_st->error, 0, 4, e->stream);
+    cudaStreamSynchronize(e->stream);
+    return fail(e, GG_E_DEVICE, "device reported error 0x%x (%s%s%s)", err, (err & GG_ERR_WAIT_FLAG) ? "activation wait timed out " : "",
+                (err & GG_ERR_WAIT_MBAR) ? "ring wait timed out " : "", (err & GG_ERR_BAD_INPUT) ? "token/pos/seq out of range" : "");
+  }
+  if (out_token) *out_token = e->h_st->out_token;
+  return GG_OK;
+}
+
+static GGState base_inputs(gg_engine* e, int seq, int mode) {
+  GGState s{};
+  s.seq = seq;
+  s.mode = mode;
+  s.timeout_ns = e->timeout_ns;
+  s.rep_penalty = 1.0f;
+  return s;
+}
+
+static void set_sampling(GGState& s, const gg_sample* sp, double u) {
+  if (sp) {
+    s.temperature = sp->temperature;
+    s.top_p = sp->top_p;
+    s.rep_penalty = sp->rep_penalty;
+  }
+  s.uniform = u;
+}
+
+extern "C" int gg_prefill(gg_engine* e, int seq, const int32_t* ids, int n, int start_pos) {
+  GG_TRY(ready(e, seq));
+  if (n <= 0 || !ids) return fail(e, GG_E_ARG, "empty prefill");
+  if (start_pos < 0 || start_pos + n > e->cfg.context_length)
+    return fail(e, GG_E_ARG, "positions %d..%d exceed context %d", start_pos, start_pos + n - 1, e->cfg.context_length);
+  for (int i = 0; i < n; i++)
+    if (ids[i] < 0 || ids[i] >= e->cfg.vocab_size) return fail(e, GG_E_ARG, "token id %d out of range", ids[i]);
+  if (e->ids_cap < n) {
+    if (e->d_ids) cudaFree(e->d_ids);
+    e->d_ids = nullptr;
+    e->ids_cap = 0;
+    GG_CUDA(e, cudaMalloc(&e->d_ids, sizeof(int32_t) * n));
+    e->ids_cap = n;
+  }
+  GG_CUDA(e, cudaMemcpyAsync(e->d_ids, ids, sizeof(int32_t) * n, cudaMemcpyHostToDevice, e->stream));
+  gg_seen_add_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(e->md.seen + (size_t)seq * e->md.seen_stride, e->d_ids, n,
+                                                             e->cfg.vocab_size, e->d_st);
+  GG_CUDA(e, cudaGetLastError());
+  GGState s = base_inputs(e, seq, GG_RUN_LAYERS | GG_PREFILL_ADVANCE);
+  s.token = ids[0];
+  s.pos = start_pos;
+  s.prefill_ids = e->d_ids + 1;
+  s.prefill_left = n - 1;
+  GG_TRY(put_inputs(e, s));
+  GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
+  for (int i = 0; i < n; i++) GG_TRY(launch(e));
+  GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
+  GG_TRY(finish(e, nullptr));
+  e->last_hidden_seq = seq;
+  return GG_OK;
+}
+
+extern "C" int gg_sample_last(gg_engine* e, int seq, const gg_sample* sp, double uniform, int32_t* out_token) {
+  GG_TRY(ready(e, seq));
+  if (!out_token) return fail(e, GG_E_ARG, "null out_token");
+  if (e->last_hidden_seq != seq) return fail(e, GG_E_STATE, "gg_sample_last(seq %d) must follow gg_prefill of that seq", seq);
+  GGState s = base_inputs(e, seq, GG_RUN_LM | GG_RUN_SAMPLE);
+  set_sampling(s, sp, uniform);
+  GG_TRY(put_inputs(e, s));
+  GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
+  GG_TRY(launch(e));
+  GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
+  return finish(e, out_token);
+}
+
+extern "C" int gg_step(gg_engine* e, int seq, int32_t token, int pos, const gg_sample* sp, double uniform,
+                       int32_t* out_token) {
+  GG_TRY(ready(e, seq));
+  if (!out_token) return fail(e, GG_E_ARG, "null out_token");
+  if (token < 0 || token >= e->cfg.vocab_size) return fail(e, GG_E_ARG, "token %d out of range", token);
+  if (pos < 0 || pos >= e->cfg.context_length) return fail(e, GG_E_ARG, "pos %d out of range", pos);
+  GGState s = base_inputs(e, seq, GG_RUN_LAYERS | GG_RUN_LM | GG_RUN_SAMPLE);
+  s.token = token;
+  s.pos = pos;
+  set_sampling(s, sp, uniform);
+  GG_TRY(put_inputs(e, s));
+  GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
+  GG_TRY(launch(e));
+  GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
+  GG_TRY(finish(e, out_token));
+  e->last_hidden_seq = seq;
+  return GG_OK;
+}
+
+extern "C" int gg_decode(gg_engine* e, int seq, int32_t token, int pos, int n, const gg_sample* sp,
+                         const double* uniforms, int32_t* out_tokens) {
+  GG_TRY(ready(e, seq));
+  if (n <= 0 || !out_tokens) return fail(e, GG_E_ARG, "bad n / out_tokens");
+  if (token < 0 || token >= e->cfg.vocab_size) return fail(e, GG_E_ARG, "token %d out of range", token);
+  if (pos < 0 || pos + n > e->cfg.context_length) return fail(e, GG_E_ARG, "positions %d..%d exceed context", pos, pos + n - 1);
+  if (e->ring_cap < n) {
+    if (e->d_ring) cudaFree(e->d_ring);
+    if (e->h_ring) cudaFreeHost(e->h_ring);
+    e->d_ring = nullptr; e->h_ring = nullptr; e->ring_cap = 0;
+    GG_CUDA(e, cudaMalloc(&e->d_ring, sizeof(int32_t) * n));
+    GG_CUDA(e, cudaMallocHost(&e->h_ring, sizeof(int32_t) * n));
+    e->ring_cap = n;
+  }
+  GGState s = base_inputs(e, seq, GG_RUN_LAYERS | GG_RUN_LM | GG_RUN_SAMPLE);
+  s.token = token;
+  s.pos = pos;
+  set_sampling(s, sp, 0.0);
+  const bool greedy = !sp || sp->temperature == 0.0f;
+  if (!greedy) {
+    if (!uniforms) return fail(e, GG_E_ARG, "uniforms required when temperature > 0");
+    if (e->unif_cap < n) {
+      if (e->d_unif) cudaFree(e->d_unif);
+      e->d_unif = nullptr; e->unif_cap = 0;
+      GG_CUDA(e, cudaMalloc(&e->d_unif, sizeof(double) * n));
+      e->unif_cap = n;
+    }
+    GG_CUDA(e, cudaMemcpyAsync(e->d_unif, uniforms, sizeof(double) * n, cudaMemcpyHostToDevice, e->stream));
+    s.uniforms = e->d_unif;
+  }
+  s.token_ring = e->d_ring;
+  s.ring_len = n;
+  s.step_index = 0;
+  GG_TRY(put_inputs(e, s));
+  GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
+  for (int i = 0; i < n; i++) GG_TRY(launch(e));
+  GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
+  GG_CUDA(e, cudaMemcpyAsync(e->h_ring, e->d_ring, sizeof(int32_t) * n, cudaMemcpyDeviceToHost, e->stream));
+  GG_TRY(finish(e, nullptr));
+  memcpy(out_tokens, e->h_ring, sizeof(int32_t) * n);
+  e->last_hidden_seq = seq;
+  return GG_OK;
+}
+
+extern "C" int gg_get_logits(gg_engine* e, float* out) {
+  GG_TRY(ready(e, 0));
+  if (!out) return fail(e, GG_E_ARG, "null out");
+  GG_CUDA(e, cudaMemcpyAsync(out, e->md.logits, 4 * (size_t)e->md.V, cudaMemcpyDeviceToHost, e->stream));
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  return GG_OK;
+}
+
+extern "C" int gg_get_hidden(gg_engine* e, float* out) {
+  GG_TRY(ready(e, 0));
+  if (!out) return fail(e, GG_E_ARG, "null out");
+  GG_CUDA(e, cudaMemcpyAsync(out, e->md.dbg_normed, 4 * (size_t)e->md.H, cudaMemcpyDeviceToHost, e->stream));
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  return GG_OK;
+}
+
+extern "C" int gg_get_kv(gg_engine* e, int seq, int layer, int pos, int which, float* out) {
+  GG_TRY(ready(e, seq));
+  if (!out || layer < 0 || layer >= e->cfg.num_layers || pos < 0 || pos >= e->cfg.context_length)
+    return fail(e, GG_E_ARG, "bad layer/pos");
+  const float* base = which ? e->md.vcache : e->md.kcache;
+  size_t off = (size_t)seq * e->md.kv_seq_stride + ((size_t)layer * e->md.CTX + pos) * e->md.KV;
+  GG_CUDA(e, cudaMemcpyAsync(out, base + off, 4 * (size_t)e->md.KV, cudaMemcpyDeviceToHost, e->stream));
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  return GG_OK;
+}
+
+__global__ void gg_untag_kernel(const uint64_t* src, float* dst, int n) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = __uint_as_float((uint32_t)src[i]);
+}
+
+extern "C" int gg_debug_read(gg_engine* e, int which, float* out, int n) {
+  GG_TRY(ready(e, 0));
+  const GGModelDev& m = e->md;
+  const uint64_t* tagged[5] = {m.t_qkv, m.t_att, m.t_proj, m.t_act, m.t_down};
+  const int tlen[5] = {m.Q + 2 * m.KV, m.Q, m.H, m.I, m.H};
+  const float* plain[4] = {m.dbg_hidden, m.dbg_residual, m.dbg_normed, m.logits};
+  const int plen[4] = {m.H, m.H, m.H, m.V};
+  if (!out || which < 0 || which > 8) return fail(e, GG_E_ARG, "bad buffer id %d", which);
+  int cap = which < 5 ? tlen[which] : plen[which - 5];
+  if (n <= 0 || n > cap) return fail(e, GG_E_ARG, "n=%d outside 1..%d", n, cap);
+  if (which < 5) {
+    float* tmp = nullptr;
+    GG_CUDA(e, cudaMalloc(&tmp, 4 * (size_t)n));
+    gg_untag_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(tagged[which], tmp, n);
+    cudaError_t r = cudaMemcpyAsync(out, tmp, 4 * (size_t)n, cudaMemcpyDeviceToHost, e->stream);
+    cudaStreamSynchronize(e->stream);
+    cudaFree(tmp);
+    if (r != cudaSuccess) return fail(e, GG_E_CUDA, "debug read: %s", cudaGetErrorString(r));
+  } else {
+    GG_CUDA(e, cudaMemcpyAsync(out, plain[which - 5], 4 * (size_t)n, cudaMemcpyDeviceToHost, e->stream));
+    GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  }
+  return GG_OK;
+}
+
+extern "C" int gg_seen_reset(gg_engine* e, int seq) {
+  GG_TRY(ready(e, seq));
+  GG_CUDA(e, cudaMemsetAsync(e->md.seen + (size_t)seq * e->md.seen_stride, 0, e->md.seen_stride, e->stream));
+  GG_CUDA(e, cudaMemsetAsync(&e->d_st->seen_count, 0, sizeof(int32_t), e->stream));
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  return GG_OK;
+}
+
+extern "C" int gg_seen_add(gg_engine* e, int seq, const int32_t* ids, int n) {
+  GG_TRY(ready(e, seq));
+  if (n <= 0) return GG_OK;
+  if (!ids) return fail(e, GG_E_ARG, "null ids");
+  if (e->ids_cap < n) {
+    if (e->d_ids) cudaFree(e->d_ids);
+    e->d_ids = nullptr; e->ids_cap = 0;
+    GG_CUDA(e, cudaMalloc(&e->d_ids, sizeof(int32_t) * n));
+    e->ids_cap = n;
+  }
+  GG_CUDA(e, cudaMemcpyAsync(e->d_ids, ids, sizeof(int32_t) * n, cudaMemcpyHostToDevice, e->stream));
+  gg_seen_add_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(e->md.seen + (size_t)seq * e->md.seen_stride, e->d_ids, n,
+                                                             e->cfg.vocab_size, e->d_st);
+  GG_CUDA(e, cudaGetLastError());
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  return GG_OK;
+}
+
+extern "C" int gg_reset_kv(gg_engine* e, int seq) {
+  GG_TRY(ready(e, seq));
+  size_t n = e->md.kv_seq_stride * 4;
+  GG_CUDA(e, cudaMemsetAsync(e->md.kcache + (size_t)seq * e->md.kv_seq_stride, 0, n, e->stream));
+  GG_CUDA(e, cudaMemsetAsync(e->md.vcache + (size_t)seq * e->md.kv_seq_stride, 0, n, e->stream));
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  return GG_OK;
+}
+
+extern "C" int gg_set_timeout(gg_engine* e, uint64_t ns) {
+  if (!e) return fail(e, GG_E_ARG, "null engine");
+  if (ns < 1000) return fail(e, GG_E_ARG, "timeout must be >= 1 us");
+  e->timeout_ns = ns;
+  return GG_OK;
+}
+
+extern "C" int gg_last_device_ms(gg_engine* e, float* ms) {
+  if (!e || !ms) return fail(e, GG_E_ARG, "null argument");
+  *ms = e->last_ms;
+  return GG_OK;
+}
+
+extern "C" int gg_destroy(gg_engine* e) {
+  if (!e) return GG_OK;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (void* p : e->allocs) cudaFree(p);
+  if (e->staging) cudaFree(e->staging);
+  if (e->d_ids) cudaFree(e->d_ids);
+  if (e->d_unif) cudaFree(e->d_unif);
+  if (e->d_ring) cudaFree(e->d_ring);
+  if (e->h_ring) cudaFreeHost(e->h_ring);
+  if (e->h_st) cudaFreeHost(e->h_st);
+  if (e->ev0) cudaEventDestroy(e->ev0);
+  if (e->ev1) cudaEventDestroy(e->ev1);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+  return GG_OK;
+}
+
+extern "C" const char* gg_last_error(const gg_engine* e) { return e ? e->err.c_str() : g_create_err.c_str(); }
+
+extern "C" const char* gg_version(void) { return "gemma_b200 0.1 (sm_100a, persistent decode kernel, ncw=16)"; }

@@ -1,0 +1,102 @@
+// gg_model.h -- descriptors shared by the host engine and the sm_100a kernels.
+//
+// Device weight layout ("row format"): a Q8_0 matrix with M rows of K inputs is stored as
+// M rows of `row_stride(K)` bytes: K int8 quants, then K/32 f16 scales, then zero padding to
+// a 16-byte multiple. A CTA's rows are contiguous, so one cp.async.bulk moves a whole stage.
+// The reference's GPU layout is 36-byte {f32 scale, 8 x u32} blocks (src/gguf.ts:126-149);
+// this layout keeps the GGUF's 34 bytes per 32 weights (f16 scale) and separates quants from
+// scales so every lane reads 16 quant bytes with one 128-bit load.
+#pragma once
+#include <stdint.h>
+#include <stddef.h>
+
+#define GG_MAX_LAYERS 64
+#define GG_NCW 16                     // consumer warps per CTA
+#define GG_NTHREADS ((GG_NCW + 1) * 32)  // + one producer warp
+#define GG_NCT (GG_NCW * 32)          // consumer threads
+
+static inline int gg_row_stride(int K) { return ((K + (K / 32) * 2) + 15) / 16 * 16; }
+
+struct GGLayerW {
+  const uint8_t* wqkv;   // Q+2KV rows (q rows, then k, then v), K = H
+  const uint8_t* wo;     // H rows, K = Q
+  const uint8_t* wgu;    // 2I rows, gate_i at row 2i and up_i at row 2i+1, K = H
+  const uint8_t* wdown;  // H rows, K = I
+  const float* attn_norm;
+  const float* ffn_norm;
+  const float* q_norm;
+  const float* k_norm;
+  const float* post_attn_norm;
+  const float* post_ffw_norm;
+  float theta;
+  int pad_;
+};
+
+struct GGModelDev {
+  int H, Q, KV, NQH, NKH, HD, I, V, L, CTX;
+  float eps, attn_scale;
+  int rs_h, rs_q, rs_i;  // row strides (bytes) for K = H, Q, I
+  int grid;              // CTAs of the persistent kernel (one per SM)
+  int stage_bytes, nstages;
+  int rps_h, rps_q, rps_i;  // whole rows per ring stage for K = H, Q, I
+  int pps_gu;               // gate/up row pairs per ring stage
+  int ks_o, ks_down;        // K-splits of the O and down projections (cross-warp reduction)
+  int pos_per_split, max_splits, ncomb, dims_per_comb;
+  int xs_floats, tmp_floats;  // shared-memory carve sizes
+  int smem_bytes;
+  const uint8_t* embd;   // V rows, K = H (tied LM head)
+  const float* out_norm;
+  float* kcache;  // [seq][L][CTX][KV]
+  float* vcache;
+  size_t kv_seq_stride;  // floats per sequence
+  // tagged activation exchange (value | tag << 32)
+  uint64_t* t_qkv;  // Q + 2KV
+  uint64_t* t_ml;   // [max_splits][NQH][2]  (running max, sum of exp)
+  uint64_t* t_o;    // [max_splits][Q]
+  uint64_t* t_att;  // Q
+  uint64_t* t_proj; // H
+  uint64_t* t_act;  // I
+  uint64_t* t_down; // H
+  float* logits;                    // V
+  unsigned long long* lane_keys;    // 256 per-lane (value, index) maxima of the LM head
+  float* dbg_hidden;    // H: hidden state after the last finished layer (CTA 0 writes)
+  float* dbg_residual;  // H
+  float* dbg_normed;    // H: final-normed hidden state (input of the LM head)
+  uint8_t* seen;        // [max_seqs][ceil(V/8)] this turn's tokens (repetition penalty)
+  int seen_stride;
+  int max_seqs;
+  GGLayerW layers[GG_MAX_LAYERS];
+};
+
+// Launch-mode bits.
+enum : int {
+  GG_RUN_LAYERS = 1,  // embedding + all transformer layers for st->token at st->pos
+  GG_RUN_LM = 2,      // final norm + LM head (+ per-lane maxima)
+  GG_RUN_SAMPLE = 4,  // sampler on the lane maxima -> st->out_token
+  GG_PREFILL_ADVANCE = 8,  // after the launch: token = ids[++i], pos += 1 (serial prefill)
+};
+
+// Per-engine device state. The prefix up to `epoch` is written by the host at the start of a
+// chain of launches; the device advances token/pos/prefill_ids/uniforms/step_index itself.
+struct GGState {
+  int32_t token;   // token fed at `pos`
+  int32_t pos;     // its position
+  int32_t seq;     // KV slot
+  int32_t mode;    // GG_RUN_* bits
+  float temperature, top_p, rep_penalty;
+  int32_t step_index;        // incremented per sampled token
+  double uniform;            // the draw replacing Math.random() when `uniforms` is null
+  const double* uniforms;    // per-step draws, advanced by one per sampled token
+  uint64_t timeout_ns;       // bounded-wait limit
+  const int32_t* prefill_ids;  // serial prefill: ids still to feed
+  int32_t prefill_left;
+  int32_t ring_len;
+  int32_t* token_ring;       // sampled tokens at [step_index % ring_len]
+  // ---- owned by the device (and reset by dedicated host calls)
+  uint32_t epoch;     // tag base; advanced by the last CTA of each launch
+  uint32_t done;      // end-of-launch ticket
+  uint32_t error;     // GG_ERR_* bits
+  int32_t out_token;  // sampled token
+  int32_t seen_count; // > 0 once this turn has tokens in the seen set
+  int32_t pad_[3];
+};
