@@ -1,0 +1,398 @@
+"""Benchmark: Gemma 3 1B Q8_0 batch-1 greedy decode on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode token of the 1B-shaped synthetic model (seed 1) at batch 1. The KV
+cache holds a 512-token prompt; decode runs over positions 512..767 (the 256 greedy tokens
+of config 1), restarting at 512 every 256 steps. `value` is decode tok/s with inputs resident
+in HBM (device time of the persistent kernel launches, CUDA events on the launching stream);
+`e2e` is the same metric through the C-ABI per-token call gg_step with a host token in and a
+host token out every step. TTFT (prefill of the 512-token prompt + first sampled token) is
+reported as its p50. With --gpus N (torchrun) every rank runs an independent replica
+(data-parallel streams, no collective on the data path); value = tokens of all ranks / max
+over ranks of the device time.
+
+--impl reference times the CPU restatement of the reference's token loop (oracle/, the
+reference itself needs WebGPU and a JS runtime, neither of which exists here) on the host
+cores, one decode token per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "webgpu-gemma_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+METRIC = "decode tok/s Gemma3-1B Q8_0 b=1 (% of HBM roofline); p50 TTFT at 512-tok prompt"
+UNIT = "tok/s"
+PROMPT_LEN = 512
+DECODE_LEN = 256
+SEED = 1
+# Reference's own published decode number for this model (reference README.md:17, M4 Pro).
+PUBLISHED_DECODE = 59.8
+# Algorithmic bytes of one decode token: Q8_0 weights at 34 B / 32 weights
+# (tied LM head included), f32 norm weights, one embedding row, and the fp32 KV rows the
+# reference reads (positions 0..pos, all layers attend the full prefix).
+KV_BYTES_PER_POS = 53248  # 2 (K,V) x 26 layers x 256 x 4 B
+
+
+def weight_bytes(tensors) -> int:
+    return sum(int(v[2].nbytes) for v in tensors.values())
+
+
+def algo_bytes_per_token(wbytes: int, hidden: int, pos: int) -> int:
+    emb_row = hidden + hidden // 16  # one Q8_0 row (quants + f16 scales)
+    return wbytes + emb_row + KV_BYTES_PER_POS * (pos + 1)
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ncu capture of the same kernel on this workload (profiles/gg_decode_kernel_1b.md):
+# dram bytes read + written per launch, or None before a capture exists.
+NCU_TRAFFIC_PER_LAUNCH = None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML while the timed region runs."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._th = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self._nv:
+            self._th = threading.Thread(target=self._run, daemon=True)
+            self._th.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._th:
+            self._th.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        return rank, local, world, dist, torch
+    return rank, local, world, None, None
+
+
+def cpu_oracle_rate(tensors, cfg, n_tokens: int, prompt_len: int = 4):
+    """Decode tok/s of the CPU restatement on a bounded sample; returns (tok/s, threads, sample)."""
+    from oracle import oracle
+    from gemma_b200 import synth
+
+    m = oracle.OracleModel.from_tensors(cfg, tensors)
+    prompt = synth.make_prompt(SEED, prompt_len, cfg.vocab_size)
+    for i, t in enumerate(prompt):
+        m.forward(int(t), i)
+    tok = oracle.argmax(m.logits())
+    pos = prompt_len
+    t0 = time.perf_counter()
+    for _ in range(n_tokens):
+        m.forward(tok, pos)
+        tok = oracle.argmax(m.logits())
+        pos += 1
+    dt = time.perf_counter() - t0
+    m.close()
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    sample = (f"1B synthetic (seed 1), {prompt_len}-token prompt then {n_tokens} greedy decode tokens at positions "
+              f"{prompt_len}..{prompt_len + n_tokens - 1}, full LM head + argmax per token, {threads} OpenMP threads")
+    return n_tokens / dt, threads, sample
+
+
+def run_reference(args):
+    rank, local, world, dist, torch = 0, 0, int(os.environ.get("WORLD_SIZE", "1")), None, None
+    if int(os.environ.get("RANK", "0")) != 0:
+        return  # only rank 0 runs the CPU arm
+    from gemma_b200 import synth
+    shape = synth.SHAPES["1b"]
+    cfg = shape.config()
+    tensors = synth.make_tensors(shape, SEED)
+    from oracle import oracle
+    m = oracle.OracleModel.from_tensors(cfg, tensors)
+    prompt = synth.make_prompt(SEED, 4, cfg.vocab_size)
+    for i, t in enumerate(prompt):
+        m.forward(int(t), i)
+    tok, pos = oracle.argmax(m.logits()), len(prompt)
+    lo = len(prompt)
+
+    def one(tok, pos):  # one decode token; positions cycle over a 256-token window like our arm
+        m.forward(tok, pos)
+        tok = oracle.argmax(m.logits())
+        pos = pos + 1 if pos + 1 < lo + DECODE_LEN else lo
+        return tok, pos
+
+    for _ in range(args.warmup):
+        tok, pos = one(tok, pos)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok, pos = one(tok, pos)
+    dt = time.perf_counter() - t0
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    v = args.steps / dt
+    sample = (f"one greedy decode token per step of the 1B synthetic model (seed 1) with LM head + argmax, "
+              f"positions cycling over {lo}..{lo + DECODE_LEN - 1} after a 4-token prompt, {threads} OpenMP threads")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * dt / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg1 decode, CPU restatement of the reference token loop (oracle/gemma_oracle.c)",
+                   "batch": 1},
+        "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference needs WebGPU + a JS runtime (unavailable on this box); this arm runs its CPU restatement",
+    }))
+
+
+def run_trace():
+    """Phase breakdown of one decode step (positions 512, after a 512-token prefill)."""
+    from gemma_b200 import synth
+    from gemma_b200.native import engine_from_tensors
+    shape = synth.SHAPES["1b"]
+    cfg = shape.config()
+    eng = engine_from_tensors(cfg, synth.make_tensors(shape, SEED))
+    prompt = synth.make_prompt(SEED, PROMPT_LEN, cfg.vocab_size)
+    eng.prefill(prompt, 0)
+    tok = eng.sample_last(0)
+    eng.decode(tok, PROMPT_LEN, 8)
+    eng.set_trace(True)
+    eng.step(tok, PROMPT_LEN)
+    L, G = cfg.num_layers, eng.grid()
+    t = eng.read_trace(G * 512 * 4).astype(np.int64).reshape(G, 512, 4)
+    t0 = t[:, 0, 0].min()
+    names = ["qkv", "attn", "combine", "o_proj", "gate_up", "down"]
+    rows = {n: {"wait_us": [], "compute_us": [], "span_us": [], "ring_wait_us": []} for n in names}
+    prev_done = None
+    for l in range(L):
+        for k in range(6):
+            ph = t[:, l * 6 + k, :]
+            ready, done, enter = ph[:, 1], ph[:, 2], ph[:, 0]
+            has = ready > 0
+            done_max = done.max()
+            if prev_done is not None and has.any():
+                rows[names[k]]["wait_us"].append((np.median(ready[has]) - prev_done) / 1e3)
+                rows[names[k]]["compute_us"].append(np.median(done[has] - ready[has]) / 1e3)
+            if prev_done is not None:
+                rows[names[k]]["span_us"].append((done_max - prev_done) / 1e3)
+                rows[names[k]]["ring_wait_us"].append(float(np.median(ph[:, 3])) / 1e3)
+            prev_done = done_max
+    out = {n: {kk: round(float(np.mean(v)), 2) if v else None for kk, v in d.items()} for n, d in rows.items()}
+    lm = t[:, 6 * L, :]
+    out["layers_total_us"] = round(float((t[:, 6 * L - 1, 2].max() - t0) / 1e3), 1)
+    out["lm_head_us"] = round(float((lm[:, 2].max() - lm[:, 0].min()) / 1e3), 1)
+    out["lm_head_ring_wait_us"] = round(float(np.median(lm[:, 3])) / 1e3, 1)
+    out["step_device_ms"] = round(eng.last_device_ms(), 4)
+    print(json.dumps({"trace_per_layer_mean": out,
+                      "legend": "span = last CTA done minus previous phase's last CTA done; wait = median CTA inputs "
+                                "ready minus previous phase's last done; compute = median done minus ready"}))
+    eng.close()
+
+
+def run_profile():
+    """Launch sequence for ncu: 16 prefill launches, 1 LM-head launch, then 4 decode launches
+    (capture the decode kernel with -k regex:gg_decode_kernel -s 17 -c 1..3)."""
+    from gemma_b200 import synth
+    from gemma_b200.native import engine_from_tensors
+    shape = synth.SHAPES["1b"]
+    cfg = shape.config()
+    eng = engine_from_tensors(cfg, synth.make_tensors(shape, SEED))
+    prompt = synth.make_prompt(SEED, 16, cfg.vocab_size)
+    eng.prefill(prompt, 0)
+    tok = eng.sample_last(0)
+    toks = eng.decode(tok, len(prompt), 4)
+    print("profile run ok", int(tok), [int(t) for t in toks])
+    eng.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=512)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ttft-runs", type=int, default=20)
+    ap.add_argument("--e2e-steps", type=int, default=256)
+    ap.add_argument("--cpu-tokens", type=int, default=6)
+    ap.add_argument("--trace", action="store_true",
+                    help="per-phase device timestamps of one decode step at position 512 (CTA 0)")
+    ap.add_argument("--profile", action="store_true",
+                    help="short fixed sequence for ncu: 16-token prefill, first token, 4 decode steps")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.profile:
+        return run_profile()
+    if args.trace:
+        return run_trace()
+
+    rank, local, world, dist, torch = dist_setup(args.gpus)
+    from gemma_b200 import synth
+    from gemma_b200.native import NativeEngine, engine_from_tensors, STATE_H2D_BYTES, STATE_D2H_BYTES
+
+    shape = synth.SHAPES["1b"]
+    cfg = shape.config()
+    tensors = synth.make_tensors(shape, SEED)
+    wbytes = weight_bytes(tensors)
+    eng = engine_from_tensors(cfg, tensors, device=local)
+    prompt = synth.make_prompt(SEED, PROMPT_LEN, cfg.vocab_size)
+
+    # ---- TTFT: prefill of the 512-token prompt + LM head + first token, through the C-ABI
+    ttft_wall, ttft_dev = [], []
+    first = None
+    for _ in range(max(1, args.ttft_runs)):
+        t0 = time.perf_counter()
+        eng.prefill(prompt, 0)
+        d_pre = eng.last_device_ms()
+        tok = eng.sample_last(0)
+        ttft_wall.append(1000 * (time.perf_counter() - t0))
+        ttft_dev.append(d_pre + eng.last_device_ms())
+        assert first is None or tok == first, "non-deterministic first token"
+        first = tok
+
+    # ---- decode, inputs resident: chained device steps over positions 512..767
+    def run_steps(n):
+        tot_ms, done, toks = 0.0, 0, []
+        while done < n:
+            k = min(DECODE_LEN, n - done)
+            toks.append(eng.decode(first, PROMPT_LEN, k))
+            tot_ms += eng.last_device_ms()
+            done += k
+        return tot_ms, toks
+
+    run_steps(args.warmup)
+    if dist:
+        dist.barrier()
+        torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        dev_ms, toks = run_steps(args.steps)
+    if dist:
+        torch.cuda.synchronize()
+        t = torch.tensor([dev_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        dev_ms_max = float(t.item())
+    else:
+        dev_ms_max = dev_ms
+    value = world * args.steps / (dev_ms_max / 1000.0)
+
+    # ---- e2e through the per-token C-ABI call (host token in, host token out)
+    e2e_n = min(args.e2e_steps, DECODE_LEN)
+    tok = first
+    eng.step(tok, PROMPT_LEN)  # untimed warm call
+    t0 = time.perf_counter()
+    for i in range(e2e_n):
+        tok = eng.step(tok, PROMPT_LEN + i)
+    e2e_s = time.perf_counter() - t0
+    e2e_local = e2e_n / e2e_s
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_value = world * e2e_n / float(t.item())
+    else:
+        e2e_value = e2e_local
+
+    if rank != 0:
+        eng.close()
+        if dist:
+            dist.destroy_process_group()
+        return
+
+    # roofline of the decode kernel over the timed positions
+    positions = [PROMPT_LEN + (i % DECODE_LEN) for i in range(args.steps)]
+    algo = sum(algo_bytes_per_token(wbytes, cfg.hidden_size, p) for p in positions) / len(positions)
+    per_launch_s = (dev_ms / 1000.0) / args.steps
+    achieved = algo / per_launch_s / 1e9
+    peak, peak_kind = measured_peaks()
+    cpu_v, cpu_threads, cpu_sample = cpu_oracle_rate(tensors, cfg, args.cpu_tokens)
+    ttft_p50 = statistics.median(ttft_wall)
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dev_ms_max / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": round(value / PUBLISHED_DECODE, 2), "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg1: Gemma3-1B-shaped Q8_0 GGUF (random init, seed 1), batch 1, 512-token prompt, "
+                               "greedy decode at positions 512..767",
+                   "batch": 1, "prompt_len": PROMPT_LEN, "decode_positions": [PROMPT_LEN, PROMPT_LEN + DECODE_LEN - 1],
+                   "replicas": world, "l2": "no flush: each step streams 1.06 GB of weights (> 126 MB L2)"},
+        "ttft_ms_p50": round(ttft_p50, 3), "ttft_device_ms_p50": round(statistics.median(ttft_dev), 3),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                     "peak_kind": peak_kind, "kernel": "gg_decode_kernel",
+                     "algo_bytes_per_launch": int(algo)},
+        "cpu_baseline": {"value": round(cpu_v, 3), "unit": UNIT, "cores": cpu_threads, "kind": "port",
+                         "sample": cpu_sample},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": STATE_H2D_BYTES,
+                "d2h_bytes_per_step": STATE_D2H_BYTES},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+        "vs_baseline_source": "reference README.md:17 (59.8 tok/s, Mac Mini M4 Pro, Chrome 134)",
+        "first_token": int(first),
+    }
+    print(json.dumps(out))
+    eng.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -108,6 +108,15 @@ int gg_seen_add(gg_engine* eng, int seq, const int32_t* ids, int n);
 /* resetKVCaches (engine.ts:930-939) for one slot. */
 int gg_reset_kv(gg_engine* eng, int seq);
 
+/* Tracing: when on, every CTA of each launch stamps the device global timer (ns) at its phase
+ * boundaries: out[(cta * 512 + phase) * 4 + event], phase = 6*layer + k (k: 0 QKV, 1 attention,
+ * 2 split combine, 3 O projection, 4 gate/up, 5 down), phase 6*L = LM head; event 0 = enter,
+ * 1 = inputs arrived, 2 = done. gg_read_trace copies the first n stamps. */
+int gg_set_trace(gg_engine* eng, int on);
+/* Number of CTAs (one per SM) of the persistent step kernel. */
+int gg_grid(gg_engine* eng, int* out);
+int gg_read_trace(gg_engine* eng, uint64_t* out, int n);
+
 /* Bounded-wait limit of the device spins, in nanoseconds (default 1e9). */
 int gg_set_timeout(gg_engine* eng, uint64_t ns);
 

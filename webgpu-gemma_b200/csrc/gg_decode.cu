@@ -8,14 +8,20 @@
 // tagged 64-bit words (f32 value | epoch << 32), so each word is its own ready flag.
 //
 // Phases per layer (reference: src/engine.ts:766-795):
-//   A  rmsNorm(hidden) -> fused QKV matvec                       (shaders.ts:25-56, 92-151)
+//   A  post-ffw norm + residual of the previous layer, rmsNorm, fused QKV matvec
+//                                                     (shaders.ts:25-56, 92-151, 386-418)
 //   B  q/k per-head norm + RoPE, KV store, split attention       (shaders.ts:209-325, 420-467)
-//   B2 combine of the attention splits (online-softmax merge)
+//   B2 merge of the attention splits (online softmax)
 //   C  O projection                                              (shaders.ts:92-151)
 //   D  post-attn norm + residual, ffn rmsNorm, gate/up + GeGLU   (shaders.ts:153-170, 386-418)
 //   E  down projection                                           (shaders.ts:92-151)
 // then F: post-ffw norm + residual, final rmsNorm, tied LM head with per-lane maxima
 // (engine.ts:797-821, shaders.ts:327-384), and the sampler in the last CTA (engine.ts:823-901).
+//
+// Matvec arithmetic: x is held as 24-bit fixed point per 16-element chunk in three byte
+// planes; q . x is three exact int32 dp4a sums per chunk, recombined in f32 and scaled by the
+// chunk exponent and the Q8_0 block scale (accumulation order differs from the shader's
+// sequential f32 loop; results agree within f32 rounding).
 #include "gg_device.cuh"
 #include "gg_model.h"
 
@@ -34,25 +40,25 @@ GG_DEV void part(int M, int G, int c, int& b, int& e) {
   e = (int)((long long)(c + 1) * M / G);
 }
 
-// Logical x element -> float index in the swizzled shared x vector.
-GG_DEV int xs_index(int e) {
-  int c = e >> 4, k = e & 15;
-  return 4 * xswz(c, k >> 2) + (k & 3);
-}
+// x operand of the dot products: each 16-element chunk as 24-bit fixed point (shared exponent)
+// split into three byte planes; p0 holds the signed top byte, p1/p2 the unsigned lower bytes.
+struct XPlanes {
+  uint8_t* p0;
+  uint8_t* p1;
+  uint8_t* p2;
+  float* inv;  // 2^(e-23) per chunk: multiply the integer dot by this to get back to x's scale
+};
 
 struct Smem {
   uint8_t* ring;
   uint64_t* full;
   uint64_t* empty;
-  float4* xs4;
-  float* xs;
-  float* hid;
-  float* res;
-  float* tmp;
-  float* cs;    // RoPE cos (first HD/2) and sin (next HD/2)
-  float* red;   // cross-warp partial sums
-  float* sc;    // attention scores / combine scratch
-  float* cmb;   // combine: max, sum, weight per split
+  XPlanes xp[2];  // double buffer: a phase builds one while the previous phase may still read the other
+  float* hid;     // residual stream (hidden state), identical in every CTA
+  float* res;     // residual after the attention block
+  float* tmp;     // attention: q | k | v of the current token
+  float* red;     // K-slice partial sums
+  int* rcnt;      // per-row count of finished K-slices
   unsigned long long* keys;
   float* scal;
   int* flag;
@@ -62,47 +68,53 @@ GG_DEV unsigned long long init_lane_key() {
   return ((unsigned long long)f32_order_key(-1e30f) << 32) | 0xffffffffull;
 }
 
-// sum over a row's 16-byte chunks [c0, c1) of (dot of 16 int8 with x) * block scale
-GG_DEV float row_dot(const uint8_t* rowp, int K, const float4* xs4, int c0, int c1, int lane) {
-  float acc = 0.f;
-#pragma unroll 2
-  for (int c = c0 + lane; c < c1; c += 32) {
-    uint4 w = *reinterpret_cast<const uint4*>(rowp + 16 * c);
-    float s = __half2float(*reinterpret_cast<const __half*>(rowp + K + 2 * (c >> 1)));
-    float4 a = xs4[xswz(c, 0)], b = xs4[xswz(c, 1)], cc = xs4[xswz(c, 2)], d = xs4[xswz(c, 3)];
-    acc = fmaf(dot16(w, a, b, cc, d), s, acc);
-  }
-  return warp_sum(acc);
+GG_DEV void ld2_volatile(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-GG_DEV void row_dot2(const uint8_t* r0, const uint8_t* r1, int K, const float4* xs4, int lane, float& o0,
-                     float& o1) {
-  float a0 = 0.f, a1 = 0.f;
-  const int nch = K >> 4;
-#pragma unroll 2
-  for (int c = lane; c < nch; c += 32) {
-    uint4 w0 = *reinterpret_cast<const uint4*>(r0 + 16 * c);
-    uint4 w1 = *reinterpret_cast<const uint4*>(r1 + 16 * c);
-    float s0 = __half2float(*reinterpret_cast<const __half*>(r0 + K + 2 * (c >> 1)));
-    float s1 = __half2float(*reinterpret_cast<const __half*>(r1 + K + 2 * (c >> 1)));
-    float4 a = xs4[xswz(c, 0)], b = xs4[xswz(c, 1)], cc = xs4[xswz(c, 2)], d = xs4[xswz(c, 3)];
-    a0 = fmaf(dot16(w0, a, b, cc, d), s0, a0);
-    a1 = fmaf(dot16(w1, a, b, cc, d), s1, a1);
+// Dot products of R Q8_0 rows (rowp, rowp + rs, ...) with x over the rows' 16-byte chunks
+// [c0, c1), by a group of GS lanes (gl = lane within the group): sum over chunks of
+// d_block * (q . x). The int8 x int8 products of q with the three byte planes of x accumulate
+// exactly in int32 (dp4a); the three partial sums are recombined in f32 and scaled by the
+// chunk's exponent and the block scale. The R rows share the loads of the x planes. Every
+// lane of the group receives the row totals.
+template <int GS, int R>
+GG_DEV void group_dot(const uint8_t* rowp, int rs, int K, const XPlanes& P, int c0, int c1, int gl, float* out) {
+  float acc[R];
+#pragma unroll
+  for (int r = 0; r < R; r++) acc[r] = 0.f;
+#pragma unroll 3
+  for (int c = c0 + gl; c < c1; c += GS) {
+    const uint4 a0 = *reinterpret_cast<const uint4*>(P.p0 + 16 * c);
+    const uint4 a1 = *reinterpret_cast<const uint4*>(P.p1 + 16 * c);
+    const uint4 a2 = *reinterpret_cast<const uint4*>(P.p2 + 16 * c);
+    const float is = P.inv[c];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const uint8_t* rp = rowp + (size_t)r * rs;
+      const uint4 w = *reinterpret_cast<const uint4*>(rp + 16 * c);
+      const float sc = __half2float(*reinterpret_cast<const __half*>(rp + K + 2 * (c >> 1))) * is;
+      int s0 = dp4a_ss((int)w.x, (int)a0.x, 0);
+      s0 = dp4a_ss((int)w.y, (int)a0.y, s0);
+      s0 = dp4a_ss((int)w.z, (int)a0.z, s0);
+      s0 = dp4a_ss((int)w.w, (int)a0.w, s0);
+      int s1 = dp4a_su((int)w.x, (int)a1.x, 0);
+      s1 = dp4a_su((int)w.y, (int)a1.y, s1);
+      s1 = dp4a_su((int)w.z, (int)a1.z, s1);
+      s1 = dp4a_su((int)w.w, (int)a1.w, s1);
+      int s2 = dp4a_su((int)w.x, (int)a2.x, 0);
+      s2 = dp4a_su((int)w.y, (int)a2.y, s2);
+      s2 = dp4a_su((int)w.z, (int)a2.z, s2);
+      s2 = dp4a_su((int)w.w, (int)a2.w, s2);
+      acc[r] = fmaf(fmaf((float)s0, 65536.f, (float)(s1 * 256 + s2)), sc, acc[r]);
+    }
   }
-  o0 = warp_sum(a0);
-  o1 = warp_sum(a1);
-}
-
-// Sum over the consumer threads; every consumer thread gets the same total.
-GG_DEV float csum(float v, float* scal) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_sum(v);
-  if (lane == 0) scal[warp] = v;
-  cbar();
-  float t = lane < NCW ? scal[lane] : 0.f;
-  t = warp_sum(t);
-  cbar();
-  return t;
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+#pragma unroll
+    for (int o = GS / 2; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+    out[r] = acc[r];
+  }
 }
 
 GG_DEV float gelu_tanh(float x) {
@@ -137,6 +149,8 @@ struct Producer {
     if (use > 0 && ok) ok = mbar_wait(&x.S.empty[slot], (use - 1) & 1, x.sc);
     if (!ok) return;
     uint8_t* dst = x.S.ring + (size_t)slot * m.stage_bytes;
+    if ((x.mode & GG_TRACE) && blockIdx.x == 0 && x.idx < 480)  // stage issue times (CTA 0)
+      m.trace[(size_t)160 * 4 + x.idx] = global_timer_ns();
     mbar_arrive_expect_tx(&x.S.full[slot], b0 + b1);
     if (b0) bulk_g2s(dst, s0, b0, &x.S.full[slot], pol);
     if (b1) bulk_g2s(dst + off1, s1, b1, &x.S.full[slot], pol);
@@ -156,7 +170,7 @@ struct Producer {
       for (int l = 0; l < m.L && ok; l++) {
         const GGLayerW& Lw = m.layers[l];
         part(m.Q + 2 * m.KV, G, c, b, e);
-        rows(Lw.wqkv, m.rs_h, b, e, m.rps_h);
+        rows(Lw.wqkv, m.rs_h, b, e, m.ph_qkv.rps);
         const int rot = (l * x.nsplit) % G;
         for (int s = (c - rot + G) % G; s < x.nsplit && ok; s += G) {
           int p0 = s * m.pos_per_split, pc = min(p0 + m.pos_per_split, x.pos);
@@ -165,16 +179,16 @@ struct Producer {
           issue(m.kcache + off, nb, m.vcache + off, nb, (uint32_t)(m.pos_per_split * m.KV * 4));
         }
         part(m.H, G, c, b, e);
-        rows(Lw.wo, m.rs_q, b, e, m.rps_q);
+        rows(Lw.wo, m.rs_q, b, e, m.ph_o.rps);
         part(m.I, G, c, b, e);
         rows(Lw.wgu, m.rs_h, 2 * b, 2 * e, 2 * m.pps_gu);
         part(m.H, G, c, b, e);
-        rows(Lw.wdown, m.rs_i, b, e, m.rps_i);
+        rows(Lw.wdown, m.rs_i, b, e, m.ph_down.rps);
       }
     }
     if ((x.mode & GG_RUN_LM) && ok) {
       part(m.V, G, c, b, e);
-      rows(m.embd, m.rs_h, b, e, m.rps_h);
+      rows(m.embd, m.rs_h, b, e, m.ph_lm.rps);
     }
     // Drain: wait until every copy issued into the ring has landed before the CTA may exit.
     SpinCtl drain = x.sc;
@@ -198,13 +212,22 @@ struct Consumer {
   // Once a ring wait gives up, this warp stops waiting on and releasing slots, so the
   // producer can never refill a slot whose copy might still be landing; it drains and exits.
   bool dead = false;
+  uint64_t ring_wait_ns = 0;  // trace: time warp 0 spent waiting for ring slots in this phase
+  int cslot = 0;              // rotating scratch slot of csum
 
   GG_DEV uint8_t* stage_acquire() {
     const GGModelDev& m = *x.m;
     int slot = x.idx % m.nstages;
     if (!dead) {
+      const bool tr = (x.mode & GG_TRACE) && tid == 0;
+      const uint64_t t0 = tr ? global_timer_ns() : 0;
       bool ok = mbar_wait(&x.S.full[slot], (x.idx / m.nstages) & 1, x.sc);
       dead = !__all_sync(0xffffffffu, ok);
+      if (tr) ring_wait_ns += global_timer_ns() - t0;
+      if (tr && blockIdx.x == 0 && x.idx < 480) {  // stage acquire times of warp 0 (CTA 0)
+        x.m->trace[(size_t)300 * 4 + x.idx] = global_timer_ns();
+        x.m->trace[(size_t)420 * 4 + x.idx] = t0;
+      }
     }
     return x.S.ring + (size_t)slot * m.stage_bytes;
   }
@@ -214,292 +237,493 @@ struct Consumer {
     x.idx++;
   }
 
-  // Wait for n tagged words and store them (optionally swizzled) into shared memory.
-  GG_DEV void gather(const uint64_t* src, int n, uint32_t tag, float* dst, bool swz) {
-    for (int i = tid; i < n; i += NCT) {
-      float v = tag_wait(src + i, tag, x.sc);
-      dst[swz ? xs_index(i) : i] = v;
-    }
-  }
-
-  // Rows [rb, re) of a matrix, one warp per row (round robin), whole rows per stage.
-  template <class Epi>
-  GG_DEV void rows_ks1(int rb, int re, int rps, int K, int rs, Epi epi) {
-    const int nrows = re - rb, nch = K >> 4;
-    for (int r0 = 0; r0 < nrows; r0 += rps) {
-      const uint8_t* stg = stage_acquire();
-      const int r1 = min(r0 + rps, nrows);
-      for (int u = r0 + ((warp - r0) % NCW + NCW) % NCW; u < r1; u += NCW) {
-        float v = row_dot(stg + (size_t)(u - r0) * rs, K, x.S.xs4, 0, nch, lane);
-        epi(rb + u, v);
+  // Trace stamps (GG_TRACE launches only): globaltimer of event ev (0 enter, 1 inputs ready,
+  // 2 done) of phase ph, per CTA: trace[(cta * GG_TRACE_PHASES + ph) * 4 + ev]; event 3 holds
+  // the ring-wait time of warp 0 during the phase.
+  GG_DEV void trace(int ph, int ev) {
+    if ((x.mode & GG_TRACE) && ev == 2) cbar();  // "done" = every warp of the CTA finished the phase
+    if ((x.mode & GG_TRACE) && tid == 0 && ph < GG_TRACE_PHASES) {
+      unsigned long long* t = x.m->trace + ((size_t)blockIdx.x * GG_TRACE_PHASES + ph) * 4;
+      t[ev] = global_timer_ns();
+      if (ev == 2) {
+        t[3] = ring_wait_ns;
+        ring_wait_ns = 0;
       }
-      stage_release();
     }
   }
 
-  // Rows [rb, re) split in `ks` K-slices (units spread over warps); the slice partials are
-  // summed in a fixed order after the phase, then passed to epi(row, value) by one thread.
-  template <class Epi>
-  GG_DEV void rows_ksn(int rb, int re, int rps, int K, int rs, int ks, Epi epi) {
-    const int nrows = re - rb, nch = K >> 4, cpk = nch / ks;
-    for (int r0 = 0; r0 < nrows; r0 += rps) {
-      const uint8_t* stg = stage_acquire();
-      const int r1 = min(r0 + rps, nrows);
-      const int u0 = r0 * ks, u1 = r1 * ks;
-      for (int u = u0 + ((warp - u0) % NCW + NCW) % NCW; u < u1; u += NCW) {
-        int r = u / ks, s = u % ks;
-        float v = row_dot(stg + (size_t)(r - r0) * rs, K, x.S.xs4, s * cpk, (s + 1) * cpk, lane);
-        if (lane == 0) x.S.red[u] = v;
+  // Four consecutive tagged words (16-byte aligned): two vector loads, re-polled as vectors
+  // until every tag matches. Bounded: on timeout (or an error raised elsewhere) the missing
+  // words read as 0 and the error word is set.
+  GG_DEV void load4(const uint64_t* p, uint32_t tag, float* v) {
+    uint64_t w0, w1, w2, w3;
+    ld2_volatile(p, w0, w1);
+    ld2_volatile(p + 2, w2, w3);
+    bool a = (uint32_t)(w0 >> 32) == tag && (uint32_t)(w1 >> 32) == tag;
+    bool b = (uint32_t)(w2 >> 32) == tag && (uint32_t)(w3 >> 32) == tag;
+    if (!(a && b)) {
+      const uint64_t t0 = global_timer_ns();
+      for (uint32_t it = 1; !(a && b); ++it) {
+        if (!a) {
+          ld2_volatile(p, w0, w1);
+          a = (uint32_t)(w0 >> 32) == tag && (uint32_t)(w1 >> 32) == tag;
+        }
+        if (!b) {
+          ld2_volatile(p + 2, w2, w3);
+          b = (uint32_t)(w2 >> 32) == tag && (uint32_t)(w3 >> 32) == tag;
+        }
+        if ((it & 31u) == 0) {
+          const uint64_t dt = global_timer_ns() - t0;
+          if (dt > GG_QUIET_SPIN_NS && (*(volatile uint32_t*)x.sc.err || dt > x.sc.timeout_ns)) {
+            if (dt > x.sc.timeout_ns) atomicOr(x.sc.err, GG_ERR_WAIT_FLAG);
+            w0 = w1 = w2 = w3 = 0;
+            break;
+          }
+        }
       }
-      stage_release();
+    }
+    v[0] = __uint_as_float((uint32_t)w0);
+    v[1] = __uint_as_float((uint32_t)w1);
+    v[2] = __uint_as_float((uint32_t)w2);
+    v[3] = __uint_as_float((uint32_t)w3);
+  }
+
+  // NV sums over the consumer threads with one barrier; every consumer thread gets the same
+  // totals (same summation order everywhere). Scratch slots rotate, so no second barrier.
+  template <int NV>
+  GG_DEV void csum(float* v) {
+    float* s = x.S.scal + (cslot & 3) * (16 * NV);
+    cslot++;
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      const float t = warp_sum(v[k]);
+      if (lane == 0) s[16 * k + warp] = t;
     }
     cbar();
-    for (int r = tid; r < nrows; r += NCT) {
-      float v = 0.f;
-      for (int s = 0; s < ks; s++) v += x.S.red[r * ks + s];
-      epi(rb + r, v);
+#pragma unroll
+    for (int k = 0; k < NV; k++) {
+      float t = 0.f;
+#pragma unroll
+      for (int w = 0; w < NCW; w++) t += s[16 * k + w];
+      v[k] = t;
     }
   }
 
-  // x = rmsNorm(v) * w into the swizzled x vector (shaders.ts:25-56)
-  GG_DEV void norm_to_xs(const float* v, const float* w, int n) {
-    const GGModelDev& m = *x.m;
-    float ss = 0.f;
-    for (int i = tid; i < n; i += NCT) ss += v[i] * v[i];
-    ss = csum(ss, x.S.scal);
-    float rms = sqrtf(ss / (float)n + m.eps);
-    for (int i = tid; i < n; i += NCT) x.S.xs[xs_index(i)] = v[i] * w[i] / rms;
+  // One element quad (4 consecutive x values) of the planes, by the thread owning quad k.
+  // The four quads of a 16-element chunk sit on four consecutive lanes and share the chunk
+  // maximum by shuffles, so every lane of the warp must call this (ok = false: no quad).
+  // Chunk c: e = exponent of max|x| (max|x| < 2^e), X = round(x * 2^(23-e)) in (-2^23, 2^23),
+  // X = 65536*p0 + 256*p1 + p2.
+  GG_DEV void plane_quad(const XPlanes& P, int k, bool ok, const float* v) {
+    float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (!ok) return;
+    const int e = max((int)((__float_as_uint(mx) >> 23) & 255) - 126, -100);
+    const float s = __int_as_float((127 + 23 - e) << 23);
+    uint32_t b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      int X = __float2int_rn(v[j] * s);
+      X = min(max(X, -8388607), 8388607);
+      b0 |= (uint32_t)((X >> 16) & 255) << (8 * j);
+      b1 |= (uint32_t)((X >> 8) & 255) << (8 * j);
+      b2 |= (uint32_t)(X & 255) << (8 * j);
+    }
+    reinterpret_cast<uint32_t*>(P.p0)[k] = b0;
+    reinterpret_cast<uint32_t*>(P.p1)[k] = b1;
+    reinterpret_cast<uint32_t*>(P.p2)[k] = b2;
+    if ((k & 3) == 0) P.inv[k >> 2] = __int_as_float((127 - 23 + e) << 23);
   }
 
-  // out = base + v * w / rms(v)   (shaders.ts:386-418)
-  GG_DEV void norm_add(const float* v, const float* w, const float* base, float* out, int n) {
-    const GGModelDev& m = *x.m;
-    float ss = 0.f;
-    for (int i = tid; i < n; i += NCT) ss += v[i] * v[i];
-    ss = csum(ss, x.S.scal);
-    float rms = sqrtf(ss / (float)n + m.eps);
-    for (int i = tid; i < n; i += NCT) out[i] = base[i] + v[i] * w[i] / rms;
+  // Planes straight from n tagged words (no normalisation): phases C and E.
+  GG_DEV void planes_tagged(const XPlanes& P, const uint64_t* src, uint32_t tag, int n) {
+    const int nq = n >> 2;
+    for (int base = 0; base < nq; base += NCT) {
+      const int k = base + tid;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (k < nq) load4(src + 4 * k, tag, v);
+      plane_quad(P, k, k < nq, v);
+    }
   }
 
-  // hidden = residual + post_ffw_norm(down)  (the end of layer l, engine.ts:794)
-  GG_DEV void finish_layer(int l) {
+  // out = base + v * wa / r1, r1 = rms(v) (shaders.ts:386-418, v = tagged words), then the
+  // planes of out * wb / r2, r2 = rms(out) (shaders.ts:25-56). One barrier: the sums of v^2,
+  // base^2, base*v*wa and (v*wa)^2 give both norms. The weights are fetched before the wait
+  // on v. Thread t owns element quad t (hidden_size <= 4 * GG_NCT).
+  GG_DEV void add_norm_planes(const XPlanes& P, const uint64_t* src, uint32_t tag, const float* wa,
+                              const float* base, float* out, const float* wb, float* dbg_out, float* dbg_x) {
     const GGModelDev& m = *x.m;
-    gather(m.t_down, m.H, make_tag(x.tagbase, l * PH_PER_LAYER + 5), x.S.tmp, false);
-    cbar();
-    norm_add(x.S.tmp, m.layers[l].post_ffw_norm, x.S.res, x.S.hid, m.H);
-    cbar();
-    if (blockIdx.x == 0)
-      for (int i = tid; i < m.H; i += NCT) m.dbg_hidden[i] = x.S.hid[i];
+    const int nq = m.H >> 2, k = tid;
+    const bool ok = k < nq;
+    float4 fa = make_float4(0.f, 0.f, 0.f, 0.f), fb = fa, fbase = fa;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+      fa = __ldg(reinterpret_cast<const float4*>(wa) + k);
+      fb = __ldg(reinterpret_cast<const float4*>(wb) + k);
+      fbase = reinterpret_cast<const float4*>(base)[k];
+      load4(src + 4 * k, tag, v);
+    }
+    const float wav[4] = {fa.x, fa.y, fa.z, fa.w}, wbv[4] = {fb.x, fb.y, fb.z, fb.w};
+    const float bv[4] = {fbase.x, fbase.y, fbase.z, fbase.w};
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float vw = v[j] * wav[j];
+      s[0] += v[j] * v[j];
+      s[1] += bv[j] * bv[j];
+      s[2] += bv[j] * vw;
+      s[3] += vw * vw;
+    }
+    csum<4>(s);
+    const float r1 = sqrtf(s[0] / (float)m.H + m.eps);
+    const float ss_out = s[1] + 2.f * s[2] / r1 + s[3] / (r1 * r1);
+    const float r2 = sqrtf(ss_out / (float)m.H + m.eps);
+    float o[4], xv[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      o[j] = bv[j] + v[j] * wav[j] / r1;
+      xv[j] = o[j] * wbv[j] / r2;
+    }
+    if (ok) {
+      reinterpret_cast<float4*>(out)[k] = make_float4(o[0], o[1], o[2], o[3]);
+      if (dbg_out) reinterpret_cast<float4*>(dbg_out)[k] = make_float4(o[0], o[1], o[2], o[3]);
+      if (dbg_x) reinterpret_cast<float4*>(dbg_x)[k] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+    }
+    plane_quad(P, k, ok, xv);
   }
 
-  GG_DEV void embed() {
-    // shaders.ts:2-23: h[i] = q * d * sqrt(H), evaluated left to right in f32
+  // shaders.ts:2-23: h[i] = q * d * sqrt(H), evaluated left to right in f32; then the planes
+  // of rmsNorm(h) * wb.
+  GG_DEV void embed_planes(const XPlanes& P, const float* wb) {
     const GGModelDev& m = *x.m;
     const uint8_t* row = m.embd + (size_t)x.token * m.rs_h;
     const float sq = sqrtf((float)m.H);
-    for (int i = tid; i < m.H; i += NCT) {
-      float q = (float)(int8_t)row[i];
-      float d = __half2float(*reinterpret_cast<const __half*>(row + m.H + 2 * (i >> 5)));
-      float v = q * d;
-      x.S.hid[i] = v * sq;
+    const int nq = m.H >> 2, k = tid;
+    const bool ok = k < nq;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    float4 fb = make_float4(0.f, 0.f, 0.f, 0.f);
+    float s[1] = {0.f};
+    if (ok) {
+      fb = __ldg(reinterpret_cast<const float4*>(wb) + k);
+      const float d = __half2float(*reinterpret_cast<const __half*>(row + m.H + 2 * ((4 * k) >> 5)));
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float qv = (float)(int8_t)row[4 * k + j];
+        float vv = qv * d;
+        vv = vv * sq;
+        o[j] = vv;
+        s[0] += vv * vv;
+      }
+      reinterpret_cast<float4*>(x.S.hid)[k] = make_float4(o[0], o[1], o[2], o[3]);
     }
-    cbar();
+    csum<1>(s);
+    const float r = sqrtf(s[0] / (float)m.H + m.eps);
+    const float wbv[4] = {fb.x, fb.y, fb.z, fb.w};
+    float xv[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) xv[j] = o[j] * wbv[j] / r;
+    plane_quad(P, k, ok, xv);
+  }
+
+  // Epilogue of a matvec row: a tagged activation word, or an LM-head logit (+ its lane key).
+  enum { EPI_TAG = 0, EPI_LOGIT = 1 };
+  GG_DEV void epilogue(int kind, uint64_t* out, uint32_t tag, int row, float v) {
+    if (kind == EPI_TAG) {
+      tag_store(out + row, v, tag);
+    } else {
+      x.m->logits[row] = v;
+      if (!isnan(v)) {  // topk256 lane rule: strict '>' from (-1e30, 0), first index wins
+        unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - (uint32_t)row);
+        atomicMax(&x.S.keys[row & 255], k);
+      }
+    }
+  }
+
+  // Rows [rb, re) of one phase, rps whole rows per ring stage. A unit is 32/GS lane groups x
+  // R rows per lane, times one of ks K-slices. Units go round robin over the consumer warps.
+  // ks == 1: the epilogue runs on the lane holding a row's total. ks > 1: each slice partial
+  // goes to shared memory and the warp that completes a row's last slice sums the partials
+  // in slice order and runs the epilogue (no CTA barrier).
+  template <int GS, int R>
+  GG_DEV void rows_phase(const XPlanes& P, int rb, int re, int rps, int K, int rs, int ks, int kind, uint64_t* out,
+                         uint32_t tag) {
+    constexpr int UR = (32 / GS) * R;
+    const int nrows = re - rb, nch = K >> 4, cpk = nch / ks;
+    const int g = lane / GS, gl = lane % GS;
+    int ubase = 0;
+    for (int r0 = 0; r0 < nrows; r0 += rps) {
+      const uint8_t* stg = stage_acquire();
+      const int r1 = min(r0 + rps, nrows);
+      const int nunits = ((r1 - r0 + UR - 1) / UR) * ks;
+      for (int u = ubase + ((warp - ubase) % NCW + NCW) % NCW; u < ubase + nunits; u += NCW) {
+        const int lu = u - ubase, grp = lu / ks, sl = lu % ks;
+        const int rl = grp * UR + g * R;  // first row (within the stage) of this lane's rows
+        float v[R];
+        group_dot<GS, R>(stg + (size_t)rl * rs, rs, K, P, sl * cpk, (sl + 1) * cpk, gl, v);
+        if (ks == 1) {
+          if (gl == 0)
+#pragma unroll
+            for (int r = 0; r < R; r++)
+              if (r0 + rl + r < r1) epilogue(kind, out, tag, rb + r0 + rl + r, v[r]);
+        } else {
+          if (gl == 0)
+#pragma unroll
+            for (int r = 0; r < R; r++)
+              if (r0 + rl + r < r1) {
+                const int row = r0 + rl + r;
+                x.S.red[row * ks + sl] = v[r];
+                __threadfence_block();
+                if (atomicAdd(&x.S.rcnt[row], 1) == ks - 1) {
+                  __threadfence_block();
+                  float t = 0.f;
+                  for (int k = 0; k < ks; k++) t += *(volatile float*)&x.S.red[row * ks + k];
+                  x.S.rcnt[row] = 0;
+                  epilogue(kind, out, tag, rb + row, t);
+                }
+              }
+        }
+      }
+      ubase += nunits;
+      stage_release();
+    }
+  }
+
+  GG_DEV void rows_dispatch(const XPlanes& P, const GGPhaseCfg& pc, int rb, int re, int K, int rs, int kind,
+                            uint64_t* out, uint32_t tag) {
+    if (pc.gs == 8) rows_phase<8, 1>(P, rb, re, pc.rps, K, rs, pc.ks, kind, out, tag);
+    else rows_phase<16, 1>(P, rb, re, pc.rps, K, rs, pc.ks, kind, out, tag);
   }
 
   GG_DEV void phase_qkv(int l) {
     const GGModelDev& m = *x.m;
-    if (l == 0) embed();
-    else finish_layer(l - 1);
-    norm_to_xs(x.S.hid, m.layers[l].attn_norm, m.H);
+    const XPlanes& P = x.S.xp[0];
+    if (l == 0) {
+      embed_planes(P, m.layers[0].attn_norm);
+    } else {  // hidden = residual + post_ffw_norm(down) (engine.ts:794), attn rmsNorm (768)
+      add_norm_planes(P, m.t_down, make_tag(x.tagbase, (l - 1) * PH_PER_LAYER + 5), m.layers[l - 1].post_ffw_norm,
+                      x.S.res, x.S.hid, m.layers[l].attn_norm, blockIdx.x == 0 ? m.dbg_hidden : nullptr, nullptr);
+    }
     cbar();
+    trace(l * 6 + 0, 1);
     int b, e;
     part(m.Q + 2 * m.KV, m.grid, blockIdx.x, b, e);
-    const uint32_t tag = make_tag(x.tagbase, l * PH_PER_LAYER + 0);
-    uint64_t* out = m.t_qkv;
-    rows_ks1(b, e, m.rps_h, m.H, m.rs_h, [&](int row, float v) {
-      if (lane == 0) tag_store(out + row, v, tag);
-    });
+    rows_dispatch(P, m.ph_qkv, b, e, m.H, m.rs_h, EPI_TAG, m.t_qkv, make_tag(x.tagbase, l * PH_PER_LAYER + 0));
   }
 
+  // q/k per-head RMSNorm + RoPE (shaders.ts:420-467), the KV store (shaders.ts:209-227) and a
+  // split of the attention (shaders.ts:229-325) with local softmax statistics. One warp per
+  // head: lane l holds elements l + 32j of its head, so the RoPE pair (i, i + HD/2) is in one
+  // lane and nothing needs a barrier except handing the heads to the split loop.
   GG_DEV void phase_attn(int l) {
     const GGModelDev& m = *x.m;
     const int G = m.grid, c = blockIdx.x, rot = (l * x.nsplit) % G;
     int s = (c - rot + G) % G;
     if (s >= x.nsplit) return;
     const int Q = m.Q, KV = m.KV, HD = m.HD, NQH = m.NQH, NKH = m.NKH, PPS = m.pos_per_split;
+    constexpr int NJ = GG_HEAD_DIM / 32;  // elements per lane of a head
     const GGLayerW& Lw = m.layers[l];
     float* t = x.S.tmp;  // q [Q] | k [KV] | v [KV]
-    cbar();              // tmp may still be read by a slow warp of the previous phase prologue
-    gather(m.t_qkv, Q + 2 * KV, make_tag(x.tagbase, l * PH_PER_LAYER + 0), t, false);
-    // RoPE table for this position (shaders.ts:457-460)
-    for (int i = tid; i < HD / 2; i += NCT) {
-      float freq = 1.0f / powf(Lw.theta, (float)(i * 2) / (float)HD);
-      float ang = (float)x.pos * freq;
-      x.S.cs[i] = cosf(ang);
-      x.S.cs[HD / 2 + i] = sinf(ang);
-    }
-    cbar();
-    // per-head RMSNorm of q heads and k heads (shaders.ts:433-452)
+    const uint32_t tagA = make_tag(x.tagbase, l * PH_PER_LAYER + 0);
     const int nh = NQH + NKH;
-    for (int h = warp; h < nh; h += NCW) {
-      const float* d = t + h * HD;
-      float ss = 0.f;
-      for (int i = lane; i < HD; i += 32) ss += d[i] * d[i];
-      ss = warp_sum(ss);
-      if (lane == 0) x.S.scal[64 + h] = sqrtf(ss / (float)HD + m.eps);
+    for (int h = warp; h < nh + NKH; h += NCW) {
+      const uint64_t* src = m.t_qkv + h * HD;
+      uint64_t w[NJ];
+#pragma unroll
+      for (int j = 0; j < NJ; j++) w[j] = tag_load(src + lane + 32 * j);
+      float v[NJ];
+#pragma unroll
+      for (int j = 0; j < NJ; j++)
+        v[j] = ((uint32_t)(w[j] >> 32) == tagA) ? __uint_as_float((uint32_t)w[j]) : tag_wait(src + lane + 32 * j, tagA, x.sc);
+      if (h < nh) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) ss += v[j] * v[j];
+        const float rms = sqrtf(warp_sum(ss) / (float)HD + m.eps);
+        const float* nw = h < NQH ? Lw.q_norm : Lw.k_norm;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) v[j] = v[j] * nw[lane + 32 * j] / rms;
+#pragma unroll
+        for (int j = 0; j < NJ / 2; j++) {
+          const int i = lane + 32 * j;
+          const float freq = 1.0f / powf(Lw.theta, (float)(i * 2) / (float)HD);
+          const float ang = (float)x.pos * freq;
+          const float cs = cosf(ang), sn = sinf(ang);
+          const float x0 = v[j], x1 = v[j + NJ / 2];
+          v[j] = x0 * cs - x1 * sn;
+          v[j + NJ / 2] = x0 * sn + x1 * cs;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NJ; j++) t[h * HD + lane + 32 * j] = v[j];
     }
     cbar();
-    for (int i = tid; i < nh * HD; i += NCT) {
-      int h = i / HD, dd = i % HD;
-      const float* w = h < NQH ? Lw.q_norm : Lw.k_norm;
-      t[i] = t[i] * w[dd] / x.S.scal[64 + h];
-    }
-    cbar();
-    // RoPE of pairs (i, i + HD/2) (shaders.ts:454-466)
-    for (int i = tid; i < nh * (HD / 2); i += NCT) {
-      int h = i / (HD / 2), k = i % (HD / 2);
-      float* d = t + h * HD;
-      float cs = x.S.cs[k], sn = x.S.cs[HD / 2 + k];
-      float x0 = d[k], x1 = d[k + HD / 2];
-      d[k] = x0 * cs - x1 * sn;
-      d[k + HD / 2] = x0 * sn + x1 * cs;
-    }
-    cbar();
+    trace(l * 6 + 1, 1);
     const uint32_t tag = make_tag(x.tagbase, l * PH_PER_LAYER + 1);
     for (; s < x.nsplit; s += G) {
       const int p0 = s * PPS, p1 = min(p0 + PPS, x.pos + 1), np = p1 - p0;
       const uint8_t* stg = stage_acquire();
       const float* Kst = reinterpret_cast<const float*>(stg);
       const float* Vst = reinterpret_cast<const float*>(stg + (size_t)PPS * KV * 4);
-      if (p1 == x.pos + 1) {  // this split owns the new position: store it (shaders.ts:209-227)
-        size_t off = (size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + x.pos) * KV;
+      if (p1 == x.pos + 1) {  // this split owns the new position: store it
+        const size_t off = (size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + x.pos) * KV;
         for (int i = tid; i < KV; i += NCT) {
           m.kcache[off + i] = t[Q + i];
           m.vcache[off + i] = t[Q + KV + i];
         }
       }
-      // scores (shaders.ts:229-252)
-      for (int pr = warp; pr < NQH * np; pr += NCW) {
-        int h = pr / np, j = pr % np, kvh = h * NKH / NQH;
-        const float* kr = (p0 + j < x.pos) ? Kst + (size_t)j * KV + kvh * HD : t + Q + kvh * HD;
-        const float* qh = t + h * HD;
-        float d = 0.f;
-        for (int i = lane; i < HD; i += 32) d = fmaf(qh[i], kr[i], d);
-        d = warp_sum(d);
-        if (lane == 0) x.S.sc[h * PPS + j] = d * m.attn_scale;
-      }
-      cbar();
-      if (tid < NQH) {  // local softmax statistics of this split
-        int h = tid;
+      for (int h = warp; h < NQH; h += NCW) {
+        const int kvh = h * NKH / NQH;
+        float qv[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; j++) qv[j] = t[h * HD + lane + 32 * j];
+        float sc[GG_POS_PER_SPLIT];
         float mx = -1e30f;
-        for (int j = 0; j < np; j++) mx = fmaxf(mx, x.S.sc[h * PPS + j]);
+#pragma unroll
+        for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+          sc[p] = 0.f;
+          if (p < np) {
+            const float* kr = (p0 + p < x.pos) ? Kst + (size_t)p * KV + kvh * HD : t + Q + kvh * HD;
+            float d = 0.f;
+#pragma unroll
+            for (int j = 0; j < NJ; j++) d = fmaf(qv[j], kr[lane + 32 * j], d);
+            sc[p] = warp_sum(d) * m.attn_scale;
+            mx = fmaxf(mx, sc[p]);
+          }
+        }
         float sum = 0.f;
-        for (int j = 0; j < np; j++) {
-          float ev = expf(x.S.sc[h * PPS + j] - mx);
-          x.S.sc[h * PPS + j] = ev;
-          sum += ev;
+#pragma unroll
+        for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+          sc[p] = p < np ? expf(sc[p] - mx) : 0.f;
+          sum += sc[p];
         }
-        tag_store(m.t_ml + ((size_t)s * NQH + h) * 2 + 0, mx, tag);
-        tag_store(m.t_ml + ((size_t)s * NQH + h) * 2 + 1, sum, tag);
-      }
-      cbar();
-      for (int o = tid; o < NQH * HD; o += NCT) {  // (shaders.ts:302-325)
-        int h = o / HD, dd = o % HD, kvh = h * NKH / NQH;
-        float acc = 0.f;
-        for (int j = 0; j < np; j++) {
-          const float* vr = (p0 + j < x.pos) ? Vst + (size_t)j * KV : t + Q + KV;
-          acc = fmaf(x.S.sc[h * PPS + j], vr[kvh * HD + dd], acc);
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+          const int dd = lane + 32 * j;
+          float acc = 0.f;
+#pragma unroll
+          for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+            if (p < np) {
+              const float* vr = (p0 + p < x.pos) ? Vst + (size_t)p * KV : t + Q + KV;
+              acc = fmaf(sc[p], vr[kvh * HD + dd], acc);
+            }
+          }
+          tag_store(m.t_o + (size_t)s * Q + h * HD + dd, acc, tag);
         }
-        tag_store(m.t_o + (size_t)s * Q + o, acc, tag);
+        if (lane == 0) {
+          tag_store(m.t_ml + ((size_t)s * NQH + h) * 2 + 0, mx, tag);
+          tag_store(m.t_ml + ((size_t)s * NQH + h) * 2 + 1, sum, tag);
+        }
       }
       stage_release();
-      cbar();
     }
   }
 
+  // Merge of the attention splits (online softmax): one warp per output dimension. Every
+  // lane loads the (max, sum, value) triples of its splits in one batch; every warp recomputes
+  // the head's global max and denominator itself, so no barrier is needed.
   GG_DEV void phase_combine(int l) {
     const GGModelDev& m = *x.m;
     const int Q = m.Q, HD = m.HD, NQH = m.NQH, DPC = m.dims_per_comb;
     const uint32_t tagB = make_tag(x.tagbase, l * PH_PER_LAYER + 1);
     const uint32_t tagC = make_tag(x.tagbase, l * PH_PER_LAYER + 2);
-    float* cm = x.S.cmb;
-    float* cl = cm + m.max_splits;
-    float* cw = cl + m.max_splits;
+    constexpr int SPL = 4;  // splits per lane per batch
     for (int cc = blockIdx.x; cc < m.ncomb; cc += m.grid) {
       const int d0 = cc * DPC, h = d0 / HD;
-      for (int s = tid; s < x.nsplit; s += NCT) {
-        cm[s] = tag_wait(m.t_ml + ((size_t)s * NQH + h) * 2 + 0, tagB, x.sc);
-        cl[s] = tag_wait(m.t_ml + ((size_t)s * NQH + h) * 2 + 1, tagB, x.sc);
-      }
-      cbar();
-      if (warp == 0) {
-        float mx = -INFINITY;
-        for (int s = lane; s < x.nsplit; s += 32) mx = fmaxf(mx, cm[s]);
-        mx = warp_max(mx);
-        float lsum = 0.f;
-        for (int s = lane; s < x.nsplit; s += 32) {
-          float w = expf(cm[s] - mx);
-          cw[s] = w;
-          lsum = fmaf(w, cl[s], lsum);
-        }
-        lsum = warp_sum(lsum);
-        if (lane == 0) x.S.scal[127] = lsum;
-      }
-      cbar();
-      const float inv = 1.0f / x.S.scal[127];
       for (int k = warp; k < DPC; k += NCW) {
         const int d = d0 + k;
-        float acc = 0.f;
-        for (int s = lane; s < x.nsplit; s += 32)
-          acc = fmaf(cw[s], tag_wait(m.t_o + (size_t)s * Q + d, tagB, x.sc), acc);
-        acc = warp_sum(acc);
-        if (lane == 0) tag_store(m.t_att + d, acc * inv, tagC);
+        float mx = -INFINITY, lsum = 0.f, acc = 0.f;
+        for (int s0 = 0; s0 < x.nsplit; s0 += 32 * SPL) {
+          uint64_t wm[SPL], wl[SPL], wo[SPL];
+#pragma unroll
+          for (int q = 0; q < SPL; q++) {
+            const int s = s0 + q * 32 + lane;
+            if (s < x.nsplit) {
+              wm[q] = tag_load(m.t_ml + ((size_t)s * NQH + h) * 2);
+              wl[q] = tag_load(m.t_ml + ((size_t)s * NQH + h) * 2 + 1);
+              wo[q] = tag_load(m.t_o + (size_t)s * Q + d);
+            }
+          }
+          float fm[SPL], fl[SPL], fo[SPL];
+#pragma unroll
+          for (int q = 0; q < SPL; q++) {
+            const int s = s0 + q * 32 + lane;
+            fm[q] = -INFINITY; fl[q] = 0.f; fo[q] = 0.f;
+            if (s < x.nsplit) {
+              const uint64_t* pm = m.t_ml + ((size_t)s * NQH + h) * 2;
+              fm[q] = ((uint32_t)(wm[q] >> 32) == tagB) ? __uint_as_float((uint32_t)wm[q]) : tag_wait(pm, tagB, x.sc);
+              fl[q] = ((uint32_t)(wl[q] >> 32) == tagB) ? __uint_as_float((uint32_t)wl[q]) : tag_wait(pm + 1, tagB, x.sc);
+              fo[q] = ((uint32_t)(wo[q] >> 32) == tagB) ? __uint_as_float((uint32_t)wo[q])
+                                                         : tag_wait(m.t_o + (size_t)s * Q + d, tagB, x.sc);
+            }
+          }
+          // rescale the running (max, sums) to include this batch (online softmax merge)
+          float bm = -INFINITY;
+#pragma unroll
+          for (int q = 0; q < SPL; q++) bm = fmaxf(bm, fm[q]);
+          const float nm = fmaxf(mx, bm);
+          const float sc0 = (mx == -INFINITY) ? 0.f : expf(mx - nm);
+          lsum *= sc0;
+          acc *= sc0;
+#pragma unroll
+          for (int q = 0; q < SPL; q++) {
+            if (fm[q] != -INFINITY) {
+              const float w = expf(fm[q] - nm);
+              lsum = fmaf(w, fl[q], lsum);
+              acc = fmaf(w, fo[q], acc);
+            }
+          }
+          mx = nm;
+        }
+        // merge lanes: global max, then rescale each lane's sums
+        const float gm = warp_max(mx);
+        const float f = (mx == -INFINITY) ? 0.f : expf(mx - gm);
+        lsum = warp_sum(lsum * f);
+        acc = warp_sum(acc * f);
+        if (lane == 0) tag_store(m.t_att + d, acc / lsum, tagC);
       }
-      cbar();
     }
   }
 
   GG_DEV void phase_o(int l) {
     const GGModelDev& m = *x.m;
-    cbar();  // x vector is about to be overwritten
-    gather(m.t_att, m.Q, make_tag(x.tagbase, l * PH_PER_LAYER + 2), x.S.xs, true);
+    const XPlanes& P = x.S.xp[1];
+    planes_tagged(P, m.t_att, make_tag(x.tagbase, l * PH_PER_LAYER + 2), m.Q);
     cbar();
+    trace(l * 6 + 3, 1);
     int b, e;
     part(m.H, m.grid, blockIdx.x, b, e);
-    const uint32_t tag = make_tag(x.tagbase, l * PH_PER_LAYER + 3);
-    uint64_t* out = m.t_proj;
-    if (m.ks_o > 1)
-      rows_ksn(b, e, m.rps_q, m.Q, m.rs_q, m.ks_o, [&](int row, float v) { tag_store(out + row, v, tag); });
-    else
-      rows_ks1(b, e, m.rps_q, m.Q, m.rs_q, [&](int row, float v) {
-        if (lane == 0) tag_store(out + row, v, tag);
-      });
+    rows_dispatch(P, m.ph_o, b, e, m.Q, m.rs_q, EPI_TAG, m.t_proj, make_tag(x.tagbase, l * PH_PER_LAYER + 3));
   }
 
   GG_DEV void phase_ffn_up(int l) {
     const GGModelDev& m = *x.m;
     const GGLayerW& Lw = m.layers[l];
-    gather(m.t_proj, m.H, make_tag(x.tagbase, l * PH_PER_LAYER + 3), x.S.tmp, false);
+    const XPlanes& P = x.S.xp[0];
+    // residual = hidden + post_attention_norm(proj) (engine.ts:785), then ffn rmsNorm (786)
+    add_norm_planes(P, m.t_proj, make_tag(x.tagbase, l * PH_PER_LAYER + 3), Lw.post_attn_norm, x.S.hid, x.S.res,
+                    Lw.ffn_norm, blockIdx.x == 0 ? m.dbg_residual : nullptr, nullptr);
     cbar();
-    // residual = hidden + post_attention_norm(proj)  (engine.ts:785)
-    norm_add(x.S.tmp, Lw.post_attn_norm, x.S.hid, x.S.res, m.H);
-    cbar();
-    if (blockIdx.x == 0)
-      for (int i = tid; i < m.H; i += NCT) m.dbg_residual[i] = x.S.res[i];
-    norm_to_xs(x.S.res, Lw.ffn_norm, m.H);  // engine.ts:786
-    cbar();
+    trace(l * 6 + 4, 1);
     int b, e;
     part(m.I, m.grid, blockIdx.x, b, e);
     const uint32_t tag = make_tag(x.tagbase, l * PH_PER_LAYER + 4);
-    const int npair = e - b, pps = m.pps_gu, rs = m.rs_h;
+    // gate_i and up_i are adjacent rows: with 8 lanes per row and 2 rows per lane, one lane
+    // holds both sums of a pair and applies GeGLU itself (shaders.ts:153-170).
+    const int npair = e - b, pps = m.pps_gu, rs = m.rs_h, nch = m.H >> 4;
+    const int g = lane >> 3, gl = lane & 7;
+    int ubase = 0;
     for (int q0 = 0; q0 < npair; q0 += pps) {
       const uint8_t* stg = stage_acquire();
       const int q1 = min(q0 + pps, npair);
-      for (int u = q0 + ((warp - q0) % NCW + NCW) % NCW; u < q1; u += NCW) {
-        const uint8_t* rg = stg + (size_t)(2 * (u - q0)) * rs;
-        float g, up;
-        row_dot2(rg, rg + rs, m.H, x.S.xs4, lane, g, up);
-        if (lane == 0) tag_store(m.t_act + b + u, gelu_tanh(g) * up, tag);  // shaders.ts:153-170
+      const int nunits = (q1 - q0 + 3) / 4;  // 4 pairs per warp unit
+      const int u_first = ((warp - ubase) % NCW + NCW) % NCW;
+      ubase += nunits;
+      for (int u = u_first; u < nunits; u += NCW) {
+        const int pr = 4 * u + g;  // pair within the stage
+        float v[2];
+        group_dot<8, 2>(stg + (size_t)(2 * pr) * rs, rs, m.H, P, 0, nch, gl, v);
+        if (gl == 0 && q0 + pr < q1) tag_store(m.t_act + b + q0 + pr, gelu_tanh(v[0]) * v[1], tag);
       }
       stage_release();
     }
@@ -507,50 +731,50 @@ struct Consumer {
 
   GG_DEV void phase_down(int l) {
     const GGModelDev& m = *x.m;
+    const XPlanes& P = x.S.xp[1];
+    planes_tagged(P, m.t_act, make_tag(x.tagbase, l * PH_PER_LAYER + 4), m.I);
     cbar();
-    gather(m.t_act, m.I, make_tag(x.tagbase, l * PH_PER_LAYER + 4), x.S.xs, true);
-    cbar();
+    trace(l * 6 + 5, 1);
     int b, e;
     part(m.H, m.grid, blockIdx.x, b, e);
-    const uint32_t tag = make_tag(x.tagbase, l * PH_PER_LAYER + 5);
-    uint64_t* out = m.t_down;
-    if (m.ks_down > 1)
-      rows_ksn(b, e, m.rps_i, m.I, m.rs_i, m.ks_down, [&](int row, float v) { tag_store(out + row, v, tag); });
-    else
-      rows_ks1(b, e, m.rps_i, m.I, m.rs_i, [&](int row, float v) {
-        if (lane == 0) tag_store(out + row, v, tag);
-      });
+    rows_dispatch(P, m.ph_down, b, e, m.I, m.rs_i, EPI_TAG, m.t_down, make_tag(x.tagbase, l * PH_PER_LAYER + 5));
   }
 
   GG_DEV void phase_lm() {
     const GGModelDev& m = *x.m;
-    if (x.mode & GG_RUN_LAYERS) {
-      finish_layer(m.L - 1);
-    } else {  // LM head on the state a previous launch left behind
-      for (int i = tid; i < m.H; i += NCT) x.S.hid[i] = m.dbg_hidden[i];
-      cbar();
-    }
-    norm_to_xs(x.S.hid, m.out_norm, m.H);  // engine.ts:797-801
+    const XPlanes& P = x.S.xp[0];
     for (int i = tid; i < 256; i += NCT) x.S.keys[i] = init_lane_key();
-    cbar();
-    if (blockIdx.x == 0)
-      for (int i = tid; i < m.H; i += NCT) {
-        m.dbg_normed[i] = x.S.xs[xs_index(i)];
-        m.dbg_hidden[i] = x.S.hid[i];
+    if (x.mode & GG_RUN_LAYERS) {  // hidden = residual + post_ffw_norm(down), final rmsNorm (engine.ts:797-801)
+      add_norm_planes(P, m.t_down, make_tag(x.tagbase, (m.L - 1) * PH_PER_LAYER + 5), m.layers[m.L - 1].post_ffw_norm,
+                      x.S.res, x.S.hid, m.out_norm, blockIdx.x == 0 ? m.dbg_hidden : nullptr,
+                      blockIdx.x == 0 ? m.dbg_normed : nullptr);
+    } else {  // LM head on the hidden state a previous launch left behind
+      const int nq = m.H >> 2, k = tid;
+      const bool ok = k < nq;
+      float h[4] = {0.f, 0.f, 0.f, 0.f};
+      float4 fw = make_float4(0.f, 0.f, 0.f, 0.f);
+      float s[1] = {0.f};
+      if (ok) {
+        const float4 f = reinterpret_cast<const float4*>(m.dbg_hidden)[k];
+        fw = __ldg(reinterpret_cast<const float4*>(m.out_norm) + k);
+        h[0] = f.x; h[1] = f.y; h[2] = f.z; h[3] = f.w;
+#pragma unroll
+        for (int j = 0; j < 4; j++) s[0] += h[j] * h[j];
+        reinterpret_cast<float4*>(x.S.hid)[k] = f;
       }
+      csum<1>(s);
+      const float r = sqrtf(s[0] / (float)m.H + m.eps);
+      const float wv[4] = {fw.x, fw.y, fw.z, fw.w};
+      float xv[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) xv[j] = h[j] * wv[j] / r;
+      if (ok && blockIdx.x == 0) reinterpret_cast<float4*>(m.dbg_normed)[k] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+      plane_quad(P, k, ok, xv);
+    }
+    cbar();
     int b, e;
     part(m.V, m.grid, blockIdx.x, b, e);
-    float* logits = m.logits;
-    unsigned long long* keys = x.S.keys;
-    rows_ks1(b, e, m.rps_h, m.H, m.rs_h, [&](int row, float v) {
-      if (lane == 0) {
-        logits[row] = v;
-        if (!isnan(v)) {  // topk256 lane rule: strict '>' from (-1e30, 0), first index wins
-          unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - (uint32_t)row);
-          atomicMax(&keys[row & 255], k);
-        }
-      }
-    });
+    rows_dispatch(P, m.ph_lm, b, e, m.H, m.rs_h, EPI_LOGIT, nullptr, 0);
     cbar();
     const unsigned long long ik = init_lane_key();
     for (int i = tid; i < 256; i += NCT)
@@ -559,20 +783,40 @@ struct Consumer {
 
   GG_DEV void run() {
     const GGModelDev& m = *x.m;
+    for (int i = tid; i < 256; i += NCT) x.S.rcnt[i] = 0;
+    cbar();
     if (x.mode & GG_RUN_LAYERS) {
       for (int l = 0; l < m.L; l++) {
+        trace(l * 6 + 0, 0);
         phase_qkv(l);
+        trace(l * 6 + 0, 2);
+        trace(l * 6 + 1, 0);
         phase_attn(l);
+        trace(l * 6 + 1, 2);
+        trace(l * 6 + 2, 0);
         phase_combine(l);
+        trace(l * 6 + 2, 2);
+        trace(l * 6 + 3, 0);
         phase_o(l);
+        trace(l * 6 + 3, 2);
+        trace(l * 6 + 4, 0);
         phase_ffn_up(l);
+        trace(l * 6 + 4, 2);
+        trace(l * 6 + 5, 0);
         phase_down(l);
+        trace(l * 6 + 5, 2);
       }
-      if (!(x.mode & GG_RUN_LM)) {  // leave hidden/residual for a later LM-head launch
-        finish_layer(m.L - 1);
+      if (!(x.mode & GG_RUN_LM)) {  // leave the hidden state for a later LM-head launch
+        add_norm_planes(x.S.xp[0], m.t_down, make_tag(x.tagbase, (m.L - 1) * PH_PER_LAYER + 5),
+                        m.layers[m.L - 1].post_ffw_norm, x.S.res, x.S.hid, m.out_norm,
+                        blockIdx.x == 0 ? m.dbg_hidden : nullptr, nullptr);
       }
     }
-    if (x.mode & GG_RUN_LM) phase_lm();
+    if (x.mode & GG_RUN_LM) {
+      trace(m.L * 6, 0);
+      phase_lm();
+      trace(m.L * 6, 2);
+    }
   }
 };
 
@@ -702,21 +946,25 @@ extern "C" __global__ void __launch_bounds__(GG_NTHREADS, 1)
   x.sc.err = &st->error;
   x.sc.timeout_ns = st->timeout_ns;
   x.idx = 0;
-  // carve shared memory
+  // carve shared memory (sizes: GGModelDev::smem_bytes, computed by the host the same way)
   uint8_t* p = smem;
   x.S.ring = p; p += (size_t)m.nstages * m.stage_bytes;
   x.S.full = reinterpret_cast<uint64_t*>(p); p += 8 * m.nstages;
   x.S.empty = reinterpret_cast<uint64_t*>(p); p += 8 * m.nstages;
   x.S.keys = reinterpret_cast<unsigned long long*>(p); p += 8 * 256;
-  x.S.xs4 = reinterpret_cast<float4*>(p); x.S.xs = reinterpret_cast<float*>(p); p += 4 * (size_t)m.xs_floats;
+  const int xsz[2] = {m.xs0, m.xs1};
+  for (int b = 0; b < 2; b++) {
+    x.S.xp[b].p0 = p; p += xsz[b];
+    x.S.xp[b].p1 = p; p += xsz[b];
+    x.S.xp[b].p2 = p; p += xsz[b];
+    x.S.xp[b].inv = reinterpret_cast<float*>(p); p += xsz[b] / 4;
+  }
   x.S.hid = reinterpret_cast<float*>(p); p += 4 * (size_t)m.H;
   x.S.res = reinterpret_cast<float*>(p); p += 4 * (size_t)m.H;
   x.S.tmp = reinterpret_cast<float*>(p); p += 4 * (size_t)m.tmp_floats;
-  x.S.cs = reinterpret_cast<float*>(p); p += 4 * (size_t)m.HD;
   x.S.red = reinterpret_cast<float*>(p); p += 4 * 1024;
-  x.S.sc = reinterpret_cast<float*>(p); p += 4 * (size_t)(m.NQH * m.pos_per_split + 32);
-  x.S.cmb = reinterpret_cast<float*>(p); p += 4 * (size_t)(3 * m.max_splits);
-  x.S.scal = reinterpret_cast<float*>(p); p += 4 * 128;
+  x.S.rcnt = reinterpret_cast<int*>(p); p += 4 * 256;
+  x.S.scal = reinterpret_cast<float*>(p); p += 4 * 256;  // 4 rotating csum slots of up to 64
   x.S.flag = reinterpret_cast<int*>(p); p += 16;
 
   const bool bad = x.token < 0 || x.token >= m.V || x.pos < 0 || x.pos >= m.CTX || x.seq < 0 || x.seq >= m.max_seqs;

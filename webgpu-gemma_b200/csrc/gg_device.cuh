@@ -89,19 +89,29 @@ struct SpinCtl {
   uint64_t timeout_ns;  // give up after this long
 };
 
+// How long a wait spins before it starts looking at the global error word. Normal waits are
+// far shorter; reading one global word from every waiting warp of every SM would turn that
+// word's L2 line into a hot spot.
+#define GG_QUIET_SPIN_NS 20000ull
+
 // Wait for a tagged word; on timeout (or an error raised elsewhere) return 0.0f and set err.
+// Polls back off with __nanosleep so waiting warps do not flood L2 with loads.
 GG_DEV float tag_wait(const uint64_t* p, uint32_t tag, const SpinCtl& sc) {
   uint64_t w = tag_load(p);
   if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
-  uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
+    __nanosleep(it < 8 ? 32 : 128);
     w = tag_load(p);
     if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
-    if ((it & 63u) == 0) {
-      if (*(volatile uint32_t*)sc.err) return 0.0f;
-      if (global_timer_ns() - t0 > sc.timeout_ns) {
-        atomicOr(sc.err, GG_ERR_WAIT_FLAG);
-        return 0.0f;
+    if ((it & 15u) == 0) {
+      const uint64_t dt = global_timer_ns() - t0;
+      if (dt > GG_QUIET_SPIN_NS) {
+        if (*(volatile uint32_t*)sc.err) return 0.0f;
+        if (dt > sc.timeout_ns) {
+          atomicOr(sc.err, GG_ERR_WAIT_FLAG);
+          return 0.0f;
+        }
       }
     }
   }
@@ -110,14 +120,17 @@ GG_DEV float tag_wait(const uint64_t* p, uint32_t tag, const SpinCtl& sc) {
 // Bounded wait on an mbarrier phase. Returns false (and sets err) on timeout.
 GG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const SpinCtl& sc) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = global_timer_ns();
+  const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 15u) == 0) {
-      if (*(volatile uint32_t*)sc.err) return false;
-      if (global_timer_ns() - t0 > sc.timeout_ns) {
-        atomicOr(sc.err, GG_ERR_WAIT_MBAR);
-        return false;
+      const uint64_t dt = global_timer_ns() - t0;
+      if (dt > GG_QUIET_SPIN_NS) {
+        if (*(volatile uint32_t*)sc.err) return false;
+        if (dt > sc.timeout_ns) {
+          atomicOr(sc.err, GG_ERR_WAIT_MBAR);
+          return false;
+        }
       }
     }
   }
@@ -174,6 +187,18 @@ GG_DEV uint32_t f32_order_key(float f) {
 GG_DEV float f32_from_order_key(uint32_t k) {
   uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
   return __uint_as_float(u);
+}
+
+// dp4a with a signed first operand and a signed / unsigned second operand.
+GG_DEV int dp4a_ss(int a, int b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+GG_DEV int dp4a_su(int a, int b, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
 // Swizzled float4 slot of logical x element chunk c (16 elements = 4 float4), sub-slot i.

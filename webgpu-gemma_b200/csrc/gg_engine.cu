@@ -91,6 +91,7 @@ struct gg_engine {
   int ring_cap = 0;
   int32_t* h_ring = nullptr;  // pinned
   int last_hidden_seq = -1;
+  int trace_on = 0;
   uint64_t timeout_ns = 1000000000ull;
   float last_ms = 0.f;
   std::string err;
@@ -204,32 +205,47 @@ static int schedule(gg_engine* e) {
   const gg_config& c = e->cfg;
   m.grid = e->sm_count;
   m.stage_bytes = 20480;
-  if (m.rs_i > m.stage_bytes || m.rs_q > m.stage_bytes || 2 * m.rs_h > m.stage_bytes)
+  if (m.rs_i > m.stage_bytes || m.rs_q > m.stage_bytes || 4 * m.rs_h > m.stage_bytes)
     return fail(e, GG_E_ARG, "rows too wide for a %d-byte ring stage", m.stage_bytes);
-  m.rps_h = m.stage_bytes / m.rs_h;
-  m.rps_q = m.stage_bytes / m.rs_q;
-  m.rps_i = m.stage_bytes / m.rs_i;
-  m.pps_gu = m.stage_bytes / (2 * m.rs_h);
-  m.pos_per_split = std::min(8, m.stage_bytes / (8 * m.KV));
-  if (m.pos_per_split < 1) return fail(e, GG_E_ARG, "kv_dim too large for a ring stage");
+  m.pps_gu = (m.stage_bytes / (2 * m.rs_h)) / 4 * 4;  // whole 4-pair warp units
+  // lanes per row and K-slices: 8 lanes per row when a stage holds 4+ rows, else 16, else 32;
+  // K-slices give every consumer warp a unit on the short phases.
+  auto pick = [&](int M, int K, int rs, bool split, int r) {
+    GGPhaseCfg p{};
+    const int cap = m.stage_bytes / rs;
+    p.gs = cap >= 4 * r ? 8 : 16;
+    p.r = r;
+    const int ur = (32 / p.gs) * r;
+    p.rps = (cap / ur) * ur;
+    if (p.rps < 1) { p.gs = 16; p.r = 1; p.rps = (cap / 2) * 2; }
+    const int nch = K / 16;
+    const int rows = (M + m.grid - 1) / m.grid;
+    const int units = (rows + ur - 1) / ur;
+    p.ks = 1;
+    if (split)
+      for (int ks = 2; ks <= 16; ks++)
+        if (nch % ks == 0 && (nch / ks) % p.gs == 0 && units * ks <= GG_NCW && rows * ks <= 1024) p.ks = ks;
+    return p;
+  };
+  m.ph_qkv = pick(m.Q + 2 * m.KV, m.H, m.rs_h, true, 1);
+  m.ph_o = pick(m.H, m.Q, m.rs_q, true, 1);
+  m.ph_down = pick(m.H, m.I, m.rs_i, true, 1);
+  m.ph_lm = pick(m.V, m.H, m.rs_h, false, 1);
+  if (m.pps_gu < 4 || m.rs_i > m.stage_bytes) return fail(e, GG_E_ARG, "rows too wide for a %d-byte ring stage", m.stage_bytes);
+  if (m.H / 4 > GG_NCT) return fail(e, GG_E_ARG, "hidden_size above %d", 4 * GG_NCT);
+  if (m.HD != GG_HEAD_DIM) return fail(e, GG_E_ARG, "head_dim must be %d (Gemma 3)", GG_HEAD_DIM);
+  m.pos_per_split = GG_POS_PER_SPLIT;
+  if (2 * GG_POS_PER_SPLIT * m.KV * 4 > m.stage_bytes) return fail(e, GG_E_ARG, "kv_dim too large for a ring stage");
   m.max_splits = (m.CTX + m.pos_per_split - 1) / m.pos_per_split;
   m.dims_per_comb = 8;
   if (m.HD % m.dims_per_comb) return fail(e, GG_E_ARG, "head_dim must be a multiple of 8");
   m.ncomb = m.Q / m.dims_per_comb;
-  // K-splits: enough units for every consumer warp on the short O / down phases
-  auto pick_ks = [&](int K) {
-    int rows = (m.H + m.grid - 1) / m.grid;
-    int nch = K / 16, ks = 1;
-    while (ks < 8 && rows * ks < GG_NCW && nch % (ks * 2) == 0) ks *= 2;
-    while (rows * ks > 1024) ks /= 2;
-    return ks;
-  };
-  m.ks_o = pick_ks(m.Q);
-  m.ks_down = pick_ks(m.I);
-  m.xs_floats = (std::max(std::max(m.H, m.Q), m.I) + 15) / 16 * 16;
-  m.tmp_floats = std::max(m.Q + 2 * m.KV, m.H);
-  size_t other = 8 * 256 + 4 * (size_t)m.xs_floats + 8 * (size_t)m.H + 4 * (size_t)m.tmp_floats + 4 * (size_t)m.HD +
-                 4 * 1024 + 4 * (size_t)(m.NQH * m.pos_per_split + 32) + 4 * (size_t)(3 * m.max_splits) + 4 * 128 + 16;
+  m.xs0 = (m.H + 63) / 64 * 64;
+  m.xs1 = (std::max(m.Q, m.I) + 63) / 64 * 64;
+  m.tmp_floats = m.Q + 2 * m.KV;
+  // keep in step with the carve at the top of gg_decode_kernel
+  size_t other = 8 * 256 + (size_t)(3 * m.xs0 + m.xs0 / 4) + (size_t)(3 * m.xs1 + m.xs1 / 4) + 8 * (size_t)m.H +
+                 4 * (size_t)m.tmp_floats + 4 * 1024 + 4 * 256 + 4 * 256 + 16;
   cudaFuncAttributes fa;
   GG_CUDA(e, cudaFuncGetAttributes(&fa, gg::gg_decode_kernel));
   int optin = 0;
@@ -378,6 +394,7 @@ extern "C" int gg_finalize(gg_engine* e) {
   GG_TRY(dalloc(e, &m.dbg_normed, 4 * (size_t)m.H));
   m.seen_stride = ((m.V + 31) / 32) * 4;
   GG_TRY(dalloc(e, &m.seen, (size_t)m.seen_stride * c.max_seqs));
+  GG_TRY(dalloc(e, &m.trace, 8 * (size_t)m.grid * GG_TRACE_PHASES * 4));
   GG_TRY(dalloc(e, &e->d_md, sizeof(GGModelDev)));
   GG_TRY(dalloc(e, &e->d_st, sizeof(GGState)));
   GG_CUDA(e, cudaMallocHost(&e->h_st, sizeof(GGState)));
@@ -451,6 +468,7 @@ static GGState base_inputs(gg_engine* e, int seq, int mode) {
   s.mode = mode;
   s.timeout_ns = e->timeout_ns;
   s.rep_penalty = 1.0f;
+  if (e->trace_on) s.mode |= GG_TRACE;
   return s;
 }
 
@@ -659,6 +677,27 @@ extern "C" int gg_reset_kv(gg_engine* e, int seq) {
   size_t n = e->md.kv_seq_stride * 4;
   GG_CUDA(e, cudaMemsetAsync(e->md.kcache + (size_t)seq * e->md.kv_seq_stride, 0, n, e->stream));
   GG_CUDA(e, cudaMemsetAsync(e->md.vcache + (size_t)seq * e->md.kv_seq_stride, 0, n, e->stream));
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  return GG_OK;
+}
+
+extern "C" int gg_grid(gg_engine* e, int* out) {
+  if (!e || !out) return fail(e, GG_E_ARG, "null argument");
+  *out = e->md.grid ? e->md.grid : e->sm_count;
+  return GG_OK;
+}
+
+extern "C" int gg_set_trace(gg_engine* e, int on) {
+  if (!e) return fail(e, GG_E_ARG, "null engine");
+  e->trace_on = on ? 1 : 0;
+  return GG_OK;
+}
+
+extern "C" int gg_read_trace(gg_engine* e, uint64_t* out, int n) {
+  GG_TRY(ready(e, 0));
+  const int cap = e->md.grid * GG_TRACE_PHASES * 4;
+  if (!out || n <= 0 || n > cap) return fail(e, GG_E_ARG, "n must be 1..%d", cap);
+  GG_CUDA(e, cudaMemcpyAsync(out, e->md.trace, 8 * (size_t)n, cudaMemcpyDeviceToHost, e->stream));
   GG_CUDA(e, cudaStreamSynchronize(e->stream));
   return GG_OK;
 }

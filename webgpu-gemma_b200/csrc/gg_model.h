@@ -11,9 +11,12 @@
 #include <stddef.h>
 
 #define GG_MAX_LAYERS 64
-#define GG_NCW 16                     // consumer warps per CTA
+#define GG_NCW 15                     // consumer warps per CTA (16 warps: 4 per SM sub-partition)
 #define GG_NTHREADS ((GG_NCW + 1) * 32)  // + one producer warp
 #define GG_NCT (GG_NCW * 32)          // consumer threads
+#define GG_HEAD_DIM 256                // Gemma 3 head size (compile-time for the attention phase)
+#define GG_POS_PER_SPLIT 8             // KV positions per attention split
+#define GG_TRACE_PHASES 512            // phases traced per CTA by GG_TRACE launches (4 stamps each)
 
 static inline int gg_row_stride(int K) { return ((K + (K / 32) * 2) + 15) / 16 * 16; }
 
@@ -32,17 +35,23 @@ struct GGLayerW {
   int pad_;
 };
 
+struct GGPhaseCfg {
+  int gs, r, ks, rps;  // lanes per row, rows per lane, K-slices, rows per ring stage
+};
+
 struct GGModelDev {
   int H, Q, KV, NQH, NKH, HD, I, V, L, CTX;
   float eps, attn_scale;
   int rs_h, rs_q, rs_i;  // row strides (bytes) for K = H, Q, I
   int grid;              // CTAs of the persistent kernel (one per SM)
   int stage_bytes, nstages;
-  int rps_h, rps_q, rps_i;  // whole rows per ring stage for K = H, Q, I
-  int pps_gu;               // gate/up row pairs per ring stage
-  int ks_o, ks_down;        // K-splits of the O and down projections (cross-warp reduction)
+  // Per matvec phase: lanes per row (gs: 8, 16 or 32), K-slices per row (ks; the slice
+  // partials are summed across warps), whole rows per ring stage (rps, a multiple of 32/gs).
+  GGPhaseCfg ph_qkv, ph_o, ph_down, ph_lm;
+  int pps_gu;               // gate/up row pairs per ring stage (16 lanes per row)
   int pos_per_split, max_splits, ncomb, dims_per_comb;
-  int xs_floats, tmp_floats;  // shared-memory carve sizes
+  int xs0, xs1;     // x-plane buffer sizes (elements, multiples of 64): xs0 >= H, xs1 >= max(Q, I)
+  int tmp_floats;   // attention scratch (q | k | v)
   int smem_bytes;
   const uint8_t* embd;   // V rows, K = H (tied LM head)
   const float* out_norm;
@@ -65,6 +74,7 @@ struct GGModelDev {
   uint8_t* seen;        // [max_seqs][ceil(V/8)] this turn's tokens (repetition penalty)
   int seen_stride;
   int max_seqs;
+  unsigned long long* trace;  // [grid][GG_TRACE_PHASES][4] globaltimer stamps
   GGLayerW layers[GG_MAX_LAYERS];
 };
 
@@ -74,6 +84,7 @@ enum : int {
   GG_RUN_LM = 2,      // final norm + LM head (+ per-lane maxima)
   GG_RUN_SAMPLE = 4,  // sampler on the lane maxima -> st->out_token
   GG_PREFILL_ADVANCE = 8,  // after the launch: token = ids[++i], pos += 1 (serial prefill)
+  GG_TRACE = 16,           // every CTA stamps its phase boundaries into GGModelDev::trace
 };
 
 // Per-engine device state. The prefix up to `epoch` is written by the host at the start of a

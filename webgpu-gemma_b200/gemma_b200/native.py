@@ -16,6 +16,12 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgemma_b2
 
 GG_OK, GG_E_ARG, GG_E_CUDA, GG_E_STATE, GG_E_DEVICE, GG_E_NOMEM = 0, -1, -2, -3, -4, -5
 
+# Bytes a gg_step call moves: the host-written prefix of GGState (token, pos, sampling options,
+# ... up to `epoch`, csrc/gg_model.h) host->device, and its device-owned tail (out_token,
+# error, ...) device->host.
+STATE_H2D_BYTES = 80
+STATE_D2H_BYTES = 32
+
 # Every symbol the header declares, with (restype, argtypes).
 _P, _I, _D = ctypes.c_void_p, ctypes.c_int, ctypes.c_double
 _I32P = ctypes.POINTER(ctypes.c_int32)
@@ -34,6 +40,9 @@ SIGNATURES = {
     "gg_seen_reset": (_I, [_P, _I]),
     "gg_seen_add": (_I, [_P, _I, _I32P, _I]),
     "gg_reset_kv": (_I, [_P, _I]),
+    "gg_grid": (_I, [_P, ctypes.POINTER(ctypes.c_int)]),
+    "gg_set_trace": (_I, [_P, _I]),
+    "gg_read_trace": (_I, [_P, _P, _I]),
     "gg_set_timeout": (_I, [_P, ctypes.c_uint64]),
     "gg_last_device_ms": (_I, [_P, ctypes.POINTER(ctypes.c_float)]),
     "gg_destroy": (_I, [_P]),
@@ -171,6 +180,20 @@ class NativeEngine:
 
     def reset_kv(self, seq: int = 0):
         self._check(self.lib.gg_reset_kv(self.h, seq))
+
+    def set_trace(self, on: bool):
+        self._check(self.lib.gg_set_trace(self.h, 1 if on else 0))
+
+    def grid(self) -> int:
+        """CTAs of the persistent decode kernel (one per SM)."""
+        v = ctypes.c_int()
+        self._check(self.lib.gg_grid(self.h, ctypes.byref(v)))
+        return v.value
+
+    def read_trace(self, n: int) -> np.ndarray:
+        out = np.zeros(n, np.uint64)
+        self._check(self.lib.gg_read_trace(self.h, out.ctypes.data_as(_P), n))
+        return out
 
     def set_timeout(self, ns: int):
         self._check(self.lib.gg_set_timeout(self.h, int(ns)))
