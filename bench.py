@@ -121,6 +121,25 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
+def aggregate(local_ms: float, steps: int, dist=None, device=None) -> tuple[float, float]:
+    """Whole-job throughput of independent replicas: every rank ran `steps` tokens in
+    `local_ms` of device time; value = world * steps / max over ranks of the time."""
+    world = 1
+    max_ms = local_ms
+    if dist is not None and dist.is_initialized():
+        import torch
+        world = dist.get_world_size()
+        t = torch.tensor([local_ms], dtype=torch.float64, device=device or "cpu")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        max_ms = float(t.item())
+    return world * steps / (max_ms / 1000.0), max_ms
+
+
+def replica_streams(n_streams: int, rank: int, world: int) -> list[int]:
+    """Independent conversation streams of this rank: round robin over the ranks."""
+    return list(range(rank, n_streams, world))
+
+
 def dist_setup(n_gpus: int):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -328,13 +347,9 @@ def main():
         dev_ms, toks = run_steps(args.steps)
     if dist:
         torch.cuda.synchronize()
-        t = torch.tensor([dev_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    value, dev_ms_max = aggregate(dev_ms, args.steps, dist, "cuda" if dist else None)
+    if dist:
         dist.barrier()
-        dev_ms_max = float(t.item())
-    else:
-        dev_ms_max = dev_ms
-    value = world * args.steps / (dev_ms_max / 1000.0)
 
     # ---- e2e through the per-token C-ABI call (host token in, host token out)
     e2e_n = min(args.e2e_steps, DECODE_LEN)
@@ -345,12 +360,7 @@ def main():
         tok = eng.step(tok, PROMPT_LEN + i)
     e2e_s = time.perf_counter() - t0
     e2e_local = e2e_n / e2e_s
-    if dist:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_value = world * e2e_n / float(t.item())
-    else:
-        e2e_value = e2e_local
+    e2e_value, _ = aggregate(e2e_s * 1000.0, e2e_n, dist, "cuda" if dist else None)
 
     if rank != 0:
         eng.close()

@@ -117,6 +117,12 @@ int gg_set_trace(gg_engine* eng, int on);
 int gg_grid(gg_engine* eng, int* out);
 int gg_read_trace(gg_engine* eng, uint64_t* out, int n);
 
+/* Failure-detection self-test: a one-CTA kernel waits on a device flag that nothing sets,
+ * with the same bounded wait the step kernel uses. Returns GG_E_DEVICE ("activation wait
+ * timed out") after about timeout_ns; the engine stays usable afterwards. No counterpart in
+ * the reference (its WebGPU device-lost handler, engine.ts:134-137, has no bounded waits). */
+int gg_selftest_wait(gg_engine* eng, uint64_t timeout_ns);
+
 /* Bounded-wait limit of the device spins, in nanoseconds (default 1e9). */
 int gg_set_timeout(gg_engine* eng, uint64_t ns);
 

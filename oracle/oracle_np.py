@@ -6,8 +6,8 @@ oracle (gemma_oracle.c). Nothing in the product imports it.
 Each function follows the same reference lines as its C twin (svenflow/webgpu-gemma
 src/shaders.ts, src/engine.ts); every float32 operation is one numpy float32 operation
 in the shader's order, so results agree with the C oracle bit for bit except in the
-transcendental functions (numpy's float32 exp/tanh/sin/cos may differ from libm by an
-ulp). PARITY UNPINNED, as for the C oracle: the reference has no tests or fixtures.
+transcendental functions, which are evaluated in f64 and rounded to f32 (a correctly rounded
+libm; glibc's float functions can differ by an ulp). PARITY UNPINNED, as for the C oracle: the reference has no tests or fixtures.
 """
 from __future__ import annotations
 
@@ -78,7 +78,7 @@ def linear_q8(x: np.ndarray, packed: np.ndarray, m: int, n: int) -> np.ndarray:
 def gelu_mul(gate, up):
     S, A = f32(0.7978845608028654), f32(0.044715)
     t = np.clip(S * gate * (f32(1.0) + A * gate * gate), f32(-15.0), f32(15.0))
-    g = f32(0.5) * gate * (f32(1.0) + np.tanh(t))
+    g = f32(0.5) * gate * (f32(1.0) + np.tanh(t.astype(np.float64)).astype(f32))
     return g * up
 
 
@@ -86,9 +86,10 @@ def fused_norm_rope(data: np.ndarray, w, nheads, hd, eps, pos, theta):
     d = data.reshape(nheads, hd).copy()
     half = hd // 2
     i = np.arange(half)
-    freq = f32(1.0) / np.power(f32(theta), (i * 2).astype(f32) / f32(hd))
+    # transcendental functions in f64, rounded to f32: a correctly rounded libm, like glibc's
+    freq = f32(1.0) / np.power(np.float64(f32(theta)), ((i * 2).astype(f32) / f32(hd)).astype(np.float64)).astype(f32)
     ang = f32(pos) * freq
-    c, s = np.cos(ang), np.sin(ang)
+    c, s = np.cos(ang.astype(np.float64)).astype(f32), np.sin(ang.astype(np.float64)).astype(f32)
     for h in range(nheads):
         d[h] = rmsnorm(d[h], w, eps)
         x0, x1 = d[h, :half].copy(), d[h, half:].copy()
@@ -113,7 +114,7 @@ def attention(q, kc, vc, nqh, nkvh, hd, seq_len, scale):
             seg = s[base:base + 256]
             sm[:seg.shape[0]] = np.maximum(sm[:seg.shape[0]], seg)
         mx = sm.max()
-        e = np.exp(s - mx).astype(f32)
+        e = np.exp((s - mx).astype(np.float64)).astype(f32)
         ss = np.zeros(256, dtype=f32)
         for base in range(0, seq_len, 256):
             seg = e[base:base + 256]

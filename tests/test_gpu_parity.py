@@ -157,3 +157,33 @@ def test_bad_inputs_are_rejected_on_host():
     eng.prefill([5, 6, 7], 0)
     eng.sample_last(0)
     eng.close()
+
+
+def test_bounded_wait_times_out_and_engine_recovers():
+    """A device wait on a flag nothing sets runs out, the host reads GG_E_DEVICE, and the next
+    step still works (no trap, no hang: the kernel returns after its limit)."""
+    from gemma_b200.native import GG_E_DEVICE, engine_from_tensors
+    cfg, tens = synthetic("tiny", 7)
+    eng = engine_from_tensors(cfg, tens)
+    rc = eng.selftest_wait(50_000_000)  # 50 ms
+    assert rc == GG_E_DEVICE
+    assert "timed out" in eng.last_error()
+    eng.prefill([5, 6, 7], 0)
+    assert 0 <= eng.sample_last(0) < cfg.vocab_size
+    eng.close()
+
+
+def test_golden_tokens_on_gpu():
+    """Greedy tokens of the committed oracle fixtures, without rerunning the oracle."""
+    import json, os
+    from gemma_b200.native import engine_from_tensors
+    gold = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "greedy.json")))
+    for case in gold["cases"]:
+        cfg, tens = synthetic(case["shape"], case["seed"])
+        eng = engine_from_tensors(cfg, tens)
+        prompt = case["prompt"]
+        eng.prefill(prompt, 0)
+        toks = [eng.sample_last(0)]
+        toks += list(eng.decode(toks[0], len(prompt), len(case["greedy"]) - 1))
+        assert toks == case["greedy"], case["shape"]
+        eng.close()

@@ -60,6 +60,13 @@ __global__ void gg_seen_add_kernel(uint8_t* seen, const int32_t* ids, int n, int
   if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&st->seen_count, n);
 }
 
+// Self-test of the bounded waits: waits (with the decode kernel's tag_wait) for a tagged
+// word that nothing writes, so the wait runs out and sets the error word.
+__global__ void gg_wait_probe_kernel(const uint64_t* word, uint32_t* err, uint64_t timeout_ns) {
+  SpinCtl sc{err, timeout_ns};
+  if (threadIdx.x == 0) (void)tag_wait(word, 0x80000001u, sc);
+}
+
 // ------------------------------------------------------------------------------ engine
 
 struct gg_engine {
@@ -700,6 +707,21 @@ extern "C" int gg_read_trace(gg_engine* e, uint64_t* out, int n) {
   GG_CUDA(e, cudaMemcpyAsync(out, e->md.trace, 8 * (size_t)n, cudaMemcpyDeviceToHost, e->stream));
   GG_CUDA(e, cudaStreamSynchronize(e->stream));
   return GG_OK;
+}
+
+extern "C" int gg_selftest_wait(gg_engine* e, uint64_t timeout_ns) {
+  GG_TRY(ready(e, 0));
+  if (timeout_ns < 1000 || timeout_ns > 10000000000ull) return fail(e, GG_E_ARG, "timeout out of range");
+  // t_att is zero between launches' own writes only by chance; use a private zeroed word
+  uint64_t* word = nullptr;
+  GG_CUDA(e, cudaMalloc(&word, 64));
+  cudaMemsetAsync(word, 0, 64, e->stream);
+  gg_wait_probe_kernel<<<1, 32, 0, e->stream>>>(word, &e->d_st->error, timeout_ns);
+  cudaError_t r = cudaGetLastError();
+  if (r == cudaSuccess) r = cudaStreamSynchronize(e->stream);
+  cudaFree(word);
+  if (r != cudaSuccess) return fail(e, GG_E_CUDA, "wait probe: %s", cudaGetErrorString(r));
+  return finish(e, nullptr);  // reads and clears the error word, GG_E_DEVICE if it is set
 }
 
 extern "C" int gg_set_timeout(gg_engine* e, uint64_t ns) {

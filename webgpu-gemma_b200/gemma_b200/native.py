@@ -43,6 +43,7 @@ SIGNATURES = {
     "gg_grid": (_I, [_P, ctypes.POINTER(ctypes.c_int)]),
     "gg_set_trace": (_I, [_P, _I]),
     "gg_read_trace": (_I, [_P, _P, _I]),
+    "gg_selftest_wait": (_I, [_P, ctypes.c_uint64]),
     "gg_set_timeout": (_I, [_P, ctypes.c_uint64]),
     "gg_last_device_ms": (_I, [_P, ctypes.POINTER(ctypes.c_float)]),
     "gg_destroy": (_I, [_P]),
@@ -194,6 +195,13 @@ class NativeEngine:
         out = np.zeros(n, np.uint64)
         self._check(self.lib.gg_read_trace(self.h, out.ctypes.data_as(_P), n))
         return out
+
+    def selftest_wait(self, timeout_ns: int) -> int:
+        """Runs the bounded-wait self-test; returns the status code (GG_E_DEVICE expected)."""
+        return self.lib.gg_selftest_wait(self.h, int(timeout_ns))
+
+    def last_error(self) -> str:
+        return self.lib.gg_last_error(self.h).decode()
 
     def set_timeout(self, ns: int):
         self._check(self.lib.gg_set_timeout(self.h, int(ns)))
