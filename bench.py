@@ -39,7 +39,7 @@ DECODE_LEN = 256
 SEED = 1
 # Reference's own published decode number for this model (reference README.md:17, M4 Pro).
 PUBLISHED_DECODE = 59.8
-# Algorithmic bytes of one decode token (see DESIGN.md): Q8_0 weights at 34 B / 32 weights
+# Algorithmic bytes of one decode token: Q8_0 weights at 34 B / 32 weights
 # (tied LM head included), f32 norm weights, one embedding row, and the fp32 KV rows the
 # reference reads (positions 0..pos, all layers attend the full prefix).
 KV_BYTES_PER_POS = 53248  # 2 (K,V) x 26 layers x 256 x 4 B
@@ -63,7 +63,7 @@ def measured_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-# ncu capture of the same kernel on this workload (profiles/gg_decode_kernel_1b.md):
+# ncu capture of the same kernel on this workload (its summary is kept under profiles/):
 # dram bytes read + written per launch, or None before a capture exists.
 NCU_TRAFFIC_PER_LAUNCH = None
 
@@ -268,17 +268,17 @@ def run_trace():
 
 
 def run_profile():
-    """Launch sequence for ncu: 16 prefill launches, 1 LM-head launch, then 4 decode launches
-    (capture the decode kernel with -k regex:gg_decode_kernel -s 17 -c 1..3)."""
+    """Launch sequence for ncu on the bench's own workload: the 1B model, decode launches at
+    positions 640..643 (the mean position of the timed decode, 512..767), so each launch reads
+    the weights plus 641..644 KV rows per layer. The KV rows hold zeros instead of a prompt's
+    keys; the bytes moved are the same. Capture with -k regex:gg_decode_kernel -s 1 -c 1..3."""
     from gemma_b200 import synth
     from gemma_b200.native import engine_from_tensors
     shape = synth.SHAPES["1b"]
     cfg = shape.config()
     eng = engine_from_tensors(cfg, synth.make_tensors(shape, SEED))
-    prompt = synth.make_prompt(SEED, 16, cfg.vocab_size)
-    eng.prefill(prompt, 0)
-    tok = eng.sample_last(0)
-    toks = eng.decode(tok, len(prompt), 4)
+    tok = eng.step(2, 640)
+    toks = eng.decode(tok, 641, 3)
     print("profile run ok", int(tok), [int(t) for t in toks])
     eng.close()
 
@@ -295,7 +295,7 @@ def main():
     ap.add_argument("--trace", action="store_true",
                     help="per-phase device timestamps of one decode step at position 512 (CTA 0)")
     ap.add_argument("--profile", action="store_true",
-                    help="short fixed sequence for ncu: 16-token prefill, first token, 4 decode steps")
+                    help="short fixed sequence for ncu: 4 decode launches at positions 640..643")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

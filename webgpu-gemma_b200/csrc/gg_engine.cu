@@ -712,11 +712,12 @@ extern "C" int gg_read_trace(gg_engine* e, uint64_t* out, int n) {
 extern "C" int gg_selftest_wait(gg_engine* e, uint64_t timeout_ns) {
   GG_TRY(ready(e, 0));
   if (timeout_ns < 1000 || timeout_ns > 10000000000ull) return fail(e, GG_E_ARG, "timeout out of range");
-  // t_att is zero between launches' own writes only by chance; use a private zeroed word
   uint64_t* word = nullptr;
   GG_CUDA(e, cudaMalloc(&word, 64));
   cudaMemsetAsync(word, 0, 64, e->stream);
+  cudaEventRecord(e->ev0, e->stream);  // finish() reads the ev0 -> ev1 time
   gg_wait_probe_kernel<<<1, 32, 0, e->stream>>>(word, &e->d_st->error, timeout_ns);
+  cudaEventRecord(e->ev1, e->stream);
   cudaError_t r = cudaGetLastError();
   if (r == cudaSuccess) r = cudaStreamSynchronize(e->stream);
   cudaFree(word);
