@@ -132,8 +132,33 @@ int gg_last_device_ms(gg_engine* eng, float* ms);
 /* dispose (engine.ts:1039-1077). */
 int gg_destroy(gg_engine* eng);
 
-/* Message of the engine's last failure ("" if none). eng may be NULL for gg_create errors. */
+/* Message of the engine's last failure ("" if none). eng = NULL gives the last failure of a
+ * call without an engine (gg_create, gg_sample_logits_noalloc). */
 const char* gg_last_error(const gg_engine* eng);
+
+/* Sampling from logits the caller already holds on the GPU, with no memory allocation.
+ * It has no counterpart in the reference: it is the step kernel's last stage -- the 256
+ * per-lane maxima of the logits and the sampler, with the same rules and results as
+ * gg_sample_last -- offered on its own to callers that cannot call cudaMalloc: code that
+ * runs while another allocator (a framework's caching allocator, a fixed arena) owns the
+ * device memory, and latency-bound loops where cudaMalloc/cudaFree would stall on a
+ * device-wide synchronisation.
+ *   logits      device pointer, vocab f32 values, on the calling thread's current device
+ *   vocab       1 .. 524288; larger values are rejected with GG_E_ARG
+ *   seen_bits   device pointer or NULL: bit (t % 32) of word t / 32 marks token t for the
+ *               repetition penalty (tokens generated this turn); NULL = no tokens
+ *   sp, uniform sampling parameters and the draw, as for gg_sample_last
+ *   out_token   device pointer, receives the sampled token
+ *   stream      a cudaStream_t, or NULL for the default stream
+ * Asynchronous: *out_token is written when the stream reaches the kernel. Its scratch is one
+ * static 256 KiB device array (held by every GPU that loads this library until the process
+ * exits). The first call on a device looks up that array's device address, so make it before
+ * any stream capture on that device. All calls on a device share the array: calls that can
+ * run at the same time on the GPU (different streams, or threads without ordering) race and
+ * must be serialised by the caller. Errors: GG_E_ARG / GG_E_CUDA, message from
+ * gg_last_error(NULL). */
+int gg_sample_logits_noalloc(const float* logits, int vocab, const uint32_t* seen_bits, const gg_sample* sp,
+                             double uniform, int32_t* out_token, void* stream);
 
 /* Library build identifier (sm_100a kernels, compiled-in limits). */
 const char* gg_version(void);

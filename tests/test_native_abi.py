@@ -58,3 +58,15 @@ def test_bad_config_rejected(lib):
     h = ctypes.c_void_p()
     assert lib.gg_create(ctypes.byref(c), 0, ctypes.byref(h)) == -1
     assert b"config" in lib.gg_last_error(None)
+
+
+def test_noalloc_sampler_rejects_oversize_vocab(lib):
+    """The size check comes before any CUDA call, so it runs without a GPU."""
+    from gemma_b200.native import GGSample
+    s = GGSample(0.0, 0.9, 1.0, 0.0)
+    out = ctypes.c_int32()
+    rc = lib.gg_sample_logits_noalloc(ctypes.c_void_p(16), 524289, None, ctypes.byref(s), 0.0,
+                                      ctypes.byref(out), None)
+    assert rc == -1
+    assert b"524288" in lib.gg_last_error(None)
+    assert lib.gg_sample_logits_noalloc(None, 1000, None, ctypes.byref(s), 0.0, ctypes.byref(out), None) == -1

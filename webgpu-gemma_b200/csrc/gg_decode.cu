@@ -1035,3 +1035,150 @@ extern "C" __global__ void __launch_bounds__(GG_NTHREADS, 1)
 }
 
 }  // namespace gg
+
+// ------------------------------------------------------------------ sampling without allocation
+//
+// gg_sample_logits_noalloc: the step kernel's last stage -- the 256 per-lane maxima of the
+// logits (shaders.ts:363-384) and the sampler (engine.ts:823-901) -- as a kernel of its own over
+// logits the caller already holds on the device. Its scratch (per-CTA lane maxima and an
+// end-of-launch ticket) lives in a static device array, so a call allocates no memory.
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "gemma_b200.h"
+
+namespace gg {
+
+constexpr int SL_THREADS = 256;                                   // thread t owns top-256 lane t
+constexpr int SL_ROWS_PER_THREAD = 16;
+constexpr int SL_ROWS_PER_CTA = SL_THREADS * SL_ROWS_PER_THREAD;  // 4096 logits per CTA
+constexpr int SL_MAX_CTAS = 128;
+constexpr int SL_MAX_VOCAB = SL_MAX_CTAS * SL_ROWS_PER_CTA;       // 524,288 (Gemma 3: 262,144)
+constexpr int SL_KEYS_OFF = 32;  // word 0: ticket; from word 32: SL_MAX_CTAS x 256 lane keys
+constexpr size_t SL_SCRATCH_WORDS = SL_KEYS_OFF + (size_t)SL_MAX_CTAS * SL_THREADS;
+
+// 262,400 bytes on every GPU that loads the library, held until the process exits. Shared by
+// all calls: the ticket (word 0) must be zero when a launch starts and is cleared by the host
+// before each launch; every CTA overwrites its own lane-key slot before anything reads it.
+static __device__ __align__(256) unsigned long long g_sample_scratch[SL_SCRATCH_WORDS];
+
+__global__ void __launch_bounds__(SL_THREADS)
+    gg_sample_logits_kernel(const float* __restrict__ logits, int V, const uint32_t* __restrict__ seen_bits,
+                            float temperature, float top_p, float rep_penalty, double uniform,
+                            int32_t* __restrict__ out_token, unsigned long long* __restrict__ scratch) {
+  __shared__ int is_last;
+  __shared__ GGModelDev sm;
+  __shared__ GGState ss;
+  const int t = threadIdx.x;
+  unsigned long long* keys = scratch + SL_KEYS_OFF;
+  // Rows base + t + 256 j all fall in lane t: (value, lowest row) maximum, strict '>' from
+  // (-1e30, 0), NaN never taken; -0 is keyed as +0 since the two compare equal.
+  const unsigned long long ik = init_lane_key();
+  unsigned long long best = ik;
+  const int base = blockIdx.x * SL_ROWS_PER_CTA;
+#pragma unroll 4
+  for (int j = 0; j < SL_ROWS_PER_THREAD; j++) {
+    const int row = base + t + j * SL_THREADS;
+    if (row < V) {
+      float v = __ldg(logits + row);
+      if (!isnan(v)) {
+        if (v == 0.0f) v = 0.0f;
+        const unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - (uint32_t)row);
+        best = k > best ? k : best;
+      }
+    }
+  }
+  keys[(size_t)blockIdx.x * SL_THREADS + t] = best;
+  __threadfence();
+  __syncthreads();
+  if (t == 0) is_last = atomicAdd(scratch, 1ull) == (unsigned long long)(gridDim.x - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  unsigned long long k = ik;
+  for (int c = 0; c < (int)gridDim.x; c++) {
+    const unsigned long long o = __ldcg(keys + (size_t)c * SL_THREADS + t);
+    k = o > k ? o : k;
+  }
+  keys[t] = k;  // slot 0 now holds the merged maxima; thread t reads back only its own lane
+  if (t == 0) {
+    sm.lane_keys = keys;
+    sm.seen = reinterpret_cast<uint8_t*>(const_cast<uint32_t*>(seen_bits));
+    sm.seen_stride = 0;
+    sm.V = V;
+    ss.seq = 0;
+    ss.temperature = temperature;
+    ss.top_p = top_p;
+    ss.rep_penalty = rep_penalty;
+    ss.uniform = uniform;
+    ss.uniforms = nullptr;
+    ss.seen_count = seen_bits ? 1 : 0;
+  }
+  __threadfence_block();
+  __syncthreads();
+  Smem unused{};
+  const int tok = sample_token(sm, &ss, unused);
+  if (t == 0) *out_token = tok;
+}
+
+}  // namespace gg
+
+void gg_set_engineless_error(const char* msg);  // gg_engine.cu: the message gg_last_error(NULL) returns
+
+namespace {
+
+constexpr int SL_MAX_DEVICES = 64;
+std::mutex g_sl_mu;
+unsigned long long* g_sl_scratch[SL_MAX_DEVICES] = {};  // device address of the array, per device
+
+int sl_fail(int code, const char* fmt, ...) {
+  char buf[320];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  gg_set_engineless_error(buf);
+  return code;
+}
+
+}  // namespace
+
+extern "C" int gg_sample_logits_noalloc(const float* logits, int vocab, const uint32_t* seen_bits,
+                                        const gg_sample* sp, double uniform, int32_t* out_token, void* stream) {
+  using namespace gg;
+  if (!logits || !sp || !out_token) return sl_fail(GG_E_ARG, "gg_sample_logits_noalloc: null logits, sample or out_token");
+  if (vocab < 1 || vocab > SL_MAX_VOCAB)
+    return sl_fail(GG_E_ARG,
+                   "gg_sample_logits_noalloc: vocab %d outside 1..%d (its static scratch holds the lane maxima "
+                   "of %d blocks of %d logits)", vocab, SL_MAX_VOCAB, SL_MAX_CTAS, SL_ROWS_PER_CTA);
+  int dev = -1;
+  cudaError_t r = cudaGetDevice(&dev);
+  if (r != cudaSuccess) return sl_fail(GG_E_CUDA, "gg_sample_logits_noalloc: cudaGetDevice: %s", cudaGetErrorString(r));
+  if (dev < 0 || dev >= SL_MAX_DEVICES) return sl_fail(GG_E_ARG, "gg_sample_logits_noalloc: device %d >= %d", dev, SL_MAX_DEVICES);
+  unsigned long long* scratch = nullptr;
+  {
+    // First call on a device: look up the array's device address with that device current.
+    // The host-side name g_sample_scratch is not a device address and is never passed to a kernel.
+    std::lock_guard<std::mutex> g(g_sl_mu);
+    if (!g_sl_scratch[dev]) {
+      void* p = nullptr;
+      r = cudaGetSymbolAddress(&p, g_sample_scratch);
+      if (r != cudaSuccess || !p)
+        return sl_fail(GG_E_CUDA, "gg_sample_logits_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
+                       cudaGetErrorString(r));
+      g_sl_scratch[dev] = static_cast<unsigned long long*>(p);
+    }
+    scratch = g_sl_scratch[dev];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  r = cudaMemsetAsync(scratch, 0, sizeof(unsigned long long), s);  // the ticket starts at zero
+  if (r != cudaSuccess) return sl_fail(GG_E_CUDA, "gg_sample_logits_noalloc: clearing the ticket: %s", cudaGetErrorString(r));
+  const int grid = (vocab + SL_ROWS_PER_CTA - 1) / SL_ROWS_PER_CTA;
+  gg_sample_logits_kernel<<<grid, SL_THREADS, 0, s>>>(logits, vocab, seen_bits, sp->temperature, sp->top_p,
+                                                      sp->rep_penalty, uniform, out_token, scratch);
+  r = cudaGetLastError();
+  if (r != cudaSuccess) return sl_fail(GG_E_CUDA, "gg_sample_logits_noalloc: launch: %s", cudaGetErrorString(r));
+  return GG_OK;
+}

@@ -106,6 +106,9 @@ struct gg_engine {
 
 static std::string g_create_err;
 
+// Failures of calls that have no engine (gg_create, gg_sample_logits_noalloc) land here.
+void gg_set_engineless_error(const char* msg) { g_create_err = msg; }
+
 static int fail(gg_engine* e, int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;

@@ -44,6 +44,7 @@ SIGNATURES = {
     "gg_set_trace": (_I, [_P, _I]),
     "gg_read_trace": (_I, [_P, _P, _I]),
     "gg_selftest_wait": (_I, [_P, ctypes.c_uint64]),
+    "gg_sample_logits_noalloc": (_I, [_P, _I, _P, _P, _D, _P, _P]),
     "gg_set_timeout": (_I, [_P, ctypes.c_uint64]),
     "gg_last_device_ms": (_I, [_P, ctypes.POINTER(ctypes.c_float)]),
     "gg_destroy": (_I, [_P]),
