@@ -117,6 +117,13 @@ int gg_set_trace(gg_engine* eng, int on);
 int gg_grid(gg_engine* eng, int* out);
 int gg_read_trace(gg_engine* eng, uint64_t* out, int n);
 
+/* linearQ8 (shaders.ts:92-151, dispatched per matrix at engine.ts:769-793, 817-821) on `batch`
+ * activation rows at once, on the tensor cores: y[b][m] = sum_k x[b][k] * W[m][k] for one of
+ * the engine's Q8_0 matrices. which: 0 fused Q|K|V rows, 1 O, 2 gate/up (gate_i at row 2i,
+ * up_i at 2i+1), 3 down, 4 the tied LM head (layer ignored). x is [batch][K] and y [batch][M],
+ * host arrays; 1 <= batch <= 4096. gg_last_device_ms gives the device time of the product. */
+int gg_linear(gg_engine* eng, int which, int layer, const float* x, int batch, float* y);
+
 /* Failure-detection self-test: a one-CTA kernel waits on a device flag that nothing sets,
  * with the same bounded wait the step kernel uses. Returns GG_E_DEVICE ("activation wait
  * timed out") after about timeout_ns; the engine stays usable afterwards. No counterpart in

@@ -18,6 +18,7 @@
 #include "../../include/gemma_b200.h"
 #include "gg_device.cuh"
 #include "gg_model.h"
+#include "gg_gemm.h"
 
 namespace gg {
 extern "C" __global__ void gg_decode_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
@@ -102,6 +103,14 @@ struct gg_engine {
   uint64_t timeout_ns = 1000000000ull;
   float last_ms = 0.f;
   std::string err;
+  // tensor-core GEMM: tensor maps per weight matrix ([layer][0 qkv, 1 o, 2 gu, 3 down]), LM head
+  std::vector<GGQ8Map> qmaps;
+  GGQ8Map lm_map{};
+  bool gemm_ok = false;
+  float* lin_x = nullptr;
+  uint8_t* lin_tiles = nullptr;
+  float* lin_y = nullptr;
+  size_t lin_x_cap = 0, lin_tiles_cap = 0, lin_y_cap = 0;
 };
 
 static std::string g_create_err;
@@ -390,6 +399,17 @@ extern "C" int gg_finalize(gg_engine* e) {
     bool swa = (l % c.swa_period) < (c.swa_period - 1);
     w.theta = swa ? c.rope_theta_swa : c.rope_theta_global;
   }
+  // Tensor maps for the batched (tensor-core) path; unusable shapes leave it off.
+  e->gemm_ok = true;
+  e->qmaps.resize((size_t)c.num_layers * 4);
+  for (int l = 0; l < c.num_layers && e->gemm_ok; l++) {
+    const uint8_t* ptr[4] = {e->wqkv[l], e->wo[l], e->wgu[l], e->wdown[l]};
+    const int M[4] = {m.Q + 2 * m.KV, m.H, 2 * m.I, m.H}, K[4] = {m.H, m.Q, m.H, m.I};
+    for (int j = 0; j < 4; j++)
+      if (gg_make_q8_map(&e->qmaps[(size_t)l * 4 + j], ptr[j], M[j], K[j]) != cudaSuccess) e->gemm_ok = false;
+  }
+  if (e->gemm_ok && gg_make_q8_map(&e->lm_map, e->embd, m.V, m.H) != cudaSuccess) e->gemm_ok = false;
+  cudaGetLastError();
   GG_TRY(dalloc(e, &m.t_qkv, 8 * (size_t)(m.Q + 2 * m.KV)));
   GG_TRY(dalloc(e, &m.t_ml, 8 * (size_t)m.max_splits * m.NQH * 2));
   GG_TRY(dalloc(e, &m.t_o, 8 * (size_t)m.max_splits * m.Q));
@@ -728,6 +748,67 @@ extern "C" int gg_selftest_wait(gg_engine* e, uint64_t timeout_ns) {
   return finish(e, nullptr);  // reads and clears the error word, GG_E_DEVICE if it is set
 }
 
+// Sum of `splits` consecutive planes of n floats, in plane order.
+__global__ void gg_sum_splits_kernel(const float* __restrict__ p, int splits, long long n, float* __restrict__ out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    float s = p[i];
+    for (int z = 1; z < splits; z++) s += p[(long long)z * n + i];
+    out[i] = s;
+  }
+}
+
+// K-splits so that the tiles of one GEMM cover the SMs without an empty split.
+static int pick_splits(int tiles, int KS, int sms) {
+  int s = 1;
+  while (tiles * (s + 1) <= sms && KS / (s + 1) >= 3) s++;
+  while (s > 1 && (long long)(s - 1) * ((KS + s - 1) / s) >= KS) s--;
+  return s;
+}
+
+static int grow(gg_engine* e, void** p, size_t* cap, size_t need) {
+  if (*cap >= need) return GG_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  *cap = 0;
+  cudaError_t r = cudaMalloc(p, need);
+  if (r != cudaSuccess) return fail(e, GG_E_NOMEM, "cudaMalloc(%zu): %s", need, cudaGetErrorString(r));
+  *cap = need;
+  return GG_OK;
+}
+
+extern "C" int gg_linear(gg_engine* e, int which, int layer, const float* x, int batch, float* y) {
+  GG_TRY(ready(e, 0));
+  if (!e->gemm_ok) return fail(e, GG_E_STATE, "tensor-core path unavailable for this model's shapes");
+  if (!x || !y || batch < 1 || batch > 4096) return fail(e, GG_E_ARG, "bad x/y/batch");
+  if (which < 0 || which > 4) return fail(e, GG_E_ARG, "matrix %d not in 0..4", which);
+  if (which < 4 && (layer < 0 || layer >= e->cfg.num_layers)) return fail(e, GG_E_ARG, "layer %d out of range", layer);
+  const GGQ8Map& w = which == 4 ? e->lm_map : e->qmaps[(size_t)layer * 4 + which];
+  const int M = w.M, K = w.K, T = batch;
+  const int tiles = ((T + (T <= 64 ? 63 : 127)) / (T <= 64 ? 64 : 128)) * (M / 128);
+  const int splits = pick_splits(tiles, K / 64, e->sm_count);
+  const size_t tb = gg_xtiles_bytes(T, K);
+  GG_TRY(grow(e, (void**)&e->lin_x, &e->lin_x_cap, sizeof(float) * (size_t)T * K));
+  GG_TRY(grow(e, (void**)&e->lin_tiles, &e->lin_tiles_cap, 2 * tb));
+  GG_TRY(grow(e, (void**)&e->lin_y, &e->lin_y_cap, sizeof(float) * (size_t)T * M * (splits + 1)));
+  GG_CUDA(e, cudaMemcpyAsync(e->lin_x, x, sizeof(float) * (size_t)T * K, cudaMemcpyHostToDevice, e->stream));
+  GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
+  GG_CUDA(e, gg_xtiles_from_f32(e->lin_x, T, K, e->lin_tiles, e->lin_tiles + tb, e->stream));
+  const long long plane = (long long)T * M;
+  float* out = e->lin_y;
+  if (splits == 1) {
+    GG_CUDA(e, gg_gemm_q8(w, e->lin_tiles, e->lin_tiles + tb, T, out, M, 1, 0, &e->d_st->error, e->timeout_ns, e->stream));
+  } else {
+    float* part = e->lin_y + plane;
+    GG_CUDA(e, gg_gemm_q8(w, e->lin_tiles, e->lin_tiles + tb, T, part, M, splits, plane, &e->d_st->error, e->timeout_ns,
+                          e->stream));
+    gg_sum_splits_kernel<<<e->sm_count * 4, 256, 0, e->stream>>>(part, splits, plane, out);
+    GG_CUDA(e, cudaGetLastError());
+  }
+  GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
+  GG_CUDA(e, cudaMemcpyAsync(y, out, sizeof(float) * (size_t)plane, cudaMemcpyDeviceToHost, e->stream));
+  return finish(e, nullptr);
+}
+
 extern "C" int gg_set_timeout(gg_engine* e, uint64_t ns) {
   if (!e) return fail(e, GG_E_ARG, "null engine");
   if (ns < 1000) return fail(e, GG_E_ARG, "timeout must be >= 1 us");
@@ -752,6 +833,9 @@ extern "C" int gg_destroy(gg_engine* e) {
   if (e->d_ring) cudaFree(e->d_ring);
   if (e->h_ring) cudaFreeHost(e->h_ring);
   if (e->h_st) cudaFreeHost(e->h_st);
+  if (e->lin_x) cudaFree(e->lin_x);
+  if (e->lin_tiles) cudaFree(e->lin_tiles);
+  if (e->lin_y) cudaFree(e->lin_y);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
   if (e->stream) cudaStreamDestroy(e->stream);

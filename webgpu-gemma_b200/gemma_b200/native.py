@@ -43,6 +43,7 @@ SIGNATURES = {
     "gg_grid": (_I, [_P, ctypes.POINTER(ctypes.c_int)]),
     "gg_set_trace": (_I, [_P, _I]),
     "gg_read_trace": (_I, [_P, _P, _I]),
+    "gg_linear": (_I, [_P, _I, _I, _P, _I, _P]),
     "gg_selftest_wait": (_I, [_P, ctypes.c_uint64]),
     "gg_sample_logits_noalloc": (_I, [_P, _I, _P, _P, _D, _P, _P]),
     "gg_set_timeout": (_I, [_P, ctypes.c_uint64]),
@@ -196,6 +197,17 @@ class NativeEngine:
         out = np.zeros(n, np.uint64)
         self._check(self.lib.gg_read_trace(self.h, out.ctypes.data_as(_P), n))
         return out
+
+    def linear(self, which: int, layer: int, x: np.ndarray) -> np.ndarray:
+        """y = x @ W.T for matrix `which` (0 qkv, 1 o, 2 gate/up interleaved, 3 down, 4 LM head)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.ndim == 1:
+            x = x[None, :]
+        rows = {0: self.cfg.q_dim + 2 * self.cfg.kv_dim, 1: self.cfg.hidden_size, 2: 2 * self.cfg.intermediate_size,
+                3: self.cfg.hidden_size, 4: self.cfg.vocab_size}[which]
+        y = np.empty((x.shape[0], rows), np.float32)
+        self._check(self.lib.gg_linear(self.h, which, layer, x.ctypes.data_as(_P), x.shape[0], y.ctypes.data_as(_P)))
+        return y
 
     def selftest_wait(self, timeout_ns: int) -> int:
         """Runs the bounded-wait self-test; returns the status code (GG_E_DEVICE expected)."""
