@@ -31,6 +31,11 @@ extern "C" {
 
 typedef struct gg_engine gg_engine;
 
+/* gg_config.flags: prefill one token per launch, as the reference does (engine.ts:923-928).
+ * Without it gg_prefill runs the prompt in chunks of up to 512 tokens through tensor-core
+ * GEMMs (same math, f32 results within rounding of the serial path). */
+#define GG_FLAG_SERIAL_PREFILL 1
+
 /* Field-for-field the reference's GemmaConfig (src/types.ts:2-17), plus the number of
  * independent KV slots and option flags. */
 typedef struct {
@@ -39,7 +44,7 @@ typedef struct {
   float rms_norm_eps, rope_theta_global, rope_theta_swa;
   int32_t swa_period;
   int32_t max_seqs; /* KV slots (sequences); 1 for the reference's single conversation */
-  int32_t flags;    /* reserved, 0 */
+  int32_t flags;    /* GG_FLAG_* bits */
 } gg_config;
 
 /* Sampling options of one step: GenerateOptions (src/types.ts:65-78). */

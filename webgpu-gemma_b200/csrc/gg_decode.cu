@@ -117,14 +117,6 @@ GG_DEV void group_dot(const uint8_t* rowp, int rs, int K, const XPlanes& P, int 
   }
 }
 
-GG_DEV float gelu_tanh(float x) {
-  // shaders.ts:153-170
-  const float S = 0.7978845608028654f, A = 0.044715f;
-  float t = S * x * (1.0f + A * x * x);
-  t = fminf(fmaxf(t, -15.0f), 15.0f);
-  return 0.5f * x * (1.0f + tanhf(t));
-}
-
 struct Ctx {
   const GGModelDev* m;
   GGState* st;

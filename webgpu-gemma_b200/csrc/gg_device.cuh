@@ -168,6 +168,14 @@ GG_DEV float dot16(uint4 w, float4 a, float4 b, float4 c, float4 d) {
   return s;
 }
 
+// GELU with the tanh approximation and the argument clamp of shaders.ts:153-170.
+GG_DEV float gelu_tanh(float x) {
+  const float S = 0.7978845608028654f, A = 0.044715f;
+  float t = S * x * (1.0f + A * x * x);
+  t = fminf(fmaxf(t, -15.0f), 15.0f);
+  return 0.5f * x * (1.0f + tanhf(t));
+}
+
 GG_DEV float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -19,6 +19,7 @@
 #include "gg_device.cuh"
 #include "gg_model.h"
 #include "gg_gemm.h"
+#include "gg_prefill.h"
 
 namespace gg {
 extern "C" __global__ void gg_decode_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
@@ -111,7 +112,16 @@ struct gg_engine {
   uint8_t* lin_tiles = nullptr;
   float* lin_y = nullptr;
   size_t lin_x_cap = 0, lin_tiles_cap = 0, lin_y_cap = 0;
+  // batched prefill buffers (one chunk of up to GG_PF_CHUNK prompt tokens)
+  float* pf_hidden = nullptr;
+  float* pf_res = nullptr;
+  float* pf_q = nullptr;
+  float* pf_y = nullptr;
+  uint8_t* pf_tiles = nullptr;
+  size_t pf_tiles_half = 0;
 };
+
+constexpr int GG_PF_CHUNK = 512;  // prompt tokens per batched-prefill chunk
 
 static std::string g_create_err;
 
@@ -410,6 +420,17 @@ extern "C" int gg_finalize(gg_engine* e) {
   }
   if (e->gemm_ok && gg_make_q8_map(&e->lm_map, e->embd, m.V, m.H) != cudaSuccess) e->gemm_ok = false;
   cudaGetLastError();
+  if (e->gemm_ok) {
+    const size_t TC = GG_PF_CHUNK;
+    const int maxM = std::max(std::max(2 * m.I, m.Q + 2 * m.KV), m.H);
+    const size_t yfl = std::max(TC * (size_t)maxM, (size_t)e->sm_count * 128 * 128);
+    e->pf_tiles_half = gg_xtiles_bytes((int)TC, std::max(std::max(m.H, m.Q), m.I));
+    GG_TRY(dalloc(e, &e->pf_hidden, 4 * TC * m.H));
+    GG_TRY(dalloc(e, &e->pf_res, 4 * TC * m.H));
+    GG_TRY(dalloc(e, &e->pf_q, 4 * TC * m.Q));
+    GG_TRY(dalloc(e, &e->pf_y, 4 * yfl));
+    GG_TRY(dalloc(e, &e->pf_tiles, 2 * e->pf_tiles_half));
+  }
   GG_TRY(dalloc(e, &m.t_qkv, 8 * (size_t)(m.Q + 2 * m.KV)));
   GG_TRY(dalloc(e, &m.t_ml, 8 * (size_t)m.max_splits * m.NQH * 2));
   GG_TRY(dalloc(e, &m.t_o, 8 * (size_t)m.max_splits * m.Q));
@@ -511,6 +532,61 @@ static void set_sampling(GGState& s, const gg_sample* sp, double u) {
   s.uniform = u;
 }
 
+static int pick_splits(int tiles, int KS, int sms);
+
+static int gemm_tiles(int T, int M) { return (T <= 64 ? 1 : (T + 127) / 128) * (M / 128); }
+
+// Batched prefill of ids already in e->d_ids: chunks of up to GG_PF_CHUNK tokens, each layer
+// as four tensor-core GEMMs over the chunk's rows and the kernels of gg_prefill.cu between them.
+static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
+  const GGModelDev& m = e->md;
+  cudaStream_t s = e->stream;
+  uint8_t* thi = e->pf_tiles;
+  uint8_t* tlo = e->pf_tiles + e->pf_tiles_half;
+  uint32_t* err = &e->d_st->error;
+  const uint64_t to = e->timeout_ns;
+  const int QKV = m.Q + 2 * m.KV;
+  int T = 0;
+  for (int c0 = 0; c0 < n; c0 += GG_PF_CHUNK) {
+    T = std::min(GG_PF_CHUNK, n - c0);
+    const int p0 = start_pos + c0;
+    GG_CUDA(e, pf_embed(e->d_ids + c0, T, m.embd, m.rs_h, m.H, e->pf_hidden, s));
+    GG_CUDA(e, pf_addnorm(nullptr, 0, 0, nullptr, e->pf_hidden, e->pf_hidden, m.layers[0].attn_norm, thi, tlo, T, m.H,
+                          m.eps, s));
+    for (int l = 0; l < m.L; l++) {
+      const GGLayerW& w = m.layers[l];
+      const GGQ8Map* mp = &e->qmaps[(size_t)l * 4];
+      float* kc = m.kcache + (size_t)seq * m.kv_seq_stride + (size_t)l * m.CTX * m.KV;
+      float* vc = m.vcache + (size_t)seq * m.kv_seq_stride + (size_t)l * m.CTX * m.KV;
+      int sp = pick_splits(gemm_tiles(T, QKV), m.H / 64, e->sm_count);
+      long long plane = (long long)T * QKV;
+      GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, T, e->pf_y, QKV, sp, plane, err, to, s));
+      GG_CUDA(e, pf_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.theta, T, p0, m.NQH, m.NKH, m.HD, m.eps,
+                                  e->pf_q, kc, vc, s));
+      GG_CUDA(e, pf_attention(e->pf_q, kc, vc, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, thi, tlo, s));
+      sp = pick_splits(gemm_tiles(T, m.H), m.Q / 64, e->sm_count);
+      plane = (long long)T * m.H;
+      GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));
+      GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_attn_norm, e->pf_hidden, e->pf_res, w.ffn_norm, thi, tlo, T,
+                            m.H, m.eps, s));
+      sp = pick_splits(gemm_tiles(T, 2 * m.I), m.H / 64, e->sm_count);
+      plane = (long long)T * 2 * m.I;
+      GG_CUDA(e, gg_gemm_q8(mp[2], thi, tlo, T, e->pf_y, 2 * m.I, sp, plane, err, to, s));
+      GG_CUDA(e, pf_geglu(e->pf_y, sp, plane, T, m.I, thi, tlo, s));
+      sp = pick_splits(gemm_tiles(T, m.H), m.I / 64, e->sm_count);
+      plane = (long long)T * m.H;
+      GG_CUDA(e, gg_gemm_q8(mp[3], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));
+      const float* next_norm = l + 1 < m.L ? m.layers[l + 1].attn_norm : nullptr;
+      GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_ffw_norm, e->pf_res, e->pf_hidden, next_norm, thi, tlo, T, m.H,
+                            m.eps, s));
+    }
+  }
+  // the LM-head launch of gg_sample_last reads the last token's hidden state from here
+  GG_CUDA(e, cudaMemcpyAsync(m.dbg_hidden, e->pf_hidden + (size_t)(T - 1) * m.H, 4 * (size_t)m.H,
+                             cudaMemcpyDeviceToDevice, s));
+  return GG_OK;
+}
+
 extern "C" int gg_prefill(gg_engine* e, int seq, const int32_t* ids, int n, int start_pos) {
   GG_TRY(ready(e, seq));
   if (n <= 0 || !ids) return fail(e, GG_E_ARG, "empty prefill");
@@ -529,6 +605,14 @@ extern "C" int gg_prefill(gg_engine* e, int seq, const int32_t* ids, int n, int 
   gg_seen_add_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(e->md.seen + (size_t)seq * e->md.seen_stride, e->d_ids, n,
                                                              e->cfg.vocab_size, e->d_st);
   GG_CUDA(e, cudaGetLastError());
+  if (e->gemm_ok && !(e->cfg.flags & GG_FLAG_SERIAL_PREFILL)) {
+    GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
+    GG_TRY(prefill_batched(e, seq, n, start_pos));
+    GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
+    GG_TRY(finish(e, nullptr));
+    e->last_hidden_seq = seq;
+    return GG_OK;
+  }
   GGState s = base_inputs(e, seq, GG_RUN_LAYERS | GG_PREFILL_ADVANCE);
   s.token = ids[0];
   s.pos = start_pos;

@@ -1,0 +1,37 @@
+// gg_prefill.h -- launchers of the batched prefill kernels (gg_prefill.cu).
+//
+// A prompt chunk of T tokens runs layer by layer over all T rows at once: the four Q8_0
+// matrices go through the tensor-core GEMM (gg_gemm.h) and these kernels do what lies between
+// them. Split-K GEMM results arrive as `splits` planes of `plane` floats that the next kernel
+// sums in plane order.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// hidden[t] = dequantised embedding row ids[t] * sqrt(H) (shaders.ts:2-23).
+cudaError_t pf_embed(const int32_t* ids, int T, const uint8_t* embd, int rs, int H, float* hidden, cudaStream_t s);
+
+// resid_out[t] = resid_in[t] + rmsnorm(sum of planes)[t] * w_post   (fusedNormAdd, shaders.ts:386-418;
+//                skipped when part == nullptr: resid_out = resid_in)
+// tiles[t]     = rmsnorm(resid_out[t]) * w_norm                      (rmsNorm, shaders.ts:25-56;
+//                skipped when w_norm == nullptr)
+// resid_out may alias resid_in.
+cudaError_t pf_addnorm(const float* part, int splits, long long plane, const float* w_post, const float* resid_in,
+                       float* resid_out, const float* w_norm, uint8_t* thi, uint8_t* tlo, int T, int H, float eps,
+                       cudaStream_t s);
+
+// Per token: sum the QKV planes, q/k per-head rmsNorm + RoPE at position p0 + t
+// (shaders.ts:420-467), q -> q_out [T][NQH*HD], k and v -> rows p0.. of this layer's cache.
+cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm,
+                             const float* k_norm, float theta, int T, int p0, int NQH, int NKH, int HD, float eps,
+                             float* q_out, float* kc, float* vc, cudaStream_t s);
+
+// Causal attention of the T queries at positions p0..p0+T-1 over cache rows 0..p0+t
+// (shaders.ts:229-325), output written as activation tiles of width NQH*HD.
+cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T, int p0, int NQH, int NKH, int HD,
+                         float scale, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
+
+// act[t][i] = gelu_tanh(gu[t][2i]) * gu[t][2i+1] (shaders.ts:153-170, gu = sum of planes) as
+// activation tiles of width I.
+cudaError_t pf_geglu(const float* gu, int splits, long long plane, int T, int I, uint8_t* thi, uint8_t* tlo,
+                     cudaStream_t s);

@@ -54,6 +54,9 @@ SIGNATURES = {
 }
 
 
+GG_FLAG_SERIAL_PREFILL = 1  # prefill one token per launch (the reference's order)
+
+
 class GGSample(ctypes.Structure):
     _fields_ = [("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("rep_penalty", ctypes.c_float),
                 ("pad_", ctypes.c_float)]
@@ -92,12 +95,12 @@ def _i32p(a: np.ndarray):
 class NativeEngine:
     """Thin object wrapper over one gg_engine handle (one GPU, one stream)."""
 
-    def __init__(self, cfg: GemmaConfig, device: int = 0, max_seqs: int = 1):
+    def __init__(self, cfg: GemmaConfig, device: int = 0, max_seqs: int = 1, flags: int = 0):
         self.lib = load()
         self.cfg = cfg
         self.max_seqs = max_seqs
         h = ctypes.c_void_p()
-        cc = to_cconfig(cfg, max_seqs=max_seqs)
+        cc = to_cconfig(cfg, max_seqs=max_seqs, flags=flags)
         rc = self.lib.gg_create(ctypes.byref(cc), device, ctypes.byref(h))
         if rc != GG_OK:
             raise GemmaB200Error(rc, self.lib.gg_last_error(None).decode())
@@ -236,9 +239,10 @@ class NativeEngine:
             pass
 
 
-def engine_from_tensors(cfg: GemmaConfig, tensors: dict, device: int = 0, max_seqs: int = 1) -> NativeEngine:
+def engine_from_tensors(cfg: GemmaConfig, tensors: dict, device: int = 0, max_seqs: int = 1,
+                        flags: int = 0) -> NativeEngine:
     """Create + upload every (name -> (dims, type, raw bytes)) tensor + finalize."""
-    eng = NativeEngine(cfg, device=device, max_seqs=max_seqs)
+    eng = NativeEngine(cfg, device=device, max_seqs=max_seqs, flags=flags)
     for name, (dims, t, raw) in tensors.items():
         eng.upload_tensor(name, t, raw, dims)
     eng.finalize()
