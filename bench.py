@@ -283,6 +283,55 @@ def run_profile():
     eng.close()
 
 
+CFG2_SHAPES = [("qkv", 0, 1536, 1152), ("o", 1, 1152, 1024), ("gate_up", 2, 13824, 1152), ("down", 3, 1152, 6912),
+               ("lm_head", 4, 262144, 1152)]
+
+
+def run_cfg2(reps: int = 10):
+    """Config 2: the Q8_0 matvec/GEMM on the 1B shapes at batch 1, 8, 64 through gg_linear.
+    One JSON line per (shape, batch): device time of the product, algorithmic bytes
+    (N*K*34/32 + 4*b*(K+N)) and the fraction of measured HBM bandwidth."""
+    from gemma_b200 import synth
+    from gemma_b200.native import engine_from_tensors
+    shape = synth.SHAPES["1b"]
+    cfg = shape.config()
+    eng = engine_from_tensors(cfg, synth.make_tensors(shape, SEED))
+    peak, kind = measured_peaks()
+    rng = np.random.default_rng(2)
+    for name, which, n, k in CFG2_SHAPES:
+        for b in (1, 8, 64):
+            x = rng.standard_normal((b, k)).astype(np.float32)
+            for _ in range(3):
+                eng.linear(which, 0, x)
+            ts = []
+            for _ in range(reps):
+                eng.linear(which, 0, x)
+                ts.append(eng.last_device_ms())
+            ms = statistics.median(ts)
+            byts = n * k * 34 // 32 + 4 * b * (k + n)
+            gbs = byts / (ms / 1000) / 1e9
+            print(json.dumps({"cfg2": name, "N": n, "K": k, "batch": b, "ms": round(ms, 5),
+                              "gb_s": round(gbs, 1), "frac_hbm": round(gbs / peak, 4), "peak_kind": kind,
+                              "tflops": round(2 * b * n * k / (ms / 1000) / 1e12, 3)}))
+    eng.close()
+
+
+def run_profile_prefill():
+    """Launch sequence for an ncu launch list of the batched prefill: the 1B model, two
+    512-token prefills (26 layers x 9 launches each) and the first token."""
+    from gemma_b200 import synth
+    from gemma_b200.native import engine_from_tensors
+    shape = synth.SHAPES["1b"]
+    cfg = shape.config()
+    eng = engine_from_tensors(cfg, synth.make_tensors(shape, SEED))
+    prompt = synth.make_prompt(SEED, PROMPT_LEN, cfg.vocab_size)
+    eng.prefill(prompt, 0)
+    tok = eng.sample_last(0)
+    eng.prefill(prompt, 0)
+    print("prefill profile run ok", int(tok), "device ms", eng.last_device_ms())
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -296,7 +345,14 @@ def main():
                     help="per-phase device timestamps of one decode step at position 512 (CTA 0)")
     ap.add_argument("--profile", action="store_true",
                     help="short fixed sequence for ncu: 4 decode launches at positions 640..643")
+    ap.add_argument("--cfg2", action="store_true", help="config 2 matvec/GEMM microbench lines")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="two 512-token batched prefills of the 1B model, for an ncu launch list")
     args = ap.parse_args()
+    if args.cfg2:
+        return run_cfg2()
+    if args.profile_prefill:
+        return run_profile_prefill()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)

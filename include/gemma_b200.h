@@ -126,7 +126,8 @@ int gg_read_trace(gg_engine* eng, uint64_t* out, int n);
  * activation rows at once, on the tensor cores: y[b][m] = sum_k x[b][k] * W[m][k] for one of
  * the engine's Q8_0 matrices. which: 0 fused Q|K|V rows, 1 O, 2 gate/up (gate_i at row 2i,
  * up_i at 2i+1), 3 down, 4 the tied LM head (layer ignored). x is [batch][K] and y [batch][M],
- * host arrays; 1 <= batch <= 4096. gg_last_device_ms gives the device time of the product. */
+ * host arrays; 1 <= batch <= 4096. gg_last_device_ms gives the device time of the product
+ * (the GEMM and, when K was split, the sum of the split planes). */
 int gg_linear(gg_engine* eng, int which, int layer, const float* x, int batch, float* y);
 
 /* Failure-detection self-test: a one-CTA kernel waits on a device flag that nothing sets,

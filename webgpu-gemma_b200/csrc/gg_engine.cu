@@ -875,8 +875,8 @@ extern "C" int gg_linear(gg_engine* e, int which, int layer, const float* x, int
   GG_TRY(grow(e, (void**)&e->lin_tiles, &e->lin_tiles_cap, 2 * tb));
   GG_TRY(grow(e, (void**)&e->lin_y, &e->lin_y_cap, sizeof(float) * (size_t)T * M * (splits + 1)));
   GG_CUDA(e, cudaMemcpyAsync(e->lin_x, x, sizeof(float) * (size_t)T * K, cudaMemcpyHostToDevice, e->stream));
-  GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
   GG_CUDA(e, gg_xtiles_from_f32(e->lin_x, T, K, e->lin_tiles, e->lin_tiles + tb, e->stream));
+  GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));  // times the product (+ split sum) only
   const long long plane = (long long)T * M;
   float* out = e->lin_y;
   if (splits == 1) {
