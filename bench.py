@@ -287,7 +287,7 @@ CFG2_SHAPES = [("qkv", 0, 1536, 1152), ("o", 1, 1152, 1024), ("gate_up", 2, 1382
                ("lm_head", 4, 262144, 1152)]
 
 
-def run_cfg2(reps: int = 10):
+def run_cfg2(reps: int = 10, shapes=None, batches=(1, 8, 64)):
     """Config 2: the Q8_0 matvec/GEMM on the 1B shapes at batch 1, 8, 64 through gg_linear.
     One JSON line per (shape, batch): device time of the product, algorithmic bytes
     (N*K*34/32 + 4*b*(K+N)) and the fraction of measured HBM bandwidth."""
@@ -299,7 +299,9 @@ def run_cfg2(reps: int = 10):
     peak, kind = measured_peaks()
     rng = np.random.default_rng(2)
     for name, which, n, k in CFG2_SHAPES:
-        for b in (1, 8, 64):
+        if shapes and name not in shapes:
+            continue
+        for b in batches:
             x = rng.standard_normal((b, k)).astype(np.float32)
             for _ in range(3):
                 eng.linear(which, 0, x)
@@ -346,11 +348,15 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="short fixed sequence for ncu: 4 decode launches at positions 640..643")
     ap.add_argument("--cfg2", action="store_true", help="config 2 matvec/GEMM microbench lines")
+    ap.add_argument("--cfg2-shapes", default="", help="comma-separated subset of qkv,o,gate_up,down,lm_head")
+    ap.add_argument("--cfg2-batches", default="1,8,64")
+    ap.add_argument("--cfg2-reps", type=int, default=10)
     ap.add_argument("--profile-prefill", action="store_true",
                     help="two 512-token batched prefills of the 1B model, for an ncu launch list")
     args = ap.parse_args()
     if args.cfg2:
-        return run_cfg2()
+        return run_cfg2(args.cfg2_reps, [x for x in args.cfg2_shapes.split(",") if x],
+                        [int(x) for x in args.cfg2_batches.split(",")])
     if args.profile_prefill:
         return run_profile_prefill()
     args.warmup = max(args.warmup, 3)

@@ -117,6 +117,7 @@ struct gg_engine {
   float* pf_res = nullptr;
   float* pf_q = nullptr;
   float* pf_y = nullptr;
+  float* pf_att = nullptr;  // attention partials per key range
   uint8_t* pf_tiles = nullptr;
   size_t pf_tiles_half = 0;
 };
@@ -429,6 +430,7 @@ extern "C" int gg_finalize(gg_engine* e) {
     GG_TRY(dalloc(e, &e->pf_res, 4 * TC * m.H));
     GG_TRY(dalloc(e, &e->pf_q, 4 * TC * m.Q));
     GG_TRY(dalloc(e, &e->pf_y, 4 * yfl));
+    GG_TRY(dalloc(e, &e->pf_att, 4 * pf_attention_part_floats((int)TC, m.CTX, m.NQH, m.NKH)));
     GG_TRY(dalloc(e, &e->pf_tiles, 2 * e->pf_tiles_half));
   }
   GG_TRY(dalloc(e, &m.t_qkv, 8 * (size_t)(m.Q + 2 * m.KV)));
@@ -563,7 +565,7 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
       GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, T, e->pf_y, QKV, sp, plane, err, to, s));
       GG_CUDA(e, pf_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.theta, T, p0, m.NQH, m.NKH, m.HD, m.eps,
                                   e->pf_q, kc, vc, s));
-      GG_CUDA(e, pf_attention(e->pf_q, kc, vc, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, thi, tlo, s));
+      GG_CUDA(e, pf_attention(e->pf_q, kc, vc, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, e->pf_att, thi, tlo, s));
       sp = pick_splits(gemm_tiles(T, m.H), m.Q / 64, e->sm_count);
       plane = (long long)T * m.H;
       GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));

@@ -4,7 +4,7 @@
 // Here a chunk of T prompt tokens moves through each layer together: the matrices become
 // GEMMs over T rows (gg_gemm.cu), and the per-token work between them -- norms, residual adds,
 // q/k norm + RoPE, the KV store, causal attention over the cache, GeGLU -- runs in the
-// kernels below, one CTA per token row (or per 8 queries for attention). The math per token
+// kernels below, one CTA per token row (attention: per block of query rows and key range). The math per token
 // is the reference's (formulas of shaders.ts, f32 throughout); only the order of some sums
 // differs, within f32 rounding.
 #include "gg_gemm_dev.cuh"
@@ -14,11 +14,7 @@ namespace gg {
 
 constexpr int PF_THREADS = 256;
 constexpr int PF_MAX_H = 4096;
-constexpr int PF_QB = 8;   // queries per attention CTA (one warp each)
-constexpr int PF_KB = 64;  // keys per attention block
 constexpr int PF_HD = 256;
-constexpr int PF_KS = PF_HD + 1;  // padded K row in shared memory (conflict-free column reads)
-constexpr int PF_ATT_SMEM = (PF_QB * PF_HD + PF_KB * PF_KS + PF_KB * PF_HD + PF_QB * PF_KB + 2 * PF_QB) * 4;
 
 GG_DEV float block_sum256(float v, float* red) {
   v = warp_sum(v);
@@ -135,89 +131,201 @@ __global__ void __launch_bounds__(PF_THREADS)
   }
 }
 
-// Online-softmax attention: CTA = (8 consecutive queries, one q head); warp i scores query i
-// against 64 keys at a time (lane -> keys lane, lane + 32); thread d accumulates output dim d.
+// Causal attention, split over key ranges. A work item is (a block of 32 query rows, a range
+// of 128 keys): the rows are QT = 32/G consecutive tokens times the G query heads that share
+// one KV head, so each K/V row loaded into shared memory serves all of them. Scores are
+// register-tiled (thread: 2 rows x 4 keys), then P.V (thread: 4 rows x 8 dims). An item
+// leaves unnormalised partial results (running max m, sum l, output o) that pf_attn_merge
+// combines with the usual online-softmax rescaling.
+constexpr int PA_ROWS = 32;
+constexpr int PA_KB = 64;                      // keys per shared-memory block
+constexpr int PA_KC = 128;                     // keys per work item
+constexpr int PA_KSTR = PF_HD + 4;             // K row stride (floats): float4-aligned, conflict-free
+constexpr int PA_PART = PA_ROWS * PF_HD + 2 * PA_ROWS;  // floats per item: o, then m, then l
+constexpr int PA_SMEM = (PA_ROWS * PF_HD + PA_KB * PA_KSTR + PA_KB * PF_HD + PA_KB * PA_ROWS + PA_ROWS) * 4;
+
 __global__ void __launch_bounds__(PF_THREADS)
-    pf_attn_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc, int T,
-                   int p0, int NQH, int NKH, float scale, uint8_t* thi, uint8_t* tlo) {
-  extern __shared__ float sm[];
-  float* qs = sm;                         // [QB][HD]
-  float* ks = qs + PF_QB * PF_HD;         // [KB][KS]
-  float* vs = ks + PF_KB * PF_KS;         // [KB][HD]
-  float* ps = vs + PF_KB * PF_HD;         // [QB][KB]
-  float* al = ps + PF_QB * PF_KB;         // [QB] rescale factors
-  float* ls = al + PF_QB;                 // [QB] softmax denominators
-  const int t0 = blockIdx.x * PF_QB, h = blockIdx.y, kvh = h * NKH / NQH;
-  const int nq = min(PF_QB, T - t0);
+    pf_attn_part_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc, int T,
+                        int p0, int NQH, int NKH, float scale, int maxc, float* __restrict__ part) {
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                         // [ROWS][HD]
+  float* ks = qs + PA_ROWS * PF_HD;       // [KB][KSTR]
+  float* vs = ks + PA_KB * PA_KSTR;       // [KB][HD]
+  float* ps = vs + PA_KB * PF_HD;         // [KB][ROWS]  probabilities, key-major
+  float* al = ps + PA_KB * PA_ROWS;       // [ROWS] rescale factors of this block
+  const int G = NQH / NKH, QT = PA_ROWS / G;
+  const int c = blockIdx.x, b = blockIdx.y, kvh = blockIdx.z;
+  const int t0 = b * QT, nq = min(QT, T - t0);
+  const int kmax = p0 + t0 + nq - 1;  // last key any row of this block needs
+  const int k_begin = c * PA_KC;
+  if (k_begin > kmax) return;
+  const int k_end = min(k_begin + PA_KC, kmax + 1);
   const int QD = NQH * PF_HD, KVD = NKH * PF_HD;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, d = threadIdx.x;
-  for (int idx = threadIdx.x; idx < PF_QB * PF_HD; idx += PF_THREADS) {
-    const int i = idx / PF_HD, dd = idx % PF_HD;
-    qs[idx] = i < nq ? q[(long long)(t0 + i) * QD + h * PF_HD + dd] : 0.f;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  // rows r = token * G + g  ->  query head kvh * G + g of token t0 + token
+  for (int idx = tid; idx < PA_ROWS * (PF_HD / 4); idx += PF_THREADS) {
+    const int r = idx / (PF_HD / 4), d4 = idx % (PF_HD / 4);
+    const int tok = r / G, hq = kvh * G + r % G;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tok < nq) v = reinterpret_cast<const float4*>(q + (long long)(t0 + tok) * QD + hq * PF_HD)[d4];
+    reinterpret_cast<float4*>(qs + r * PF_HD)[d4] = v;
   }
-  const int kmax = p0 + t0 + nq - 1;
-  const int qpos = p0 + t0 + warp;
-  float m = -1e30f, l = 0.f;
-  float o[PF_QB];
+  // score tile of this thread: rows 2*qg, 2*qg+1; keys kg + 16*u
+  const int kg = tid & 15, qg = tid >> 4;
+  const int r0 = 2 * qg, r1 = r0 + 1;
+  const int pos0 = p0 + t0 + r0 / G, pos1 = p0 + t0 + r1 / G;
+  float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
+  // output tile of this thread: rows 4*warp..+3; dims 4*dg..+3 and 128+4*dg..+3
+  const int dg = tid & 31;
+  float o[4][8];
 #pragma unroll
-  for (int i = 0; i < PF_QB; i++) o[i] = 0.f;
-  for (int j0 = 0; j0 <= kmax; j0 += PF_KB) {
-    const int nk = min(PF_KB, kmax + 1 - j0);
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) o[i][j] = 0.f;
+
+  for (int j0 = k_begin; j0 < k_end; j0 += PA_KB) {
+    const int nk = min(PA_KB, k_end - j0);
     __syncthreads();
-    for (int idx = threadIdx.x; idx < nk * PF_HD; idx += PF_THREADS) {
-      const int j = idx / PF_HD, dd = idx % PF_HD;
-      const long long g = (long long)(j0 + j) * KVD + kvh * PF_HD + dd;
-      ks[j * PF_KS + dd] = kc[g];
-      vs[j * PF_HD + dd] = vc[g];
+    for (int idx = tid; idx < nk * (PF_HD / 4); idx += PF_THREADS) {
+      const int j = idx / (PF_HD / 4), d4 = idx % (PF_HD / 4);
+      const long long g = (long long)(j0 + j) * KVD + kvh * PF_HD;
+      reinterpret_cast<float4*>(ks + j * PA_KSTR)[d4] = reinterpret_cast<const float4*>(kc + g)[d4];
+      reinterpret_cast<float4*>(vs + j * PF_HD)[d4] = reinterpret_cast<const float4*>(vc + g)[d4];
     }
     __syncthreads();
-    if (warp < nq) {
-      const float* qr = qs + warp * PF_HD;
-      const float* k0 = ks + lane * PF_KS;
-      const float* k1 = ks + (lane + 32) * PF_KS;
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll 8
-      for (int dd = 0; dd < PF_HD; dd++) {
-        const float qd = qr[dd];
-        s0 = fmaf(qd, k0[dd], s0);
-        s1 = fmaf(qd, k1[dd], s1);
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+    const float4* qa = reinterpret_cast<const float4*>(qs + r0 * PF_HD);
+    const float4* qb = reinterpret_cast<const float4*>(qs + r1 * PF_HD);
+#pragma unroll 4
+    for (int d4 = 0; d4 < PF_HD / 4; d4++) {
+      const float4 x0 = qa[d4], x1 = qb[d4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float4 kv = reinterpret_cast<const float4*>(ks + (kg + 16 * u) * PA_KSTR)[d4];
+        sa[u] = fmaf(x0.x, kv.x, sa[u]); sa[u] = fmaf(x0.y, kv.y, sa[u]);
+        sa[u] = fmaf(x0.z, kv.z, sa[u]); sa[u] = fmaf(x0.w, kv.w, sa[u]);
+        sb[u] = fmaf(x1.x, kv.x, sb[u]); sb[u] = fmaf(x1.y, kv.y, sb[u]);
+        sb[u] = fmaf(x1.z, kv.z, sb[u]); sb[u] = fmaf(x1.w, kv.w, sb[u]);
       }
-      const bool v0 = lane < nk && j0 + lane <= qpos, v1 = lane + 32 < nk && j0 + lane + 32 <= qpos;
-      s0 = v0 ? s0 * scale : -INFINITY;
-      s1 = v1 ? s1 * scale : -INFINITY;
-      const float mnew = fmaxf(m, warp_max(fmaxf(s0, s1)));
-      const float e0 = v0 ? expf(s0 - mnew) : 0.f, e1 = v1 ? expf(s1 - mnew) : 0.f;
-      const float alpha = expf(m - mnew);
-      l = l * alpha + warp_sum(e0 + e1);
-      m = mnew;
-      ps[warp * PF_KB + lane] = e0;
-      ps[warp * PF_KB + lane + 32] = e1;
-      if (lane == 0) al[warp] = alpha;
-    } else if (lane == 0) {
-      al[warp] = 1.f;
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int key = j0 + kg + 16 * u;
+      const bool in = kg + 16 * u < nk;
+      sa[u] = (in && key <= pos0) ? sa[u] * scale : -INFINITY;
+      sb[u] = (in && key <= pos1) ? sb[u] * scale : -INFINITY;
+      mx0 = fmaxf(mx0, sa[u]);
+      mx1 = fmaxf(mx1, sb[u]);
+    }
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    float e0s = 0.f, e1s = 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const float e0 = sa[u] == -INFINITY ? 0.f : expf(sa[u] - n0);
+      const float e1 = sb[u] == -INFINITY ? 0.f : expf(sb[u] - n1);
+      ps[(kg + 16 * u) * PA_ROWS + r0] = e0;
+      ps[(kg + 16 * u) * PA_ROWS + r1] = e1;
+      e0s += e0;
+      e1s += e1;
+    }
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) {
+      e0s += __shfl_xor_sync(0xffffffffu, e0s, off);
+      e1s += __shfl_xor_sync(0xffffffffu, e1s, off);
+    }
+    const float a0 = expf(m0 - n0), a1 = expf(m1 - n1);
+    l0 = l0 * a0 + e0s;
+    l1 = l1 * a1 + e1s;
+    m0 = n0;
+    m1 = n1;
+    if (kg == 0) {
+      al[r0] = a0;
+      al[r1] = a1;
     }
     __syncthreads();
+    float av[4];
 #pragma unroll
-    for (int i = 0; i < PF_QB; i++) {
-      if (i >= nq) break;
-      float acc = o[i] * al[i];
-      const float* pr = ps + i * PF_KB;
-      for (int j = 0; j < nk; j++) acc = fmaf(pr[j], vs[j * PF_HD + d], acc);
-      o[i] = acc;
+    for (int i = 0; i < 4; i++) av[i] = al[4 * warp + i];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) o[i][j] *= av[i];
+    for (int j = 0; j < nk; j++) {
+      const float4 pr = reinterpret_cast<const float4*>(ps + j * PA_ROWS)[warp];
+      const float4 va = reinterpret_cast<const float4*>(vs + j * PF_HD)[dg];
+      const float4 vb = reinterpret_cast<const float4*>(vs + j * PF_HD + 128)[dg];
+      const float pv[4] = {pr.x, pr.y, pr.z, pr.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        o[i][0] = fmaf(pv[i], va.x, o[i][0]); o[i][1] = fmaf(pv[i], va.y, o[i][1]);
+        o[i][2] = fmaf(pv[i], va.z, o[i][2]); o[i][3] = fmaf(pv[i], va.w, o[i][3]);
+        o[i][4] = fmaf(pv[i], vb.x, o[i][4]); o[i][5] = fmaf(pv[i], vb.y, o[i][5]);
+        o[i][6] = fmaf(pv[i], vb.z, o[i][6]); o[i][7] = fmaf(pv[i], vb.w, o[i][7]);
+      }
     }
   }
-  if (lane == 0 && warp < nq) ls[warp] = l;
-  __syncthreads();
+  float* dst = part + ((size_t)(kvh * gridDim.y + b) * maxc + c) * PA_PART;
 #pragma unroll
-  for (int i = 0; i < PF_QB; i++)
-    if (i < nq) qs[i * PF_HD + d] = o[i] / ls[i];
+  for (int i = 0; i < 4; i++) {
+    float* row = dst + (4 * warp + i) * PF_HD;
+    reinterpret_cast<float4*>(row)[dg] = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
+    reinterpret_cast<float4*>(row + 128)[dg] = make_float4(o[i][4], o[i][5], o[i][6], o[i][7]);
+  }
+  if (kg == 0) {
+    dst[PA_ROWS * PF_HD + r0] = m0;
+    dst[PA_ROWS * PF_HD + r1] = m1;
+    dst[PA_ROWS * PF_HD + PA_ROWS + r0] = l0;
+    dst[PA_ROWS * PF_HD + PA_ROWS + r1] = l1;
+  }
+}
+
+// Merge the key-range items of one row block and write the attention output as tiles.
+__global__ void __launch_bounds__(PF_THREADS)
+    pf_attn_merge_kernel(const float* __restrict__ part, int T, int p0, int NQH, int NKH, int maxc, uint8_t* thi,
+                         uint8_t* tlo) {
+  __shared__ float wgt[16][PA_ROWS];
+  __shared__ float inv[PA_ROWS];
+  const int G = NQH / NKH, QT = PA_ROWS / G;
+  const int b = blockIdx.x, kvh = blockIdx.y;
+  const int t0 = b * QT, nq = min(QT, T - t0);
+  const int nch = min(maxc, (p0 + t0 + nq - 1) / PA_KC + 1);
+  const float* base = part + ((size_t)(kvh * gridDim.x + b) * maxc) * PA_PART;
+  if (threadIdx.x < PA_ROWS) {
+    const int r = threadIdx.x;
+    float M = -1e30f;
+    for (int c = 0; c < nch; c++) M = fmaxf(M, base[(size_t)c * PA_PART + PA_ROWS * PF_HD + r]);
+    float L = 0.f;
+    for (int c = 0; c < nch; c++) {
+      const float* pc = base + (size_t)c * PA_PART + PA_ROWS * PF_HD;
+      const float w = expf(pc[r] - M);
+      wgt[c][r] = w;
+      L += pc[PA_ROWS + r] * w;
+    }
+    inv[r] = 1.0f / L;
+  }
   __syncthreads();
-  const int i = threadIdx.x >> 5, c = threadIdx.x & 31;
-  if (i < nq) {
-    float v[8];
+  const int QD = NQH * PF_HD;
+  for (int idx = threadIdx.x; idx < PA_ROWS * (PF_HD / 8); idx += PF_THREADS) {
+    const int r = idx / (PF_HD / 8), c8 = idx % (PF_HD / 8);
+    const int tok = r / G, hq = kvh * G + r % G;
+    if (tok >= nq) continue;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < nch; c++) {
+      const float* src = base + (size_t)c * PA_PART + r * PF_HD + 8 * c8;
+      const float4 a = reinterpret_cast<const float4*>(src)[0], bq = reinterpret_cast<const float4*>(src)[1];
+      const float w = wgt[c][r];
+      v[0] = fmaf(a.x, w, v[0]); v[1] = fmaf(a.y, w, v[1]); v[2] = fmaf(a.z, w, v[2]); v[3] = fmaf(a.w, w, v[3]);
+      v[4] = fmaf(bq.x, w, v[4]); v[5] = fmaf(bq.y, w, v[5]); v[6] = fmaf(bq.z, w, v[6]); v[7] = fmaf(bq.w, w, v[7]);
+    }
 #pragma unroll
-    for (int j = 0; j < 8; j++) v[j] = qs[i * PF_HD + 8 * c + j];
-    xtile_put8(thi, tlo, QD / 64, t0 + i, h * PF_HD + 8 * c, v);
+    for (int j = 0; j < 8; j++) v[j] *= inv[r];
+    xtile_put8(thi, tlo, QD / 64, t0 + tok, hq * PF_HD + 8 * c8, v);
   }
 }
 
@@ -274,21 +382,35 @@ cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, con
   return cudaGetLastError();
 }
 
+size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH) {
+  const int G = NQH / NKH, QT = PA_ROWS / G;
+  const size_t nb = (size_t)(max_tokens + QT - 1) / QT, maxc = (size_t)(ctx + PA_KC - 1) / PA_KC;
+  return nb * maxc * NKH * PA_PART;
+}
+
 cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T, int p0, int NQH, int NKH, int HD,
-                         float scale, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
-  if (T <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
+                         float scale, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
+  if (T <= 0 || HD != PF_HD || NKH <= 0 || NQH % NKH) return cudaErrorInvalidValue;
+  const int G = NQH / NKH;
+  if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) return cudaErrorInvalidValue;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaError_t r = cudaGetDevice(&dev);
   if (r != cudaSuccess) return r;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    r = cudaFuncSetAttribute(pf_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_ATT_SMEM);
+    r = cudaFuncSetAttribute(pf_attn_part_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
     if (r != cudaSuccess) return r;
     attr_set[dev] = true;
   }
-  dim3 grid((T + PF_QB - 1) / PF_QB, NQH);
-  pf_attn_kernel<<<grid, PF_THREADS, PF_ATT_SMEM, s>>>(q, kc, vc, T, p0, NQH, NKH, scale, thi, tlo);
+  const int QT = PA_ROWS / G;
+  const int nb = (T + QT - 1) / QT;
+  const int maxc = (p0 + T - 1) / PA_KC + 1;
+  if (maxc > 16) return cudaErrorInvalidValue;  // merge weights hold 16 key ranges (2048 positions)
+  pf_attn_part_kernel<<<dim3(maxc, nb, NKH), PF_THREADS, PA_SMEM, s>>>(q, kc, vc, T, p0, NQH, NKH, scale, maxc, part);
+  r = cudaGetLastError();
+  if (r != cudaSuccess) return r;
+  pf_attn_merge_kernel<<<dim3(nb, NKH), PF_THREADS, 0, s>>>(part, T, p0, NQH, NKH, maxc, thi, tlo);
   return cudaGetLastError();
 }
 

@@ -27,9 +27,11 @@ cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, con
                              float* q_out, float* kc, float* vc, cudaStream_t s);
 
 // Causal attention of the T queries at positions p0..p0+T-1 over cache rows 0..p0+t
-// (shaders.ts:229-325), output written as activation tiles of width NQH*HD.
+// (shaders.ts:229-325), output written as activation tiles of width NQH*HD. `part` is scratch
+// of pf_attention_part_floats(T, p0 + T, NQH, NKH) floats (partial results per key range).
+size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH);
 cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T, int p0, int NQH, int NKH, int HD,
-                         float scale, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
+                         float scale, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
 
 // act[t][i] = gelu_tanh(gu[t][2i]) * gu[t][2i+1] (shaders.ts:153-170, gu = sum of planes) as
 // activation tiles of width I.
