@@ -2,9 +2,9 @@
 //
 // One CTA computes a 128-row x NT-token tile of Y over a K-slice:
 //   warp 0      TMA loads of the raw Q8_0 tile (128 rows x 64 quants + the 256-wide scale
-//               window) into a 6-stage ring;
-//   warp 1      bulk copies of the activation tiles (bf16 hi and lo, NT x 64) into the
-//               operand ring;
+//               window) into a ring;
+//   warp 1      bulk copies of the activation tiles (bf16 hi and lo, NT x 64) into their
+//               own ring, running ahead of the MMAs;
 //   warp 2      TMEM allocation and the MMA issue: per 64-wide K slab, 4 K-steps of
 //               three MMAs (Whi*Xhi + Whi*Xlo + Wlo*Xhi) into one f32 accumulator;
 //   warps 3-10  dequantise: each lane turns one Q8_0 block (32 int8 x f16 scale) into exact
@@ -24,19 +24,23 @@
 namespace gg {
 
 constexpr int GM_THREADS = 352;
-constexpr int GM_RAW_STAGES = 6;
 constexpr int GM_RAW_Q = 128 * 64;
 constexpr int GM_RAW_S = 128 * 16;
 constexpr int GM_RAW_BYTES = GM_RAW_Q + GM_RAW_S;
 constexpr int GM_A_BYTES = 128 * 128;  // 128 rows x 64 bf16
 
+// Three rings: raw Q8_0 tiles (TMA), dequantised weight operands (hi, lo), activation
+// operands (hi, lo). The activation ring is separate so its loads run ahead of the MMAs.
 template <int NT>
 struct GemmCfg {
-  static constexpr int OS = NT == 128 ? 2 : 3;
+  static constexpr int RS = NT == 128 ? 5 : 6;
+  static constexpr int AS = NT == 128 ? 2 : 3;
+  static constexpr int BS = NT == 128 ? 3 : 4;
+  static constexpr int A_STAGE = 2 * GM_A_BYTES;
   static constexpr int B_BYTES = NT * 128;
-  static constexpr int OP_BYTES = 2 * GM_A_BYTES + 2 * B_BYTES;
+  static constexpr int B_STAGE = 2 * B_BYTES;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = 1024 + OS * OP_BYTES + GM_RAW_STAGES * GM_RAW_BYTES + BAR_BYTES;
+  static constexpr int SMEM = 1024 + AS * A_STAGE + BS * B_STAGE + RS * GM_RAW_BYTES + BAR_BYTES;
 };
 
 struct GemmArgs {
@@ -49,20 +53,28 @@ struct GemmArgs {
   uint64_t timeout_ns;
 };
 
+// Exact int8 -> f32 of byte b of wx = raw ^ 0x80808080 (2^23 + u with u = q + 128, minus 2^23 + 128).
+GG_DEV float q8_at(uint32_t wx, int b) {
+  return __int_as_float((int)__byte_perm(wx, 0x4B000000u, 0x7440u + (uint32_t)b)) - 8388736.0f;
+}
+
 template <int NT>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gg_gemm_q8_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap ts,
                       const GemmArgs a) {
   using C = GemmCfg<NT>;
-  constexpr int RS = GM_RAW_STAGES, OS = C::OS;
+  constexpr int RS = C::RS, AS = C::AS, BS = C::BS;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* op = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* raw = op + OS * C::OP_BYTES;
+  uint8_t* aring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* bring = aring + AS * C::A_STAGE;
+  uint8_t* raw = bring + BS * C::B_STAGE;
   uint64_t* full_raw = reinterpret_cast<uint64_t*>(raw + RS * GM_RAW_BYTES);
   uint64_t* empty_raw = full_raw + RS;
-  uint64_t* full_op = empty_raw + RS;
-  uint64_t* empty_op = full_op + OS;
-  uint64_t* acc_bar = empty_op + OS;
+  uint64_t* full_a = empty_raw + RS;
+  uint64_t* empty_a = full_a + AS;
+  uint64_t* full_b = empty_a + AS;
+  uint64_t* empty_b = full_b + BS;
+  uint64_t* acc_bar = empty_b + BS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -77,9 +89,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       mbar_init(&full_raw[i], 1);
       mbar_init(&empty_raw[i], 8);
     }
-    for (int i = 0; i < OS; i++) {
-      mbar_init(&full_op[i], 9);
-      mbar_init(&empty_op[i], 1);
+    for (int i = 0; i < AS; i++) {
+      mbar_init(&full_a[i], 8);
+      mbar_init(&empty_a[i], 1);
+    }
+    for (int i = 0; i < BS; i++) {
+      mbar_init(&full_b[i], 1);
+      mbar_init(&empty_b[i], 1);
     }
     mbar_init(acc_bar, 1);
     *abort_flag = 0;
@@ -115,35 +131,38 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {  // activation tiles
       const size_t KS = (size_t)a.KS;
+      int issued = 0;
       for (int i = 0; i < ns; i++) {
-        const int o = i % OS;
+        const int o = i % BS;
         if (*abort_flag) break;
-        if (i >= OS && !mbar_wait(&empty_op[o], ((i / OS) - 1) & 1, sc)) {
+        if (i >= BS && !mbar_wait(&empty_b[o], ((i / BS) - 1) & 1, sc)) {
           *abort_flag = 1;
           break;
         }
-        uint8_t* dst = op + o * C::OP_BYTES + 2 * GM_A_BYTES;
-        mbar_arrive_expect_tx(&full_op[o], 2 * C::B_BYTES);
+        uint8_t* dst = bring + o * C::B_STAGE;
+        mbar_arrive_expect_tx(&full_b[o], C::B_STAGE);
 #pragma unroll
         for (int h = 0; h < NT / 64; h++) {
           const size_t blk = ((size_t)(n_tile * (NT / 64) + h) * KS + (size_t)(s0 + i)) * 8192u;
-          bulk_g2s_plain(dst + h * 8192, a.xhi + blk, 8192, &full_op[o]);
-          bulk_g2s_plain(dst + C::B_BYTES + h * 8192, a.xlo + blk, 8192, &full_op[o]);
+          bulk_g2s_plain(dst + h * 8192, a.xhi + blk, 8192, &full_b[o]);
+          bulk_g2s_plain(dst + C::B_BYTES + h * 8192, a.xlo + blk, 8192, &full_b[o]);
         }
+        issued++;
       }
+      for (int i = issued > BS ? issued - BS : 0; i < issued; i++) mbar_wait(&full_b[i % BS], (i / BS) & 1, sc);
     }
   } else if (warp == 2) {
     if (lane == 0) {  // MMA issue
       const uint32_t idesc = umma_idesc_bf16_m128(NT);
       for (int i = 0; i < ns; i++) {
-        const int o = i % OS;
-        if (!mbar_wait(&full_op[o], (i / OS) & 1, sc)) {
+        const int ia = i % AS, ib = i % BS;
+        if (!mbar_wait(&full_b[ib], (i / BS) & 1, sc) || !mbar_wait(&full_a[ia], (i / AS) & 1, sc)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t ahi = smem_u32(op + o * C::OP_BYTES);
-        const uint32_t alo = ahi + GM_A_BYTES, bhi = ahi + 2 * GM_A_BYTES, blo = bhi + C::B_BYTES;
+        const uint32_t ahi = smem_u32(aring + ia * C::A_STAGE), alo = ahi + GM_A_BYTES;
+        const uint32_t bhi = smem_u32(bring + ib * C::B_STAGE), blo = bhi + C::B_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
           const uint32_t off = kk * 32;
@@ -151,7 +170,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           umma_bf16(tmem, umma_desc_sw128(ahi + off), umma_desc_sw128(blo + off), idesc, 1u);
           umma_bf16(tmem, umma_desc_sw128(alo + off), umma_desc_sw128(bhi + off), idesc, 1u);
         }
-        umma_commit(&empty_op[o]);
+        umma_commit(&empty_a[ia]);
+        umma_commit(&empty_b[ib]);
       }
       umma_commit(acc_bar);  // arrives once every MMA issued above has completed
     }
@@ -161,7 +181,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     const int r = tw * 16 + (lane >> 1), h = lane & 1;
     const uint32_t rowoff = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     for (int i = 0; i < ns; i++) {
-      const int rr = i % RS, o = i % OS;
+      const int rr = i % RS, ia = i % AS;
       if (*abort_flag) break;
       if (!mbar_wait(&full_raw[rr], (i / RS) & 1, sc)) {
         *abort_flag = 1;
@@ -176,27 +196,28 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       const float d = __half2float(dh);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_raw[rr]);
-      if (i >= OS && !mbar_wait(&empty_op[o], ((i / OS) - 1) & 1, sc)) {
+      if (i >= AS && !mbar_wait(&empty_a[ia], ((i / AS) - 1) & 1, sc)) {
         *abort_flag = 1;
         break;
       }
-      uint8_t* ahi = op + o * C::OP_BYTES;
+      uint8_t* ahi = aring + ia * C::A_STAGE;
       uint8_t* alo = ahi + GM_A_BYTES;
-      const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+      const uint32_t words[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u, q0.w ^ 0x80808080u,
+                                 q1.x ^ 0x80808080u, q1.y ^ 0x80808080u, q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
 #pragma unroll
       for (int j = 0; j < 4; j++) {  // chunk j: weights 8j..8j+7 of this block
         uint32_t hw[4], lw[4];
 #pragma unroll
         for (int p = 0; p < 4; p++) {
-          const uint32_t wd = words[2 * j + (p >> 1)];
+          // w = q * d exactly in f32; hi = w truncated to bf16, lo = (w - hi) rounded to bf16:
+          // hi + lo = w to 2^-16 relative.
+          const uint32_t wx = words[2 * j + (p >> 1)];
           const int b0 = (p & 1) * 2;
-          const float w0 = (float)(int8_t)(wd >> (8 * b0)) * d;
-          const float w1 = (float)(int8_t)(wd >> (8 * (b0 + 1))) * d;
-          __nv_bfloat16 h0, l0, h1, l1;
-          split_bf16(w0, h0, l0);
-          split_bf16(w1, h1, l1);
-          hw[p] = pack_bf16x2(h0, h1);
-          lw[p] = pack_bf16x2(l0, l1);
+          const float w0 = q8_at(wx, b0) * d, w1 = q8_at(wx, b0 + 1) * d;
+          const uint32_t u0 = __float_as_uint(w0) & 0xFFFF0000u, u1 = __float_as_uint(w1) & 0xFFFF0000u;
+          hw[p] = __byte_perm(u0, u1, 0x7632u);
+          const __nv_bfloat162 l2 = __floats2bfloat162_rn(w0 - __uint_as_float(u0), w1 - __uint_as_float(u1));
+          lw[p] = *reinterpret_cast<const uint32_t*>(&l2);
         }
         const int c = h * 4 + j;
         const uint32_t off = rowoff + ((uint32_t)((c ^ (r & 7)) & 7) << 4);
@@ -205,7 +226,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&full_op[o]);
+      if (lane == 0) mbar_arrive(&full_a[ia]);
     }
     if (tw < 4) {  // epilogue: warp w reads TMEM lanes 32*(w%4)..
       const int q = warp & 3;
