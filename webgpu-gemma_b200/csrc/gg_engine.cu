@@ -410,16 +410,24 @@ extern "C" int gg_finalize(gg_engine* e) {
     bool swa = (l % c.swa_period) < (c.swa_period - 1);
     w.theta = swa ? c.rope_theta_swa : c.rope_theta_global;
   }
-  // Tensor maps for the batched (tensor-core) path; unusable shapes leave it off.
-  e->gemm_ok = true;
+  // Tiled weight copies for the batched (tensor-core) path; unusable shapes leave it off.
+  e->gemm_ok = (m.H % 128 == 0) && (m.Q % 64 == 0) && ((m.Q + 2 * m.KV) % 128 == 0) && (m.I % 64 == 0) &&
+               ((2 * m.I) % 128 == 0) && (m.V % 128 == 0) && (m.H % 64 == 0);
   e->qmaps.resize((size_t)c.num_layers * 4);
   for (int l = 0; l < c.num_layers && e->gemm_ok; l++) {
     const uint8_t* ptr[4] = {e->wqkv[l], e->wo[l], e->wgu[l], e->wdown[l]};
     const int M[4] = {m.Q + 2 * m.KV, m.H, 2 * m.I, m.H}, K[4] = {m.H, m.Q, m.H, m.I};
-    for (int j = 0; j < 4; j++)
-      if (gg_make_q8_map(&e->qmaps[(size_t)l * 4 + j], ptr[j], M[j], K[j]) != cudaSuccess) e->gemm_ok = false;
+    for (int j = 0; j < 4; j++) {
+      uint8_t* t = nullptr;
+      GG_TRY(dalloc(e, &t, gg_q8_tiles_bytes(M[j], K[j])));
+      GG_CUDA(e, gg_make_q8_tiles(&e->qmaps[(size_t)l * 4 + j], ptr[j], M[j], K[j], t, e->stream));
+    }
   }
-  if (e->gemm_ok && gg_make_q8_map(&e->lm_map, e->embd, m.V, m.H) != cudaSuccess) e->gemm_ok = false;
+  if (e->gemm_ok) {
+    uint8_t* t = nullptr;
+    GG_TRY(dalloc(e, &t, gg_q8_tiles_bytes(m.V, m.H)));
+    GG_CUDA(e, gg_make_q8_tiles(&e->lm_map, e->embd, m.V, m.H, t, e->stream));
+  }
   cudaGetLastError();
   if (e->gemm_ok) {
     const size_t TC = GG_PF_CHUNK;

@@ -9,18 +9,24 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// A weight matrix as the GEMM reads it: a tiled copy of the device rows in which every
+// 128-row x 64-column slab is one contiguous block of GG_Q8_TILE_BYTES (128 x 64 int8 quants,
+// then the 128 x 2 f16 scales of its two Q8_0 blocks), blocks ordered (m_tile * K/64 + slab).
+// One bulk copy then moves a whole slab.
+#define GG_Q8_TILE_BYTES 8704
 struct GGQ8Map {
-  CUtensorMap q;  // quants: box 64 B x 128 rows
-  CUtensorMap s;  // scales: box 16 B (8 f16) x 128 rows
-  const uint8_t* base;
-  int M, K, rs;
+  const uint8_t* tiles;
+  int M, K;
 };
+
+size_t gg_q8_tiles_bytes(int M, int K);
+
+// Fill `tiles` (gg_q8_tiles_bytes(M, K) bytes) from a matrix in the device row format.
+// M % 128 == 0 and K % 64 == 0 are required.
+cudaError_t gg_make_q8_tiles(GGQ8Map* out, const uint8_t* rows, int M, int K, uint8_t* tiles, cudaStream_t s);
 
 // Bytes of one activation tile array for T rows of width K (T rounded up to 128).
 size_t gg_xtiles_bytes(int T, int K);
-
-// Tensor maps for a weight matrix. Returns cudaSuccess or an error (M % 128, K % 64 required).
-cudaError_t gg_make_q8_map(GGQ8Map* out, const uint8_t* base, int M, int K);
 
 // x [T][K] f32 -> tile arrays (rows T..round128(T)-1 zero).
 cudaError_t gg_xtiles_from_f32(const float* x, int T, int K, uint8_t* xhi, uint8_t* xlo, cudaStream_t s);
