@@ -318,6 +318,50 @@ def run_cfg2(reps: int = 10, shapes=None, batches=(1, 8, 64)):
     eng.close()
 
 
+CFG4_SEQS, CFG4_PROMPT, CFG4_TOKENS = 64, 256, 256
+CFG4_SAMPLE = (0.7, 0.9, 1.2)
+
+
+def run_cfg4(args):
+    """Config 4: the 1B model with 64 independent sequences per GPU (one engine per GPU, data
+    parallel, no collective on the data path): 256-token random prompts (batched prefill), then
+    256 tokens per sequence sampled with T 0.7, top-p 0.9, rep 1.2 and per-sequence Philox
+    draws, 64 sequences per step (gg_decode_batch). value = tokens of all ranks / max over ranks
+    of the device time of the decode."""
+    from gemma_b200 import synth
+    from gemma_b200.engine import philox_uniforms
+    from gemma_b200.native import engine_from_tensors
+    rank, local, world, dist, torch = dist_setup(args.gpus)
+    shape = synth.SHAPES["1b"]
+    cfg = shape.config()
+    eng = engine_from_tensors(cfg, synth.make_tensors(shape, SEED), device=local, max_seqs=CFG4_SEQS)
+    B, P, N = CFG4_SEQS, CFG4_PROMPT, min(CFG4_TOKENS, args.steps)
+    seq_ids = [rank * B + i for i in range(B)]  # global stream ids (Philox streams)
+    draws = np.stack([philox_uniforms(SEED, sid, N + 1) for sid in seq_ids], axis=1)  # [N+1][B]
+    T, TP, R = CFG4_SAMPLE
+    first = []
+    for i, sid in enumerate(seq_ids):
+        prompt = synth.make_prompt(SEED * 100003 + sid, P, cfg.vocab_size)
+        eng.prefill(prompt, 0, seq=i)
+        first.append(eng.sample_last(i, temperature=T, top_p=TP, rep=R, uniform=float(draws[0, i])))
+    samples = [CFG4_SAMPLE] * B
+    # warm-up steps at the first positions; the timed run then rewrites those rows
+    eng.decode_batch(np.arange(B), first, [P] * B, max(args.warmup, 3), samples, draws[1:1 + max(args.warmup, 3)])
+    toks = eng.decode_batch(np.arange(B), first, [P] * B, N, samples, draws[1:N + 1])
+    dev_ms = eng.last_device_ms()
+    value, max_ms = aggregate(dev_ms, B * N, dist, f"cuda:{local}")
+    if rank == 0:
+        print(json.dumps({"cfg4": "1B, 64 sequences per GPU, 256-token prompts, 256 sampled tokens (T 0.7, top-p 0.9, rep 1.2)",
+                          "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "seqs_per_gpu": B,
+                          "tokens_per_seq": N, "ms_per_step": round(max_ms / N, 4), "scaling": "weak",
+                          "parallelism": f"dp{world} (independent engines)",
+                          "first_tokens": [int(t) for t in toks[0, :4]]}))
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_profile_prefill():
     """Launch sequence for an ncu launch list of the batched prefill: the 1B model, two
     512-token prefills (26 layers x 9 launches each) and the first token."""
@@ -348,12 +392,15 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="short fixed sequence for ncu: 4 decode launches at positions 640..643")
     ap.add_argument("--cfg2", action="store_true", help="config 2 matvec/GEMM microbench lines")
+    ap.add_argument("--cfg4", action="store_true", help="config 4: 64 sequences per GPU, batched sampled decode")
     ap.add_argument("--cfg2-shapes", default="", help="comma-separated subset of qkv,o,gate_up,down,lm_head")
     ap.add_argument("--cfg2-batches", default="1,8,64")
     ap.add_argument("--cfg2-reps", type=int, default=10)
     ap.add_argument("--profile-prefill", action="store_true",
                     help="two 512-token batched prefills of the 1B model, for an ncu launch list")
     args = ap.parse_args()
+    if args.cfg4:
+        return run_cfg4(args)
     if args.cfg2:
         return run_cfg2(args.cfg2_reps, [x for x in args.cfg2_shapes.split(",") if x],
                         [int(x) for x in args.cfg2_batches.split(",")])

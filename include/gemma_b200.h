@@ -122,6 +122,15 @@ int gg_set_trace(gg_engine* eng, int on);
 int gg_grid(gg_engine* eng, int* out);
 int gg_read_trace(gg_engine* eng, uint64_t* out, int n);
 
+/* forwardPassAndGetToken (engine.ts:904-915) for n independent conversations at once, `steps`
+ * times in a row: row i is KV slot seqs[i] (distinct), fed tokens[i] at position pos[i]; each
+ * step samples row i with sp[i] and draw uniforms[k * n + i] (k = step), appends the token to
+ * the slot's repetition-penalty set, and feeds it at the next position. out_tokens[k * n + i]
+ * receives the token of step k. All layers and the LM head run as tensor-core GEMMs over the n
+ * rows. Requires 4 query heads sharing one KV head; 1 <= n <= min(max_seqs, 128). */
+int gg_decode_batch(gg_engine* eng, int n, const int32_t* seqs, const int32_t* tokens, const int32_t* pos, int steps,
+                    const gg_sample* sp, const double* uniforms, int32_t* out_tokens);
+
 /* linearQ8 (shaders.ts:92-151, dispatched per matrix at engine.ts:769-793, 817-821) on `batch`
  * activation rows at once, on the tensor cores: y[b][m] = sum_k x[b][k] * W[m][k] for one of
  * the engine's Q8_0 matrices. which: 0 fused Q|K|V rows, 1 O, 2 gate/up (gate_i at row 2i,

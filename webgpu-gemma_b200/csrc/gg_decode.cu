@@ -1009,6 +1009,7 @@ extern "C" __global__ void __launch_bounds__(GG_NTHREADS, 1)
         uint8_t* seen = m.seen + (size_t)x.seq * m.seen_stride;
         seen[tok >> 3] |= (uint8_t)(1u << (tok & 7));
         st->seen_count = st->seen_count + 1;
+        if (m.seen_cnt) m.seen_cnt[x.seq] += 1;
       }
       if (st->token_ring && st->ring_len > 0) st->token_ring[st->step_index % st->ring_len] = tok;
       st->step_index = st->step_index + 1;
@@ -1027,6 +1028,75 @@ extern "C" __global__ void __launch_bounds__(GG_NTHREADS, 1)
 }
 
 }  // namespace gg
+
+namespace gg {
+
+// ---------------------------------------------------------------------- batched sampling
+
+// One CTA per row of a [B][V] logits matrix: the 256 lane maxima of the row, then the sampler
+// (sample_token, engine.ts:823-901) with that row's parameters, draw and KV slot's seen set.
+// The sampled token is added to the slot's seen set, becomes the row's next input token, and
+// the row's position advances.
+__global__ void __launch_bounds__(256)
+    gg_batch_sample_kernel(const float* __restrict__ logits, int V, const int32_t* __restrict__ seqs,
+                           const GGSampleDev* __restrict__ sp, const double* __restrict__ unif, uint8_t* seen,
+                           int seen_stride, int32_t* seen_cnt, unsigned long long* keys, int32_t* tokens,
+                           int32_t* pos, int32_t* out) {
+  __shared__ GGModelDev sm;
+  __shared__ GGState ss;
+  const int b = blockIdx.x, t = threadIdx.x;
+  const float* row = logits + (size_t)b * V;
+  const unsigned long long ik = init_lane_key();
+  unsigned long long best = ik;
+  for (int i = t; i < V; i += 256) {
+    float v = __ldcs(row + i);
+    if (!isnan(v)) {
+      if (v == 0.0f) v = 0.0f;  // -0 and +0 compare equal under '>': key them alike
+      const unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - (uint32_t)i);
+      best = k > best ? k : best;
+    }
+  }
+  unsigned long long* rk = keys + (size_t)b * 256;
+  rk[t] = best;
+  const int seq = seqs[b];
+  if (t == 0) {
+    sm.lane_keys = rk;
+    sm.seen = seen;
+    sm.seen_stride = seen_stride;
+    sm.V = V;
+    ss.seq = seq;
+    ss.temperature = sp[b].temperature;
+    ss.top_p = sp[b].top_p;
+    ss.rep_penalty = sp[b].rep_penalty;
+    ss.uniform = unif[b];
+    ss.uniforms = nullptr;
+    ss.seen_count = seen_cnt[seq];
+  }
+  __threadfence_block();
+  __syncthreads();
+  Smem unused{};
+  const int tok = sample_token(sm, &ss, unused);
+  if (t == 0) {
+    out[b] = tok;
+    if (tok >= 0 && tok < V) {
+      atomicOr(reinterpret_cast<unsigned int*>(seen + (size_t)seq * seen_stride) + (tok >> 5), 1u << (tok & 31));
+      seen_cnt[seq] += 1;
+    }
+    tokens[b] = tok;
+    pos[b] += 1;
+  }
+}
+
+}  // namespace gg
+
+cudaError_t gg_batch_sample(const float* logits, int B, int V, const int32_t* seqs, const GGSampleDev* sp,
+                            const double* unif, uint8_t* seen, int seen_stride, int32_t* seen_cnt,
+                            unsigned long long* keys, int32_t* tokens, int32_t* pos, int32_t* out, cudaStream_t s) {
+  if (B <= 0) return cudaErrorInvalidValue;
+  gg::gg_batch_sample_kernel<<<B, 256, 0, s>>>(logits, V, seqs, sp, unif, seen, seen_stride, seen_cnt, keys, tokens,
+                                                pos, out);
+  return cudaGetLastError();
+}
 
 // ------------------------------------------------------------------ sampling without allocation
 //

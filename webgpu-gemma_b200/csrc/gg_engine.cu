@@ -54,12 +54,15 @@ __global__ void gg_init_keys_kernel(unsigned long long* keys) {
   if (i < 256) keys[i] = ((unsigned long long)f32_order_key(-1e30f) << 32) | 0xffffffffull;
 }
 
-__global__ void gg_seen_add_kernel(uint8_t* seen, const int32_t* ids, int n, int V, GGState* st) {
+__global__ void gg_seen_add_kernel(uint8_t* seen, const int32_t* ids, int n, int V, GGState* st, int32_t* slot_cnt) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     int t = ids[i];
     if (t >= 0 && t < V) atomicOr(reinterpret_cast<unsigned int*>(seen) + (t >> 5), 1u << (t & 31));
   }
-  if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&st->seen_count, n);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    atomicAdd(&st->seen_count, n);
+    atomicAdd(slot_cnt, n);
+  }
 }
 
 // Self-test of the bounded waits: waits (with the decode kernel's tag_wait) for a tagged
@@ -120,7 +123,23 @@ struct gg_engine {
   float* pf_att = nullptr;  // attention partials per key range
   uint8_t* pf_tiles = nullptr;
   size_t pf_tiles_half = 0;
+  // batched decode: one token for each of up to bd_max sequences per step
+  int bd_max = 0;
+  float* bd_logits = nullptr;            // [bd_max][V]
+  float* bd_att = nullptr;               // attention partials
+  unsigned long long* bd_keys = nullptr; // [bd_max][256] lane maxima
+  int32_t* bd_seq = nullptr;
+  int32_t* bd_tok = nullptr;
+  int32_t* bd_pos = nullptr;
+  GGSampleDev* bd_sp = nullptr;
+  double* bd_unif = nullptr;
+  int32_t* bd_out = nullptr;
+  int32_t* bd_out_h = nullptr;  // pinned
+  size_t bd_io_cap = 0;         // entries of bd_unif / bd_out / bd_out_h
 };
+
+constexpr int GG_BATCH_MAX = 128;  // sequences per batched step
+static_assert(sizeof(GGSampleDev) == sizeof(gg_sample), "gg_sample layout");
 
 constexpr int GG_PF_CHUNK = 512;  // prompt tokens per batched-prefill chunk
 
@@ -455,6 +474,7 @@ extern "C" int gg_finalize(gg_engine* e) {
   GG_TRY(dalloc(e, &m.dbg_normed, 4 * (size_t)m.H));
   m.seen_stride = ((m.V + 31) / 32) * 4;
   GG_TRY(dalloc(e, &m.seen, (size_t)m.seen_stride * c.max_seqs));
+  GG_TRY(dalloc(e, &m.seen_cnt, sizeof(int32_t) * (size_t)c.max_seqs));
   GG_TRY(dalloc(e, &m.trace, 8 * (size_t)m.grid * GG_TRACE_PHASES * 4));
   GG_TRY(dalloc(e, &e->d_md, sizeof(GGModelDev)));
   GG_TRY(dalloc(e, &e->d_st, sizeof(GGState)));
@@ -597,6 +617,118 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
   return GG_OK;
 }
 
+cudaError_t gg_batch_sample(const float* logits, int B, int V, const int32_t* seqs, const GGSampleDev* sp,
+                            const double* unif, uint8_t* seen, int seen_stride, int32_t* seen_cnt,
+                            unsigned long long* keys, int32_t* tokens, int32_t* pos, int32_t* out, cudaStream_t s);
+
+// One batched decode step for the B sequences in bd_seq / bd_tok / bd_pos (device arrays):
+// all layers on the tensor-core path, LM head as a GEMM, one sampler CTA per row. Leaves the
+// sampled tokens in d_out and in bd_tok, and advances bd_pos.
+static int batch_step(gg_engine* e, int B, int max_pos, const double* d_unif, int32_t* d_out) {
+  const GGModelDev& m = e->md;
+  cudaStream_t s = e->stream;
+  uint8_t* thi = e->pf_tiles;
+  uint8_t* tlo = e->pf_tiles + e->pf_tiles_half;
+  uint32_t* err = &e->d_st->error;
+  const uint64_t to = e->timeout_ns;
+  const int QKV = m.Q + 2 * m.KV;
+  GG_CUDA(e, pf_embed(e->bd_tok, B, m.embd, m.rs_h, m.H, e->pf_hidden, s));
+  GG_CUDA(e, pf_addnorm(nullptr, 0, 0, nullptr, e->pf_hidden, e->pf_hidden, m.layers[0].attn_norm, thi, tlo, B, m.H,
+                        m.eps, s));
+  for (int l = 0; l < m.L; l++) {
+    const GGLayerW& w = m.layers[l];
+    const GGQ8Map* mp = &e->qmaps[(size_t)l * 4];
+    float* kc = m.kcache + (size_t)l * m.CTX * m.KV;
+    float* vc = m.vcache + (size_t)l * m.CTX * m.KV;
+    int sp = pick_splits(gemm_tiles(B, QKV), m.H / 64, e->sm_count);
+    long long plane = (long long)B * QKV;
+    GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, B, e->pf_y, QKV, sp, plane, err, to, s));
+    GG_CUDA(e, bd_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.theta, B, e->bd_pos, e->bd_seq,
+                                m.kv_seq_stride, m.NQH, m.NKH, m.HD, m.eps, e->pf_q, kc, vc, s));
+    GG_CUDA(e, bd_attention(e->pf_q, kc, vc, B, e->bd_pos, e->bd_seq, m.kv_seq_stride, max_pos, m.NQH, m.NKH, m.HD,
+                            m.attn_scale, e->bd_att, thi, tlo, s));
+    sp = pick_splits(gemm_tiles(B, m.H), m.Q / 64, e->sm_count);
+    plane = (long long)B * m.H;
+    GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, B, e->pf_y, m.H, sp, plane, err, to, s));
+    GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_attn_norm, e->pf_hidden, e->pf_res, w.ffn_norm, thi, tlo, B, m.H,
+                          m.eps, s));
+    sp = pick_splits(gemm_tiles(B, 2 * m.I), m.H / 64, e->sm_count);
+    plane = (long long)B * 2 * m.I;
+    GG_CUDA(e, gg_gemm_q8(mp[2], thi, tlo, B, e->pf_y, 2 * m.I, sp, plane, err, to, s));
+    GG_CUDA(e, pf_geglu(e->pf_y, sp, plane, B, m.I, thi, tlo, s));
+    sp = pick_splits(gemm_tiles(B, m.H), m.I / 64, e->sm_count);
+    plane = (long long)B * m.H;
+    GG_CUDA(e, gg_gemm_q8(mp[3], thi, tlo, B, e->pf_y, m.H, sp, plane, err, to, s));
+    // the last layer's output goes through the final norm (output_norm) into the LM-head tiles
+    const float* next_norm = l + 1 < m.L ? m.layers[l + 1].attn_norm : m.out_norm;
+    GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_ffw_norm, e->pf_res, e->pf_hidden, next_norm, thi, tlo, B, m.H,
+                          m.eps, s));
+  }
+  GG_CUDA(e, gg_gemm_q8(e->lm_map, thi, tlo, B, e->bd_logits, m.V, 1, 0, err, to, s));
+  GG_CUDA(e, gg_batch_sample(e->bd_logits, B, m.V, e->bd_seq, e->bd_sp, d_unif, m.seen, m.seen_stride, m.seen_cnt,
+                             e->bd_keys, e->bd_tok, e->bd_pos, d_out, s));
+  return GG_OK;
+}
+
+extern "C" int gg_decode_batch(gg_engine* e, int n, const int32_t* seqs, const int32_t* tokens, const int32_t* pos,
+                               int steps, const gg_sample* sp, const double* uniforms, int32_t* out_tokens) {
+  GG_TRY(ready(e, 0));
+  const gg_config& c = e->cfg;
+  const GGModelDev& m = e->md;
+  if (!e->gemm_ok || m.NQH != 4 || m.NKH != 1)
+    return fail(e, GG_E_STATE, "batched decode needs the tensor-core path and 4 query heads sharing 1 KV head");
+  if (n < 1 || n > std::min(c.max_seqs, GG_BATCH_MAX)) return fail(e, GG_E_ARG, "batch of %d sequences (1..%d)", n, std::min(c.max_seqs, GG_BATCH_MAX));
+  if (steps < 1 || !seqs || !tokens || !pos || !sp || !uniforms || !out_tokens) return fail(e, GG_E_ARG, "bad arguments");
+  int max_pos = 0;
+  std::vector<char> used(c.max_seqs, 0);
+  for (int i = 0; i < n; i++) {
+    if (seqs[i] < 0 || seqs[i] >= c.max_seqs) return fail(e, GG_E_ARG, "seq %d out of range", seqs[i]);
+    if (used[seqs[i]]++) return fail(e, GG_E_ARG, "seq %d appears twice in one batch", seqs[i]);
+    if (tokens[i] < 0 || tokens[i] >= c.vocab_size) return fail(e, GG_E_ARG, "token %d out of range", tokens[i]);
+    if (pos[i] < 0 || pos[i] + steps > c.context_length)
+      return fail(e, GG_E_ARG, "positions %d..%d exceed context %d", pos[i], pos[i] + steps - 1, c.context_length);
+    max_pos = std::max(max_pos, pos[i]);
+  }
+  if (e->bd_max == 0) {  // first batched call: buffers for up to bd_max rows
+    const int bm = std::min(c.max_seqs, GG_BATCH_MAX);
+    GG_TRY(dalloc(e, &e->bd_logits, sizeof(float) * (size_t)bm * m.V));
+    GG_TRY(dalloc(e, &e->bd_att, sizeof(float) * bd_attention_part_floats(bm, m.CTX)));
+    GG_TRY(dalloc(e, &e->bd_keys, 8 * (size_t)bm * 256));
+    GG_TRY(dalloc(e, &e->bd_seq, 4 * (size_t)bm));
+    GG_TRY(dalloc(e, &e->bd_tok, 4 * (size_t)bm));
+    GG_TRY(dalloc(e, &e->bd_pos, 4 * (size_t)bm));
+    GG_TRY(dalloc(e, &e->bd_sp, sizeof(GGSampleDev) * (size_t)bm));
+    e->bd_max = bm;
+  }
+  const size_t io = (size_t)steps * n;
+  if (e->bd_io_cap < io) {
+    if (e->bd_unif) cudaFree(e->bd_unif);
+    if (e->bd_out) cudaFree(e->bd_out);
+    if (e->bd_out_h) cudaFreeHost(e->bd_out_h);
+    e->bd_unif = nullptr;
+    e->bd_out = nullptr;
+    e->bd_out_h = nullptr;
+    e->bd_io_cap = 0;
+    GG_CUDA(e, cudaMalloc(&e->bd_unif, sizeof(double) * io));
+    GG_CUDA(e, cudaMalloc(&e->bd_out, sizeof(int32_t) * io));
+    GG_CUDA(e, cudaMallocHost(&e->bd_out_h, sizeof(int32_t) * io));
+    e->bd_io_cap = io;
+  }
+  cudaStream_t s = e->stream;
+  GG_CUDA(e, cudaMemcpyAsync(e->bd_seq, seqs, 4 * (size_t)n, cudaMemcpyHostToDevice, s));
+  GG_CUDA(e, cudaMemcpyAsync(e->bd_tok, tokens, 4 * (size_t)n, cudaMemcpyHostToDevice, s));
+  GG_CUDA(e, cudaMemcpyAsync(e->bd_pos, pos, 4 * (size_t)n, cudaMemcpyHostToDevice, s));
+  GG_CUDA(e, cudaMemcpyAsync(e->bd_sp, sp, sizeof(GGSampleDev) * (size_t)n, cudaMemcpyHostToDevice, s));
+  GG_CUDA(e, cudaMemcpyAsync(e->bd_unif, uniforms, sizeof(double) * io, cudaMemcpyHostToDevice, s));
+  GG_CUDA(e, cudaEventRecord(e->ev0, s));
+  for (int k = 0; k < steps; k++) GG_TRY(batch_step(e, n, max_pos + k, e->bd_unif + (size_t)k * n, e->bd_out + (size_t)k * n));
+  GG_CUDA(e, cudaEventRecord(e->ev1, s));
+  GG_CUDA(e, cudaMemcpyAsync(e->bd_out_h, e->bd_out, sizeof(int32_t) * io, cudaMemcpyDeviceToHost, s));
+  GG_TRY(finish(e, nullptr));
+  memcpy(out_tokens, e->bd_out_h, sizeof(int32_t) * io);
+  return GG_OK;
+}
+
 extern "C" int gg_prefill(gg_engine* e, int seq, const int32_t* ids, int n, int start_pos) {
   GG_TRY(ready(e, seq));
   if (n <= 0 || !ids) return fail(e, GG_E_ARG, "empty prefill");
@@ -613,7 +745,7 @@ extern "C" int gg_prefill(gg_engine* e, int seq, const int32_t* ids, int n, int 
   }
   GG_CUDA(e, cudaMemcpyAsync(e->d_ids, ids, sizeof(int32_t) * n, cudaMemcpyHostToDevice, e->stream));
   gg_seen_add_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(e->md.seen + (size_t)seq * e->md.seen_stride, e->d_ids, n,
-                                                             e->cfg.vocab_size, e->d_st);
+                                                             e->cfg.vocab_size, e->d_st, e->md.seen_cnt + seq);
   GG_CUDA(e, cudaGetLastError());
   if (e->gemm_ok && !(e->cfg.flags & GG_FLAG_SERIAL_PREFILL)) {
     GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
@@ -774,6 +906,7 @@ extern "C" int gg_seen_reset(gg_engine* e, int seq) {
   GG_TRY(ready(e, seq));
   GG_CUDA(e, cudaMemsetAsync(e->md.seen + (size_t)seq * e->md.seen_stride, 0, e->md.seen_stride, e->stream));
   GG_CUDA(e, cudaMemsetAsync(&e->d_st->seen_count, 0, sizeof(int32_t), e->stream));
+  GG_CUDA(e, cudaMemsetAsync(e->md.seen_cnt + seq, 0, sizeof(int32_t), e->stream));
   GG_CUDA(e, cudaStreamSynchronize(e->stream));
   return GG_OK;
 }
@@ -790,7 +923,7 @@ extern "C" int gg_seen_add(gg_engine* e, int seq, const int32_t* ids, int n) {
   }
   GG_CUDA(e, cudaMemcpyAsync(e->d_ids, ids, sizeof(int32_t) * n, cudaMemcpyHostToDevice, e->stream));
   gg_seen_add_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(e->md.seen + (size_t)seq * e->md.seen_stride, e->d_ids, n,
-                                                             e->cfg.vocab_size, e->d_st);
+                                                             e->cfg.vocab_size, e->d_st, e->md.seen_cnt + seq);
   GG_CUDA(e, cudaGetLastError());
   GG_CUDA(e, cudaStreamSynchronize(e->stream));
   return GG_OK;
@@ -927,6 +1060,9 @@ extern "C" int gg_destroy(gg_engine* e) {
   if (e->d_ring) cudaFree(e->d_ring);
   if (e->h_ring) cudaFreeHost(e->h_ring);
   if (e->h_st) cudaFreeHost(e->h_st);
+  if (e->bd_unif) cudaFree(e->bd_unif);
+  if (e->bd_out) cudaFree(e->bd_out);
+  if (e->bd_out_h) cudaFreeHost(e->bd_out_h);
   if (e->lin_x) cudaFree(e->lin_x);
   if (e->lin_tiles) cudaFree(e->lin_tiles);
   if (e->lin_y) cudaFree(e->lin_y);

@@ -73,6 +73,7 @@ struct GGModelDev {
   float* dbg_normed;    // H: final-normed hidden state (input of the LM head)
   uint8_t* seen;        // [max_seqs][ceil(V/8)] this turn's tokens (repetition penalty)
   int seen_stride;
+  int32_t* seen_cnt;    // [max_seqs] tokens added to each slot's seen set since its last reset
   int max_seqs;
   unsigned long long* trace;  // [grid][GG_TRACE_PHASES][4] globaltimer stamps
   GGLayerW layers[GG_MAX_LAYERS];
@@ -89,6 +90,11 @@ enum : int {
 
 // Per-engine device state. The prefix up to `epoch` is written by the host at the start of a
 // chain of launches; the device advances token/pos/prefill_ids/uniforms/step_index itself.
+// Sampling parameters of one sequence (the C-ABI's gg_sample).
+struct GGSampleDev {
+  float temperature, top_p, rep_penalty, pad_;
+};
+
 struct GGState {
   int32_t token;   // token fed at `pos`
   int32_t pos;     // its position

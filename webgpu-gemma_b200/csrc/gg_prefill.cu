@@ -82,12 +82,20 @@ __global__ void __launch_bounds__(PF_THREADS)
   }
 }
 
+// BATCH: row t is a different sequence, in KV slot seq_arr[t] (slot stride seq_stride floats)
+// at position pos_arr[t]; otherwise row t is prompt position p0 + t of one slot.
+template <bool BATCH>
 __global__ void __launch_bounds__(PF_THREADS)
     pf_qk_kernel(const float* __restrict__ part, int splits, long long plane, const float* __restrict__ q_norm,
                  const float* __restrict__ k_norm, float theta, int p0, int NQH, int NKH, float eps,
-                 float* __restrict__ q_out, float* __restrict__ kc, float* __restrict__ vc) {
+                 float* __restrict__ q_out, float* __restrict__ kc, float* __restrict__ vc,
+                 const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride) {
   constexpr int NJ = PF_HD / 32;
-  const int t = blockIdx.x, pos = p0 + t;
+  const int t = blockIdx.x, pos = BATCH ? pos_arr[t] : p0 + t;
+  if (BATCH) {
+    kc += (size_t)seq_arr[t] * seq_stride;
+    vc += (size_t)seq_arr[t] * seq_stride;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int QD = NQH * PF_HD, KVD = NKH * PF_HD, W = QD + 2 * KVD;
   const long long base = (long long)t * W;
@@ -329,6 +337,134 @@ __global__ void __launch_bounds__(PF_THREADS)
   }
 }
 
+// Decode attention for a batch of sequences: row b has one query token (NQH = 4 heads sharing
+// the single KV head) at position pos[b] of KV slot seqs[b]. A work item is (row, 128-key
+// range); thread (h, j) scores head h against key j of a 64-key block; thread d accumulates
+// output dim d of the four heads. Partial results are merged by bd_attn_merge_kernel.
+constexpr int BD_NH = 4;
+constexpr int BD_PART = BD_NH * PF_HD + 2 * BD_NH;
+constexpr int BD_SMEM = (BD_NH * PF_HD + PA_KB * (PF_HD + 1) + PA_KB * PF_HD + BD_NH * PA_KB + 4 * BD_NH + 8) * 4;
+
+__global__ void __launch_bounds__(PF_THREADS)
+    bd_attn_part_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                        const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride,
+                        float scale, int maxc, float* __restrict__ part) {
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                          // [NH][HD]
+  float* ks = qs + BD_NH * PF_HD;          // [KB][HD+1]
+  float* vs = ks + PA_KB * (PF_HD + 1);    // [KB][HD]
+  float* ps = vs + PA_KB * PF_HD;          // [NH][KB]
+  float* st = ps + BD_NH * PA_KB;          // m[NH], l[NH], alpha[NH], bmax/bsum scratch [NH]
+  float* wred = st + 4 * BD_NH;            // [8] per-warp reductions
+  const int c = blockIdx.x, b = blockIdx.y;
+  const int pos = pos_arr[b];
+  const int k_begin = c * PA_KC;
+  if (k_begin > pos) return;
+  const int k_end = min(k_begin + PA_KC, pos + 1);
+  const float* kb = kc + (size_t)seq_arr[b] * seq_stride;
+  const float* vb = vc + (size_t)seq_arr[b] * seq_stride;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = tid / PA_KB, j = tid % PA_KB;  // score thread: head h, key j of the block
+  for (int i = tid; i < BD_NH * PF_HD; i += PF_THREADS) qs[i] = q[(size_t)b * BD_NH * PF_HD + i];
+  if (tid < BD_NH) {
+    st[tid] = -1e30f;          // m
+    st[BD_NH + tid] = 0.f;     // l
+  }
+  float o[BD_NH] = {0.f, 0.f, 0.f, 0.f};
+  for (int j0 = k_begin; j0 < k_end; j0 += PA_KB) {
+    const int nk = min(PA_KB, k_end - j0);
+    __syncthreads();
+    for (int idx = tid; idx < nk * (PF_HD / 4); idx += PF_THREADS) {
+      const int jj = idx / (PF_HD / 4), d4 = idx % (PF_HD / 4);
+      const float4 kv = reinterpret_cast<const float4*>(kb + (size_t)(j0 + jj) * PF_HD)[d4];
+      float* kd = ks + jj * (PF_HD + 1) + 4 * d4;
+      kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
+      reinterpret_cast<float4*>(vs + jj * PF_HD)[d4] = reinterpret_cast<const float4*>(vb + (size_t)(j0 + jj) * PF_HD)[d4];
+    }
+    __syncthreads();
+    float sc = -INFINITY;
+    if (j < nk) {
+      const float* qr = qs + h * PF_HD;
+      const float* kr = ks + j * (PF_HD + 1);
+      float acc = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < PF_HD; d++) acc = fmaf(qr[d], kr[d], acc);
+      sc = acc * scale;
+    }
+    // per-head block max (two warps per head)
+    float mx = warp_max(sc);
+    if (lane == 0) wred[warp] = mx;
+    __syncthreads();
+    const float bmax = fmaxf(wred[2 * h], wred[2 * h + 1]);
+    const float mold = st[h];
+    const float mnew = fmaxf(mold, bmax);
+    const float e = j < nk ? expf(sc - mnew) : 0.f;
+    ps[h * PA_KB + j] = e;
+    float es = warp_sum(e);
+    __syncthreads();  // wred reuse
+    if (lane == 0) wred[warp] = es;
+    __syncthreads();
+    if (j == 0) {
+      const float alpha = expf(mold - mnew);
+      st[2 * BD_NH + h] = alpha;
+      st[BD_NH + h] = st[BD_NH + h] * alpha + wred[2 * h] + wred[2 * h + 1];
+      st[h] = mnew;
+    }
+    __syncthreads();
+    const int d = tid;
+#pragma unroll
+    for (int hh = 0; hh < BD_NH; hh++) {
+      float acc = o[hh] * st[2 * BD_NH + hh];
+      const float* pr = ps + hh * PA_KB;
+      for (int jj = 0; jj < nk; jj++) acc = fmaf(pr[jj], vs[jj * PF_HD + d], acc);
+      o[hh] = acc;
+    }
+  }
+  float* dst = part + ((size_t)b * maxc + c) * BD_PART;
+#pragma unroll
+  for (int hh = 0; hh < BD_NH; hh++) dst[hh * PF_HD + tid] = o[hh];
+  if (tid < BD_NH) {
+    dst[BD_NH * PF_HD + tid] = st[tid];
+    dst[BD_NH * PF_HD + BD_NH + tid] = st[BD_NH + tid];
+  }
+}
+
+__global__ void __launch_bounds__(PF_THREADS)
+    bd_attn_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_arr, int maxc, uint8_t* thi,
+                         uint8_t* tlo) {
+  __shared__ float wgt[16][BD_NH];
+  __shared__ float inv[BD_NH];
+  const int b = blockIdx.x;
+  const int nch = min(maxc, pos_arr[b] / PA_KC + 1);
+  const float* base = part + (size_t)b * maxc * BD_PART;
+  if (threadIdx.x < BD_NH) {
+    const int h = threadIdx.x;
+    float M = -1e30f;
+    for (int c = 0; c < nch; c++) M = fmaxf(M, base[(size_t)c * BD_PART + BD_NH * PF_HD + h]);
+    float L = 0.f;
+    for (int c = 0; c < nch; c++) {
+      const float* pc = base + (size_t)c * BD_PART + BD_NH * PF_HD;
+      const float w = expf(pc[h] - M);
+      wgt[c][h] = w;
+      L += pc[BD_NH + h] * w;
+    }
+    inv[h] = 1.0f / L;
+  }
+  __syncthreads();
+  if (threadIdx.x >= BD_NH * (PF_HD / 8)) return;
+  const int h = threadIdx.x / (PF_HD / 8), c8 = threadIdx.x % (PF_HD / 8);
+  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int c = 0; c < nch; c++) {
+    const float* src = base + (size_t)c * BD_PART + h * PF_HD + 8 * c8;
+    const float w = wgt[c][h];
+#pragma unroll
+    for (int jj = 0; jj < 8; jj++) v[jj] = fmaf(src[jj], w, v[jj]);
+  }
+#pragma unroll
+  for (int jj = 0; jj < 8; jj++) v[jj] *= inv[h];
+  xtile_put8(thi, tlo, BD_NH * PF_HD / 64, b, h * PF_HD + 8 * c8, v);
+}
+
 __global__ void __launch_bounds__(PF_THREADS) pf_geglu_kernel(const float* __restrict__ gu, int splits, long long plane,
                                                               int T, int I, uint8_t* thi, uint8_t* tlo) {
   const int c8 = I / 8;
@@ -378,7 +514,17 @@ cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, con
                              const float* k_norm, float theta, int T, int p0, int NQH, int NKH, int HD, float eps,
                              float* q_out, float* kc, float* vc, cudaStream_t s) {
   if (T <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
-  pf_qk_kernel<<<T, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, theta, p0, NQH, NKH, eps, q_out, kc, vc);
+  pf_qk_kernel<false><<<T, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, theta, p0, NQH, NKH, eps, q_out,
+                                               kc, vc, nullptr, nullptr, 0);
+  return cudaGetLastError();
+}
+
+cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm, const float* k_norm,
+                             float theta, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
+                             int NKH, int HD, float eps, float* q_out, float* kc, float* vc, cudaStream_t s) {
+  if (B <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
+  pf_qk_kernel<true><<<B, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, theta, 0, NQH, NKH, eps, q_out, kc,
+                                              vc, pos, seqs, seq_stride);
   return cudaGetLastError();
 }
 
@@ -411,6 +557,33 @@ cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T
   r = cudaGetLastError();
   if (r != cudaSuccess) return r;
   pf_attn_merge_kernel<<<dim3(nb, NKH), PF_THREADS, 0, s>>>(part, T, p0, NQH, NKH, maxc, thi, tlo);
+  return cudaGetLastError();
+}
+
+size_t bd_attention_part_floats(int max_rows, int ctx) {
+  return (size_t)max_rows * ((ctx + PA_KC - 1) / PA_KC) * BD_PART;
+}
+
+cudaError_t bd_attention(const float* q, const float* kc, const float* vc, int B, const int32_t* pos,
+                         const int32_t* seqs, size_t seq_stride, int max_pos, int NQH, int NKH, int HD, float scale,
+                         float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
+  if (B <= 0 || HD != PF_HD || NQH != BD_NH || NKH != 1) return cudaErrorInvalidValue;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t r = cudaGetDevice(&dev);
+  if (r != cudaSuccess) return r;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    r = cudaFuncSetAttribute(bd_attn_part_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BD_SMEM);
+    if (r != cudaSuccess) return r;
+    attr_set[dev] = true;
+  }
+  const int maxc = max_pos / PA_KC + 1;
+  if (maxc > 16) return cudaErrorInvalidValue;
+  bd_attn_part_kernel<<<dim3(maxc, B), PF_THREADS, BD_SMEM, s>>>(q, kc, vc, pos, seqs, seq_stride, scale, maxc, part);
+  r = cudaGetLastError();
+  if (r != cudaSuccess) return r;
+  bd_attn_merge_kernel<<<B, PF_THREADS, 0, s>>>(part, pos, maxc, thi, tlo);
   return cudaGetLastError();
 }
 

@@ -37,3 +37,19 @@ cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T
 // activation tiles of width I.
 cudaError_t pf_geglu(const float* gu, int splits, long long plane, int T, int I, uint8_t* thi, uint8_t* tlo,
                      cudaStream_t s);
+
+// ---- batched decode: row b is one token of the sequence in KV slot seqs[b] at position pos[b]
+
+// As pf_qk_rope_store, per row: kc/vc point at this layer's rows of slot 0, slots seq_stride
+// floats apart.
+cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm, const float* k_norm,
+                             float theta, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
+                             int NKH, int HD, float eps, float* q_out, float* kc, float* vc, cudaStream_t s);
+
+// Attention of each row's query over its slot's cache rows 0..pos[b] (4 query heads sharing one
+// KV head), written as activation tiles. max_pos >= every pos[b]; `part` holds
+// bd_attention_part_floats(B, ctx) floats.
+size_t bd_attention_part_floats(int max_rows, int ctx);
+cudaError_t bd_attention(const float* q, const float* kc, const float* vc, int B, const int32_t* pos,
+                         const int32_t* seqs, size_t seq_stride, int max_pos, int NQH, int NKH, int HD, float scale,
+                         float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);

@@ -44,6 +44,7 @@ SIGNATURES = {
     "gg_set_trace": (_I, [_P, _I]),
     "gg_read_trace": (_I, [_P, _P, _I]),
     "gg_linear": (_I, [_P, _I, _I, _P, _I, _P]),
+    "gg_decode_batch": (_I, [_P, _I, _P, _P, _P, _I, _P, _P, _P]),
     "gg_selftest_wait": (_I, [_P, ctypes.c_uint64]),
     "gg_sample_logits_noalloc": (_I, [_P, _I, _P, _P, _D, _P, _P]),
     "gg_set_timeout": (_I, [_P, ctypes.c_uint64]),
@@ -199,6 +200,21 @@ class NativeEngine:
     def read_trace(self, n: int) -> np.ndarray:
         out = np.zeros(n, np.uint64)
         self._check(self.lib.gg_read_trace(self.h, out.ctypes.data_as(_P), n))
+        return out
+
+    def decode_batch(self, seqs, tokens, pos, steps: int, samples, uniforms) -> np.ndarray:
+        """Batched decode: row i = KV slot seqs[i] fed tokens[i] at pos[i]; `samples` is one
+        (temperature, top_p, rep) per row; uniforms [steps][n]. Returns tokens [steps][n]."""
+        seqs = np.ascontiguousarray(seqs, np.int32)
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        n = seqs.size
+        sp = (GGSample * n)(*[GGSample(float(t), float(p), float(r), 0.0) for (t, p, r) in samples])
+        u = np.ascontiguousarray(np.asarray(uniforms, np.float64).reshape(steps, n))
+        out = np.empty((steps, n), np.int32)
+        self._check(self.lib.gg_decode_batch(self.h, n, seqs.ctypes.data_as(_P), tokens.ctypes.data_as(_P),
+                                             pos.ctypes.data_as(_P), int(steps), ctypes.cast(sp, _P),
+                                             u.ctypes.data_as(_P), out.ctypes.data_as(_P)))
         return out
 
     def linear(self, which: int, layer: int, x: np.ndarray) -> np.ndarray:
