@@ -160,6 +160,7 @@ def cpu_oracle_rate(tensors, cfg, n_tokens: int, prompt_len: int = 4):
     from oracle import oracle
     from gemma_b200 import synth
 
+    threads = oracle.use_all_host_cores()
     m = oracle.OracleModel.from_tensors(cfg, tensors)
     prompt = synth.make_prompt(SEED, prompt_len, cfg.vocab_size)
     for i, t in enumerate(prompt):
@@ -173,7 +174,6 @@ def cpu_oracle_rate(tensors, cfg, n_tokens: int, prompt_len: int = 4):
         pos += 1
     dt = time.perf_counter() - t0
     m.close()
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     sample = (f"1B synthetic (seed 1), {prompt_len}-token prompt then {n_tokens} greedy decode tokens at positions "
               f"{prompt_len}..{prompt_len + n_tokens - 1}, full LM head + argmax per token, {threads} OpenMP threads")
     return n_tokens / dt, threads, sample
@@ -188,6 +188,7 @@ def run_reference(args):
     cfg = shape.config()
     tensors = synth.make_tensors(shape, SEED)
     from oracle import oracle
+    threads = oracle.use_all_host_cores()
     m = oracle.OracleModel.from_tensors(cfg, tensors)
     prompt = synth.make_prompt(SEED, 4, cfg.vocab_size)
     for i, t in enumerate(prompt):
@@ -207,7 +208,6 @@ def run_reference(args):
     for _ in range(args.steps):
         tok, pos = one(tok, pos)
     dt = time.perf_counter() - t0
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     v = args.steps / dt
     sample = (f"one greedy decode token per step of the 1B synthetic model (seed 1) with LM head + argmax, "
               f"positions cycling over {lo}..{lo + DECODE_LEN - 1} after a 4-token prompt, {threads} OpenMP threads")

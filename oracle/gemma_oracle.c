@@ -39,6 +39,9 @@
 #include <stdlib.h>
 #include <string.h>
 #include <stdio.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 #define OR_EXPORT __attribute__((visibility("default")))
 
@@ -444,4 +447,22 @@ OR_EXPORT int or_lm_head(or_model *m, int seq, float *logits) {
 OR_EXPORT const float *or_kv_row(or_model *m, int seq, int layer, int pos, int which) {
     size_t off = ((size_t)seq * m->c.num_layers + layer) * kv_layer_elems(&m->c) + (size_t)pos * m->c.kv_dim;
     return (which ? m->vc : m->kc) + off;
+}
+
+/* Thread count of the parallel loops (the benchmark's CPU legs pin it to the host's cores, since
+ * process launchers may set OMP_NUM_THREADS=1). */
+OR_EXPORT void or_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
+OR_EXPORT int or_get_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
 }

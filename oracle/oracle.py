@@ -68,6 +68,8 @@ def lib() -> ctypes.CDLL:
             "or_forward": (I, [P, I, I, I, P]),
             "or_lm_head": (I, [P, I, P]),
             "or_kv_row": (P, [P, I, I, I, I]),
+            "or_set_threads": (None, [I]),
+            "or_get_threads": (I, []),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -237,3 +239,10 @@ class OracleModel:
                 all_logits.append(lg)
             toks.append(argmax(lg))
         return (toks, all_logits) if return_logits else toks
+
+
+def use_all_host_cores() -> int:
+    """Run the parallel loops on every core this process may use; returns the thread count."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    lib().or_set_threads(n)
+    return int(lib().or_get_threads())
