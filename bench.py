@@ -362,6 +362,50 @@ def run_cfg4(args):
         dist.destroy_process_group()
 
 
+def run_turns(name: str, shape_name: str, seed: int, turns, reps: int = 3):
+    """Greedy multi-turn run through the C-ABI: each turn prefills its new ids after the cached
+    prefix (the last sampled token of the previous turn is fed first, as generate() does),
+    then decodes. Reports per turn the TTFT (prefill + first token, wall clock, median of
+    `reps` runs) and the decode tok/s (device time of the chained decode)."""
+    from gemma_b200 import synth
+    from gemma_b200.native import engine_from_tensors
+    shape = synth.SHAPES[shape_name]
+    cfg = shape.config()
+    eng = engine_from_tensors(cfg, synth.make_tensors(shape, seed))
+    out = []
+    for rep in range(reps):
+        eng.reset_kv(0)
+        eng.seen_reset(0)
+        pos, last = 0, None
+        res = []
+        for ti, (plen, ngen) in enumerate(turns):
+            ids = [int(t) for t in synth.make_prompt(seed * 1000 + ti, plen, cfg.vocab_size)]
+            if last is not None:
+                ids = [last] + ids[:-1]
+            t0 = time.perf_counter()
+            eng.prefill(ids, pos)
+            tok = eng.sample_last(0)
+            ttft = 1000 * (time.perf_counter() - t0)
+            pos += len(ids)
+            toks = eng.decode(tok, pos, ngen - 1)
+            dev = eng.last_device_ms()
+            pos += ngen - 1
+            last = int(toks[-1])
+            res.append({"turn": ti + 1, "prompt": len(ids), "start_pos": pos - len(ids) - (ngen - 1),
+                        "ttft_ms": round(ttft, 3), "decode_tok_s": round((ngen - 1) / (dev / 1000), 1),
+                        "end_pos": pos})
+        out.append(res)
+    med = []
+    for ti in range(len(turns)):
+        rows = [o[ti] for o in out]
+        r = dict(rows[0])
+        r["ttft_ms"] = statistics.median(x["ttft_ms"] for x in rows)
+        r["decode_tok_s"] = statistics.median(x["decode_tok_s"] for x in rows)
+        med.append(r)
+    print(json.dumps({name: f"{shape_name} synthetic (seed {seed}), greedy, batch 1", "turns": med}))
+    eng.close()
+
+
 def run_profile_prefill():
     """Launch sequence for an ncu launch list of the batched prefill: the 1B model, two
     512-token prefills (26 layers x 9 launches each) and the first token."""
@@ -393,6 +437,8 @@ def main():
                     help="short fixed sequence for ncu: 4 decode launches at positions 640..643")
     ap.add_argument("--cfg2", action="store_true", help="config 2 matvec/GEMM microbench lines")
     ap.add_argument("--cfg4", action="store_true", help="config 4: 64 sequences per GPU, batched sampled decode")
+    ap.add_argument("--cfg0", action="store_true", help="config 0: 270M, 32-token prompt, 64 greedy tokens")
+    ap.add_argument("--cfg3", action="store_true", help="config 3: 1B two-turn long context (1536+128, +256+128)")
     ap.add_argument("--cfg2-shapes", default="", help="comma-separated subset of qkv,o,gate_up,down,lm_head")
     ap.add_argument("--cfg2-batches", default="1,8,64")
     ap.add_argument("--cfg2-reps", type=int, default=10)
@@ -401,6 +447,10 @@ def main():
     args = ap.parse_args()
     if args.cfg4:
         return run_cfg4(args)
+    if args.cfg0:
+        return run_turns("cfg0", "270m", 0, [(32, 64)])
+    if args.cfg3:
+        return run_turns("cfg3", "1b", 1, [(1536, 128), (256, 128)])
     if args.cfg2:
         return run_cfg2(args.cfg2_reps, [x for x in args.cfg2_shapes.split(",") if x],
                         [int(x) for x in args.cfg2_batches.split(",")])
