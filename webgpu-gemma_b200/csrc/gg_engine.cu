@@ -562,9 +562,10 @@ static void set_sampling(GGState& s, const gg_sample* sp, double u) {
   s.uniform = u;
 }
 
-static int pick_splits(int tiles, int KS, int sms);
+static int pick_splits(int tiles, int KS, int slots);
 
 static int gemm_tiles(int T, int M) { return (T <= 64 ? 1 : (T + 127) / 128) * (M / 128); }
+static int gemm_slots(const gg_engine* e, int T) { return e->sm_count * (T <= 64 ? 2 : 1); }
 
 // Batched prefill of ids already in e->d_ids: chunks of up to GG_PF_CHUNK tokens, each layer
 // as four tensor-core GEMMs over the chunk's rows and the kernels of gg_prefill.cu between them.
@@ -588,22 +589,22 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
       const GGQ8Map* mp = &e->qmaps[(size_t)l * 4];
       float* kc = m.kcache + (size_t)seq * m.kv_seq_stride + (size_t)l * m.CTX * m.KV;
       float* vc = m.vcache + (size_t)seq * m.kv_seq_stride + (size_t)l * m.CTX * m.KV;
-      int sp = pick_splits(gemm_tiles(T, QKV), m.H / 64, e->sm_count);
+      int sp = pick_splits(gemm_tiles(T, QKV), m.H / 64, gemm_slots(e, T));
       long long plane = (long long)T * QKV;
       GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, T, e->pf_y, QKV, sp, plane, err, to, s));
       GG_CUDA(e, pf_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.theta, T, p0, m.NQH, m.NKH, m.HD, m.eps,
                                   e->pf_q, kc, vc, s));
       GG_CUDA(e, pf_attention(e->pf_q, kc, vc, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, e->pf_att, thi, tlo, s));
-      sp = pick_splits(gemm_tiles(T, m.H), m.Q / 64, e->sm_count);
+      sp = pick_splits(gemm_tiles(T, m.H), m.Q / 64, gemm_slots(e, T));
       plane = (long long)T * m.H;
       GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));
       GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_attn_norm, e->pf_hidden, e->pf_res, w.ffn_norm, thi, tlo, T,
                             m.H, m.eps, s));
-      sp = pick_splits(gemm_tiles(T, 2 * m.I), m.H / 64, e->sm_count);
+      sp = pick_splits(gemm_tiles(T, 2 * m.I), m.H / 64, gemm_slots(e, T));
       plane = (long long)T * 2 * m.I;
       GG_CUDA(e, gg_gemm_q8(mp[2], thi, tlo, T, e->pf_y, 2 * m.I, sp, plane, err, to, s));
       GG_CUDA(e, pf_geglu(e->pf_y, sp, plane, T, m.I, thi, tlo, s));
-      sp = pick_splits(gemm_tiles(T, m.H), m.I / 64, e->sm_count);
+      sp = pick_splits(gemm_tiles(T, m.H), m.I / 64, gemm_slots(e, T));
       plane = (long long)T * m.H;
       GG_CUDA(e, gg_gemm_q8(mp[3], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));
       const float* next_norm = l + 1 < m.L ? m.layers[l + 1].attn_norm : nullptr;
@@ -640,23 +641,23 @@ static int batch_step(gg_engine* e, int B, int max_pos, const double* d_unif, in
     const GGQ8Map* mp = &e->qmaps[(size_t)l * 4];
     float* kc = m.kcache + (size_t)l * m.CTX * m.KV;
     float* vc = m.vcache + (size_t)l * m.CTX * m.KV;
-    int sp = pick_splits(gemm_tiles(B, QKV), m.H / 64, e->sm_count);
+    int sp = pick_splits(gemm_tiles(B, QKV), m.H / 64, gemm_slots(e, B));
     long long plane = (long long)B * QKV;
     GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, B, e->pf_y, QKV, sp, plane, err, to, s));
     GG_CUDA(e, bd_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.theta, B, e->bd_pos, e->bd_seq,
                                 m.kv_seq_stride, m.NQH, m.NKH, m.HD, m.eps, e->pf_q, kc, vc, s));
     GG_CUDA(e, bd_attention(e->pf_q, kc, vc, B, e->bd_pos, e->bd_seq, m.kv_seq_stride, max_pos, m.NQH, m.NKH, m.HD,
                             m.attn_scale, e->bd_att, thi, tlo, s));
-    sp = pick_splits(gemm_tiles(B, m.H), m.Q / 64, e->sm_count);
+    sp = pick_splits(gemm_tiles(B, m.H), m.Q / 64, gemm_slots(e, B));
     plane = (long long)B * m.H;
     GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, B, e->pf_y, m.H, sp, plane, err, to, s));
     GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_attn_norm, e->pf_hidden, e->pf_res, w.ffn_norm, thi, tlo, B, m.H,
                           m.eps, s));
-    sp = pick_splits(gemm_tiles(B, 2 * m.I), m.H / 64, e->sm_count);
+    sp = pick_splits(gemm_tiles(B, 2 * m.I), m.H / 64, gemm_slots(e, B));
     plane = (long long)B * 2 * m.I;
     GG_CUDA(e, gg_gemm_q8(mp[2], thi, tlo, B, e->pf_y, 2 * m.I, sp, plane, err, to, s));
     GG_CUDA(e, pf_geglu(e->pf_y, sp, plane, B, m.I, thi, tlo, s));
-    sp = pick_splits(gemm_tiles(B, m.H), m.I / 64, e->sm_count);
+    sp = pick_splits(gemm_tiles(B, m.H), m.I / 64, gemm_slots(e, B));
     plane = (long long)B * m.H;
     GG_CUDA(e, gg_gemm_q8(mp[3], thi, tlo, B, e->pf_y, m.H, sp, plane, err, to, s));
     // the last layer's output goes through the final norm (output_norm) into the LM-head tiles
@@ -984,10 +985,11 @@ __global__ void gg_sum_splits_kernel(const float* __restrict__ p, int splits, lo
   }
 }
 
-// K-splits so that the tiles of one GEMM cover the SMs without an empty split.
-static int pick_splits(int tiles, int KS, int sms) {
+// K-splits so that the tiles of one GEMM fill the CTA slots without an empty split (at most 16,
+// at least 3 K slabs each). Tiles of up to 64 rows run two CTAs per SM.
+static int pick_splits(int tiles, int KS, int slots) {
   int s = 1;
-  while (tiles * (s + 1) <= sms && KS / (s + 1) >= 3) s++;
+  while (s < 16 && tiles * (s + 1) <= slots && KS / (s + 1) >= 3) s++;
   while (s > 1 && (long long)(s - 1) * ((KS + s - 1) / s) >= KS) s--;
   return s;
 }
@@ -1011,8 +1013,7 @@ extern "C" int gg_linear(gg_engine* e, int which, int layer, const float* x, int
   if (which < 4 && (layer < 0 || layer >= e->cfg.num_layers)) return fail(e, GG_E_ARG, "layer %d out of range", layer);
   const GGQ8Map& w = which == 4 ? e->lm_map : e->qmaps[(size_t)layer * 4 + which];
   const int M = w.M, K = w.K, T = batch;
-  const int tiles = ((T + (T <= 64 ? 63 : 127)) / (T <= 64 ? 64 : 128)) * (M / 128);
-  const int splits = pick_splits(tiles, K / 64, e->sm_count);
+  const int splits = pick_splits(gemm_tiles(T, M), K / 64, gemm_slots(e, T));
   const size_t tb = gg_xtiles_bytes(T, K);
   GG_TRY(grow(e, (void**)&e->lin_x, &e->lin_x_cap, sizeof(float) * (size_t)T * K));
   GG_TRY(grow(e, (void**)&e->lin_tiles, &e->lin_tiles_cap, 2 * tb));
