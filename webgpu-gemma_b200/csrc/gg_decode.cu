@@ -538,9 +538,8 @@ struct Consumer {
 #pragma unroll
         for (int j = 0; j < NJ / 2; j++) {
           const int i = lane + 32 * j;
-          const float freq = 1.0f / powf(Lw.theta, (float)(i * 2) / (float)HD);
-          const float ang = (float)x.pos * freq;
-          const float cs = cosf(ang), sn = sinf(ang);
+          const float2 cr = Lw.rope[(size_t)x.pos * (HD / 2) + i];  // (cos, sin) of pos * freq_i
+          const float cs = cr.x, sn = cr.y;
           const float x0 = v[j], x1 = v[j + NJ / 2];
           v[j] = x0 * cs - x1 * sn;
           v[j + NJ / 2] = x0 * sn + x1 * cs;

@@ -95,13 +95,12 @@ struct SpinCtl {
 #define GG_QUIET_SPIN_NS 20000ull
 
 // Wait for a tagged word; on timeout (or an error raised elsewhere) return 0.0f and set err.
-// Polls back off with __nanosleep so waiting warps do not flood L2 with loads.
+// Polls without a back-off: a sleep between polls adds its length to every hand-over.
 GG_DEV float tag_wait(const uint64_t* p, uint32_t tag, const SpinCtl& sc) {
   uint64_t w = tag_load(p);
   if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
-    __nanosleep(it < 8 ? 32 : 128);
     w = tag_load(p);
     if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
     if ((it & 15u) == 0) {
@@ -119,7 +118,9 @@ GG_DEV float tag_wait(const uint64_t* p, uint32_t tag, const SpinCtl& sc) {
 
 // Bounded wait on an mbarrier phase. Returns false (and sets err) on timeout.
 GG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const SpinCtl& sc) {
-  if (mbar_try_wait(bar, parity)) return true;
+  // Fast path without reading the clock; the timed loop below bounds the wait.
+  for (int it = 0; it < 64; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;

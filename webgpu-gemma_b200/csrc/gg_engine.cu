@@ -429,6 +429,22 @@ extern "C" int gg_finalize(gg_engine* e) {
     bool swa = (l % c.swa_period) < (c.swa_period - 1);
     w.theta = swa ? c.rope_theta_swa : c.rope_theta_global;
   }
+  // RoPE tables, one per distinct theta
+  {
+    std::vector<std::pair<float, float2*>> tabs;
+    for (int l = 0; l < c.num_layers; l++) {
+      GGLayerW& w = m.layers[l];
+      float2* tab = nullptr;
+      for (auto& t : tabs)
+        if (t.first == w.theta) tab = t.second;
+      if (!tab) {
+        GG_TRY(dalloc(e, &tab, sizeof(float2) * (size_t)m.CTX * (m.HD / 2)));
+        GG_CUDA(e, gg_rope_table(w.theta, m.HD, m.CTX, tab, e->stream));
+        tabs.push_back({w.theta, tab});
+      }
+      w.rope = tab;
+    }
+  }
   // Tiled weight copies for the batched (tensor-core) path; unusable shapes leave it off.
   e->gemm_ok = (m.H % 128 == 0) && (m.Q % 64 == 0) && ((m.Q + 2 * m.KV) % 128 == 0) && (m.I % 64 == 0) &&
                ((2 * m.I) % 128 == 0) && (m.V % 128 == 0) && (m.H % 64 == 0);
@@ -592,7 +608,7 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
       int sp = pick_splits(gemm_tiles(T, QKV), m.H / 64, gemm_slots(e, T));
       long long plane = (long long)T * QKV;
       GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, T, e->pf_y, QKV, sp, plane, err, to, s));
-      GG_CUDA(e, pf_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.theta, T, p0, m.NQH, m.NKH, m.HD, m.eps,
+      GG_CUDA(e, pf_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, T, p0, m.NQH, m.NKH, m.HD, m.eps,
                                   e->pf_q, kc, vc, s));
       GG_CUDA(e, pf_attention(e->pf_q, kc, vc, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, e->pf_att, thi, tlo, s));
       sp = pick_splits(gemm_tiles(T, m.H), m.Q / 64, gemm_slots(e, T));
@@ -644,7 +660,7 @@ static int batch_step(gg_engine* e, int B, int max_pos, const double* d_unif, in
     int sp = pick_splits(gemm_tiles(B, QKV), m.H / 64, gemm_slots(e, B));
     long long plane = (long long)B * QKV;
     GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, B, e->pf_y, QKV, sp, plane, err, to, s));
-    GG_CUDA(e, bd_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.theta, B, e->bd_pos, e->bd_seq,
+    GG_CUDA(e, bd_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, B, e->bd_pos, e->bd_seq,
                                 m.kv_seq_stride, m.NQH, m.NKH, m.HD, m.eps, e->pf_q, kc, vc, s));
     GG_CUDA(e, bd_attention(e->pf_q, kc, vc, B, e->bd_pos, e->bd_seq, m.kv_seq_stride, max_pos, m.NQH, m.NKH, m.HD,
                             m.attn_scale, e->bd_att, thi, tlo, s));

@@ -33,6 +33,7 @@ struct GGLayerW {
   const float* post_ffw_norm;
   float theta;
   int pad_;
+  const float2* rope;  // [CTX][HD/2] (cos, sin) of pos * theta^(-2i/HD) for this layer's theta
 };
 
 struct GGPhaseCfg {

@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(PF_THREADS)
 template <bool BATCH>
 __global__ void __launch_bounds__(PF_THREADS)
     pf_qk_kernel(const float* __restrict__ part, int splits, long long plane, const float* __restrict__ q_norm,
-                 const float* __restrict__ k_norm, float theta, int p0, int NQH, int NKH, float eps,
+                 const float* __restrict__ k_norm, const float2* __restrict__ rope, int p0, int NQH, int NKH, float eps,
                  float* __restrict__ q_out, float* __restrict__ kc, float* __restrict__ vc,
                  const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride) {
   constexpr int NJ = PF_HD / 32;
@@ -117,9 +117,8 @@ __global__ void __launch_bounds__(PF_THREADS)
 #pragma unroll
     for (int j = 0; j < NJ / 2; j++) {
       const int i = lane + 32 * j;
-      const float freq = 1.0f / powf(theta, (float)(i * 2) / (float)PF_HD);
-      const float ang = (float)pos * freq;
-      const float cs = cosf(ang), sn = sinf(ang);
+      const float2 cr = rope[(size_t)pos * (PF_HD / 2) + i];  // (cos, sin) of pos * freq_i
+      const float cs = cr.x, sn = cr.y;
       const float x0 = v[j], x1 = v[j + NJ / 2];
       v[j] = x0 * cs - x1 * sn;
       v[j + NJ / 2] = x0 * sn + x1 * cs;
@@ -492,9 +491,26 @@ __global__ void __launch_bounds__(PF_THREADS) pf_geglu_kernel(const float* __res
   }
 }
 
+// RoPE table: (cos, sin) of pos * freq_i, freq_i = 1 / theta^(2i/HD), the same f32 expressions
+// the shader evaluates per step (shaders.ts:420-467).
+__global__ void pf_rope_table_kernel(float theta, int HD, int ctx, float2* out) {
+  const int half = HD / 2;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < ctx * half; idx += gridDim.x * blockDim.x) {
+    const int pos = idx / half, i = idx % half;
+    const float freq = 1.0f / powf(theta, (float)(i * 2) / (float)HD);
+    const float ang = (float)pos * freq;
+    out[idx] = make_float2(cosf(ang), sinf(ang));
+  }
+}
+
 }  // namespace gg
 
 using namespace gg;
+
+cudaError_t gg_rope_table(float theta, int HD, int ctx, float2* out, cudaStream_t s) {
+  pf_rope_table_kernel<<<148 * 4, 256, 0, s>>>(theta, HD, ctx, out);
+  return cudaGetLastError();
+}
 
 cudaError_t pf_embed(const int32_t* ids, int T, const uint8_t* embd, int rs, int H, float* hidden, cudaStream_t s) {
   if (T <= 0) return cudaErrorInvalidValue;
@@ -511,19 +527,19 @@ cudaError_t pf_addnorm(const float* part, int splits, long long plane, const flo
 }
 
 cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm,
-                             const float* k_norm, float theta, int T, int p0, int NQH, int NKH, int HD, float eps,
+                             const float* k_norm, const float2* rope, int T, int p0, int NQH, int NKH, int HD, float eps,
                              float* q_out, float* kc, float* vc, cudaStream_t s) {
   if (T <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
-  pf_qk_kernel<false><<<T, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, theta, p0, NQH, NKH, eps, q_out,
+  pf_qk_kernel<false><<<T, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, p0, NQH, NKH, eps, q_out,
                                                kc, vc, nullptr, nullptr, 0);
   return cudaGetLastError();
 }
 
 cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm, const float* k_norm,
-                             float theta, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
+                             const float2* rope, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
                              int NKH, int HD, float eps, float* q_out, float* kc, float* vc, cudaStream_t s) {
   if (B <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
-  pf_qk_kernel<true><<<B, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, theta, 0, NQH, NKH, eps, q_out, kc,
+  pf_qk_kernel<true><<<B, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, 0, NQH, NKH, eps, q_out, kc,
                                               vc, pos, seqs, seq_stride);
   return cudaGetLastError();
 }

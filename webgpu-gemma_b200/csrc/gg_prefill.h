@@ -8,6 +8,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// (cos, sin) table [ctx][HD/2] of pos * theta^(-2i/HD) (the RoPE rotation of shaders.ts:420-467).
+cudaError_t gg_rope_table(float theta, int HD, int ctx, float2* out, cudaStream_t s);
+
 // hidden[t] = dequantised embedding row ids[t] * sqrt(H) (shaders.ts:2-23).
 cudaError_t pf_embed(const int32_t* ids, int T, const uint8_t* embd, int rs, int H, float* hidden, cudaStream_t s);
 
@@ -23,7 +26,7 @@ cudaError_t pf_addnorm(const float* part, int splits, long long plane, const flo
 // Per token: sum the QKV planes, q/k per-head rmsNorm + RoPE at position p0 + t
 // (shaders.ts:420-467), q -> q_out [T][NQH*HD], k and v -> rows p0.. of this layer's cache.
 cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm,
-                             const float* k_norm, float theta, int T, int p0, int NQH, int NKH, int HD, float eps,
+                             const float* k_norm, const float2* rope, int T, int p0, int NQH, int NKH, int HD, float eps,
                              float* q_out, float* kc, float* vc, cudaStream_t s);
 
 // Causal attention of the T queries at positions p0..p0+T-1 over cache rows 0..p0+t
@@ -43,7 +46,7 @@ cudaError_t pf_geglu(const float* gu, int splits, long long plane, int T, int I,
 // As pf_qk_rope_store, per row: kc/vc point at this layer's rows of slot 0, slots seq_stride
 // floats apart.
 cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm, const float* k_norm,
-                             float theta, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
+                             const float2* rope, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
                              int NKH, int HD, float eps, float* q_out, float* kc, float* vc, cudaStream_t s);
 
 // Attention of each row's query over its slot's cache rows 0..pos[b] (4 query heads sharing one
