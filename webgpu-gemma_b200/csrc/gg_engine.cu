@@ -456,6 +456,9 @@ extern "C" int gg_finalize(gg_engine* e) {
       uint8_t* t = nullptr;
       GG_TRY(dalloc(e, &t, gg_q8_tiles_bytes(M[j], K[j])));
       GG_CUDA(e, gg_make_q8_tiles(&e->qmaps[(size_t)l * 4 + j], ptr[j], M[j], K[j], t, e->stream));
+      uint8_t* dt = nullptr;  // dequantised copy for prompt chunks
+      GG_TRY(dalloc(e, &dt, gg_dense_tiles_bytes(M[j], K[j])));
+      GG_CUDA(e, gg_make_dense_tiles(&e->qmaps[(size_t)l * 4 + j], dt, e->stream));
     }
   }
   if (e->gemm_ok) {

@@ -72,6 +72,33 @@ GG_DEV uint32_t ldg_nc_u16(const void* p) {
   return v;
 }
 
+// One Q8_0 block (32 int8 in q0, q1; f16 scale d) of row r, block h of a 128 x 64 slab, into
+// the swizzled bf16 operand tiles: w = q * d exactly in f32; hi = w truncated to bf16,
+// lo = (w - hi) rounded to bf16, so hi + lo = w to 2^-16 relative.
+GG_DEV void dequant_block32(uint4 q0, uint4 q1, float d, uint8_t* ahi, uint8_t* alo, int r, int h) {
+  const uint32_t words[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u, q0.w ^ 0x80808080u,
+                             q1.x ^ 0x80808080u, q1.y ^ 0x80808080u, q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
+  const uint32_t rowoff = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+#pragma unroll
+  for (int j = 0; j < 4; j++) {  // chunk 4h + j: weights 8j..8j+7 of this block
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+      const uint32_t wx = words[2 * j + (p >> 1)];
+      const int b0 = (p & 1) * 2;
+      const float w0 = q8_at(wx, b0) * d, w1 = q8_at(wx, b0 + 1) * d;
+      const uint32_t u0 = __float_as_uint(w0) & 0xFFFF0000u, u1 = __float_as_uint(w1) & 0xFFFF0000u;
+      hw[p] = __byte_perm(u0, u1, 0x7632u);
+      const __nv_bfloat162 l2 = __floats2bfloat162_rn(w0 - __uint_as_float(u0), w1 - __uint_as_float(u1));
+      lw[p] = *reinterpret_cast<const uint32_t*>(&l2);
+    }
+    const int c = h * 4 + j;
+    const uint32_t off = rowoff + ((uint32_t)((c ^ (r & 7)) & 7) << 4);
+    *reinterpret_cast<uint4*>(ahi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(alo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(GM_THREADS, GemmCfg<NT>::MIN_CTAS) gg_gemm_q8_kernel(const GemmArgs a) {
   using C = GemmCfg<NT>;
@@ -167,7 +194,6 @@ __global__ void __launch_bounds__(GM_THREADS, GemmCfg<NT>::MIN_CTAS) gg_gemm_q8_
     // dequantise: lane -> (row r, block h) of each 128 x 64 slab; raw data GM_PF slabs ahead
     const int tw = warp - 2;
     const int r = tw * 16 + (lane >> 1), h = lane & 1;
-    const uint32_t rowoff = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     const uint8_t* wbase = a.wt + ((size_t)m_tile * a.KS + (size_t)s0) * GG_Q8_TILE_BYTES;
     const uint8_t* qoff = wbase + r * 64 + h * 32;
     const uint8_t* soff = wbase + GM_RAW_Q + r * 4 + h * 2;
@@ -194,36 +220,14 @@ __global__ void __launch_bounds__(GM_THREADS, GemmCfg<NT>::MIN_CTAS) gg_gemm_q8_
           break;
         }
         const float d = __half2float(__ushort_as_half((unsigned short)sv[u]));
-        const uint32_t words[8] = {qa[u].x ^ 0x80808080u, qa[u].y ^ 0x80808080u, qa[u].z ^ 0x80808080u,
-                                   qa[u].w ^ 0x80808080u, qb[u].x ^ 0x80808080u, qb[u].y ^ 0x80808080u,
-                                   qb[u].z ^ 0x80808080u, qb[u].w ^ 0x80808080u};
+        const uint4 words0 = qa[u], words1 = qb[u];
         if (i + GM_PF < ns) {  // refill this slot with the slab GM_PF ahead
           qa[u] = ldg_nc16(qoff + (size_t)(i + GM_PF) * GG_Q8_TILE_BYTES);
           qb[u] = ldg_nc16(qoff + (size_t)(i + GM_PF) * GG_Q8_TILE_BYTES + 16);
           sv[u] = ldg_nc_u16(soff + (size_t)(i + GM_PF) * GG_Q8_TILE_BYTES);
         }
         uint8_t* ahi = aring + ia * C::A_STAGE;
-        uint8_t* alo = ahi + GM_A_BYTES;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {  // chunk 4h + j: weights 8j..8j+7 of this block
-          uint32_t hw[4], lw[4];
-#pragma unroll
-          for (int p = 0; p < 4; p++) {
-            // w = q * d exactly in f32; hi = w truncated to bf16, lo = (w - hi) rounded to bf16:
-            // hi + lo = w to 2^-16 relative.
-            const uint32_t wx = words[2 * j + (p >> 1)];
-            const int b0 = (p & 1) * 2;
-            const float w0 = q8_at(wx, b0) * d, w1 = q8_at(wx, b0 + 1) * d;
-            const uint32_t u0 = __float_as_uint(w0) & 0xFFFF0000u, u1 = __float_as_uint(w1) & 0xFFFF0000u;
-            hw[p] = __byte_perm(u0, u1, 0x7632u);
-            const __nv_bfloat162 l2 = __floats2bfloat162_rn(w0 - __uint_as_float(u0), w1 - __uint_as_float(u1));
-            lw[p] = *reinterpret_cast<const uint32_t*>(&l2);
-          }
-          const int c = h * 4 + j;
-          const uint32_t off = rowoff + ((uint32_t)((c ^ (r & 7)) & 7) << 4);
-          *reinterpret_cast<uint4*>(ahi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          *reinterpret_cast<uint4*>(alo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
+        dequant_block32(words0, words1, d, ahi, ahi + GM_A_BYTES, r, h);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full_a[ia]);
@@ -265,6 +269,147 @@ __global__ void __launch_bounds__(GM_THREADS, GemmCfg<NT>::MIN_CTAS) gg_gemm_q8_
   }
 }
 
+// ---------------------------------------------------------------------------- dense path
+// For many activation rows (prompt chunks) the weights are dequantised once, at load, into
+// bf16 (hi, lo) operand tiles in HBM (32 KB per 128 x 64 slab: hi then lo, swizzled as the
+// tensor core reads them). The kernel is then only copies and MMAs:
+//   warp 0     bulk copies of a slab's weight tile and the NT x 64 activation tile into a ring;
+//   warp 1     TMEM allocation and the MMAs (three products per K step into two accumulators);
+//   warps 2-5  epilogue.
+constexpr int GD_THREADS = 192;
+constexpr int GD_A_STAGE = 2 * GM_A_BYTES;  // hi, lo
+
+template <int NT>
+struct DenseCfg {
+  static constexpr int B_BYTES = NT * 128;
+  static constexpr int STAGE = GD_A_STAGE + 2 * B_BYTES;
+  static constexpr int S = NT == 256 ? 2 : 3;
+  static constexpr int SMEM = 1024 + S * STAGE + 128;
+  static constexpr int TMEM_COLS = NT == 256 ? 512 : 256;  // two accumulators of NT columns
+};
+
+template <int NT>
+__global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const GemmArgs a) {
+  using C = DenseCfg<NT>;
+  constexpr int S = C::S;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + S * C::STAGE);
+  uint64_t* empty = full + S;
+  uint64_t* acc_bar = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y;
+  const int s0 = blockIdx.z * a.slabs_per_split;
+  const int ns = min(a.slabs_per_split, a.KS - s0);
+  const SpinCtl sc{a.err, a.timeout_ns};
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_bar, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0) {
+    if (lane == 0) {
+      const size_t KS = (size_t)a.KS;
+      int issued = 0;
+      for (int i = 0; i < ns; i++) {
+        const int o = i % S;
+        if (*abort_flag) break;
+        if (i >= S && !mbar_wait(&empty[o], ((i / S) - 1) & 1, sc)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* dst = ring + o * C::STAGE;
+        mbar_arrive_expect_tx(&full[o], C::STAGE);
+        bulk_g2s_plain(dst, a.wt + ((size_t)m_tile * KS + (size_t)(s0 + i)) * GD_A_STAGE, GD_A_STAGE, &full[o]);
+#pragma unroll
+        for (int hh = 0; hh < NT / 64; hh++) {
+          const size_t blk = ((size_t)(n_tile * (NT / 64) + hh) * KS + (size_t)(s0 + i)) * 8192u;
+          bulk_g2s_plain(dst + GD_A_STAGE + hh * 8192, a.xhi + blk, 8192, &full[o]);
+          bulk_g2s_plain(dst + GD_A_STAGE + C::B_BYTES + hh * 8192, a.xlo + blk, 8192, &full[o]);
+        }
+        issued++;
+      }
+      for (int i = issued > S ? issued - S : 0; i < issued; i++) mbar_wait(&full[i % S], (i / S) & 1, sc);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16_m128(NT);
+      for (int i = 0; i < ns; i++) {
+        const int o = i % S;
+        if (!mbar_wait(&full[o], (i / S) & 1, sc)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ahi = smem_u32(ring + o * C::STAGE), alo = ahi + GM_A_BYTES;
+        const uint32_t bhi = ahi + GD_A_STAGE, blo = bhi + C::B_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+          const uint32_t off = kk * 32;
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          umma_bf16(tmem, umma_desc_sw128(ahi + off), umma_desc_sw128(bhi + off), idesc, acc);
+          umma_bf16(tmem + NT, umma_desc_sw128(ahi + off), umma_desc_sw128(blo + off), idesc, acc);
+          umma_bf16(tmem + NT, umma_desc_sw128(alo + off), umma_desc_sw128(bhi + off), idesc, 1u);
+        }
+        umma_commit(&empty[o]);
+      }
+      umma_commit(acc_bar);
+    }
+  } else {  // warps 2..5: epilogue (warp w reads TMEM lanes 32*(w%4)..)
+    const int q = warp & 3;
+    const bool ok = mbar_wait(acc_bar, 0, sc);
+    tc_fence_after();
+    const int go = __shfl_sync(0xffffffffu, (ok && !*abort_flag) ? 1 : 0, 0);
+    if (go) {
+      const int m = m_tile * 128 + q * 32 + lane;
+      float* yb = a.y + (long long)blockIdx.z * a.split_stride + m;
+#pragma unroll 1
+      for (int c = 0; c < NT; c += 16) {
+        float v[16], u[16];
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(NT + c), u);
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int t = n_tile * NT + c + j;
+          if (t < a.T) yb[(long long)t * a.ldy] = v[j] + u[j];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// Tiled Q8_0 copy -> dense (hi, lo) operand tiles: one CTA per 128 x 64 slab, one thread per
+// Q8_0 block (same dequantisation as the GEMM's dequantising warps).
+__global__ void __launch_bounds__(256) gg_dense_tile_kernel(const uint8_t* __restrict__ q8tiles, uint8_t* __restrict__ dense) {
+  const uint8_t* src = q8tiles + (size_t)blockIdx.x * GG_Q8_TILE_BYTES;
+  uint8_t* dst = dense + (size_t)blockIdx.x * GD_A_STAGE;
+  const int r = threadIdx.x >> 1, h = threadIdx.x & 1;
+  const uint4 q0 = *reinterpret_cast<const uint4*>(src + r * 64 + h * 32);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(src + r * 64 + h * 32 + 16);
+  const float d = __half2float(*reinterpret_cast<const __half*>(src + GM_RAW_Q + r * 4 + h * 2));
+  dequant_block32(q0, q1, d, dst, dst + GM_A_BYTES, r, h);
+}
+
 // Device rows -> tiled copy: block (mt, s) = rows 128*mt.. x columns 64*s.. quants, then the two
 // f16 scales of each row's blocks 2s, 2s+1.
 __global__ void gg_q8_tile_kernel(const uint8_t* __restrict__ rows, int rs, int K, uint8_t* __restrict__ tiles) {
@@ -303,7 +448,7 @@ __global__ void gg_xtiles_kernel(const float* __restrict__ x, int T, int Tpad, i
 
 using namespace gg;
 
-size_t gg_xtiles_bytes(int T, int K) { return (size_t)((T + 127) / 128 * 128) * (size_t)K * 2; }
+size_t gg_xtiles_bytes(int T, int K) { return (size_t)((T + 255) / 256 * 256) * (size_t)K * 2; }
 
 size_t gg_q8_tiles_bytes(int M, int K) { return (size_t)(M / 128) * (size_t)(K / 64) * GG_Q8_TILE_BYTES; }
 
@@ -318,9 +463,18 @@ cudaError_t gg_make_q8_tiles(GGQ8Map* out, const uint8_t* rows, int M, int K, ui
   return cudaGetLastError();
 }
 
+size_t gg_dense_tiles_bytes(int M, int K) { return (size_t)(M / 128) * (size_t)(K / 64) * GD_A_STAGE; }
+
+cudaError_t gg_make_dense_tiles(GGQ8Map* w, uint8_t* dense, cudaStream_t s) {
+  if (!w->tiles) return cudaErrorInvalidValue;
+  gg_dense_tile_kernel<<<(w->M / 128) * (w->K / 64), 256, 0, s>>>(w->tiles, dense);
+  w->dense = dense;
+  return cudaGetLastError();
+}
+
 cudaError_t gg_xtiles_from_f32(const float* x, int T, int K, uint8_t* xhi, uint8_t* xlo, cudaStream_t s) {
   if (T <= 0 || K % 64) return cudaErrorInvalidValue;
-  const int Tpad = (T + 127) / 128 * 128;
+  const int Tpad = (T + 255) / 256 * 256;  // whole tiles of the widest (256-row) kernel
   const long long n = (long long)Tpad * (K / 8);
   const int blocks = (int)((n + 255) / 256 < 148 * 8 ? (n + 255) / 256 : 148 * 8);
   gg_xtiles_kernel<<<blocks, 256, 0, s>>>(x, T, Tpad, K, xhi, xlo);
@@ -344,6 +498,23 @@ static cudaError_t launch_nt(const GGQ8Map& w, const GemmArgs& a, int splits, cu
   return cudaGetLastError();
 }
 
+template <int NT>
+static cudaError_t launch_dense(const GemmArgs& a, int m_tiles, int splits, cudaStream_t s) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t r = cudaGetDevice(&dev);
+  if (r != cudaSuccess) return r;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    r = cudaFuncSetAttribute(gg_gemm_dense_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DenseCfg<NT>::SMEM);
+    if (r != cudaSuccess) return r;
+    attr_set[dev] = true;
+  }
+  dim3 grid((a.T + NT - 1) / NT, m_tiles, splits);
+  gg_gemm_dense_kernel<NT><<<grid, GD_THREADS, DenseCfg<NT>::SMEM, s>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo, int T, float* y, long long ldy,
                        int splits, long long split_stride, uint32_t* err, uint64_t timeout_ns, cudaStream_t s) {
   if (T <= 0 || splits <= 0) return cudaErrorInvalidValue;
@@ -362,5 +533,9 @@ cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo,
   if ((long long)(splits - 1) * a.slabs_per_split >= a.KS) return cudaErrorInvalidValue;  // an empty split
   a.err = err;
   a.timeout_ns = timeout_ns;
+  if (T > 64 && w.dense) {  // prompt chunks: dequantised weights, copies and MMAs only
+    a.wt = w.dense;
+    return T > 128 ? launch_dense<256>(a, w.M / 128, splits, s) : launch_dense<128>(a, w.M / 128, splits, s);
+  }
   return T <= 64 ? launch_nt<64>(w, a, splits, s) : launch_nt<128>(w, a, splits, s);
 }

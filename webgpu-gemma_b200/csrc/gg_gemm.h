@@ -17,6 +17,7 @@
 struct GGQ8Map {
   const uint8_t* tiles;
   int M, K;
+  const uint8_t* dense = nullptr;  // optional: bf16 (hi, lo) operand tiles, 32 KB per slab
 };
 
 size_t gg_q8_tiles_bytes(int M, int K);
@@ -25,10 +26,15 @@ size_t gg_q8_tiles_bytes(int M, int K);
 // M % 128 == 0 and K % 64 == 0 are required.
 cudaError_t gg_make_q8_tiles(GGQ8Map* out, const uint8_t* rows, int M, int K, uint8_t* tiles, cudaStream_t s);
 
-// Bytes of one activation tile array for T rows of width K (T rounded up to 128).
+// Optional dequantised copy used for more than 64 activation rows (prompt chunks):
+// gg_dense_tiles_bytes(M, K) bytes, built from the tiled Q8_0 copy.
+size_t gg_dense_tiles_bytes(int M, int K);
+cudaError_t gg_make_dense_tiles(GGQ8Map* w, uint8_t* dense, cudaStream_t s);
+
+// Bytes of one activation tile array for T rows of width K (T rounded up to 256).
 size_t gg_xtiles_bytes(int T, int K);
 
-// x [T][K] f32 -> tile arrays (rows T..round128(T)-1 zero).
+// x [T][K] f32 -> tile arrays (rows T..round256(T)-1 zero).
 cudaError_t gg_xtiles_from_f32(const float* x, int T, int K, uint8_t* xhi, uint8_t* xlo, cudaStream_t s);
 
 // Y (+ split * split_stride) [t][m] with row stride ldy; K is cut into `splits` slices whose
