@@ -16,6 +16,30 @@ constexpr int PF_THREADS = 256;
 constexpr int PF_MAX_H = 4096;
 constexpr int PF_HD = 256;
 
+// 16-byte global -> shared copies that stay in flight together (cp.async), then one wait.
+GG_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+GG_DEV void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// Sum of `splits` planes at offset o (loads issued four at a time, added in plane order).
+GG_DEV float sum_planes(const float* __restrict__ part, int splits, long long plane, long long o) {
+  float v = part[o];
+  int z = 1;
+  for (; z + 3 < splits; z += 4) {
+    const float a = part[(long long)z * plane + o], b = part[(long long)(z + 1) * plane + o];
+    const float c = part[(long long)(z + 2) * plane + o], d = part[(long long)(z + 3) * plane + o];
+    v += a;
+    v += b;
+    v += c;
+    v += d;
+  }
+  for (; z < splits; z++) v += part[(long long)z * plane + o];
+  return v;
+}
+
 GG_DEV float block_sum256(float v, float* red) {
   v = warp_sum(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -52,8 +76,7 @@ __global__ void __launch_bounds__(PF_THREADS)
   if (part) {
     float ss = 0.f;
     for (int i = threadIdx.x; i < H; i += PF_THREADS) {
-      float v = part[base + i];
-      for (int z = 1; z < splits; z++) v += part[(long long)z * plane + base + i];
+      const float v = sum_planes(part, splits, plane, base + i);
       row[i] = v;
       ss += v * v;
     }
@@ -104,9 +127,7 @@ __global__ void __launch_bounds__(PF_THREADS)
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < NJ; j++) {
-      const long long o = base + h * PF_HD + lane + 32 * j;
-      float a = part[o];
-      for (int z = 1; z < splits; z++) a += part[(long long)z * plane + o];
+      const float a = sum_planes(part, splits, plane, base + h * PF_HD + lane + 32 * j);
       v[j] = a;
       ss += a * a;
     }
@@ -131,10 +152,7 @@ __global__ void __launch_bounds__(PF_THREADS)
     }
   }
   for (int i = threadIdx.x; i < KVD; i += PF_THREADS) {
-    const long long o = base + QD + KVD + i;
-    float a = part[o];
-    for (int z = 1; z < splits; z++) a += part[(long long)z * plane + o];
-    vc[(long long)pos * KVD + i] = a;
+    vc[(long long)pos * KVD + i] = sum_planes(part, splits, plane, base + QD + KVD + i);
   }
 }
 
@@ -195,10 +213,11 @@ __global__ void __launch_bounds__(PF_THREADS)
     __syncthreads();
     for (int idx = tid; idx < nk * (PF_HD / 4); idx += PF_THREADS) {
       const int j = idx / (PF_HD / 4), d4 = idx % (PF_HD / 4);
-      const long long g = (long long)(j0 + j) * KVD + kvh * PF_HD;
-      reinterpret_cast<float4*>(ks + j * PA_KSTR)[d4] = reinterpret_cast<const float4*>(kc + g)[d4];
-      reinterpret_cast<float4*>(vs + j * PF_HD)[d4] = reinterpret_cast<const float4*>(vc + g)[d4];
+      const long long g = (long long)(j0 + j) * KVD + kvh * PF_HD + 4 * d4;
+      cp_async16(ks + j * PA_KSTR + 4 * d4, kc + g);
+      cp_async16(vs + j * PF_HD + 4 * d4, vc + g);
     }
+    cp_async_wait_all();
     __syncthreads();
     float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
     const float4* qa = reinterpret_cast<const float4*>(qs + r0 * PF_HD);
@@ -373,13 +392,17 @@ __global__ void __launch_bounds__(PF_THREADS)
   for (int j0 = k_begin; j0 < k_end; j0 += PA_KB) {
     const int nk = min(PA_KB, k_end - j0);
     __syncthreads();
-    for (int idx = tid; idx < nk * (PF_HD / 4); idx += PF_THREADS) {
+    for (int idx = tid; idx < nk * (PF_HD / 4); idx += PF_THREADS)  // V rows: async 16-byte copies
+      cp_async16(vs + (idx / (PF_HD / 4)) * PF_HD + 4 * (idx % (PF_HD / 4)),
+                 vb + (size_t)(j0 + idx / (PF_HD / 4)) * PF_HD + 4 * (idx % (PF_HD / 4)));
+#pragma unroll 4
+    for (int idx = tid; idx < nk * (PF_HD / 4); idx += PF_THREADS) {  // K rows, padded: loads first
       const int jj = idx / (PF_HD / 4), d4 = idx % (PF_HD / 4);
       const float4 kv = reinterpret_cast<const float4*>(kb + (size_t)(j0 + jj) * PF_HD)[d4];
       float* kd = ks + jj * (PF_HD + 1) + 4 * d4;
       kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
-      reinterpret_cast<float4*>(vs + jj * PF_HD)[d4] = reinterpret_cast<const float4*>(vb + (size_t)(j0 + jj) * PF_HD)[d4];
     }
+    cp_async_wait_all();
     __syncthreads();
     float sc = -INFINITY;
     if (j < nk) {
