@@ -1044,19 +1044,44 @@ __global__ void __launch_bounds__(256)
   __shared__ GGModelDev sm;
   __shared__ GGState ss;
   const int b = blockIdx.x, t = threadIdx.x;
+  __shared__ unsigned long long sk[4][256];
   const float* row = logits + (size_t)b * V;
   const unsigned long long ik = init_lane_key();
-  unsigned long long best = ik;
-  for (int i = t; i < V; i += 256) {
-    float v = __ldcs(row + i);
+  // Element i belongs to lane i % 256. Thread t reads 16-byte groups c = t, t + 256, ...:
+  // elements 4c..4c+3 are lanes 4 (c % 64) + j; threads t, t+64, t+128, t+192 share lanes.
+  unsigned long long best[4] = {ik, ik, ik, ik};
+  const int n4 = V >> 2;
+  for (int c = t; c < n4; c += 256) {
+    const float4 f = __ldcs(reinterpret_cast<const float4*>(row) + c);
+    const float fv[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      float v = fv[j];
+      if (!isnan(v)) {
+        if (v == 0.0f) v = 0.0f;  // -0 and +0 compare equal under '>': key them alike
+        const uint32_t i = 4u * (uint32_t)c + j;
+        const unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - i);
+        best[j] = k > best[j] ? k : best[j];
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; j++) sk[t >> 6][4 * (t & 63) + j] = best[j];
+  __syncthreads();
+  unsigned long long kb = ik;
+#pragma unroll
+  for (int q = 0; q < 4; q++) kb = sk[q][t] > kb ? sk[q][t] : kb;
+  for (int i = 4 * n4; i < V; i++) {  // tail when V % 4 != 0 (< 4 elements): lane i % 256
+    if ((i & 255) != t) continue;
+    float v = row[i];
     if (!isnan(v)) {
-      if (v == 0.0f) v = 0.0f;  // -0 and +0 compare equal under '>': key them alike
+      if (v == 0.0f) v = 0.0f;
       const unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - (uint32_t)i);
-      best = k > best ? k : best;
+      kb = k > kb ? k : kb;
     }
   }
   unsigned long long* rk = keys + (size_t)b * 256;
-  rk[t] = best;
+  rk[t] = kb;
   const int seq = seqs[b];
   if (t == 0) {
     sm.lane_keys = rk;

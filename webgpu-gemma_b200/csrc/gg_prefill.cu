@@ -65,43 +65,72 @@ __global__ void __launch_bounds__(PF_THREADS) pf_embed_kernel(const int32_t* __r
   }
 }
 
-__global__ void __launch_bounds__(PF_THREADS)
+// One CTA per row; thread k owns the element quad 4k..4k+3 (H / 4 threads, up to 1024), so
+// every load of the row (all split planes, residual, weights) is in flight at once.
+__global__ void __launch_bounds__(1024)
     pf_addnorm_kernel(const float* __restrict__ part, int splits, long long plane, const float* __restrict__ w_post,
                       const float* rin, float* rout, const float* __restrict__ w_norm, uint8_t* thi, uint8_t* tlo,
                       int H, float eps) {
-  __shared__ float row[PF_MAX_H];
-  __shared__ float red[PF_THREADS / 32];
-  const int t = blockIdx.x;
-  const long long base = (long long)t * H;
+  __shared__ float red[32];
+  __shared__ float tot[2];
+  const int t = blockIdx.x, k = threadIdx.x, nq = H >> 2;
+  const bool ok = k < nq;
+  const long long base = (long long)t * H + 4 * k;
+  float r[4] = {0.f, 0.f, 0.f, 0.f};
+  if (ok) {
+    const float4 ri = *reinterpret_cast<const float4*>(rin + base);
+    r[0] = ri.x; r[1] = ri.y; r[2] = ri.z; r[3] = ri.w;
+  }
+  auto bsum = [&](float v, int slot) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float x = threadIdx.x < (int)(blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+      x = warp_sum(x);
+      if (threadIdx.x == 0) tot[slot] = x;
+    }
+    __syncthreads();
+    return tot[slot];
+  };
   if (part) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += PF_THREADS) {
-      const float v = sum_planes(part, splits, plane, base + i);
-      row[i] = v;
-      ss += v * v;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+      float4 acc = *reinterpret_cast<const float4*>(part + base);
+      int z = 1;
+      for (; z + 1 < splits; z += 2) {
+        const float4 a = *reinterpret_cast<const float4*>(part + (long long)z * plane + base);
+        const float4 c = *reinterpret_cast<const float4*>(part + (long long)(z + 1) * plane + base);
+        acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+        acc.x += c.x; acc.y += c.y; acc.z += c.z; acc.w += c.w;
+      }
+      for (; z < splits; z++) {
+        const float4 a = *reinterpret_cast<const float4*>(part + (long long)z * plane + base);
+        acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+      }
+      v[0] = acc.x; v[1] = acc.y; v[2] = acc.z; v[3] = acc.w;
     }
-    const float rms = sqrtf(block_sum256(ss, red) / (float)H + eps);
-    for (int i = threadIdx.x; i < H; i += PF_THREADS) {
-      const float r = rin[base + i] + row[i] * w_post[i] / rms;
-      row[i] = r;
-      if (rout) rout[base + i] = r;
-    }
-  } else {
-    for (int i = threadIdx.x; i < H; i += PF_THREADS) {
-      const float r = rin[base + i];
-      row[i] = r;
-      if (rout && rout != rin) rout[base + i] = r;
+    const float rms = sqrtf(bsum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3], 0) / (float)H + eps);
+    if (ok) {
+      const float4 wp = *reinterpret_cast<const float4*>(w_post + 4 * k);
+      const float wv[4] = {wp.x, wp.y, wp.z, wp.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) r[j] = r[j] + v[j] * wv[j] / rms;
     }
   }
+  if (ok && rout && (part || rout != rin))
+    *reinterpret_cast<float4*>(rout + base) = make_float4(r[0], r[1], r[2], r[3]);
   if (!w_norm) return;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += PF_THREADS) ss += row[i] * row[i];
-  const float rms = sqrtf(block_sum256(ss, red) / (float)H + eps);
-  for (int c = threadIdx.x; c < H / 8; c += PF_THREADS) {
-    float v[8];
+  const float rms2 = sqrtf(bsum(r[0] * r[0] + r[1] * r[1] + r[2] * r[2] + r[3] * r[3], 1) / (float)H + eps);
+  // two quads per tile chunk of 8: the even thread gathers its neighbour's quad
+  const float4 wn = ok ? *reinterpret_cast<const float4*>(w_norm + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float x[4] = {r[0] * wn.x / rms2, r[1] * wn.y / rms2, r[2] * wn.z / rms2, r[3] * wn.w / rms2};
+  float y[4];
 #pragma unroll
-    for (int j = 0; j < 8; j++) v[j] = row[8 * c + j] * w_norm[8 * c + j] / rms;
-    xtile_put8(thi, tlo, H / 64, t, 8 * c, v);
+  for (int j = 0; j < 4; j++) y[j] = __shfl_down_sync(0xffffffffu, x[j], 1);
+  if (ok && (k & 1) == 0) {
+    float v8[8] = {x[0], x[1], x[2], x[3], y[0], y[1], y[2], y[3]};
+    xtile_put8(thi, tlo, H / 64, t, 4 * k, v8);
   }
 }
 
@@ -360,6 +389,7 @@ __global__ void __launch_bounds__(PF_THREADS)
 // range); thread (h, j) scores head h against key j of a 64-key block; thread d accumulates
 // output dim d of the four heads. Partial results are merged by bd_attn_merge_kernel.
 constexpr int BD_NH = 4;
+constexpr int BD_KC = 64;  // keys per work item (one shared-memory block)
 constexpr int BD_PART = BD_NH * PF_HD + 2 * BD_NH;
 constexpr int BD_SMEM = (BD_NH * PF_HD + PA_KB * (PF_HD + 1) + PA_KB * PF_HD + BD_NH * PA_KB + 4 * BD_NH + 8) * 4;
 
@@ -376,9 +406,9 @@ __global__ void __launch_bounds__(PF_THREADS)
   float* wred = st + 4 * BD_NH;            // [8] per-warp reductions
   const int c = blockIdx.x, b = blockIdx.y;
   const int pos = pos_arr[b];
-  const int k_begin = c * PA_KC;
+  const int k_begin = c * BD_KC;
   if (k_begin > pos) return;
-  const int k_end = min(k_begin + PA_KC, pos + 1);
+  const int k_end = min(k_begin + BD_KC, pos + 1);
   const float* kb = kc + (size_t)seq_arr[b] * seq_stride;
   const float* vb = vc + (size_t)seq_arr[b] * seq_stride;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -454,10 +484,10 @@ __global__ void __launch_bounds__(PF_THREADS)
 __global__ void __launch_bounds__(PF_THREADS)
     bd_attn_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_arr, int maxc, uint8_t* thi,
                          uint8_t* tlo) {
-  __shared__ float wgt[16][BD_NH];
+  __shared__ float wgt[32][BD_NH];
   __shared__ float inv[BD_NH];
   const int b = blockIdx.x;
-  const int nch = min(maxc, pos_arr[b] / PA_KC + 1);
+  const int nch = min(maxc, pos_arr[b] / BD_KC + 1);
   const float* base = part + (size_t)b * maxc * BD_PART;
   if (threadIdx.x < BD_NH) {
     const int h = threadIdx.x;
@@ -545,7 +575,8 @@ cudaError_t pf_addnorm(const float* part, int splits, long long plane, const flo
                        float* resid_out, const float* w_norm, uint8_t* thi, uint8_t* tlo, int T, int H, float eps,
                        cudaStream_t s) {
   if (T <= 0 || H > PF_MAX_H || H % 64) return cudaErrorInvalidValue;
-  pf_addnorm_kernel<<<T, PF_THREADS, 0, s>>>(part, splits, plane, w_post, resid_in, resid_out, w_norm, thi, tlo, H, eps);
+  const int threads = ((H / 4) + 31) / 32 * 32;
+  pf_addnorm_kernel<<<T, threads, 0, s>>>(part, splits, plane, w_post, resid_in, resid_out, w_norm, thi, tlo, H, eps);
   return cudaGetLastError();
 }
 
@@ -600,7 +631,7 @@ cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T
 }
 
 size_t bd_attention_part_floats(int max_rows, int ctx) {
-  return (size_t)max_rows * ((ctx + PA_KC - 1) / PA_KC) * BD_PART;
+  return (size_t)max_rows * ((ctx + BD_KC - 1) / BD_KC) * BD_PART;
 }
 
 cudaError_t bd_attention(const float* q, const float* kc, const float* vc, int B, const int32_t* pos,
@@ -617,8 +648,8 @@ cudaError_t bd_attention(const float* q, const float* kc, const float* vc, int B
     if (r != cudaSuccess) return r;
     attr_set[dev] = true;
   }
-  const int maxc = max_pos / PA_KC + 1;
-  if (maxc > 16) return cudaErrorInvalidValue;
+  const int maxc = max_pos / BD_KC + 1;
+  if (maxc > 32) return cudaErrorInvalidValue;  // merge weights hold 32 key ranges (2048 positions)
   bd_attn_part_kernel<<<dim3(maxc, B), PF_THREADS, BD_SMEM, s>>>(q, kc, vc, pos, seqs, seq_stride, scale, maxc, part);
   r = cudaGetLastError();
   if (r != cudaSuccess) return r;
