@@ -530,6 +530,16 @@ struct Consumer {
     const int nh = NQH + NKH;
     for (int h = warp; h < nh + NKH; h += NCW) {
       const uint64_t* src = m.t_qkv + h * HD;
+      // inputs that do not depend on this step's activations are fetched before the wait
+      float nwv[NJ];
+      float2 cr[NJ / 2];
+      if (h < nh) {
+        const float* nw = h < NQH ? Lw.q_norm : Lw.k_norm;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) nwv[j] = __ldg(nw + lane + 32 * j);
+#pragma unroll
+        for (int j = 0; j < NJ / 2; j++) cr[j] = __ldg(Lw.rope + (size_t)x.pos * (HD / 2) + lane + 32 * j);
+      }
       uint64_t w[NJ];
 #pragma unroll
       for (int j = 0; j < NJ; j++) w[j] = tag_load(src + lane + 32 * j);
@@ -542,14 +552,11 @@ struct Consumer {
 #pragma unroll
         for (int j = 0; j < NJ; j++) ss += v[j] * v[j];
         const float rms = sqrtf(warp_sum(ss) / (float)HD + m.eps);
-        const float* nw = h < NQH ? Lw.q_norm : Lw.k_norm;
 #pragma unroll
-        for (int j = 0; j < NJ; j++) v[j] = v[j] * nw[lane + 32 * j] / rms;
+        for (int j = 0; j < NJ; j++) v[j] = v[j] * nwv[j] / rms;
 #pragma unroll
         for (int j = 0; j < NJ / 2; j++) {
-          const int i = lane + 32 * j;
-          const float2 cr = Lw.rope[(size_t)x.pos * (HD / 2) + i];  // (cos, sin) of pos * freq_i
-          const float cs = cr.x, sn = cr.y;
+          const float cs = cr[j].x, sn = cr[j].y;  // (cos, sin) of pos * freq_i, i = lane + 32 j
           const float x0 = v[j], x1 = v[j + NJ / 2];
           v[j] = x0 * cs - x1 * sn;
           v[j + NJ / 2] = x0 * sn + x1 * cs;
