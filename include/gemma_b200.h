@@ -45,6 +45,10 @@ typedef struct {
   int32_t swa_period;
   int32_t max_seqs; /* KV slots (sequences); 1 for the reference's single conversation */
   int32_t flags;    /* GG_FLAG_* bits */
+  /* 0: every layer attends the whole prefix, as the reference does. W > 0: the sliding-window
+   * layers (isSwaLayer, types.ts:38-40) attend only positions pos-W+1..pos, as Gemma 3 is
+   * specified (W = 512 for the 270M and 1B models). */
+  int32_t sliding_window;
 } gg_config;
 
 /* Sampling options of one step: GenerateOptions (src/types.ts:65-78). */

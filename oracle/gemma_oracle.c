@@ -286,6 +286,7 @@ typedef struct {
         vocab_size, num_layers, context_length;
     float rms_norm_eps, rope_theta_global, rope_theta_swa;
     int32_t swa_period, max_seqs, flags;
+    int32_t sliding_window; /* 0: whole prefix (the reference); W: last W positions on SWA layers */
 } or_config;
 
 typedef struct {
@@ -421,7 +422,11 @@ OR_EXPORT int or_forward(or_model *m, int seq, int token, int pos, float *normed
         or_fused_norm_rope(k, L->k_norm, NKH, HD, eps, pos, theta);
         memcpy(kc + (size_t)pos * KV, k, (size_t)KV * 4);
         memcpy(vc + (size_t)pos * KV, v, (size_t)KV * 4);
-        or_attention(q, kc, vc, NQH, NKH, HD, seq_len, scale, scores, att);
+        /* Gemma 3's sliding window on the local layers (off unless sliding_window > 0) */
+        int lo = 0;
+        if (c->sliding_window > 0 && (il % c->swa_period) < (c->swa_period - 1) && pos + 1 > c->sliding_window)
+            lo = pos + 1 - c->sliding_window;
+        or_attention(q, kc + (size_t)lo * KV, vc + (size_t)lo * KV, NQH, NKH, HD, seq_len - lo, scale, scores, att);
         or_linear_q8(att, L->o, proj, H, Q);
         or_fused_norm_add(proj, L->post_attn_norm, hidden, residual, H, eps);
         or_rmsnorm(residual, L->ffn_norm, normed, H, eps);

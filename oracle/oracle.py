@@ -36,7 +36,7 @@ class OrConfig(ctypes.Structure):
         "intermediate_size", "vocab_size", "num_layers", "context_length")] + [
         ("rms_norm_eps", ctypes.c_float), ("rope_theta_global", ctypes.c_float),
         ("rope_theta_swa", ctypes.c_float), ("swa_period", ctypes.c_int32),
-        ("max_seqs", ctypes.c_int32), ("flags", ctypes.c_int32)]
+        ("max_seqs", ctypes.c_int32), ("flags", ctypes.c_int32), ("sliding_window", ctypes.c_int32)]
 
 
 _lib = None
@@ -182,7 +182,7 @@ class OracleModel:
             elif name == "flags":
                 c.flags = 0
             else:
-                setattr(c, name, getattr(cfg, name))
+                setattr(c, name, getattr(cfg, name, 0))
         self.cfg = cfg
         self.max_seqs = max_seqs
         self._h = lib().or_create(ctypes.byref(c))

@@ -202,3 +202,26 @@ def test_oracle_rejects_bad_input(oracle_mod):
         m.forward(1, cfg.context_length)
     with pytest.raises(ValueError):
         m.set_tensor("blk.99.attn_q.weight", 8, np.zeros(34, np.uint8), 32)
+
+
+def test_oracle_sliding_window_semantics():
+    """A window at least as long as the prefix changes nothing; swa_period 1 makes every layer
+    global (no window at all)."""
+    import dataclasses
+    from oracle import oracle
+    from gemma_b200 import synth
+    cfg, tens = synthetic("tiny", 7)
+    prompt = synth.make_prompt(7, 12, cfg.vocab_size)
+
+    def run(c):
+        m = oracle.OracleModel.from_tensors(c, tens)
+        for i, t in enumerate(prompt):
+            out = m.forward(int(t), i)
+        lg = m.logits()
+        m.close()
+        return lg
+
+    base = run(cfg)
+    assert (run(dataclasses.replace(cfg, sliding_window=64)) == base).all()
+    assert (run(dataclasses.replace(cfg, sliding_window=4, swa_period=1)) == base).all()
+    assert not (run(dataclasses.replace(cfg, sliding_window=4)) == base).all()

@@ -129,6 +129,12 @@ struct Ctx {
 
 // ---------------------------------------------------------------------------------- producer
 
+// First attention split holding a position inside this layer's window, and the first such
+// position (0, 0 when the layer attends the whole prefix).
+GG_DEV int window_lo(const GGLayerW& Lw, int pos) {
+  return (Lw.window > 0 && pos + 1 > Lw.window) ? pos + 1 - Lw.window : 0;
+}
+
 struct Producer {
   Ctx& x;
   uint64_t pol;
@@ -163,8 +169,8 @@ struct Producer {
         const GGLayerW& Lw = m.layers[l];
         part(m.Q + 2 * m.KV, G, c, b, e);
         rows(Lw.wqkv, m.rs_h, b, e, m.ph_qkv.rps);
-        const int rot = (l * x.nsplit) % G;
-        for (int s = (c - rot + G) % G; s < x.nsplit && ok; s += G) {
+        const int rot = (l * x.nsplit) % G, slo = window_lo(Lw, x.pos) / m.pos_per_split;
+        for (int s = slo + (c - rot + G) % G; s < x.nsplit && ok; s += G) {
           int p0 = s * m.pos_per_split, pc = min(p0 + m.pos_per_split, x.pos);
           uint32_t nb = pc > p0 ? (uint32_t)((pc - p0) * m.KV * 4) : 0u;
           size_t off = (size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + p0) * m.KV;
@@ -520,7 +526,8 @@ struct Consumer {
   GG_DEV void phase_attn(int l) {
     const GGModelDev& m = *x.m;
     const int G = m.grid, c = blockIdx.x, rot = (l * x.nsplit) % G;
-    int s = (c - rot + G) % G;
+    const int plo = window_lo(m.layers[l], x.pos), slo = plo / m.pos_per_split;
+    int s = slo + (c - rot + G) % G;
     if (s >= x.nsplit) return;
     const int Q = m.Q, KV = m.KV, HD = m.HD, NQH = m.NQH, NKH = m.NKH, PPS = m.pos_per_split;
     constexpr int NJ = GG_HEAD_DIM / 32;  // elements per lane of a head
@@ -570,6 +577,7 @@ struct Consumer {
     const uint32_t tag = make_tag(x.tagbase, l * PH_PER_LAYER + 1);
     for (; s < x.nsplit; s += G) {
       const int p0 = s * PPS, p1 = min(p0 + PPS, x.pos + 1), np = p1 - p0;
+      const int pv = max(plo - p0, 0);  // positions before pv are outside the window
       const uint8_t* stg = stage_acquire();
       const float* Kst = reinterpret_cast<const float*>(stg);
       const float* Vst = reinterpret_cast<const float*>(stg + (size_t)PPS * KV * 4);
@@ -590,7 +598,7 @@ struct Consumer {
 #pragma unroll
         for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
           sc[p] = 0.f;
-          if (p < np) {
+          if (p >= pv && p < np) {
             const float* kr = (p0 + p < x.pos) ? Kst + (size_t)p * KV + kvh * HD : t + Q + kvh * HD;
             float d = 0.f;
 #pragma unroll
@@ -602,7 +610,7 @@ struct Consumer {
         float sum = 0.f;
 #pragma unroll
         for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-          sc[p] = p < np ? expf(sc[p] - mx) : 0.f;
+          sc[p] = (p >= pv && p < np) ? expf(sc[p] - mx) : 0.f;
           sum += sc[p];
         }
 #pragma unroll
@@ -611,7 +619,7 @@ struct Consumer {
           float acc = 0.f;
 #pragma unroll
           for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-            if (p < np) {
+            if (p >= pv && p < np) {
               const float* vr = (p0 + p < x.pos) ? Vst + (size_t)p * KV : t + Q + KV;
               acc = fmaf(sc[p], vr[kvh * HD + dd], acc);
             }
@@ -641,7 +649,7 @@ struct Consumer {
       for (int k = warp; k < DPC; k += NCW) {
         const int d = d0 + k;
         float mx = -INFINITY, lsum = 0.f, acc = 0.f;
-        for (int s0 = 0; s0 < x.nsplit; s0 += 32 * SPL) {
+        for (int s0 = window_lo(m.layers[l], x.pos) / m.pos_per_split; s0 < x.nsplit; s0 += 32 * SPL) {
           uint64_t wm[SPL], wl[SPL], wo[SPL];
 #pragma unroll
           for (int q = 0; q < SPL; q++) {

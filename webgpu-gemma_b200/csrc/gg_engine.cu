@@ -199,6 +199,8 @@ extern "C" int gg_create(const gg_config* cfg, int device, gg_engine** out) {
       c.kv_dim != c.num_kv_heads * c.head_dim || c.intermediate_size <= 0 || c.intermediate_size % 32 ||
       c.vocab_size < 256 || c.context_length <= 0 || c.max_seqs <= 0 || c.q_dim % 32)
     return fail(nullptr, GG_E_ARG, "unsupported config (dims must be positive multiples of 32, q_dim = heads*head_dim)");
+  if (c.swa_period < 1 || c.sliding_window < 0)
+    return fail(nullptr, GG_E_ARG, "unsupported config (swa_period >= 1, sliding_window >= 0)");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
     return fail(nullptr, GG_E_CUDA, "no CUDA device %d", device);
@@ -431,6 +433,7 @@ extern "C" int gg_finalize(gg_engine* e) {
     // getRopeTheta (types.ts:38-44)
     bool swa = (l % c.swa_period) < (c.swa_period - 1);
     w.theta = swa ? c.rope_theta_swa : c.rope_theta_global;
+    w.window = (swa && c.sliding_window > 0) ? c.sliding_window : 0;
   }
   // RoPE tables, one per distinct theta
   {
@@ -616,7 +619,8 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
       GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, T, e->pf_y, QKV, sp, plane, err, to, s));
       GG_CUDA(e, pf_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, T, p0, m.NQH, m.NKH, m.HD, m.eps,
                                   e->pf_q, kc, vc, s));
-      GG_CUDA(e, pf_attention(e->pf_q, kc, vc, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, e->pf_att, thi, tlo, s));
+      GG_CUDA(e, pf_attention(e->pf_q, kc, vc, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, w.window, e->pf_att, thi, tlo,
+                              s));
       sp = pick_splits(gemm_tiles(T, m.H), m.Q / 64, gemm_slots(e, T));
       plane = (long long)T * m.H;
       GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));
@@ -669,7 +673,7 @@ static int batch_step(gg_engine* e, int B, int max_pos, const double* d_unif, in
     GG_CUDA(e, bd_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, B, e->bd_pos, e->bd_seq,
                                 m.kv_seq_stride, m.NQH, m.NKH, m.HD, m.eps, e->pf_q, kc, vc, s));
     GG_CUDA(e, bd_attention(e->pf_q, kc, vc, B, e->bd_pos, e->bd_seq, m.kv_seq_stride, max_pos, m.NQH, m.NKH, m.HD,
-                            m.attn_scale, e->bd_att, thi, tlo, s));
+                            m.attn_scale, w.window, e->bd_att, thi, tlo, s));
     sp = pick_splits(gemm_tiles(B, m.H), m.Q / 64, gemm_slots(e, B));
     plane = (long long)B * m.H;
     GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, B, e->pf_y, m.H, sp, plane, err, to, s));

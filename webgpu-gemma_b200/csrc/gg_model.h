@@ -32,7 +32,7 @@ struct GGLayerW {
   const float* post_attn_norm;
   const float* post_ffw_norm;
   float theta;
-  int pad_;
+  int window;  // 0: attend the whole prefix; W: only positions pos-W+1..pos (sliding-window layer)
   const float2* rope;  // [CTX][HD/2] (cos, sin) of pos * theta^(-2i/HD) for this layer's theta
 };
 

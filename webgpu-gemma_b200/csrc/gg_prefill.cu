@@ -200,7 +200,7 @@ constexpr int PA_SMEM = (PA_ROWS * PF_HD + PA_KB * PA_KSTR + PA_KB * PF_HD + PA_
 
 __global__ void __launch_bounds__(PF_THREADS)
     pf_attn_part_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc, int T,
-                        int p0, int NQH, int NKH, float scale, int maxc, float* __restrict__ part) {
+                        int p0, int NQH, int NKH, float scale, int window, int maxc, float* __restrict__ part) {
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                         // [ROWS][HD]
   float* ks = qs + PA_ROWS * PF_HD;       // [KB][KSTR]
@@ -214,6 +214,9 @@ __global__ void __launch_bounds__(PF_THREADS)
   const int k_begin = c * PA_KC;
   if (k_begin > kmax) return;
   const int k_end = min(k_begin + PA_KC, kmax + 1);
+  // sliding window: key range of the block's first row; ranges wholly below it are not needed
+  const int klo0 = window > 0 ? max(0, p0 + t0 + 1 - window) : 0;
+  if (k_end <= klo0) return;
   const int QD = NQH * PF_HD, KVD = NKH * PF_HD;
   const int tid = threadIdx.x, warp = tid >> 5;
   // rows r = token * G + g  ->  query head kvh * G + g of token t0 + token
@@ -228,6 +231,7 @@ __global__ void __launch_bounds__(PF_THREADS)
   const int kg = tid & 15, qg = tid >> 4;
   const int r0 = 2 * qg, r1 = r0 + 1;
   const int pos0 = p0 + t0 + r0 / G, pos1 = p0 + t0 + r1 / G;
+  const int lo0 = window > 0 ? max(0, pos0 + 1 - window) : 0, lo1 = window > 0 ? max(0, pos1 + 1 - window) : 0;
   float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
   // output tile of this thread: rows 4*warp..+3; dims 4*dg..+3 and 128+4*dg..+3
   const int dg = tid & 31;
@@ -268,8 +272,8 @@ __global__ void __launch_bounds__(PF_THREADS)
     for (int u = 0; u < 4; u++) {
       const int key = j0 + kg + 16 * u;
       const bool in = kg + 16 * u < nk;
-      sa[u] = (in && key <= pos0) ? sa[u] * scale : -INFINITY;
-      sb[u] = (in && key <= pos1) ? sb[u] * scale : -INFINITY;
+      sa[u] = (in && key <= pos0 && key >= lo0) ? sa[u] * scale : -INFINITY;
+      sb[u] = (in && key <= pos1 && key >= lo1) ? sb[u] * scale : -INFINITY;
       mx0 = fmaxf(mx0, sa[u]);
       mx1 = fmaxf(mx1, sb[u]);
     }
@@ -342,21 +346,22 @@ __global__ void __launch_bounds__(PF_THREADS)
 
 // Merge the key-range items of one row block and write the attention output as tiles.
 __global__ void __launch_bounds__(PF_THREADS)
-    pf_attn_merge_kernel(const float* __restrict__ part, int T, int p0, int NQH, int NKH, int maxc, uint8_t* thi,
-                         uint8_t* tlo) {
+    pf_attn_merge_kernel(const float* __restrict__ part, int T, int p0, int NQH, int NKH, int window, int maxc,
+                         uint8_t* thi, uint8_t* tlo) {
   __shared__ float wgt[16][PA_ROWS];
   __shared__ float inv[PA_ROWS];
   const int G = NQH / NKH, QT = PA_ROWS / G;
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int t0 = b * QT, nq = min(QT, T - t0);
   const int nch = min(maxc, (p0 + t0 + nq - 1) / PA_KC + 1);
+  const int c0 = window > 0 ? max(0, p0 + t0 + 1 - window) / PA_KC : 0;  // as in the part kernel
   const float* base = part + ((size_t)(kvh * gridDim.x + b) * maxc) * PA_PART;
   if (threadIdx.x < PA_ROWS) {
     const int r = threadIdx.x;
     float M = -1e30f;
-    for (int c = 0; c < nch; c++) M = fmaxf(M, base[(size_t)c * PA_PART + PA_ROWS * PF_HD + r]);
+    for (int c = c0; c < nch; c++) M = fmaxf(M, base[(size_t)c * PA_PART + PA_ROWS * PF_HD + r]);
     float L = 0.f;
-    for (int c = 0; c < nch; c++) {
+    for (int c = c0; c < nch; c++) {
       const float* pc = base + (size_t)c * PA_PART + PA_ROWS * PF_HD;
       const float w = expf(pc[r] - M);
       wgt[c][r] = w;
@@ -371,7 +376,7 @@ __global__ void __launch_bounds__(PF_THREADS)
     const int tok = r / G, hq = kvh * G + r % G;
     if (tok >= nq) continue;
     float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < nch; c++) {
+    for (int c = c0; c < nch; c++) {
       const float* src = base + (size_t)c * PA_PART + r * PF_HD + 8 * c8;
       const float4 a = reinterpret_cast<const float4*>(src)[0], bq = reinterpret_cast<const float4*>(src)[1];
       const float w = wgt[c][r];
@@ -396,7 +401,7 @@ constexpr int BD_SMEM = (BD_NH * PF_HD + PA_KB * (PF_HD + 1) + PA_KB * PF_HD + B
 __global__ void __launch_bounds__(PF_THREADS)
     bd_attn_part_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                         const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride,
-                        float scale, int maxc, float* __restrict__ part) {
+                        float scale, int window, int maxc, float* __restrict__ part) {
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                          // [NH][HD]
   float* ks = qs + BD_NH * PF_HD;          // [KB][HD+1]
@@ -409,6 +414,8 @@ __global__ void __launch_bounds__(PF_THREADS)
   const int k_begin = c * BD_KC;
   if (k_begin > pos) return;
   const int k_end = min(k_begin + BD_KC, pos + 1);
+  const int klo = window > 0 ? max(0, pos + 1 - window) : 0;  // sliding window
+  if (k_end <= klo) return;
   const float* kb = kc + (size_t)seq_arr[b] * seq_stride;
   const float* vb = vc + (size_t)seq_arr[b] * seq_stride;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -435,7 +442,8 @@ __global__ void __launch_bounds__(PF_THREADS)
     cp_async_wait_all();
     __syncthreads();
     float sc = -INFINITY;
-    if (j < nk) {
+    const bool kin = j < nk && j0 + j >= klo;
+    if (kin) {
       const float* qr = qs + h * PF_HD;
       const float* kr = ks + j * (PF_HD + 1);
       float acc = 0.f;
@@ -450,7 +458,7 @@ __global__ void __launch_bounds__(PF_THREADS)
     const float bmax = fmaxf(wred[2 * h], wred[2 * h + 1]);
     const float mold = st[h];
     const float mnew = fmaxf(mold, bmax);
-    const float e = j < nk ? expf(sc - mnew) : 0.f;
+    const float e = kin ? expf(sc - mnew) : 0.f;
     ps[h * PA_KB + j] = e;
     float es = warp_sum(e);
     __syncthreads();  // wred reuse
@@ -482,19 +490,20 @@ __global__ void __launch_bounds__(PF_THREADS)
 }
 
 __global__ void __launch_bounds__(PF_THREADS)
-    bd_attn_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_arr, int maxc, uint8_t* thi,
-                         uint8_t* tlo) {
+    bd_attn_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_arr, int window, int maxc,
+                         uint8_t* thi, uint8_t* tlo) {
   __shared__ float wgt[32][BD_NH];
   __shared__ float inv[BD_NH];
   const int b = blockIdx.x;
   const int nch = min(maxc, pos_arr[b] / BD_KC + 1);
+  const int c0 = window > 0 ? max(0, pos_arr[b] + 1 - window) / BD_KC : 0;
   const float* base = part + (size_t)b * maxc * BD_PART;
   if (threadIdx.x < BD_NH) {
     const int h = threadIdx.x;
     float M = -1e30f;
-    for (int c = 0; c < nch; c++) M = fmaxf(M, base[(size_t)c * BD_PART + BD_NH * PF_HD + h]);
+    for (int c = c0; c < nch; c++) M = fmaxf(M, base[(size_t)c * BD_PART + BD_NH * PF_HD + h]);
     float L = 0.f;
-    for (int c = 0; c < nch; c++) {
+    for (int c = c0; c < nch; c++) {
       const float* pc = base + (size_t)c * BD_PART + BD_NH * PF_HD;
       const float w = expf(pc[h] - M);
       wgt[c][h] = w;
@@ -506,7 +515,7 @@ __global__ void __launch_bounds__(PF_THREADS)
   if (threadIdx.x >= BD_NH * (PF_HD / 8)) return;
   const int h = threadIdx.x / (PF_HD / 8), c8 = threadIdx.x % (PF_HD / 8);
   float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int c = 0; c < nch; c++) {
+  for (int c = c0; c < nch; c++) {
     const float* src = base + (size_t)c * BD_PART + h * PF_HD + 8 * c8;
     const float w = wgt[c][h];
 #pragma unroll
@@ -605,7 +614,7 @@ size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH) {
 }
 
 cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T, int p0, int NQH, int NKH, int HD,
-                         float scale, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
+                         float scale, int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
   if (T <= 0 || HD != PF_HD || NKH <= 0 || NQH % NKH) return cudaErrorInvalidValue;
   const int G = NQH / NKH;
   if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) return cudaErrorInvalidValue;
@@ -623,10 +632,11 @@ cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T
   const int nb = (T + QT - 1) / QT;
   const int maxc = (p0 + T - 1) / PA_KC + 1;
   if (maxc > 16) return cudaErrorInvalidValue;  // merge weights hold 16 key ranges (2048 positions)
-  pf_attn_part_kernel<<<dim3(maxc, nb, NKH), PF_THREADS, PA_SMEM, s>>>(q, kc, vc, T, p0, NQH, NKH, scale, maxc, part);
+  pf_attn_part_kernel<<<dim3(maxc, nb, NKH), PF_THREADS, PA_SMEM, s>>>(q, kc, vc, T, p0, NQH, NKH, scale, window, maxc,
+                                                                       part);
   r = cudaGetLastError();
   if (r != cudaSuccess) return r;
-  pf_attn_merge_kernel<<<dim3(nb, NKH), PF_THREADS, 0, s>>>(part, T, p0, NQH, NKH, maxc, thi, tlo);
+  pf_attn_merge_kernel<<<dim3(nb, NKH), PF_THREADS, 0, s>>>(part, T, p0, NQH, NKH, window, maxc, thi, tlo);
   return cudaGetLastError();
 }
 
@@ -636,7 +646,7 @@ size_t bd_attention_part_floats(int max_rows, int ctx) {
 
 cudaError_t bd_attention(const float* q, const float* kc, const float* vc, int B, const int32_t* pos,
                          const int32_t* seqs, size_t seq_stride, int max_pos, int NQH, int NKH, int HD, float scale,
-                         float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
+                         int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
   if (B <= 0 || HD != PF_HD || NQH != BD_NH || NKH != 1) return cudaErrorInvalidValue;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -650,10 +660,11 @@ cudaError_t bd_attention(const float* q, const float* kc, const float* vc, int B
   }
   const int maxc = max_pos / BD_KC + 1;
   if (maxc > 32) return cudaErrorInvalidValue;  // merge weights hold 32 key ranges (2048 positions)
-  bd_attn_part_kernel<<<dim3(maxc, B), PF_THREADS, BD_SMEM, s>>>(q, kc, vc, pos, seqs, seq_stride, scale, maxc, part);
+  bd_attn_part_kernel<<<dim3(maxc, B), PF_THREADS, BD_SMEM, s>>>(q, kc, vc, pos, seqs, seq_stride, scale, window, maxc,
+                                                                 part);
   r = cudaGetLastError();
   if (r != cudaSuccess) return r;
-  bd_attn_merge_kernel<<<B, PF_THREADS, 0, s>>>(part, pos, maxc, thi, tlo);
+  bd_attn_merge_kernel<<<B, PF_THREADS, 0, s>>>(part, pos, window, maxc, thi, tlo);
   return cudaGetLastError();
 }
 

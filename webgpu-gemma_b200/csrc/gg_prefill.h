@@ -33,8 +33,9 @@ cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, con
 // (shaders.ts:229-325), output written as activation tiles of width NQH*HD. `part` is scratch
 // of pf_attention_part_floats(T, p0 + T, NQH, NKH) floats (partial results per key range).
 size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH);
+// window > 0: each query at position p sees only keys p-window+1..p (sliding-window layer).
 cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T, int p0, int NQH, int NKH, int HD,
-                         float scale, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
+                         float scale, int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
 
 // act[t][i] = gelu_tanh(gu[t][2i]) * gu[t][2i+1] (shaders.ts:153-170, gu = sum of planes) as
 // activation tiles of width I.
@@ -55,4 +56,4 @@ cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, con
 size_t bd_attention_part_floats(int max_rows, int ctx);
 cudaError_t bd_attention(const float* q, const float* kc, const float* vc, int B, const int32_t* pos,
                          const int32_t* seqs, size_t seq_stride, int max_pos, int NQH, int NKH, int HD, float scale,
-                         float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
+                         int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);

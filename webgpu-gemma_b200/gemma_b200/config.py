@@ -32,6 +32,9 @@ class GemmaConfig:
     # (src/types.ts:32-33); a spec-faithful 10k is opt-in, not the default.
     rope_theta_swa: float = 1000000.0
     swa_period: int = 6
+    # Not in the reference (which attends the whole prefix on every layer): > 0 limits the
+    # sliding-window layers to the last `sliding_window` positions, as Gemma 3 is specified.
+    sliding_window: int = 0
 
     def as_dict(self) -> dict:
         return asdict(self)
@@ -42,8 +45,17 @@ def default_config() -> GemmaConfig:
     return GemmaConfig()
 
 
+def gemma3_spec(cfg: GemmaConfig, window: int = 512, theta_local: float = 10000.0) -> GemmaConfig:
+    """The configuration as Gemma 3 is specified rather than as the reference runs it: sliding
+    window of `window` positions and RoPE base `theta_local` on the local layers."""
+    cfg.sliding_window = window
+    cfg.rope_theta_swa = theta_local
+    return cfg
+
+
 def is_swa_layer(il: int, config: GemmaConfig) -> bool:
-    """``isSwaLayer`` (src/types.ts:38-40). Only used to pick the RoPE theta."""
+    """``isSwaLayer`` (src/types.ts:38-40): picks the RoPE theta, and the window when
+    ``sliding_window`` > 0."""
     return (il % config.swa_period) < (config.swa_period - 1)
 
 
@@ -72,6 +84,7 @@ class CConfig(ctypes.Structure):
         ("swa_period", ctypes.c_int32),
         ("max_seqs", ctypes.c_int32),
         ("flags", ctypes.c_int32),
+        ("sliding_window", ctypes.c_int32),
     ]
 
 
