@@ -362,15 +362,18 @@ def run_cfg4(args):
         dist.destroy_process_group()
 
 
-def run_turns(name: str, shape_name: str, seed: int, turns, reps: int = 3):
+def run_turns(name: str, shape_name: str, seed: int, turns, reps: int = 3, spec: bool = False):
     """Greedy multi-turn run through the C-ABI: each turn prefills its new ids after the cached
     prefix (the last sampled token of the previous turn is fed first, as generate() does),
     then decodes. Reports per turn the TTFT (prefill + first token, wall clock, median of
     `reps` runs) and the decode tok/s (device time of the chained decode)."""
     from gemma_b200 import synth
     from gemma_b200.native import engine_from_tensors
+    from gemma_b200.config import gemma3_spec
     shape = synth.SHAPES[shape_name]
     cfg = shape.config()
+    if spec:
+        cfg = gemma3_spec(cfg)
     eng = engine_from_tensors(cfg, synth.make_tensors(shape, seed))
     out = []
     for rep in range(reps):
@@ -402,7 +405,8 @@ def run_turns(name: str, shape_name: str, seed: int, turns, reps: int = 3):
         r["ttft_ms"] = statistics.median(x["ttft_ms"] for x in rows)
         r["decode_tok_s"] = statistics.median(x["decode_tok_s"] for x in rows)
         med.append(r)
-    print(json.dumps({name: f"{shape_name} synthetic (seed {seed}), greedy, batch 1", "turns": med}))
+    mode = ", gemma3_spec (window 512, local theta 1e4)" if spec else ""
+    print(json.dumps({name: f"{shape_name} synthetic (seed {seed}), greedy, batch 1{mode}", "turns": med}))
     eng.close()
 
 
@@ -439,6 +443,8 @@ def main():
     ap.add_argument("--cfg4", action="store_true", help="config 4: 64 sequences per GPU, batched sampled decode")
     ap.add_argument("--cfg0", action="store_true", help="config 0: 270M, 32-token prompt, 64 greedy tokens")
     ap.add_argument("--cfg3", action="store_true", help="config 3: 1B two-turn long context (1536+128, +256+128)")
+    ap.add_argument("--spec", action="store_true",
+                    help="with --cfg0/--cfg3: Gemma 3 as specified (sliding window 512, local RoPE base 1e4)")
     ap.add_argument("--cfg2-shapes", default="", help="comma-separated subset of qkv,o,gate_up,down,lm_head")
     ap.add_argument("--cfg2-batches", default="1,8,64")
     ap.add_argument("--cfg2-reps", type=int, default=10)
@@ -448,9 +454,9 @@ def main():
     if args.cfg4:
         return run_cfg4(args)
     if args.cfg0:
-        return run_turns("cfg0", "270m", 0, [(32, 64)])
+        return run_turns("cfg0", "270m", 0, [(32, 64)], spec=args.spec)
     if args.cfg3:
-        return run_turns("cfg3", "1b", 1, [(1536, 128), (256, 128)])
+        return run_turns("cfg3", "1b", 1, [(1536, 128), (256, 128)], spec=args.spec)
     if args.cfg2:
         return run_cfg2(args.cfg2_reps, [x for x in args.cfg2_shapes.split(",") if x],
                         [int(x) for x in args.cfg2_batches.split(",")])
