@@ -1061,23 +1061,23 @@ namespace gg {
 // (sample_token, engine.ts:823-901) with that row's parameters, draw and KV slot's seen set.
 // The sampled token is added to the slot's seen set, becomes the row's next input token, and
 // the row's position advances.
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(512)
     gg_batch_sample_kernel(const float* __restrict__ logits, int V, const int32_t* __restrict__ seqs,
                            const GGSampleDev* __restrict__ sp, const double* __restrict__ unif, uint8_t* seen,
                            int seen_stride, int32_t* seen_cnt, unsigned long long* keys, int32_t* tokens,
                            int32_t* pos, int32_t* out) {
   __shared__ GGModelDev sm;
   __shared__ GGState ss;
+  __shared__ unsigned long long sk[8][256];
   const int b = blockIdx.x, t = threadIdx.x;
-  __shared__ unsigned long long sk[4][256];
   const float* row = logits + (size_t)b * V;
   const unsigned long long ik = init_lane_key();
-  // Element i belongs to lane i % 256. Thread t reads 16-byte groups c = t, t + 256, ...:
-  // elements 4c..4c+3 are lanes 4 (c % 64) + j; threads t, t+64, t+128, t+192 share lanes.
+  // Element i belongs to lane i % 256. Thread t reads 16-byte groups c = t, t + 512, ... (eight
+  // loads in flight): elements 4c..4c+3 are lanes 4 (c % 64) + j, shared by the eight threads
+  // t % 64 + 64 k.
   unsigned long long best[4] = {ik, ik, ik, ik};
   const int n4 = V >> 2;
-  for (int c = t; c < n4; c += 256) {
-    const float4 f = __ldcs(reinterpret_cast<const float4*>(row) + c);
+  auto take = [&](const float4 f, int c) {
     const float fv[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -1089,24 +1089,36 @@ __global__ void __launch_bounds__(256)
         best[j] = k > best[j] ? k : best[j];
       }
     }
+  };
+  const float4* row4 = reinterpret_cast<const float4*>(row);
+  int c = t;
+  for (; c + 7 * 512 < n4; c += 8 * 512) {
+    float4 f[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) f[u] = __ldcs(row4 + c + u * 512);
+#pragma unroll
+    for (int u = 0; u < 8; u++) take(f[u], c + u * 512);
   }
+  for (; c < n4; c += 512) take(__ldcs(row4 + c), c);
 #pragma unroll
   for (int j = 0; j < 4; j++) sk[t >> 6][4 * (t & 63) + j] = best[j];
   __syncthreads();
   unsigned long long kb = ik;
+  if (t < 256) {
 #pragma unroll
-  for (int q = 0; q < 4; q++) kb = sk[q][t] > kb ? sk[q][t] : kb;
-  for (int i = 4 * n4; i < V; i++) {  // tail when V % 4 != 0 (< 4 elements): lane i % 256
-    if ((i & 255) != t) continue;
-    float v = row[i];
-    if (!isnan(v)) {
-      if (v == 0.0f) v = 0.0f;
-      const unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - (uint32_t)i);
-      kb = k > kb ? k : kb;
+    for (int q = 0; q < 8; q++) kb = sk[q][t] > kb ? sk[q][t] : kb;
+    for (int i = 4 * n4; i < V; i++) {  // tail when V % 4 != 0 (< 4 elements): lane i % 256
+      if ((i & 255) != t) continue;
+      float v = row[i];
+      if (!isnan(v)) {
+        if (v == 0.0f) v = 0.0f;
+        const unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - (uint32_t)i);
+        kb = k > kb ? k : kb;
+      }
     }
   }
   unsigned long long* rk = keys + (size_t)b * 256;
-  rk[t] = kb;
+  if (t < 256) rk[t] = kb;
   const int seq = seqs[b];
   if (t == 0) {
     sm.lane_keys = rk;
@@ -1142,7 +1154,7 @@ cudaError_t gg_batch_sample(const float* logits, int B, int V, const int32_t* se
                             const double* unif, uint8_t* seen, int seen_stride, int32_t* seen_cnt,
                             unsigned long long* keys, int32_t* tokens, int32_t* pos, int32_t* out, cudaStream_t s) {
   if (B <= 0) return cudaErrorInvalidValue;
-  gg::gg_batch_sample_kernel<<<B, 256, 0, s>>>(logits, V, seqs, sp, unif, seen, seen_stride, seen_cnt, keys, tokens,
+  gg::gg_batch_sample_kernel<<<B, 512, 0, s>>>(logits, V, seqs, sp, unif, seen, seen_stride, seen_cnt, keys, tokens,
                                                 pos, out);
   return cudaGetLastError();
 }

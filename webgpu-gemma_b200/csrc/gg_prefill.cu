@@ -152,14 +152,21 @@ __global__ void __launch_bounds__(PF_THREADS)
   const int QD = NQH * PF_HD, KVD = NKH * PF_HD, W = QD + 2 * KVD;
   const long long base = (long long)t * W;
   for (int h = warp; h < NQH + NKH; h += PF_THREADS / 32) {
+    // the head's NJ elements of every split plane: NJ loads in flight per plane, planes in order
+    const long long ob = base + h * PF_HD + lane;
     float v[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; j++) v[j] = part[ob + 32 * j];
+    for (int z = 1; z < splits; z++) {
+      float a[NJ];
+#pragma unroll
+      for (int j = 0; j < NJ; j++) a[j] = part[(long long)z * plane + ob + 32 * j];
+#pragma unroll
+      for (int j = 0; j < NJ; j++) v[j] += a[j];
+    }
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < NJ; j++) {
-      const float a = sum_planes(part, splits, plane, base + h * PF_HD + lane + 32 * j);
-      v[j] = a;
-      ss += a * a;
-    }
+    for (int j = 0; j < NJ; j++) ss += v[j] * v[j];
     const float rms = sqrtf(warp_sum(ss) / (float)PF_HD + eps);
     const float* nw = h < NQH ? q_norm : k_norm;
 #pragma unroll
