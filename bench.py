@@ -334,6 +334,8 @@ def run_cfg4(args):
     rank, local, world, dist, torch = dist_setup(args.gpus)
     shape = synth.SHAPES["1b"]
     cfg = shape.config()
+    if args.kv_bf16:
+        cfg.kv_dtype = "bf16"
     eng = engine_from_tensors(cfg, synth.make_tensors(shape, SEED), device=local, max_seqs=CFG4_SEQS)
     B, P, N = CFG4_SEQS, CFG4_PROMPT, min(CFG4_TOKENS, args.steps)
     seq_ids = [rank * B + i for i in range(B)]  # global stream ids (Philox streams)
@@ -354,6 +356,7 @@ def run_cfg4(args):
         print(json.dumps({"cfg4": "1B, 64 sequences per GPU, 256-token prompts, 256 sampled tokens (T 0.7, top-p 0.9, rep 1.2)",
                           "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "seqs_per_gpu": B,
                           "tokens_per_seq": N, "ms_per_step": round(max_ms / N, 4), "scaling": "weak",
+                          "kv_cache": cfg.kv_dtype,
                           "parallelism": f"dp{world} (independent engines)",
                           "first_tokens": [int(t) for t in toks[0, :4]]}))
     eng.close()
@@ -362,7 +365,8 @@ def run_cfg4(args):
         dist.destroy_process_group()
 
 
-def run_turns(name: str, shape_name: str, seed: int, turns, reps: int = 3, spec: bool = False):
+def run_turns(name: str, shape_name: str, seed: int, turns, reps: int = 3, spec: bool = False,
+              kv_bf16: bool = False):
     """Greedy multi-turn run through the C-ABI: each turn prefills its new ids after the cached
     prefix (the last sampled token of the previous turn is fed first, as generate() does),
     then decodes. Reports per turn the TTFT (prefill + first token, wall clock, median of
@@ -374,6 +378,8 @@ def run_turns(name: str, shape_name: str, seed: int, turns, reps: int = 3, spec:
     cfg = shape.config()
     if spec:
         cfg = gemma3_spec(cfg)
+    if kv_bf16:
+        cfg.kv_dtype = "bf16"
     eng = engine_from_tensors(cfg, synth.make_tensors(shape, seed))
     out = []
     for rep in range(reps):
@@ -405,7 +411,7 @@ def run_turns(name: str, shape_name: str, seed: int, turns, reps: int = 3, spec:
         r["ttft_ms"] = statistics.median(x["ttft_ms"] for x in rows)
         r["decode_tok_s"] = statistics.median(x["decode_tok_s"] for x in rows)
         med.append(r)
-    mode = ", gemma3_spec (window 512, local theta 1e4)" if spec else ""
+    mode = (", gemma3_spec (window 512, local theta 1e4)" if spec else "") + (", bf16 KV" if kv_bf16 else "")
     print(json.dumps({name: f"{shape_name} synthetic (seed {seed}), greedy, batch 1{mode}", "turns": med}))
     eng.close()
 
@@ -445,6 +451,8 @@ def main():
     ap.add_argument("--cfg3", action="store_true", help="config 3: 1B two-turn long context (1536+128, +256+128)")
     ap.add_argument("--spec", action="store_true",
                     help="with --cfg0/--cfg3: Gemma 3 as specified (sliding window 512, local RoPE base 1e4)")
+    ap.add_argument("--kv-bf16", action="store_true",
+                    help="with --cfg0/--cfg3/--cfg4: bf16 KV cache (GG_FLAG_KV_BF16) instead of f32")
     ap.add_argument("--cfg2-shapes", default="", help="comma-separated subset of qkv,o,gate_up,down,lm_head")
     ap.add_argument("--cfg2-batches", default="1,8,64")
     ap.add_argument("--cfg2-reps", type=int, default=10)
@@ -454,9 +462,9 @@ def main():
     if args.cfg4:
         return run_cfg4(args)
     if args.cfg0:
-        return run_turns("cfg0", "270m", 0, [(32, 64)], spec=args.spec)
+        return run_turns("cfg0", "270m", 0, [(32, 64)], spec=args.spec, kv_bf16=args.kv_bf16)
     if args.cfg3:
-        return run_turns("cfg3", "1b", 1, [(1536, 128), (256, 128)], spec=args.spec)
+        return run_turns("cfg3", "1b", 1, [(1536, 128), (256, 128)], spec=args.spec, kv_bf16=args.kv_bf16)
     if args.cfg2:
         return run_cfg2(args.cfg2_reps, [x for x in args.cfg2_shapes.split(",") if x],
                         [int(x) for x in args.cfg2_batches.split(",")])

@@ -35,6 +35,10 @@ typedef struct gg_engine gg_engine;
  * Without it gg_prefill runs the prompt in chunks of up to 512 tokens through tensor-core
  * GEMMs (same math, f32 results within rounding of the serial path). */
 #define GG_FLAG_SERIAL_PREFILL 1
+/* gg_config.flags: keep the KV cache in bf16 (round to nearest even at the store) instead of
+ * the reference's f32 (engine.ts:440-447): half the cache memory and half the attention bytes.
+ * Attention reads the stored (rounded) rows, the current position's included. */
+#define GG_FLAG_KV_BF16 2
 
 /* Field-for-field the reference's GemmaConfig (src/types.ts:2-17), plus the number of
  * independent KV slots and option flags. */
@@ -101,7 +105,8 @@ int gg_get_logits(gg_engine* eng, float* out);
 /* Final-normed hidden state of the last step (hidden_size floats), engine.ts:797-801. */
 int gg_get_hidden(gg_engine* eng, float* out);
 
-/* One row of the KV cache (kv_dim floats; which = 0 for K, 1 for V). */
+/* One row of the KV cache (kv_dim floats, widened from bf16 under GG_FLAG_KV_BF16;
+ * which = 0 for K, 1 for V). */
 int gg_get_kv(gg_engine* eng, int seq, int layer, int pos, int which, float* out);
 
 /* Debug/parity aid: copy `n` floats of an internal buffer of the last launch.

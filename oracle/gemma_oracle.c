@@ -279,6 +279,31 @@ OR_EXPORT int32_t or_sample(const float *vals, const uint32_t *ids, double tempe
     return (int32_t)id[ord[cutoff - 1]];
 }
 
+/* ------------------------------------------------------------------ bf16 KV option */
+
+/* Not in the reference (its caches are f32, engine.ts:440-447): the optional bf16 KV cache.
+ * f32 -> bf16 with round-to-nearest-even on the upper 16 bits (add 0x7fff plus the lowest kept
+ * bit, truncate); NaN stays NaN (quiet bit set), infinities stay infinite. Returns the
+ * rounded value widened back to f32, which is what attention reads. */
+static float or_bf16_round1(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u) {
+        if (u & 0x007fffffu) u |= 0x00400000u;
+    } else {
+        u += 0x7fffu + ((u >> 16) & 1u);
+    }
+    u &= 0xffff0000u;
+    memcpy(&x, &u, 4);
+    return x;
+}
+
+OR_EXPORT void or_bf16_round(const float *x, float *y, int64_t n) {
+    for (int64_t i = 0; i < n; i++) y[i] = or_bf16_round1(x[i]);
+}
+
+#define OR_FLAG_KV_BF16 2 /* the engine's GG_FLAG_KV_BF16 */
+
 /* ------------------------------------------------------------------ model */
 
 typedef struct {
@@ -420,8 +445,13 @@ OR_EXPORT int or_forward(or_model *m, int seq, int token, int pos, float *normed
         or_linear_q8(normed, L->v, v, KV, H);
         or_fused_norm_rope(q, L->q_norm, NQH, HD, eps, pos, theta);
         or_fused_norm_rope(k, L->k_norm, NKH, HD, eps, pos, theta);
-        memcpy(kc + (size_t)pos * KV, k, (size_t)KV * 4);
-        memcpy(vc + (size_t)pos * KV, v, (size_t)KV * 4);
+        if (c->flags & OR_FLAG_KV_BF16) {
+            or_bf16_round(k, kc + (size_t)pos * KV, KV);
+            or_bf16_round(v, vc + (size_t)pos * KV, KV);
+        } else {
+            memcpy(kc + (size_t)pos * KV, k, (size_t)KV * 4);
+            memcpy(vc + (size_t)pos * KV, v, (size_t)KV * 4);
+        }
         /* Gemma 3's sliding window on the local layers (off unless sliding_window > 0) */
         int lo = 0;
         if (c->sliding_window > 0 && (il % c->swa_period) < (c->swa_period - 1) && pos + 1 > c->sliding_window)

@@ -14,6 +14,7 @@ import subprocess
 
 import numpy as np
 
+OR_FLAG_KV_BF16 = 2  # or_config.flags bit: bf16 KV cache (GG_FLAG_KV_BF16)
 HERE = os.path.dirname(os.path.abspath(__file__))
 SRC = os.path.join(HERE, "gemma_oracle.c")
 LIB = os.path.join(HERE, "liboracle.so")
@@ -70,6 +71,7 @@ def lib() -> ctypes.CDLL:
             "or_kv_row": (P, [P, I, I, I, I]),
             "or_set_threads": (None, [I]),
             "or_get_threads": (I, []),
+            "or_bf16_round": (None, [P, P, i64]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -87,6 +89,14 @@ def _p(a: np.ndarray):
 
 def f16_to_f32(bits: int) -> float:
     return lib().or_f16_to_f32(bits)
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """f32 values rounded to bf16 (nearest even) and widened back: the optional bf16 KV store."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().or_bf16_round(_p(x), _p(y), x.size)
+    return y
 
 
 def pack_q8_0(raw: np.ndarray) -> np.ndarray:
@@ -180,7 +190,7 @@ class OracleModel:
             if name == "max_seqs":
                 c.max_seqs = max_seqs
             elif name == "flags":
-                c.flags = 0
+                c.flags = OR_FLAG_KV_BF16 if getattr(cfg, "kv_dtype", "f32") == "bf16" else 0
             else:
                 setattr(c, name, getattr(cfg, name, 0))
         self.cfg = cfg

@@ -29,6 +29,24 @@ def f16_to_f32(bits: np.ndarray) -> np.ndarray:
     return v.astype(np.float32)
 
 
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """The optional bf16 KV store (not in the reference): each f32 value goes to the nearer of
+    the two bf16 values around it, ties to the one with an even last mantissa bit, and is
+    widened back to f32. Stated by that definition (distances in f64), independently of the C
+    oracle's integer rounding; finite inputs only."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32)
+    lo_u = u & np.uint32(0xFFFF0000)                # truncation: toward zero
+    hi_u = lo_u + np.uint32(0x10000)                # next bf16 value away from zero
+    lo = lo_u.view(np.float32).astype(np.float64)
+    hi = hi_u.view(np.float32).astype(np.float64)
+    xd = x.astype(np.float64)
+    dlo, dhi = np.abs(xd - lo), np.abs(hi - xd)
+    lo_even = ((lo_u >> np.uint32(16)) & np.uint32(1)) == 0
+    pick_lo = (dlo < dhi) | ((dlo == dhi) & lo_even)
+    return np.where(pick_lo, lo_u, hi_u).astype(np.uint32).view(np.float32)
+
+
 def unpack(packed: np.ndarray, m: int, n: int) -> tuple[np.ndarray, np.ndarray]:
     """packQ8_0ForGPU words -> (q int8 [m, n/32, 32], scale f32 [m, n/32])."""
     w = np.asarray(packed, dtype=np.uint32).reshape(m, n // 32, 9)

@@ -139,10 +139,37 @@ def test_sampler_rules(oracle_mod):
     assert oracle_mod.sample(vals, ids, 0.0, 0.9, 1.0, [], 0.0, vocab) == int(ids[int(np.argmax(vals))])
 
 
-def test_tiny_forward_c_vs_numpy():
+def test_bf16_round_c_vs_numpy_vs_torch(oracle_mod):
+    """The optional bf16 KV store's rounding: the C oracle's integer method, the numpy
+    restatement by definition and torch's f32 -> bf16 cast agree on every value, ties included."""
+    import torch
+    from oracle import oracle_np
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal(20000) * np.exp2(rng.integers(-30, 30, 20000))).astype(np.float32)
+    u = x.view(np.uint32).copy()
+    u[:4000] = (u[:4000] & np.uint32(0xFFFF0000)) | np.uint32(0x8000)  # exact ties, both parities
+    u[4000:4100] = rng.integers(0, 1 << 23, 100).astype(np.uint32)   # subnormals
+    u[4100:4200] = (u[4100:4200] & np.uint32(0xFFFF0000)) | np.uint32(0x7FFF)
+    u[4200] = 0
+    u[4201] = 0x80000000
+    u[4202] = 0x7F7FFFFF  # largest finite f32 rounds up to infinity
+    x = u.view(np.float32)
+    c = oracle_mod.bf16_round(x)
+    t = torch.from_numpy(x.copy()).to(torch.bfloat16).to(torch.float32).numpy()
+    assert (c.view(np.uint32) == t.view(np.uint32)).all()
+    fin = np.isfinite(x) & (np.abs(x) < 3e38)
+    n = oracle_np.bf16_round(x[fin])
+    assert (c[fin].view(np.uint32) == n.view(np.uint32)).all()
+
+
+@pytest.mark.parametrize("kv_dtype", ["f32", "bf16"])
+def test_tiny_forward_c_vs_numpy(kv_dtype):
+    import dataclasses
     from oracle import oracle, oracle_np
     from gemma_b200 import synth
     cfg, tens = synthetic("tiny", 7)
+    cfg = dataclasses.replace(cfg, kv_dtype=kv_dtype)
+    store = oracle_np.bf16_round if kv_dtype == "bf16" else (lambda a: a)
     P = {}
     for name, (dims, t, raw) in tens.items():
         P[name] = oracle.pack_q8_0(raw) if t == 8 else raw.view(np.float32)
@@ -161,7 +188,7 @@ def test_tiny_forward_c_vs_numpy():
             v = oracle_np.linear_q8(x, g("attn_v"), KV, H)
             q = oracle_np.fused_norm_rope(q, g("attn_q_norm"), 4, HD, 1e-6, pos, 1e6)
             k = oracle_np.fused_norm_rope(k, g("attn_k_norm"), 1, HD, 1e-6, pos, 1e6)
-            kc[l, pos], vc[l, pos] = k, v
+            kc[l, pos], vc[l, pos] = store(k), store(v)
             att = oracle_np.attention(q, kc[l], vc[l], 4, 1, HD, pos + 1, 0.0625)
             res = oracle_np.fused_norm_add(oracle_np.linear_q8(att, g("attn_output"), H, Q),
                                            g("post_attention_norm"), hidden, 1e-6)

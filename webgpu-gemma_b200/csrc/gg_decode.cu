@@ -135,6 +135,7 @@ GG_DEV int window_lo(const GGLayerW& Lw, int pos) {
   return (Lw.window > 0 && pos + 1 > Lw.window) ? pos + 1 - Lw.window : 0;
 }
 
+template <bool KV16>
 struct Producer {
   Ctx& x;
   uint64_t pol;
@@ -172,9 +173,10 @@ struct Producer {
         const int rot = (l * x.nsplit) % G, slo = window_lo(Lw, x.pos) / m.pos_per_split;
         for (int s = slo + (c - rot + G) % G; s < x.nsplit && ok; s += G) {
           int p0 = s * m.pos_per_split, pc = min(p0 + m.pos_per_split, x.pos);
-          uint32_t nb = pc > p0 ? (uint32_t)((pc - p0) * m.KV * 4) : 0u;
-          size_t off = (size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + p0) * m.KV;
-          issue(m.kcache + off, nb, m.vcache + off, nb, (uint32_t)(m.pos_per_split * m.KV * 4));
+          constexpr int es = KV16 ? 2 : 4;  // bytes per cache element
+          uint32_t nb = pc > p0 ? (uint32_t)((pc - p0) * m.KV * es) : 0u;
+          size_t off = ((size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + p0) * m.KV) * es;
+          issue(m.kcache + off, nb, m.vcache + off, nb, (uint32_t)(m.pos_per_split * m.KV * es));
         }
         part(m.H, G, c, b, e);
         rows(Lw.wo, m.rs_q, b, e, m.ph_o.rps);
@@ -204,6 +206,9 @@ struct Producer {
 
 // ---------------------------------------------------------------------------------- consumers
 
+// KV16: the KV cache holds bf16 elements (GG_FLAG_KV_BF16); one kernel is built per element
+// type so neither carries the other's attention code.
+template <bool KV16>
 struct Consumer {
   Ctx& x;
   int tid, lane, warp;
@@ -529,7 +534,7 @@ struct Consumer {
     const int plo = window_lo(m.layers[l], x.pos), slo = plo / m.pos_per_split;
     int s = slo + (c - rot + G) % G;
     if (s >= x.nsplit) return;
-    const int Q = m.Q, KV = m.KV, HD = m.HD, NQH = m.NQH, NKH = m.NKH, PPS = m.pos_per_split;
+    const int HD = m.HD, NQH = m.NQH, NKH = m.NKH;
     constexpr int NJ = GG_HEAD_DIM / 32;  // elements per lane of a head
     const GGLayerW& Lw = m.layers[l];
     float* t = x.S.tmp;  // q [Q] | k [KV] | v [KV]
@@ -569,6 +574,10 @@ struct Consumer {
           v[j + NJ / 2] = x0 * sn + x1 * cs;
         }
       }
+      if (KV16 && h >= NQH) {  // bf16 cache: attention reads the stored (rounded) k, v
+#pragma unroll
+        for (int j = 0; j < NJ; j++) v[j] = bf16_rne(v[j]);
+      }
 #pragma unroll
       for (int j = 0; j < NJ; j++) t[h * HD + lane + 32 * j] = v[j];
     }
@@ -576,62 +585,86 @@ struct Consumer {
     trace(l * 6 + 1, 1);
     const uint32_t tag = make_tag(x.tagbase, l * PH_PER_LAYER + 1);
     for (; s < x.nsplit; s += G) {
-      const int p0 = s * PPS, p1 = min(p0 + PPS, x.pos + 1), np = p1 - p0;
-      const int pv = max(plo - p0, 0);  // positions before pv are outside the window
       const uint8_t* stg = stage_acquire();
-      const float* Kst = reinterpret_cast<const float*>(stg);
-      const float* Vst = reinterpret_cast<const float*>(stg + (size_t)PPS * KV * 4);
-      if (p1 == x.pos + 1) {  // this split owns the new position: store it
-        const size_t off = (size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + x.pos) * KV;
-        for (int i = tid; i < KV; i += NCT) {
-          m.kcache[off + i] = t[Q + i];
-          m.vcache[off + i] = t[Q + KV + i];
-        }
-      }
-      for (int h = warp; h < NQH; h += NCW) {
-        const int kvh = h * NKH / NQH;
-        float qv[NJ];
-#pragma unroll
-        for (int j = 0; j < NJ; j++) qv[j] = t[h * HD + lane + 32 * j];
-        float sc[GG_POS_PER_SPLIT];
-        float mx = -1e30f;
-#pragma unroll
-        for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-          sc[p] = 0.f;
-          if (p >= pv && p < np) {
-            const float* kr = (p0 + p < x.pos) ? Kst + (size_t)p * KV + kvh * HD : t + Q + kvh * HD;
-            float d = 0.f;
-#pragma unroll
-            for (int j = 0; j < NJ; j++) d = fmaf(qv[j], kr[lane + 32 * j], d);
-            sc[p] = warp_sum(d) * m.attn_scale;
-            mx = fmaxf(mx, sc[p]);
-          }
-        }
-        float sum = 0.f;
-#pragma unroll
-        for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-          sc[p] = (p >= pv && p < np) ? expf(sc[p] - mx) : 0.f;
-          sum += sc[p];
-        }
-#pragma unroll
-        for (int j = 0; j < NJ; j++) {
-          const int dd = lane + 32 * j;
-          float acc = 0.f;
-#pragma unroll
-          for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-            if (p >= pv && p < np) {
-              const float* vr = (p0 + p < x.pos) ? Vst + (size_t)p * KV : t + Q + KV;
-              acc = fmaf(sc[p], vr[kvh * HD + dd], acc);
-            }
-          }
-          tag_store(m.t_o + (size_t)s * Q + h * HD + dd, acc, tag);
-        }
-        if (lane == 0) {
-          tag_store(m.t_ml + ((size_t)s * NQH + h) * 2 + 0, mx, tag);
-          tag_store(m.t_ml + ((size_t)s * NQH + h) * 2 + 1, sum, tag);
-        }
-      }
+      attn_split(l, s, plo, stg, tag);
       stage_release();
+    }
+  }
+
+  // One split of PPS positions: K rows at the start of the stage, V rows after PPS K rows; the
+  // current position's k and v come from the scratch vector instead (stored here as well).
+  GG_DEV void attn_split(int l, int s, int plo, const uint8_t* stg, uint32_t tag) {
+    using KT = kv_t<KV16>;
+    const GGModelDev& m = *x.m;
+    const int Q = m.Q, KV = m.KV, HD = m.HD, NQH = m.NQH, NKH = m.NKH, PPS = m.pos_per_split;
+    static_assert(GG_HEAD_DIM == 8 * 32, "a lane holds 8 dims of a head");
+    const float* t = x.S.tmp;
+    const int p0 = s * PPS, p1 = min(p0 + PPS, x.pos + 1), np = p1 - p0;
+    const int pv = max(plo - p0, 0);  // positions before pv are outside the window
+    const KT* Kst = reinterpret_cast<const KT*>(stg);
+    const KT* Vst = reinterpret_cast<const KT*>(stg + (size_t)PPS * KV * sizeof(KT));
+    if (p1 == x.pos + 1) {  // this split owns the new position: store it
+      const size_t off = (size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + x.pos) * KV;
+      KT* kc = reinterpret_cast<KT*>(m.kcache);
+      KT* vc = reinterpret_cast<KT*>(m.vcache);
+      for (int i = tid; i < KV; i += NCT) {
+        kc[off + i] = kv_narrow<KV16>(t[Q + i]);
+        vc[off + i] = kv_narrow<KV16>(t[Q + KV + i]);
+      }
+    }
+    // lane l takes dims 8l..8l+7 of a head: one 16-byte shared load per K or V row
+    const auto row8 = [&](const KT* st_row, const float* cur_row, bool cached, float* f) {
+      if (cached && KV16) {
+        bf16x8_widen(*reinterpret_cast<const uint4*>(st_row + 8 * lane), f);
+      } else {
+        if (cached) cur_row = reinterpret_cast<const float*>(st_row);  // f32 cache: same as scratch
+        const float4 a = reinterpret_cast<const float4*>(cur_row + 8 * lane)[0];
+        const float4 b = reinterpret_cast<const float4*>(cur_row + 8 * lane)[1];
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+      }
+    };
+    for (int h = warp; h < NQH; h += NCW) {
+      const int kvh = h * NKH / NQH;
+      float qv[8];
+      row8(nullptr, t + h * HD, false, qv);
+      float sc[GG_POS_PER_SPLIT];
+      float mx = -1e30f;
+#pragma unroll
+      for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+        sc[p] = 0.f;
+        if (p >= pv && p < np) {
+          float kf[8];
+          row8(Kst + (size_t)p * KV + kvh * HD, t + Q + kvh * HD, p0 + p < x.pos, kf);
+          float d = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; j++) d = fmaf(qv[j], kf[j], d);
+          sc[p] = warp_sum(d) * m.attn_scale;
+          mx = fmaxf(mx, sc[p]);
+        }
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+        sc[p] = (p >= pv && p < np) ? expf(sc[p] - mx) : 0.f;
+        sum += sc[p];
+      }
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+        if (p >= pv && p < np) {
+          float vf[8];
+          row8(Vst + (size_t)p * KV + kvh * HD, t + Q + KV + kvh * HD, p0 + p < x.pos, vf);
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[j] = fmaf(sc[p], vf[j], acc[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) tag_store(m.t_o + (size_t)s * Q + h * HD + 8 * lane + j, acc[j], tag);
+      if (lane == 0) {
+        tag_store(m.t_ml + ((size_t)s * NQH + h) * 2 + 0, mx, tag);
+        tag_store(m.t_ml + ((size_t)s * NQH + h) * 2 + 1, sum, tag);
+      }
     }
   }
 
@@ -947,8 +980,8 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st, Smem& S) {
 
 // ---------------------------------------------------------------------------------- kernel
 
-extern "C" __global__ void __launch_bounds__(GG_NTHREADS, 1)
-    gg_decode_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
+template <bool KV16>
+GG_DEV void decode_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
   extern __shared__ __align__(128) uint8_t smem[];
   const GGModelDev& m = *mp;
   Ctx x;
@@ -1002,11 +1035,11 @@ extern "C" __global__ void __launch_bounds__(GG_NTHREADS, 1)
 
   if (warp == NCW) {
     if (lane == 0) {
-      Producer pr{x, l2_policy_evict_first()};
+      Producer<KV16> pr{x, l2_policy_evict_first()};
       pr.run();
     }
   } else {
-    Consumer cs{x, (int)threadIdx.x, lane, warp};
+    Consumer<KV16> cs{x, (int)threadIdx.x, lane, warp};
     cs.run();
   }
   __syncthreads();
@@ -1049,6 +1082,17 @@ extern "C" __global__ void __launch_bounds__(GG_NTHREADS, 1)
       st->pos = x.pos + 1;
     }
   }
+}
+
+extern "C" __global__ void __launch_bounds__(GG_NTHREADS, 1)
+    gg_decode_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
+  decode_body<false>(mp, st);
+}
+
+// The same kernel for a bf16 KV cache (GG_FLAG_KV_BF16).
+extern "C" __global__ void __launch_bounds__(GG_NTHREADS, 1)
+    gg_decode_kernel_kv16(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
+  decode_body<true>(mp, st);
 }
 
 }  // namespace gg

@@ -6,8 +6,11 @@
 // conversion used by the Q8_0 dot products.
 #pragma once
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+
+#include <type_traits>
 
 #define GG_DEV __device__ __forceinline__
 
@@ -179,6 +182,29 @@ GG_DEV float gelu_tanh(float x) {
   float t = S * x * (1.0f + A * x * x);
   t = fminf(fmaxf(t, -15.0f), 15.0f);
   return 0.5f * x * (1.0f + tanhf(t));
+}
+
+// KV cache elements: f32 (the reference's layout) or bf16 (GG_FLAG_KV_BF16; stored rounded to
+// nearest even, widened exactly when read).
+template <bool KV16>
+using kv_t = typename std::conditional<KV16, __nv_bfloat16, float>::type;
+GG_DEV float kv_widen(float v) { return v; }
+GG_DEV float kv_widen(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <bool KV16>
+GG_DEV kv_t<KV16> kv_narrow(float v) {
+  if constexpr (KV16) return __float2bfloat16_rn(v);
+  else return v;
+}
+// The value a bf16 cache holds for v (rounded to nearest even), as f32.
+GG_DEV float bf16_rne(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+// Eight bf16 (one 16-byte load) widened to f32: each is the upper half of its f32 pattern.
+GG_DEV void bf16x8_widen(const uint4 w, float* f) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    f[2 * i] = __uint_as_float(u[i] << 16);
+    f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+  }
 }
 
 GG_DEV float warp_sum(float v) {

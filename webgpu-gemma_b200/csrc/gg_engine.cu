@@ -23,7 +23,12 @@
 
 namespace gg {
 extern "C" __global__ void gg_decode_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
+extern "C" __global__ void gg_decode_kernel_kv16(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
 }
+
+// The persistent step kernel built for the engine's KV element type.
+using DecodeFn = void (*)(const GGModelDev*, GGState*);
+static DecodeFn decode_fn(const GGModelDev& m) { return m.kv_es == 2 ? gg::gg_decode_kernel_kv16 : gg::gg_decode_kernel; }
 
 // ------------------------------------------------------------------------------ utility kernels
 
@@ -245,8 +250,9 @@ extern "C" int gg_create(const gg_config* cfg, int device, gg_engine** out) {
   if (rc == GG_OK) rc = dalloc(e, &e->embd, (size_t)V * m.rs_h);
   if (rc == GG_OK) rc = dalloc(e, &e->out_norm, (size_t)H * 4);
   m.kv_seq_stride = (size_t)L * m.CTX * KV;
-  if (rc == GG_OK) rc = dalloc(e, &m.kcache, m.kv_seq_stride * 4 * c.max_seqs);
-  if (rc == GG_OK) rc = dalloc(e, &m.vcache, m.kv_seq_stride * 4 * c.max_seqs);
+  m.kv_es = (c.flags & GG_FLAG_KV_BF16) ? 2 : 4;
+  if (rc == GG_OK) rc = dalloc(e, &m.kcache, m.kv_seq_stride * m.kv_es * c.max_seqs);
+  if (rc == GG_OK) rc = dalloc(e, &m.vcache, m.kv_seq_stride * m.kv_es * c.max_seqs);
   if (rc != GG_OK) return bail(rc);
   return (*out = e, GG_OK);
 }
@@ -301,7 +307,7 @@ static int schedule(gg_engine* e) {
   size_t other = 8 * 256 + (size_t)(3 * m.xs0 + m.xs0 / 4) + (size_t)(3 * m.xs1 + m.xs1 / 4) + 8 * (size_t)m.H +
                  4 * (size_t)m.tmp_floats + 4 * 1024 + 4 * 256 + 4 * 256 + 16;
   cudaFuncAttributes fa;
-  GG_CUDA(e, cudaFuncGetAttributes(&fa, gg::gg_decode_kernel));
+  GG_CUDA(e, cudaFuncGetAttributes(&fa, decode_fn(m)));
   int optin = 0;
   GG_CUDA(e, cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->device));
   long avail = (long)optin - (long)fa.sharedSizeBytes - (long)other;
@@ -309,9 +315,9 @@ static int schedule(gg_engine* e) {
   if (ns < 2) return fail(e, GG_E_ARG, "not enough shared memory for the weight ring (%ld bytes left)", avail);
   m.nstages = ns;
   m.smem_bytes = (int)(other + (size_t)ns * (m.stage_bytes + 16));
-  GG_CUDA(e, cudaFuncSetAttribute(gg::gg_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, m.smem_bytes));
+  GG_CUDA(e, cudaFuncSetAttribute(decode_fn(m), cudaFuncAttributeMaxDynamicSharedMemorySize, m.smem_bytes));
   int nb = 0;
-  GG_CUDA(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, gg::gg_decode_kernel, GG_NTHREADS, m.smem_bytes));
+  GG_CUDA(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, decode_fn(m), GG_NTHREADS, m.smem_bytes));
   if (nb < 1) return fail(e, GG_E_CUDA, "decode kernel cannot be resident (smem %d)", m.smem_bytes);
   (void)c;
   return GG_OK;
@@ -547,7 +553,7 @@ static int launch(gg_engine* e) {
   at[0].val.cooperative = 1;
   lc.attrs = at;
   lc.numAttrs = 1;
-  GG_CUDA(e, cudaLaunchKernelEx(&lc, gg::gg_decode_kernel, (const GGModelDev*)e->d_md, e->d_st));
+  GG_CUDA(e, cudaLaunchKernelEx(&lc, decode_fn(e->md), (const GGModelDev*)e->d_md, e->d_st));
   return GG_OK;
 }
 
@@ -612,15 +618,16 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
     for (int l = 0; l < m.L; l++) {
       const GGLayerW& w = m.layers[l];
       const GGQ8Map* mp = &e->qmaps[(size_t)l * 4];
-      float* kc = m.kcache + (size_t)seq * m.kv_seq_stride + (size_t)l * m.CTX * m.KV;
-      float* vc = m.vcache + (size_t)seq * m.kv_seq_stride + (size_t)l * m.CTX * m.KV;
+      const size_t kvo = ((size_t)seq * m.kv_seq_stride + (size_t)l * m.CTX * m.KV) * m.kv_es;
+      uint8_t* kc = m.kcache + kvo;
+      uint8_t* vc = m.vcache + kvo;
       int sp = pick_splits(gemm_tiles(T, QKV), m.H / 64, gemm_slots(e, T));
       long long plane = (long long)T * QKV;
       GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, T, e->pf_y, QKV, sp, plane, err, to, s));
       GG_CUDA(e, pf_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, T, p0, m.NQH, m.NKH, m.HD, m.eps,
-                                  e->pf_q, kc, vc, s));
-      GG_CUDA(e, pf_attention(e->pf_q, kc, vc, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, w.window, e->pf_att, thi, tlo,
-                              s));
+                                  e->pf_q, kc, vc, m.kv_es == 2, s));
+      GG_CUDA(e, pf_attention(e->pf_q, kc, vc, m.kv_es == 2, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, w.window,
+                              e->pf_att, thi, tlo, s));
       sp = pick_splits(gemm_tiles(T, m.H), m.Q / 64, gemm_slots(e, T));
       plane = (long long)T * m.H;
       GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));
@@ -665,14 +672,14 @@ static int batch_step(gg_engine* e, int B, int max_pos, const double* d_unif, in
   for (int l = 0; l < m.L; l++) {
     const GGLayerW& w = m.layers[l];
     const GGQ8Map* mp = &e->qmaps[(size_t)l * 4];
-    float* kc = m.kcache + (size_t)l * m.CTX * m.KV;
-    float* vc = m.vcache + (size_t)l * m.CTX * m.KV;
+    uint8_t* kc = m.kcache + (size_t)l * m.CTX * m.KV * m.kv_es;
+    uint8_t* vc = m.vcache + (size_t)l * m.CTX * m.KV * m.kv_es;
     int sp = pick_splits(gemm_tiles(B, QKV), m.H / 64, gemm_slots(e, B));
     long long plane = (long long)B * QKV;
     GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, B, e->pf_y, QKV, sp, plane, err, to, s));
     GG_CUDA(e, bd_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, B, e->bd_pos, e->bd_seq,
-                                m.kv_seq_stride, m.NQH, m.NKH, m.HD, m.eps, e->pf_q, kc, vc, s));
-    GG_CUDA(e, bd_attention(e->pf_q, kc, vc, B, e->bd_pos, e->bd_seq, m.kv_seq_stride, max_pos, m.NQH, m.NKH, m.HD,
+                                m.kv_seq_stride, m.NQH, m.NKH, m.HD, m.eps, e->pf_q, kc, vc, m.kv_es == 2, s));
+    GG_CUDA(e, bd_attention(e->pf_q, kc, vc, m.kv_es == 2, B, e->bd_pos, e->bd_seq, m.kv_seq_stride, max_pos, m.NQH, m.NKH, m.HD,
                             m.attn_scale, w.window, e->bd_att, thi, tlo, s));
     sp = pick_splits(gemm_tiles(B, m.H), m.Q / 64, gemm_slots(e, B));
     plane = (long long)B * m.H;
@@ -892,10 +899,17 @@ extern "C" int gg_get_kv(gg_engine* e, int seq, int layer, int pos, int which, f
   GG_TRY(ready(e, seq));
   if (!out || layer < 0 || layer >= e->cfg.num_layers || pos < 0 || pos >= e->cfg.context_length)
     return fail(e, GG_E_ARG, "bad layer/pos");
-  const float* base = which ? e->md.vcache : e->md.kcache;
-  size_t off = (size_t)seq * e->md.kv_seq_stride + ((size_t)layer * e->md.CTX + pos) * e->md.KV;
-  GG_CUDA(e, cudaMemcpyAsync(out, base + off, 4 * (size_t)e->md.KV, cudaMemcpyDeviceToHost, e->stream));
+  const uint8_t* base = which ? e->md.vcache : e->md.kcache;
+  const int es = e->md.kv_es, KV = e->md.KV;
+  size_t off = ((size_t)seq * e->md.kv_seq_stride + ((size_t)layer * e->md.CTX + pos) * KV) * es;
+  std::vector<uint16_t> raw(es == 2 ? KV : 0);
+  void* dst = es == 2 ? (void*)raw.data() : (void*)out;
+  GG_CUDA(e, cudaMemcpyAsync(dst, base + off, (size_t)es * KV, cudaMemcpyDeviceToHost, e->stream));
   GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  for (int i = 0; es == 2 && i < KV; i++) {  // bf16 -> f32: the upper half of the f32 pattern
+    const uint32_t u = (uint32_t)raw[i] << 16;
+    std::memcpy(out + i, &u, 4);
+  }
   return GG_OK;
 }
 
@@ -958,9 +972,9 @@ extern "C" int gg_seen_add(gg_engine* e, int seq, const int32_t* ids, int n) {
 
 extern "C" int gg_reset_kv(gg_engine* e, int seq) {
   GG_TRY(ready(e, seq));
-  size_t n = e->md.kv_seq_stride * 4;
-  GG_CUDA(e, cudaMemsetAsync(e->md.kcache + (size_t)seq * e->md.kv_seq_stride, 0, n, e->stream));
-  GG_CUDA(e, cudaMemsetAsync(e->md.vcache + (size_t)seq * e->md.kv_seq_stride, 0, n, e->stream));
+  size_t n = e->md.kv_seq_stride * e->md.kv_es;
+  GG_CUDA(e, cudaMemsetAsync(e->md.kcache + (size_t)seq * n, 0, n, e->stream));
+  GG_CUDA(e, cudaMemsetAsync(e->md.vcache + (size_t)seq * n, 0, n, e->stream));
   GG_CUDA(e, cudaStreamSynchronize(e->stream));
   return GG_OK;
 }

@@ -56,9 +56,9 @@ struct GGModelDev {
   int smem_bytes;
   const uint8_t* embd;   // V rows, K = H (tied LM head)
   const float* out_norm;
-  float* kcache;  // [seq][L][CTX][KV]
-  float* vcache;
-  size_t kv_seq_stride;  // floats per sequence
+  uint8_t* kcache;  // [seq][L][CTX][KV] elements of kv_es bytes: f32, or bf16 (GG_FLAG_KV_BF16)
+  uint8_t* vcache;
+  size_t kv_seq_stride;  // elements per sequence
   // tagged activation exchange (value | tag << 32)
   uint64_t* t_qkv;  // Q + 2KV
   uint64_t* t_ml;   // [max_splits][NQH][2]  (running max, sum of exp)
@@ -78,6 +78,7 @@ struct GGModelDev {
   int max_seqs;
   unsigned long long* trace;  // [grid][GG_TRACE_PHASES][4] globaltimer stamps
   GGLayerW layers[GG_MAX_LAYERS];
+  int kv_es;  // bytes per KV cache element: 4 (f32), or 2 (bf16)
 };
 
 // Launch-mode bits.

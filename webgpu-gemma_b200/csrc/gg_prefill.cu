@@ -136,11 +136,11 @@ __global__ void __launch_bounds__(1024)
 
 // BATCH: row t is a different sequence, in KV slot seq_arr[t] (slot stride seq_stride floats)
 // at position pos_arr[t]; otherwise row t is prompt position p0 + t of one slot.
-template <bool BATCH>
+template <bool BATCH, bool KV16>
 __global__ void __launch_bounds__(PF_THREADS)
     pf_qk_kernel(const float* __restrict__ part, int splits, long long plane, const float* __restrict__ q_norm,
                  const float* __restrict__ k_norm, const float2* __restrict__ rope, int p0, int NQH, int NKH, float eps,
-                 float* __restrict__ q_out, float* __restrict__ kc, float* __restrict__ vc,
+                 float* __restrict__ q_out, kv_t<KV16>* __restrict__ kc, kv_t<KV16>* __restrict__ vc,
                  const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride) {
   constexpr int NJ = PF_HD / 32;
   const int t = blockIdx.x, pos = BATCH ? pos_arr[t] : p0 + t;
@@ -184,11 +184,11 @@ __global__ void __launch_bounds__(PF_THREADS)
     for (int j = 0; j < NJ; j++) {
       const int i = lane + 32 * j;
       if (h < NQH) q_out[(long long)t * QD + h * PF_HD + i] = v[j];
-      else kc[(long long)pos * KVD + (h - NQH) * PF_HD + i] = v[j];
+      else kc[(long long)pos * KVD + (h - NQH) * PF_HD + i] = kv_narrow<KV16>(v[j]);
     }
   }
   for (int i = threadIdx.x; i < KVD; i += PF_THREADS) {
-    vc[(long long)pos * KVD + i] = sum_planes(part, splits, plane, base + QD + KVD + i);
+    vc[(long long)pos * KVD + i] = kv_narrow<KV16>(sum_planes(part, splits, plane, base + QD + KVD + i));
   }
 }
 
@@ -205,8 +205,53 @@ constexpr int PA_KSTR = PF_HD + 4;             // K row stride (floats): float4-
 constexpr int PA_PART = PA_ROWS * PF_HD + 2 * PA_ROWS;  // floats per item: o, then m, then l
 constexpr int PA_SMEM = (PA_ROWS * PF_HD + PA_KB * PA_KSTR + PA_KB * PF_HD + PA_KB * PA_ROWS + PA_ROWS) * 4;
 
+// Rows of a 64-key block of K and V (PF_HD cache elements each) into f32 shared memory (row r
+// at ks + r * kstride, vs + r * PF_HD): 16-byte async copies from an f32 cache; from a bf16
+// cache, every 16-byte load of the block is issued before the first one is widened and stored.
+template <bool KV16>
+GG_DEV void kv_block_to_smem(float* ks, int kstride, float* vs, const kv_t<KV16>* kg, const kv_t<KV16>* vg,
+                             long long sstride, int nrows) {
+  if constexpr (KV16) {
+    constexpr int PER = PF_HD / 8;                  // 16-byte chunks per row
+    constexpr int IT = PA_KB * PER / PF_THREADS;    // chunks per thread per matrix
+    uint4 wk[IT], wv[IT];
+#pragma unroll
+    for (int k = 0; k < IT; k++) {
+      const int idx = threadIdx.x + k * PF_THREADS, r = idx / PER, c8 = idx % PER;
+      if (r < nrows) {
+        wk[k] = __ldg(reinterpret_cast<const uint4*>(kg + r * sstride + 8 * c8));
+        wv[k] = __ldg(reinterpret_cast<const uint4*>(vg + r * sstride + 8 * c8));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < IT; k++) {
+      const int idx = threadIdx.x + k * PF_THREADS, r = idx / PER, c8 = idx % PER;
+      if (r < nrows) {
+        float f[8];
+        bf16x8_widen(wk[k], f);
+        float4* d = reinterpret_cast<float4*>(ks + r * kstride + 8 * c8);
+        d[0] = make_float4(f[0], f[1], f[2], f[3]);
+        d[1] = make_float4(f[4], f[5], f[6], f[7]);
+        bf16x8_widen(wv[k], f);
+        d = reinterpret_cast<float4*>(vs + r * PF_HD + 8 * c8);
+        d[0] = make_float4(f[0], f[1], f[2], f[3]);
+        d[1] = make_float4(f[4], f[5], f[6], f[7]);
+      }
+    }
+  } else {
+    constexpr int PER = PF_HD / 4;
+    for (int idx = threadIdx.x; idx < nrows * PER; idx += PF_THREADS) {
+      const int r = idx / PER, c4 = idx % PER;
+      cp_async16(ks + r * kstride + 4 * c4, kg + r * sstride + 4 * c4);
+      cp_async16(vs + r * PF_HD + 4 * c4, vg + r * sstride + 4 * c4);
+    }
+  }
+}
+
+template <bool KV16>
 __global__ void __launch_bounds__(PF_THREADS)
-    pf_attn_part_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc, int T,
+    pf_attn_part_kernel(const float* __restrict__ q, const kv_t<KV16>* __restrict__ kc,
+                        const kv_t<KV16>* __restrict__ vc, int T,
                         int p0, int NQH, int NKH, float scale, int window, int maxc, float* __restrict__ part) {
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                         // [ROWS][HD]
@@ -251,12 +296,8 @@ __global__ void __launch_bounds__(PF_THREADS)
   for (int j0 = k_begin; j0 < k_end; j0 += PA_KB) {
     const int nk = min(PA_KB, k_end - j0);
     __syncthreads();
-    for (int idx = tid; idx < nk * (PF_HD / 4); idx += PF_THREADS) {
-      const int j = idx / (PF_HD / 4), d4 = idx % (PF_HD / 4);
-      const long long g = (long long)(j0 + j) * KVD + kvh * PF_HD + 4 * d4;
-      cp_async16(ks + j * PA_KSTR + 4 * d4, kc + g);
-      cp_async16(vs + j * PF_HD + 4 * d4, vc + g);
-    }
+    kv_block_to_smem<KV16>(ks, PA_KSTR, vs, kc + (long long)j0 * KVD + kvh * PF_HD,
+                           vc + (long long)j0 * KVD + kvh * PF_HD, KVD, nk);
     cp_async_wait_all();
     __syncthreads();
     float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
@@ -397,25 +438,40 @@ __global__ void __launch_bounds__(PF_THREADS)
 }
 
 // Decode attention for a batch of sequences: row b has one query token (NQH = 4 heads sharing
-// the single KV head) at position pos[b] of KV slot seqs[b]. A work item is (row, 128-key
-// range); thread (h, j) scores head h against key j of a 64-key block; thread d accumulates
-// output dim d of the four heads. Partial results are merged by bd_attn_merge_kernel.
+// the single KV head) at position pos[b] of KV slot seqs[b]. A work item (CTA) is (row, 64-key
+// range); each of its warps takes 16 of the keys, lane l holding dims 8l..8l+7 of the four
+// query heads, so a key row is one coalesced 1 KB (f32) or 512 B (bf16) warp load straight into
+// registers, four keys' K and V rows in flight at a time. The warp keeps an online softmax
+// (running max, sum, output) per head; the CTA merges its warps in shared memory and leaves one
+// partial result per work item, merged over the ranges by bd_attn_merge_kernel.
 constexpr int BD_NH = 4;
-constexpr int BD_KC = 64;  // keys per work item (one shared-memory block)
+constexpr int BD_KC = 64;                  // keys per work item
+constexpr int BD_WARPS = 4;                // warps per work item
+constexpr int BD_KW = BD_KC / BD_WARPS;    // keys per warp
+constexpr int BD_KB = 4;                   // keys per batch (rows in flight per warp)
 constexpr int BD_PART = BD_NH * PF_HD + 2 * BD_NH;
-constexpr int BD_SMEM = (BD_NH * PF_HD + PA_KB * (PF_HD + 1) + PA_KB * PF_HD + BD_NH * PA_KB + 4 * BD_NH + 8) * 4;
+static_assert(PF_HD == 8 * 32, "a lane holds 8 dims of a 256-wide head");
 
-__global__ void __launch_bounds__(PF_THREADS)
-    bd_attn_part_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                        const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride,
-                        float scale, int window, int maxc, float* __restrict__ part) {
-  extern __shared__ __align__(16) float sm[];
-  float* qs = sm;                          // [NH][HD]
-  float* ks = qs + BD_NH * PF_HD;          // [KB][HD+1]
-  float* vs = ks + PA_KB * (PF_HD + 1);    // [KB][HD]
-  float* ps = vs + PA_KB * PF_HD;          // [NH][KB]
-  float* st = ps + BD_NH * PA_KB;          // m[NH], l[NH], alpha[NH], bmax/bsum scratch [NH]
-  float* wred = st + 4 * BD_NH;            // [8] per-warp reductions
+// Eight consecutive cache elements (16-byte aligned when f32: two loads; bf16: one load) as f32.
+template <bool KV16>
+GG_DEV void kv_load8(const kv_t<KV16>* p, float* f) {
+  if constexpr (KV16) {
+    bf16x8_widen(__ldg(reinterpret_cast<const uint4*>(p)), f);
+  } else {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+}
+
+template <bool KV16>
+__global__ void __launch_bounds__(BD_WARPS * 32)
+    bd_attn_part_kernel(const float* __restrict__ q, const kv_t<KV16>* __restrict__ kc,
+                        const kv_t<KV16>* __restrict__ vc, const int32_t* __restrict__ pos_arr,
+                        const int32_t* __restrict__ seq_arr, size_t seq_stride, float scale, int window, int maxc,
+                        float* __restrict__ part) {
+  __shared__ float sm_m[BD_WARPS][BD_NH], sm_l[BD_WARPS][BD_NH];
+  __shared__ __align__(16) float sm_o[BD_WARPS][BD_NH][PF_HD];
   const int c = blockIdx.x, b = blockIdx.y;
   const int pos = pos_arr[b];
   const int k_begin = c * BD_KC;
@@ -423,76 +479,107 @@ __global__ void __launch_bounds__(PF_THREADS)
   const int k_end = min(k_begin + BD_KC, pos + 1);
   const int klo = window > 0 ? max(0, pos + 1 - window) : 0;  // sliding window
   if (k_end <= klo) return;
-  const float* kb = kc + (size_t)seq_arr[b] * seq_stride;
-  const float* vb = vc + (size_t)seq_arr[b] * seq_stride;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = tid / PA_KB, j = tid % PA_KB;  // score thread: head h, key j of the block
-  for (int i = tid; i < BD_NH * PF_HD; i += PF_THREADS) qs[i] = q[(size_t)b * BD_NH * PF_HD + i];
-  if (tid < BD_NH) {
-    st[tid] = -1e30f;          // m
-    st[BD_NH + tid] = 0.f;     // l
-  }
-  float o[BD_NH] = {0.f, 0.f, 0.f, 0.f};
-  for (int j0 = k_begin; j0 < k_end; j0 += PA_KB) {
-    const int nk = min(PA_KB, k_end - j0);
-    __syncthreads();
-    for (int idx = tid; idx < nk * (PF_HD / 4); idx += PF_THREADS)  // V rows: async 16-byte copies
-      cp_async16(vs + (idx / (PF_HD / 4)) * PF_HD + 4 * (idx % (PF_HD / 4)),
-                 vb + (size_t)(j0 + idx / (PF_HD / 4)) * PF_HD + 4 * (idx % (PF_HD / 4)));
-#pragma unroll 4
-    for (int idx = tid; idx < nk * (PF_HD / 4); idx += PF_THREADS) {  // K rows, padded: loads first
-      const int jj = idx / (PF_HD / 4), d4 = idx % (PF_HD / 4);
-      const float4 kv = reinterpret_cast<const float4*>(kb + (size_t)(j0 + jj) * PF_HD)[d4];
-      float* kd = ks + jj * (PF_HD + 1) + 4 * d4;
-      kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    float sc = -INFINITY;
-    const bool kin = j < nk && j0 + j >= klo;
-    if (kin) {
-      const float* qr = qs + h * PF_HD;
-      const float* kr = ks + j * (PF_HD + 1);
-      float acc = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < PF_HD; d++) acc = fmaf(qr[d], kr[d], acc);
-      sc = acc * scale;
-    }
-    // per-head block max (two warps per head)
-    float mx = warp_max(sc);
-    if (lane == 0) wred[warp] = mx;
-    __syncthreads();
-    const float bmax = fmaxf(wred[2 * h], wred[2 * h + 1]);
-    const float mold = st[h];
-    const float mnew = fmaxf(mold, bmax);
-    const float e = kin ? expf(sc - mnew) : 0.f;
-    ps[h * PA_KB + j] = e;
-    float es = warp_sum(e);
-    __syncthreads();  // wred reuse
-    if (lane == 0) wred[warp] = es;
-    __syncthreads();
-    if (j == 0) {
-      const float alpha = expf(mold - mnew);
-      st[2 * BD_NH + h] = alpha;
-      st[BD_NH + h] = st[BD_NH + h] * alpha + wred[2 * h] + wred[2 * h + 1];
-      st[h] = mnew;
-    }
-    __syncthreads();
-    const int d = tid;
+  const kv_t<KV16>* kb = kc + (size_t)seq_arr[b] * seq_stride + 8 * (threadIdx.x & 31);
+  const kv_t<KV16>* vb = vc + (size_t)seq_arr[b] * seq_stride + 8 * (threadIdx.x & 31);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float qv[BD_NH][8];
 #pragma unroll
-    for (int hh = 0; hh < BD_NH; hh++) {
-      float acc = o[hh] * st[2 * BD_NH + hh];
-      const float* pr = ps + hh * PA_KB;
-      for (int jj = 0; jj < nk; jj++) acc = fmaf(pr[jj], vs[jj * PF_HD + d], acc);
-      o[hh] = acc;
+  for (int h = 0; h < BD_NH; h++) {
+    const float4* qp = reinterpret_cast<const float4*>(q + ((size_t)b * BD_NH + h) * PF_HD + 8 * lane);
+    const float4 a = qp[0], bq = qp[1];
+    qv[h][0] = a.x; qv[h][1] = a.y; qv[h][2] = a.z; qv[h][3] = a.w;
+    qv[h][4] = bq.x; qv[h][5] = bq.y; qv[h][6] = bq.z; qv[h][7] = bq.w;
+  }
+  float m[BD_NH], l[BD_NH], o[BD_NH][8];
+#pragma unroll
+  for (int h = 0; h < BD_NH; h++) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int d = 0; d < 8; d++) o[h][d] = 0.f;
+  }
+  const int w0 = max(k_begin + warp * BD_KW, klo), w1 = min(k_begin + (warp + 1) * BD_KW, k_end);
+  for (int j0 = w0; j0 < w1; j0 += BD_KB) {
+    float kf[BD_KB][8], vf[BD_KB][8];
+#pragma unroll
+    for (int k = 0; k < BD_KB; k++) {
+      if (j0 + k < w1) {
+        kv_load8<KV16>(kb + (size_t)(j0 + k) * PF_HD, kf[k]);
+        kv_load8<KV16>(vb + (size_t)(j0 + k) * PF_HD, vf[k]);
+      } else {
+#pragma unroll
+        for (int d = 0; d < 8; d++) kf[k][d] = vf[k][d] = 0.f;
+      }
+    }
+    float sc[BD_KB][BD_NH];
+#pragma unroll
+    for (int k = 0; k < BD_KB; k++)
+#pragma unroll
+      for (int h = 0; h < BD_NH; h++) {
+        float a = 0.f;
+#pragma unroll
+        for (int d = 0; d < 8; d++) a = fmaf(qv[h][d], kf[k][d], a);
+        sc[k][h] = a;
+      }
+#pragma unroll
+    for (int k = 0; k < BD_KB; k++)
+#pragma unroll
+      for (int h = 0; h < BD_NH; h++) sc[k][h] = j0 + k < w1 ? warp_sum(sc[k][h]) * scale : -INFINITY;
+#pragma unroll
+    for (int h = 0; h < BD_NH; h++) {
+      float bm = sc[0][h];
+#pragma unroll
+      for (int k = 1; k < BD_KB; k++) bm = fmaxf(bm, sc[k][h]);
+      const float nm = fmaxf(m[h], bm);  // finite: key j0 is in range
+      const float alpha = expf(m[h] - nm);
+      float p[BD_KB], ps = 0.f;
+#pragma unroll
+      for (int k = 0; k < BD_KB; k++) {
+        p[k] = expf(sc[k][h] - nm);
+        ps += p[k];
+      }
+      l[h] = l[h] * alpha + ps;
+      m[h] = nm;
+#pragma unroll
+      for (int d = 0; d < 8; d++) {
+        float acc = o[h][d] * alpha;
+#pragma unroll
+        for (int k = 0; k < BD_KB; k++) acc = fmaf(p[k], vf[k][d], acc);
+        o[h][d] = acc;
+      }
     }
   }
+  // merge the warps: each keeps (m, l, o) of its keys; a warp without keys has m = -inf
+#pragma unroll
+  for (int h = 0; h < BD_NH; h++) {
+    float4* op = reinterpret_cast<float4*>(&sm_o[warp][h][8 * lane]);
+    op[0] = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
+    op[1] = make_float4(o[h][4], o[h][5], o[h][6], o[h][7]);
+    if (lane == 0) {
+      sm_m[warp][h] = m[h];
+      sm_l[warp][h] = l[h];
+    }
+  }
+  __syncthreads();
   float* dst = part + ((size_t)b * maxc + c) * BD_PART;
+  for (int i = threadIdx.x; i < BD_NH * PF_HD; i += BD_WARPS * 32) {
+    const int h = i / PF_HD, d = i % PF_HD;
+    float M = -INFINITY;
 #pragma unroll
-  for (int hh = 0; hh < BD_NH; hh++) dst[hh * PF_HD + tid] = o[hh];
-  if (tid < BD_NH) {
-    dst[BD_NH * PF_HD + tid] = st[tid];
-    dst[BD_NH * PF_HD + BD_NH + tid] = st[BD_NH + tid];
+    for (int w = 0; w < BD_WARPS; w++) M = fmaxf(M, sm_m[w][h]);
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < BD_WARPS; w++)
+      if (sm_m[w][h] != -INFINITY) acc = fmaf(expf(sm_m[w][h] - M), sm_o[w][h][d], acc);
+    dst[i] = acc;
+    if (d == 0) {
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < BD_WARPS; w++)
+        if (sm_m[w][h] != -INFINITY) L = fmaf(expf(sm_m[w][h] - M), sm_l[w][h], L);
+      dst[BD_NH * PF_HD + h] = M;
+      dst[BD_NH * PF_HD + BD_NH + h] = L;
+    }
   }
 }
 
@@ -598,19 +685,30 @@ cudaError_t pf_addnorm(const float* part, int splits, long long plane, const flo
 
 cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm,
                              const float* k_norm, const float2* rope, int T, int p0, int NQH, int NKH, int HD, float eps,
-                             float* q_out, float* kc, float* vc, cudaStream_t s) {
+                             float* q_out, void* kc, void* vc, bool kv16, cudaStream_t s) {
   if (T <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
-  pf_qk_kernel<false><<<T, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, p0, NQH, NKH, eps, q_out,
-                                               kc, vc, nullptr, nullptr, 0);
+  if (kv16)
+    pf_qk_kernel<false, true><<<T, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, p0, NQH, NKH, eps,
+                                                       q_out, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, nullptr, nullptr,
+                                                       0);
+  else
+    pf_qk_kernel<false, false><<<T, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, p0, NQH, NKH, eps,
+                                                        q_out, (float*)kc, (float*)vc, nullptr, nullptr, 0);
   return cudaGetLastError();
 }
 
 cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm, const float* k_norm,
                              const float2* rope, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
-                             int NKH, int HD, float eps, float* q_out, float* kc, float* vc, cudaStream_t s) {
+                             int NKH, int HD, float eps, float* q_out, void* kc, void* vc, bool kv16,
+                             cudaStream_t s) {
   if (B <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
-  pf_qk_kernel<true><<<B, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, 0, NQH, NKH, eps, q_out, kc,
-                                              vc, pos, seqs, seq_stride);
+  if (kv16)
+    pf_qk_kernel<true, true><<<B, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, 0, NQH, NKH, eps,
+                                                      q_out, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, pos, seqs,
+                                                      seq_stride);
+  else
+    pf_qk_kernel<true, false><<<B, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, 0, NQH, NKH, eps,
+                                                       q_out, (float*)kc, (float*)vc, pos, seqs, seq_stride);
   return cudaGetLastError();
 }
 
@@ -620,8 +718,8 @@ size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH) {
   return nb * maxc * NKH * PA_PART;
 }
 
-cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T, int p0, int NQH, int NKH, int HD,
-                         float scale, int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
+cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv16, int T, int p0, int NQH, int NKH,
+                         int HD, float scale, int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
   if (T <= 0 || HD != PF_HD || NKH <= 0 || NQH % NKH) return cudaErrorInvalidValue;
   const int G = NQH / NKH;
   if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) return cudaErrorInvalidValue;
@@ -631,7 +729,9 @@ cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T
   if (r != cudaSuccess) return r;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    r = cudaFuncSetAttribute(pf_attn_part_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
+    r = cudaFuncSetAttribute(pf_attn_part_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(pf_attn_part_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
     if (r != cudaSuccess) return r;
     attr_set[dev] = true;
   }
@@ -639,8 +739,12 @@ cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T
   const int nb = (T + QT - 1) / QT;
   const int maxc = (p0 + T - 1) / PA_KC + 1;
   if (maxc > 16) return cudaErrorInvalidValue;  // merge weights hold 16 key ranges (2048 positions)
-  pf_attn_part_kernel<<<dim3(maxc, nb, NKH), PF_THREADS, PA_SMEM, s>>>(q, kc, vc, T, p0, NQH, NKH, scale, window, maxc,
-                                                                       part);
+  if (kv16)
+    pf_attn_part_kernel<true><<<dim3(maxc, nb, NKH), PF_THREADS, PA_SMEM, s>>>(
+        q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
+  else
+    pf_attn_part_kernel<false><<<dim3(maxc, nb, NKH), PF_THREADS, PA_SMEM, s>>>(
+        q, (const float*)kc, (const float*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
   r = cudaGetLastError();
   if (r != cudaSuccess) return r;
   pf_attn_merge_kernel<<<dim3(nb, NKH), PF_THREADS, 0, s>>>(part, T, p0, NQH, NKH, window, maxc, thi, tlo);
@@ -651,25 +755,19 @@ size_t bd_attention_part_floats(int max_rows, int ctx) {
   return (size_t)max_rows * ((ctx + BD_KC - 1) / BD_KC) * BD_PART;
 }
 
-cudaError_t bd_attention(const float* q, const float* kc, const float* vc, int B, const int32_t* pos,
+cudaError_t bd_attention(const float* q, const void* kc, const void* vc, bool kv16, int B, const int32_t* pos,
                          const int32_t* seqs, size_t seq_stride, int max_pos, int NQH, int NKH, int HD, float scale,
                          int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
   if (B <= 0 || HD != PF_HD || NQH != BD_NH || NKH != 1) return cudaErrorInvalidValue;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaError_t r = cudaGetDevice(&dev);
-  if (r != cudaSuccess) return r;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
-    r = cudaFuncSetAttribute(bd_attn_part_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BD_SMEM);
-    if (r != cudaSuccess) return r;
-    attr_set[dev] = true;
-  }
   const int maxc = max_pos / BD_KC + 1;
   if (maxc > 32) return cudaErrorInvalidValue;  // merge weights hold 32 key ranges (2048 positions)
-  bd_attn_part_kernel<<<dim3(maxc, B), PF_THREADS, BD_SMEM, s>>>(q, kc, vc, pos, seqs, seq_stride, scale, window, maxc,
-                                                                 part);
-  r = cudaGetLastError();
+  if (kv16)
+    bd_attn_part_kernel<true><<<dim3(maxc, B), BD_WARPS * 32, 0, s>>>(
+        q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
+  else
+    bd_attn_part_kernel<false><<<dim3(maxc, B), BD_WARPS * 32, 0, s>>>(
+        q, (const float*)kc, (const float*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
+  cudaError_t r = cudaGetLastError();
   if (r != cudaSuccess) return r;
   bd_attn_merge_kernel<<<B, PF_THREADS, 0, s>>>(part, pos, window, maxc, thi, tlo);
   return cudaGetLastError();

@@ -24,18 +24,19 @@ cudaError_t pf_addnorm(const float* part, int splits, long long plane, const flo
                        cudaStream_t s);
 
 // Per token: sum the QKV planes, q/k per-head rmsNorm + RoPE at position p0 + t
-// (shaders.ts:420-467), q -> q_out [T][NQH*HD], k and v -> rows p0.. of this layer's cache.
+// (shaders.ts:420-467), q -> q_out [T][NQH*HD], k and v -> rows p0.. of this layer's cache
+// (f32 elements, or bf16 rounded to nearest even when kv16).
 cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm,
                              const float* k_norm, const float2* rope, int T, int p0, int NQH, int NKH, int HD, float eps,
-                             float* q_out, float* kc, float* vc, cudaStream_t s);
+                             float* q_out, void* kc, void* vc, bool kv16, cudaStream_t s);
 
 // Causal attention of the T queries at positions p0..p0+T-1 over cache rows 0..p0+t
 // (shaders.ts:229-325), output written as activation tiles of width NQH*HD. `part` is scratch
 // of pf_attention_part_floats(T, p0 + T, NQH, NKH) floats (partial results per key range).
 size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH);
 // window > 0: each query at position p sees only keys p-window+1..p (sliding-window layer).
-cudaError_t pf_attention(const float* q, const float* kc, const float* vc, int T, int p0, int NQH, int NKH, int HD,
-                         float scale, int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
+cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv16, int T, int p0, int NQH, int NKH,
+                         int HD, float scale, int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
 
 // act[t][i] = gelu_tanh(gu[t][2i]) * gu[t][2i+1] (shaders.ts:153-170, gu = sum of planes) as
 // activation tiles of width I.
@@ -45,15 +46,16 @@ cudaError_t pf_geglu(const float* gu, int splits, long long plane, int T, int I,
 // ---- batched decode: row b is one token of the sequence in KV slot seqs[b] at position pos[b]
 
 // As pf_qk_rope_store, per row: kc/vc point at this layer's rows of slot 0, slots seq_stride
-// floats apart.
+// elements apart.
 cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm, const float* k_norm,
                              const float2* rope, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
-                             int NKH, int HD, float eps, float* q_out, float* kc, float* vc, cudaStream_t s);
+                             int NKH, int HD, float eps, float* q_out, void* kc, void* vc, bool kv16,
+                             cudaStream_t s);
 
 // Attention of each row's query over its slot's cache rows 0..pos[b] (4 query heads sharing one
 // KV head), written as activation tiles. max_pos >= every pos[b]; `part` holds
 // bd_attention_part_floats(B, ctx) floats.
 size_t bd_attention_part_floats(int max_rows, int ctx);
-cudaError_t bd_attention(const float* q, const float* kc, const float* vc, int B, const int32_t* pos,
+cudaError_t bd_attention(const float* q, const void* kc, const void* vc, bool kv16, int B, const int32_t* pos,
                          const int32_t* seqs, size_t seq_stride, int max_pos, int NQH, int NKH, int HD, float scale,
                          int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);

@@ -35,6 +35,9 @@ class GemmaConfig:
     # Not in the reference (which attends the whole prefix on every layer): > 0 limits the
     # sliding-window layers to the last `sliding_window` positions, as Gemma 3 is specified.
     sliding_window: int = 0
+    # KV cache element type: "f32" as the reference (engine.ts:440-447), or "bf16" (rows
+    # rounded to nearest even when stored; GG_FLAG_KV_BF16 in the C-ABI).
+    kv_dtype: str = "f32"
 
     def as_dict(self) -> dict:
         return asdict(self)
@@ -88,13 +91,24 @@ class CConfig(ctypes.Structure):
     ]
 
 
+GG_FLAG_KV_BF16 = 2  # include/gemma_b200.h
+
+
+def kv_flags(cfg) -> int:
+    """gg_config.flags bits that follow from the configuration itself (the KV element type)."""
+    kv = getattr(cfg, "kv_dtype", "f32")
+    if kv not in ("f32", "bf16"):
+        raise ValueError(f"kv_dtype must be 'f32' or 'bf16', not {kv!r}")
+    return GG_FLAG_KV_BF16 if kv == "bf16" else 0
+
+
 def to_cconfig(cfg: GemmaConfig, max_seqs: int = 1, flags: int = 0) -> CConfig:
     c = CConfig()
     for name, _ in CConfig._fields_:
         if name == "max_seqs":
             c.max_seqs = max_seqs
         elif name == "flags":
-            c.flags = flags
+            c.flags = flags | kv_flags(cfg)
         else:
             setattr(c, name, getattr(cfg, name))
     return c

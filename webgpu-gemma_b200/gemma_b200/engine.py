@@ -17,7 +17,7 @@ from typing import Callable, Iterator
 import numpy as np
 
 from . import gguf, synth
-from .config import GemmaConfig, default_config
+from .config import GemmaConfig, default_config, gemma3_spec
 from .conversation import build_chat_prompt
 from .native import NativeEngine
 from .tokenizer import Tokenizer
@@ -39,7 +39,7 @@ class GemmaEngine:
 
     def __init__(self, model: str = "synthetic:1b", on_progress: Callable[[dict], None] | None = None,
                  context_length: int | None = None, device: int = 0,
-                 random: Callable[[], float] | None = None):
+                 random: Callable[[], float] | None = None, kv_dtype: str = "f32", spec: bool = False):
         self.config: GemmaConfig = default_config()
         if context_length:
             self.config.context_length = context_length
@@ -53,6 +53,10 @@ class GemmaEngine:
             self._mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
         parsed = gguf.parse(memoryview(self._mm))
         gguf.update_config_from_gguf(parsed, self.config, context_length)
+        # options beyond the reference's: KV element type, Gemma 3's sliding window + local theta
+        self.config.kv_dtype = kv_dtype
+        if spec:
+            gemma3_spec(self.config)
         self.tokenizer = Tokenizer.from_gguf(parsed)
         self._native = NativeEngine(self.config, device=device)
         total = sum(gguf.tensor_byte_size(t) for t in parsed.tensors)
@@ -141,10 +145,12 @@ class GemmaEngine:
 
 
 def create_gemma_engine(model: str = "synthetic:1b", on_progress=None, context_length: int | None = None,
-                        device: int = 0, random=None) -> GemmaEngine:
-    """``createGemmaEngine`` (src/index.ts:34-38)."""
+                        device: int = 0, random=None, kv_dtype: str = "f32", spec: bool = False) -> GemmaEngine:
+    """``createGemmaEngine`` (src/index.ts:34-38). ``kv_dtype`` ("f32" as the reference, or
+    "bf16") and ``spec`` (Gemma 3's 512-position window and local theta 1e4, off as in the
+    reference) are options the reference does not have."""
     return GemmaEngine(model=model, on_progress=on_progress, context_length=context_length, device=device,
-                       random=random)
+                       random=random, kv_dtype=kv_dtype, spec=spec)
 
 
 def philox_uniforms(seed: int, stream: int, n: int) -> np.ndarray:
