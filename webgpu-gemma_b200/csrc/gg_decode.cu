@@ -23,6 +23,7 @@
 // chunk exponent and the Q8_0 block scale (accumulation order differs from the shader's
 // sequential f32 loop; results agree within f32 rounding).
 #include "gg_device.cuh"
+#include "gg_launch.h"
 #include "gg_model.h"
 
 namespace gg {
@@ -1110,6 +1111,8 @@ __global__ void __launch_bounds__(512)
                            const GGSampleDev* __restrict__ sp, const double* __restrict__ unif, uint8_t* seen,
                            int seen_stride, int32_t* seen_cnt, unsigned long long* keys, int32_t* tokens,
                            int32_t* pos, int32_t* out) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   __shared__ GGModelDev sm;
   __shared__ GGState ss;
   __shared__ unsigned long long sk[8][256];
@@ -1198,9 +1201,8 @@ cudaError_t gg_batch_sample(const float* logits, int B, int V, const int32_t* se
                             const double* unif, uint8_t* seen, int seen_stride, int32_t* seen_cnt,
                             unsigned long long* keys, int32_t* tokens, int32_t* pos, int32_t* out, cudaStream_t s) {
   if (B <= 0) return cudaErrorInvalidValue;
-  gg::gg_batch_sample_kernel<<<B, 512, 0, s>>>(logits, V, seqs, sp, unif, seen, seen_stride, seen_cnt, keys, tokens,
-                                                pos, out);
-  return cudaGetLastError();
+  return gg::launch_pdl(gg::gg_batch_sample_kernel, dim3(B), dim3(512), 0, s, logits, V, seqs, sp, unif, seen,
+                        seen_stride, seen_cnt, keys, tokens, pos, out);
 }
 
 // ------------------------------------------------------------------ sampling without allocation

@@ -207,6 +207,12 @@ GG_DEV void bf16x8_widen(const uint4 w, float* f) {
   }
 }
 
+// Programmatic dependent launch (see gg_launch.h): let the next kernel of the stream become
+// resident now / wait until the kernels this one depends on have completed and their writes
+// are visible. Both are no-ops in a kernel launched without the attribute.
+GG_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+GG_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 GG_DEV float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -19,6 +19,7 @@
 #include "gg_device.cuh"
 #include "gg_model.h"
 #include "gg_gemm.h"
+#include "gg_launch.h"
 #include "gg_prefill.h"
 
 namespace gg {
@@ -1018,6 +1019,8 @@ extern "C" int gg_selftest_wait(gg_engine* e, uint64_t timeout_ns) {
 
 // Sum of `splits` consecutive planes of n floats, in plane order.
 __global__ void gg_sum_splits_kernel(const float* __restrict__ p, int splits, long long n, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     float s = p[i];
     for (int z = 1; z < splits; z++) s += p[(long long)z * n + i];
@@ -1069,8 +1072,8 @@ extern "C" int gg_linear(gg_engine* e, int which, int layer, const float* x, int
     float* part = e->lin_y + plane;
     GG_CUDA(e, gg_gemm_q8(w, e->lin_tiles, e->lin_tiles + tb, T, part, M, splits, plane, &e->d_st->error, e->timeout_ns,
                           e->stream));
-    gg_sum_splits_kernel<<<e->sm_count * 4, 256, 0, e->stream>>>(part, splits, plane, out);
-    GG_CUDA(e, cudaGetLastError());
+    GG_CUDA(e, gg::launch_pdl(gg_sum_splits_kernel, dim3(e->sm_count * 4), dim3(256), 0, e->stream, (const float*)part,
+                              splits, (long long)plane, out));
   }
   GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
   GG_CUDA(e, cudaMemcpyAsync(y, out, sizeof(float) * (size_t)plane, cudaMemcpyDeviceToHost, e->stream));

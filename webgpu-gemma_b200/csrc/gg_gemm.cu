@@ -19,6 +19,7 @@
 
 #include "gg_gemm.h"
 #include "gg_gemm_dev.cuh"
+#include "gg_launch.h"
 
 namespace gg {
 
@@ -119,6 +120,9 @@ __global__ void __launch_bounds__(GM_THREADS, GemmCfg<NT>::MIN_CTAS) gg_gemm_q8_
   const int s0 = blockIdx.z * a.slabs_per_split;
   const int ns = min(a.slabs_per_split, a.KS - s0);
   const SpinCtl sc{a.err, a.timeout_ns};
+  // Under programmatic dependent launch the weights (never written by any kernel) stream in
+  // before pdl_wait(); the activation copies (warp 0) and the output writes wait for it.
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < AS; i++) {
@@ -144,6 +148,7 @@ __global__ void __launch_bounds__(GM_THREADS, GemmCfg<NT>::MIN_CTAS) gg_gemm_q8_
 
   if (warp == 0) {
     if (lane == 0) {  // activation tiles
+      pdl_wait();
       const size_t KS = (size_t)a.KS;
       int issued = 0;
       for (int i = 0; i < ns; i++) {
@@ -235,6 +240,7 @@ __global__ void __launch_bounds__(GM_THREADS, GemmCfg<NT>::MIN_CTAS) gg_gemm_q8_
     }
     if (tw < 4) {  // epilogue: warp w reads TMEM lanes 32*(w%4)..
       const int q = warp & 3;
+      pdl_wait();
       const bool ok = mbar_wait(acc_bar, 0, sc);
       tc_fence_after();
       const int go = __shfl_sync(0xffffffffu, (ok && !*abort_flag) ? 1 : 0, 0);
@@ -304,6 +310,7 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const Gemm
   const int s0 = blockIdx.z * a.slabs_per_split;
   const int ns = min(a.slabs_per_split, a.KS - s0);
   const SpinCtl sc{a.err, a.timeout_ns};
+  pdl_trigger();  // weight tiles of the first stages load before pdl_wait(), activations after
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; i++) {
       mbar_init(&full[i], 1);
@@ -324,6 +331,13 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const Gemm
   if (warp == 0) {
     if (lane == 0) {
       const size_t KS = (size_t)a.KS;
+      const int pre = min(ns, S);  // stages whose weight tile is issued before the wait
+      for (int i = 0; i < pre; i++) {
+        mbar_arrive_expect_tx(&full[i], C::STAGE);
+        bulk_g2s_plain(ring + i * C::STAGE, a.wt + ((size_t)m_tile * KS + (size_t)(s0 + i)) * GD_A_STAGE, GD_A_STAGE,
+                       &full[i]);
+      }
+      pdl_wait();
       int issued = 0;
       for (int i = 0; i < ns; i++) {
         const int o = i % S;
@@ -333,8 +347,10 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const Gemm
           break;
         }
         uint8_t* dst = ring + o * C::STAGE;
-        mbar_arrive_expect_tx(&full[o], C::STAGE);
-        bulk_g2s_plain(dst, a.wt + ((size_t)m_tile * KS + (size_t)(s0 + i)) * GD_A_STAGE, GD_A_STAGE, &full[o]);
+        if (i >= pre) {
+          mbar_arrive_expect_tx(&full[o], C::STAGE);
+          bulk_g2s_plain(dst, a.wt + ((size_t)m_tile * KS + (size_t)(s0 + i)) * GD_A_STAGE, GD_A_STAGE, &full[o]);
+        }
 #pragma unroll
         for (int hh = 0; hh < NT / 64; hh++) {
           const size_t blk = ((size_t)(n_tile * (NT / 64) + hh) * KS + (size_t)(s0 + i)) * 8192u;
@@ -371,6 +387,7 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const Gemm
     }
   } else {  // warps 2..5: epilogue (warp w reads TMEM lanes 32*(w%4)..)
     const int q = warp & 3;
+    pdl_wait();
     const bool ok = mbar_wait(acc_bar, 0, sc);
     tc_fence_after();
     const int go = __shfl_sync(0xffffffffu, (ok && !*abort_flag) ? 1 : 0, 0);
@@ -427,6 +444,8 @@ __global__ void gg_q8_tile_kernel(const uint8_t* __restrict__ rows, int rs, int 
 
 // f32 rows -> activation tiles; one thread per 8 columns.
 __global__ void gg_xtiles_kernel(const float* __restrict__ x, int T, int Tpad, int K, uint8_t* hi, uint8_t* lo) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   const int KS = K / 64, k8 = K / 8;
   const long long n = (long long)Tpad * k8;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -477,7 +496,8 @@ cudaError_t gg_xtiles_from_f32(const float* x, int T, int K, uint8_t* xhi, uint8
   const int Tpad = (T + 255) / 256 * 256;  // whole tiles of the widest (256-row) kernel
   const long long n = (long long)Tpad * (K / 8);
   const int blocks = (int)((n + 255) / 256 < 148 * 8 ? (n + 255) / 256 : 148 * 8);
-  gg_xtiles_kernel<<<blocks, 256, 0, s>>>(x, T, Tpad, K, xhi, xlo);
+  cudaError_t r = launch_pdl(gg_xtiles_kernel, dim3(blocks), dim3(256), 0, s, x, T, Tpad, K, xhi, xlo);
+  if (r != cudaSuccess) return r;
   return cudaGetLastError();
 }
 
@@ -494,7 +514,8 @@ static cudaError_t launch_nt(const GGQ8Map& w, const GemmArgs& a, int splits, cu
     attr_set[dev] = true;
   }
   dim3 grid((a.T + NT - 1) / NT, w.M / 128, splits);
-  gg_gemm_q8_kernel<NT><<<grid, GM_THREADS, GemmCfg<NT>::SMEM, s>>>(a);
+  r = launch_pdl(gg_gemm_q8_kernel<NT>, grid, dim3(GM_THREADS), GemmCfg<NT>::SMEM, s, a);
+  if (r != cudaSuccess) return r;
   return cudaGetLastError();
 }
 
@@ -511,7 +532,8 @@ static cudaError_t launch_dense(const GemmArgs& a, int m_tiles, int splits, cuda
     attr_set[dev] = true;
   }
   dim3 grid((a.T + NT - 1) / NT, m_tiles, splits);
-  gg_gemm_dense_kernel<NT><<<grid, GD_THREADS, DenseCfg<NT>::SMEM, s>>>(a);
+  r = launch_pdl(gg_gemm_dense_kernel<NT>, grid, dim3(GD_THREADS), DenseCfg<NT>::SMEM, s, a);
+  if (r != cudaSuccess) return r;
   return cudaGetLastError();
 }
 

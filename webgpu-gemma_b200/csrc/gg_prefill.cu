@@ -8,6 +8,7 @@
 // is the reference's (formulas of shaders.ts, f32 throughout); only the order of some sums
 // differs, within f32 rounding.
 #include "gg_gemm_dev.cuh"
+#include "gg_launch.h"
 #include "gg_prefill.h"
 
 namespace gg {
@@ -55,6 +56,8 @@ GG_DEV float block_sum256(float v, float* red) {
 __global__ void __launch_bounds__(PF_THREADS) pf_embed_kernel(const int32_t* __restrict__ ids,
                                                               const uint8_t* __restrict__ embd, int rs, int H,
                                                               float* __restrict__ hidden) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   const int t = blockIdx.x;
   const uint8_t* row = embd + (size_t)ids[t] * rs;
   const float sq = sqrtf((float)H);
@@ -71,6 +74,8 @@ __global__ void __launch_bounds__(1024)
     pf_addnorm_kernel(const float* __restrict__ part, int splits, long long plane, const float* __restrict__ w_post,
                       const float* rin, float* rout, const float* __restrict__ w_norm, uint8_t* thi, uint8_t* tlo,
                       int H, float eps) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   __shared__ float red[32];
   __shared__ float tot[2];
   const int t = blockIdx.x, k = threadIdx.x, nq = H >> 2;
@@ -142,6 +147,8 @@ __global__ void __launch_bounds__(PF_THREADS)
                  const float* __restrict__ k_norm, const float2* __restrict__ rope, int p0, int NQH, int NKH, float eps,
                  float* __restrict__ q_out, kv_t<KV16>* __restrict__ kc, kv_t<KV16>* __restrict__ vc,
                  const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   constexpr int NJ = PF_HD / 32;
   const int t = blockIdx.x, pos = BATCH ? pos_arr[t] : p0 + t;
   if (BATCH) {
@@ -253,6 +260,8 @@ __global__ void __launch_bounds__(PF_THREADS)
     pf_attn_part_kernel(const float* __restrict__ q, const kv_t<KV16>* __restrict__ kc,
                         const kv_t<KV16>* __restrict__ vc, int T,
                         int p0, int NQH, int NKH, float scale, int window, int maxc, float* __restrict__ part) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                         // [ROWS][HD]
   float* ks = qs + PA_ROWS * PF_HD;       // [KB][KSTR]
@@ -396,6 +405,8 @@ __global__ void __launch_bounds__(PF_THREADS)
 __global__ void __launch_bounds__(PF_THREADS)
     pf_attn_merge_kernel(const float* __restrict__ part, int T, int p0, int NQH, int NKH, int window, int maxc,
                          uint8_t* thi, uint8_t* tlo) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   __shared__ float wgt[16][PA_ROWS];
   __shared__ float inv[PA_ROWS];
   const int G = NQH / NKH, QT = PA_ROWS / G;
@@ -470,6 +481,8 @@ __global__ void __launch_bounds__(BD_WARPS * 32)
                         const kv_t<KV16>* __restrict__ vc, const int32_t* __restrict__ pos_arr,
                         const int32_t* __restrict__ seq_arr, size_t seq_stride, float scale, int window, int maxc,
                         float* __restrict__ part) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   __shared__ float sm_m[BD_WARPS][BD_NH], sm_l[BD_WARPS][BD_NH];
   __shared__ __align__(16) float sm_o[BD_WARPS][BD_NH][PF_HD];
   const int c = blockIdx.x, b = blockIdx.y;
@@ -586,6 +599,8 @@ __global__ void __launch_bounds__(BD_WARPS * 32)
 __global__ void __launch_bounds__(PF_THREADS)
     bd_attn_merge_kernel(const float* __restrict__ part, const int32_t* __restrict__ pos_arr, int window, int maxc,
                          uint8_t* thi, uint8_t* tlo) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   __shared__ float wgt[32][BD_NH];
   __shared__ float inv[BD_NH];
   const int b = blockIdx.x;
@@ -622,6 +637,8 @@ __global__ void __launch_bounds__(PF_THREADS)
 
 __global__ void __launch_bounds__(PF_THREADS) pf_geglu_kernel(const float* __restrict__ gu, int splits, long long plane,
                                                               int T, int I, uint8_t* thi, uint8_t* tlo) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   const int c8 = I / 8;
   const long long n = (long long)T * c8;
   for (long long idx = blockIdx.x * (long long)PF_THREADS + threadIdx.x; idx < n;
@@ -670,8 +687,7 @@ cudaError_t gg_rope_table(float theta, int HD, int ctx, float2* out, cudaStream_
 
 cudaError_t pf_embed(const int32_t* ids, int T, const uint8_t* embd, int rs, int H, float* hidden, cudaStream_t s) {
   if (T <= 0) return cudaErrorInvalidValue;
-  pf_embed_kernel<<<T, PF_THREADS, 0, s>>>(ids, embd, rs, H, hidden);
-  return cudaGetLastError();
+  return launch_pdl(pf_embed_kernel, dim3(T), dim3(PF_THREADS), 0, s, ids, embd, rs, H, hidden);
 }
 
 cudaError_t pf_addnorm(const float* part, int splits, long long plane, const float* w_post, const float* resid_in,
@@ -679,8 +695,8 @@ cudaError_t pf_addnorm(const float* part, int splits, long long plane, const flo
                        cudaStream_t s) {
   if (T <= 0 || H > PF_MAX_H || H % 64) return cudaErrorInvalidValue;
   const int threads = ((H / 4) + 31) / 32 * 32;
-  pf_addnorm_kernel<<<T, threads, 0, s>>>(part, splits, plane, w_post, resid_in, resid_out, w_norm, thi, tlo, H, eps);
-  return cudaGetLastError();
+  return launch_pdl(pf_addnorm_kernel, dim3(T), dim3(threads), 0, s, part, splits, plane, w_post, resid_in, resid_out,
+                    w_norm, thi, tlo, H, eps);
 }
 
 cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm,
@@ -688,13 +704,11 @@ cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, con
                              float* q_out, void* kc, void* vc, bool kv16, cudaStream_t s) {
   if (T <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
   if (kv16)
-    pf_qk_kernel<false, true><<<T, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, p0, NQH, NKH, eps,
-                                                       q_out, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, nullptr, nullptr,
-                                                       0);
-  else
-    pf_qk_kernel<false, false><<<T, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, p0, NQH, NKH, eps,
-                                                        q_out, (float*)kc, (float*)vc, nullptr, nullptr, 0);
-  return cudaGetLastError();
+    return launch_pdl(pf_qk_kernel<false, true>, dim3(T), dim3(PF_THREADS), 0, s, part, splits, plane, q_norm, k_norm,
+                      rope, p0, NQH, NKH, eps, q_out, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, nullptr, nullptr,
+                      (size_t)0);
+  return launch_pdl(pf_qk_kernel<false, false>, dim3(T), dim3(PF_THREADS), 0, s, part, splits, plane, q_norm, k_norm,
+                    rope, p0, NQH, NKH, eps, q_out, (float*)kc, (float*)vc, nullptr, nullptr, (size_t)0);
 }
 
 cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm, const float* k_norm,
@@ -703,13 +717,10 @@ cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, con
                              cudaStream_t s) {
   if (B <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
   if (kv16)
-    pf_qk_kernel<true, true><<<B, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, 0, NQH, NKH, eps,
-                                                      q_out, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, pos, seqs,
-                                                      seq_stride);
-  else
-    pf_qk_kernel<true, false><<<B, PF_THREADS, 0, s>>>(part, splits, plane, q_norm, k_norm, rope, 0, NQH, NKH, eps,
-                                                       q_out, (float*)kc, (float*)vc, pos, seqs, seq_stride);
-  return cudaGetLastError();
+    return launch_pdl(pf_qk_kernel<true, true>, dim3(B), dim3(PF_THREADS), 0, s, part, splits, plane, q_norm, k_norm,
+                      rope, 0, NQH, NKH, eps, q_out, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, pos, seqs, seq_stride);
+  return launch_pdl(pf_qk_kernel<true, false>, dim3(B), dim3(PF_THREADS), 0, s, part, splits, plane, q_norm, k_norm,
+                    rope, 0, NQH, NKH, eps, q_out, (float*)kc, (float*)vc, pos, seqs, seq_stride);
 }
 
 size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH) {
@@ -739,16 +750,16 @@ cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv
   const int nb = (T + QT - 1) / QT;
   const int maxc = (p0 + T - 1) / PA_KC + 1;
   if (maxc > 16) return cudaErrorInvalidValue;  // merge weights hold 16 key ranges (2048 positions)
+  const dim3 grid(maxc, nb, NKH);
   if (kv16)
-    pf_attn_part_kernel<true><<<dim3(maxc, nb, NKH), PF_THREADS, PA_SMEM, s>>>(
-        q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
+    r = launch_pdl(pf_attn_part_kernel<true>, grid, dim3(PF_THREADS), PA_SMEM, s, q, (const __nv_bfloat16*)kc,
+                   (const __nv_bfloat16*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
   else
-    pf_attn_part_kernel<false><<<dim3(maxc, nb, NKH), PF_THREADS, PA_SMEM, s>>>(
-        q, (const float*)kc, (const float*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
-  r = cudaGetLastError();
+    r = launch_pdl(pf_attn_part_kernel<false>, grid, dim3(PF_THREADS), PA_SMEM, s, q, (const float*)kc,
+                   (const float*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
   if (r != cudaSuccess) return r;
-  pf_attn_merge_kernel<<<dim3(nb, NKH), PF_THREADS, 0, s>>>(part, T, p0, NQH, NKH, window, maxc, thi, tlo);
-  return cudaGetLastError();
+  return launch_pdl(pf_attn_merge_kernel, dim3(nb, NKH), dim3(PF_THREADS), 0, s, (const float*)part, T, p0, NQH, NKH,
+                    window, maxc, thi, tlo);
 }
 
 size_t bd_attention_part_floats(int max_rows, int ctx) {
@@ -761,16 +772,16 @@ cudaError_t bd_attention(const float* q, const void* kc, const void* vc, bool kv
   if (B <= 0 || HD != PF_HD || NQH != BD_NH || NKH != 1) return cudaErrorInvalidValue;
   const int maxc = max_pos / BD_KC + 1;
   if (maxc > 32) return cudaErrorInvalidValue;  // merge weights hold 32 key ranges (2048 positions)
+  cudaError_t r;
   if (kv16)
-    bd_attn_part_kernel<true><<<dim3(maxc, B), BD_WARPS * 32, 0, s>>>(
-        q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
+    r = launch_pdl(bd_attn_part_kernel<true>, dim3(maxc, B), dim3(BD_WARPS * 32), 0, s, q, (const __nv_bfloat16*)kc,
+                   (const __nv_bfloat16*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
   else
-    bd_attn_part_kernel<false><<<dim3(maxc, B), BD_WARPS * 32, 0, s>>>(
-        q, (const float*)kc, (const float*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
-  cudaError_t r = cudaGetLastError();
+    r = launch_pdl(bd_attn_part_kernel<false>, dim3(maxc, B), dim3(BD_WARPS * 32), 0, s, q, (const float*)kc,
+                   (const float*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
   if (r != cudaSuccess) return r;
-  bd_attn_merge_kernel<<<B, PF_THREADS, 0, s>>>(part, pos, window, maxc, thi, tlo);
-  return cudaGetLastError();
+  return launch_pdl(bd_attn_merge_kernel, dim3(B), dim3(PF_THREADS), 0, s, (const float*)part, pos, window, maxc, thi,
+                    tlo);
 }
 
 cudaError_t pf_geglu(const float* gu, int splits, long long plane, int T, int I, uint8_t* thi, uint8_t* tlo,
@@ -778,6 +789,5 @@ cudaError_t pf_geglu(const float* gu, int splits, long long plane, int T, int I,
   if (T <= 0 || I % 64 || splits < 1) return cudaErrorInvalidValue;
   const long long n = (long long)T * (I / 8);
   const int blocks = (int)((n + PF_THREADS - 1) / PF_THREADS < 148 * 8 ? (n + PF_THREADS - 1) / PF_THREADS : 148 * 8);
-  pf_geglu_kernel<<<blocks, PF_THREADS, 0, s>>>(gu, splits, plane, T, I, thi, tlo);
-  return cudaGetLastError();
+  return launch_pdl(pf_geglu_kernel, dim3(blocks), dim3(PF_THREADS), 0, s, gu, splits, plane, T, I, thi, tlo);
 }
