@@ -224,6 +224,30 @@ GG_DEV float warp_max(float v) {
   return v;
 }
 
+// Warp totals of 16 values at once: afterwards every lane holds v[i] summed over the warp, for
+// all i. A butterfly reduce-scatter (8 + 4 + 2 + 1 shuffles, 1 more to finish each lane pair)
+// leaves lane L with the total of value 8*L4 + 4*L3 + 2*L2 + L1 (Lk = bit k of L), then 16
+// shuffles broadcast the totals: 32 shuffles instead of 16 separate 5-step reductions.
+GG_DEV void warp_sum16(float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+  float a8[8], a4[4], a2[2];
+  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+    a8[i] = (u16 ? v[i + 8] : v[i]) + __shfl_xor_sync(0xffffffffu, u16 ? v[i] : v[i + 8], 16);
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+    a4[i] = (u8 ? a8[i + 4] : a8[i]) + __shfl_xor_sync(0xffffffffu, u8 ? a8[i] : a8[i + 4], 8);
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+    a2[i] = (u4 ? a4[i + 2] : a4[i]) + __shfl_xor_sync(0xffffffffu, u4 ? a4[i] : a4[i + 2], 4);
+  float a1 = (u2 ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, u2 ? a2[0] : a2[1], 2);
+  a1 += __shfl_xor_sync(0xffffffffu, a1, 1);
+#pragma unroll
+  for (int j = 0; j < 16; j++)
+    v[j] = __shfl_sync(0xffffffffu, a1, 16 * ((j >> 3) & 1) + 8 * ((j >> 2) & 1) + 4 * ((j >> 1) & 1) + 2 * (j & 1));
+}
+
 // Order-preserving map f32 -> u32 (larger float => larger key); NaN is never produced here.
 GG_DEV uint32_t f32_order_key(float f) {
   uint32_t u = __float_as_uint(f);

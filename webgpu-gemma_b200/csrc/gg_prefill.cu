@@ -524,7 +524,8 @@ __global__ void __launch_bounds__(BD_WARPS * 32)
         for (int d = 0; d < 8; d++) kf[k][d] = vf[k][d] = 0.f;
       }
     }
-    float sc[BD_KB][BD_NH];
+    static_assert(BD_KB * BD_NH == 16, "one 16-value warp reduction per batch");
+    float dots[16];
 #pragma unroll
     for (int k = 0; k < BD_KB; k++)
 #pragma unroll
@@ -532,12 +533,14 @@ __global__ void __launch_bounds__(BD_WARPS * 32)
         float a = 0.f;
 #pragma unroll
         for (int d = 0; d < 8; d++) a = fmaf(qv[h][d], kf[k][d], a);
-        sc[k][h] = a;
+        dots[k * BD_NH + h] = a;
       }
+    warp_sum16(dots);
+    float sc[BD_KB][BD_NH];
 #pragma unroll
     for (int k = 0; k < BD_KB; k++)
 #pragma unroll
-      for (int h = 0; h < BD_NH; h++) sc[k][h] = j0 + k < w1 ? warp_sum(sc[k][h]) * scale : -INFINITY;
+      for (int h = 0; h < BD_NH; h++) sc[k][h] = j0 + k < w1 ? dots[k * BD_NH + h] * scale : -INFINITY;
 #pragma unroll
     for (int h = 0; h < BD_NH; h++) {
       float bm = sc[0][h];
@@ -601,37 +604,48 @@ __global__ void __launch_bounds__(PF_THREADS)
                          uint8_t* thi, uint8_t* tlo) {
   pdl_trigger();
   pdl_wait();  // before touching any buffer shared with the other kernels of the chain
-  __shared__ float wgt[32][BD_NH];
-  __shared__ float inv[BD_NH];
+  __shared__ float wm[32][BD_NH], wl[32][BD_NH];  // (max, sum) of every key range and head
   const int b = blockIdx.x;
   const int nch = min(maxc, pos_arr[b] / BD_KC + 1);
   const int c0 = window > 0 ? max(0, pos_arr[b] + 1 - window) / BD_KC : 0;
-  const float* base = part + (size_t)b * maxc * BD_PART;
-  if (threadIdx.x < BD_NH) {
-    const int h = threadIdx.x;
-    float M = -1e30f;
-    for (int c = c0; c < nch; c++) M = fmaxf(M, base[(size_t)c * BD_PART + BD_NH * PF_HD + h]);
-    float L = 0.f;
-    for (int c = c0; c < nch; c++) {
-      const float* pc = base + (size_t)c * BD_PART + BD_NH * PF_HD;
-      const float w = expf(pc[h] - M);
-      wgt[c][h] = w;
-      L += pc[BD_NH + h] * w;
-    }
-    inv[h] = 1.0f / L;
+  const int nc = nch - c0;
+  const float* base = part + ((size_t)b * maxc + c0) * BD_PART;
+  for (int i = threadIdx.x; i < nc * BD_NH; i += PF_THREADS) {  // all pairs in one round of loads
+    const float* pc = base + (size_t)(i / BD_NH) * BD_PART + BD_NH * PF_HD + i % BD_NH;
+    wm[i / BD_NH][i % BD_NH] = pc[0];
+    wl[i / BD_NH][i % BD_NH] = pc[BD_NH];
   }
   __syncthreads();
   if (threadIdx.x >= BD_NH * (PF_HD / 8)) return;
   const int h = threadIdx.x / (PF_HD / 8), c8 = threadIdx.x % (PF_HD / 8);
-  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int c = c0; c < nch; c++) {
-    const float* src = base + (size_t)c * BD_PART + h * PF_HD + 8 * c8;
-    const float w = wgt[c][h];
+  float M = -1e30f;
+  for (int i = 0; i < nc; i++) M = fmaxf(M, wm[i][h]);
+  float L = 0.f, v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  constexpr int MB = 8;  // key ranges whose outputs are loaded together
+  for (int i0 = 0; i0 < nc; i0 += MB) {
+    float4 va[MB], vb[MB];
 #pragma unroll
-    for (int jj = 0; jj < 8; jj++) v[jj] = fmaf(src[jj], w, v[jj]);
+    for (int k = 0; k < MB; k++) {
+      if (i0 + k < nc) {
+        const float4* src = reinterpret_cast<const float4*>(base + (size_t)(i0 + k) * BD_PART + h * PF_HD + 8 * c8);
+        va[k] = src[0];
+        vb[k] = src[1];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < MB; k++) {
+      if (i0 + k >= nc) break;
+      const float w = expf(wm[i0 + k][h] - M);
+      L = fmaf(wl[i0 + k][h], w, L);
+      v[0] = fmaf(va[k].x, w, v[0]); v[1] = fmaf(va[k].y, w, v[1]);
+      v[2] = fmaf(va[k].z, w, v[2]); v[3] = fmaf(va[k].w, w, v[3]);
+      v[4] = fmaf(vb[k].x, w, v[4]); v[5] = fmaf(vb[k].y, w, v[5]);
+      v[6] = fmaf(vb[k].z, w, v[6]); v[7] = fmaf(vb[k].w, w, v[7]);
+    }
   }
+  const float inv = 1.0f / L;
 #pragma unroll
-  for (int jj = 0; jj < 8; jj++) v[jj] *= inv[h];
+  for (int jj = 0; jj < 8; jj++) v[jj] *= inv;
   xtile_put8(thi, tlo, BD_NH * PF_HD / 64, b, h * PF_HD + 8 * c8, v);
 }
 
