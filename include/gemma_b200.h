@@ -191,6 +191,31 @@ const char* gg_last_error(const gg_engine* eng);
 int gg_sample_logits_noalloc(const float* logits, int vocab, const uint32_t* seen_bits, const gg_sample* sp,
                              double uniform, int32_t* out_token, void* stream);
 
+/* ---- Tokenizer (host only; no GPU involved). Replaces src/tokenizer.ts: the greedy
+ * longest-match encoder the reference runs in JavaScript, with its UTF-16 code-unit semantics
+ * (lengths, prefix search and the skip over unknown input count UTF-16 units). Strings cross
+ * the boundary as UTF-8. */
+typedef struct gg_tokenizer gg_tokenizer;
+
+/* extractFromGGUF + buildTokenIndex + initFunctionTokens (tokenizer.ts:26-68): the vocabulary
+ * as n UTF-8 strings (tokens[i], lens[i] bytes; the GGUF tokenizer.ggml.tokens array). The
+ * caller keeps ownership of the strings. */
+int gg_tokenizer_create(const char* const* tokens, const size_t* lens, int n, gg_tokenizer** out);
+
+/* encode (tokenizer.ts:106-126): <bos> first, then the text split on the special-token names,
+ * each piece greedily matched. *n_out receives the number of ids; at most cap are written. */
+int gg_tokenizer_encode(const gg_tokenizer* tk, const char* text, size_t len, int32_t* ids, int cap, int* n_out);
+
+/* decodeTokens (tokenizer.ts:128-141) as UTF-8: '\u2581' becomes a space, unknown ids
+ * "<unk:ID>". *len_out receives the byte length; at most cap bytes are written (no NUL). */
+int gg_tokenizer_decode(const gg_tokenizer* tk, const int32_t* ids, int n, char* text, size_t cap, size_t* len_out);
+
+/* Id of a token text (tokenByText lookup, first id wins), or -1 (e.g. "<end_function_call>"
+ * for the stop check of engine.ts:1014-1019). */
+int gg_tokenizer_token_id(const gg_tokenizer* tk, const char* name, int32_t* id);
+
+void gg_tokenizer_destroy(gg_tokenizer* tk);
+
 /* Library build identifier (sm_100a kernels, compiled-in limits). */
 const char* gg_version(void);
 

@@ -52,6 +52,11 @@ SIGNATURES = {
     "gg_destroy": (_I, [_P]),
     "gg_last_error": (ctypes.c_char_p, [_P]),
     "gg_version": (ctypes.c_char_p, []),
+    "gg_tokenizer_create": (_I, [_P, _P, _I, ctypes.POINTER(_P)]),
+    "gg_tokenizer_encode": (_I, [_P, ctypes.c_char_p, ctypes.c_size_t, _P, _I, ctypes.POINTER(ctypes.c_int)]),
+    "gg_tokenizer_decode": (_I, [_P, _P, _I, _P, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    "gg_tokenizer_token_id": (_I, [_P, ctypes.c_char_p, _I32P]),
+    "gg_tokenizer_destroy": (None, [_P]),
 }
 
 

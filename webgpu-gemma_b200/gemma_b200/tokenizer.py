@@ -1,37 +1,34 @@
-"""Greedy longest-match tokenizer, restated from the reference (src/tokenizer.ts:1-142).
-
-Same special ids (1 <eos>, 2 <bos>, 105 <start_of_turn>, 106 <end_of_turn>), the same
-function-call tokens when the vocabulary has them, the same '▁' space marker and the same
-longest-prefix-first search; unknown characters are skipped (tokenizer.ts:96-97).
+"""The reference's tokenizer (src/tokenizer.ts) through the C-ABI: libgemma_b200.so's
+gg_tokenizer_* functions (csrc/gg_tokenizer.cpp), the greedy longest-match encoder with the
+reference's UTF-16 code-unit semantics. Host only: it needs the library, not a GPU.
 """
 from __future__ import annotations
 
-import re
+import ctypes
+
+import numpy as np
 
 from . import gguf
 
-SPECIAL_TOKENS = {"<start_of_turn>": 105, "<end_of_turn>": 106, "<eos>": 1, "<bos>": 2}
 FUNC_TOKEN_NAMES = ["<start_function_declaration>", "<end_function_declaration>", "<start_function_call>",
                     "<end_function_call>", "<start_function_response>", "<end_function_response>", "<escape>"]
 
 
 class Tokenizer:
     def __init__(self, vocab: list[str]):
+        from . import native
+        self._lib = native.load()
         self.vocab = vocab
-        self.token_by_text: dict[str, int] = {}
-        self.max_token_len = 0
-        for i, t in enumerate(vocab):  # buildTokenIndex (tokenizer.ts:43-57): first id wins
-            if t:
-                self.token_by_text.setdefault(t, i)
-                self.max_token_len = max(self.max_token_len, len(t))
-        self.special_tokens = dict(SPECIAL_TOKENS)
-        self.func_tokens: dict[str, int] = {}
-        for name in FUNC_TOKEN_NAMES:  # initFunctionTokens (tokenizer.ts:59-68)
-            if name in self.token_by_text:
-                self.func_tokens[name] = self.token_by_text[name]
-                self.special_tokens[name] = self.token_by_text[name]
-        names = sorted(self.special_tokens, key=len, reverse=True)
-        self._special_re = re.compile("|".join(re.escape(n) for n in names))
+        raw = [t.encode("utf-8", "surrogatepass") for t in vocab]
+        arr = (ctypes.c_char_p * len(raw))(*raw)
+        lens = (ctypes.c_size_t * len(raw))(*[len(b) for b in raw])
+        h = ctypes.c_void_p()
+        rc = self._lib.gg_tokenizer_create(arr, lens, len(raw), ctypes.byref(h))
+        if rc != 0:
+            raise native.GemmaB200Error(f"gg_tokenizer_create failed ({rc})")
+        self._h = h
+        # funcTokens (tokenizer.ts:59-68): the function-call tokens the vocabulary has
+        self.func_tokens = {n: i for n in FUNC_TOKEN_NAMES if (i := self.token_id(n)) >= 0}
 
     @classmethod
     def from_gguf(cls, parsed: "gguf.GGUFParsed") -> "Tokenizer":
@@ -41,44 +38,37 @@ class Tokenizer:
             raise ValueError("No tokenizer found in GGUF metadata")
         return cls([v.value for v in kv.value])
 
-    def _encode_segment(self, text: str, add_prefix: bool = True) -> list[int]:
-        out: list[int] = []
-        rem = text.replace(" ", "▁")
-        if add_prefix:
-            rem = "▁" + rem
-        while rem:
-            best_len, best_id = 0, -1
-            for ln in range(min(len(rem), self.max_token_len), 0, -1):
-                tid = self.token_by_text.get(rem[:ln])
-                if tid is not None:
-                    best_len, best_id = ln, tid
-                    break
-            if best_len == 0:
-                rem = rem[1:]
-            else:
-                out.append(best_id)
-                rem = rem[best_len:]
-        return out
+    def token_id(self, text: str) -> int:
+        out = ctypes.c_int32()
+        self._lib.gg_tokenizer_token_id(self._h, text.encode("utf-8"), ctypes.byref(out))
+        return out.value
 
     def encode(self, text: str) -> list[int]:
-        """encode (tokenizer.ts:106-126): BOS, then segments split on special tokens."""
-        toks = [2]
-        last, after_special = 0, False
-        for mt in self._special_re.finditer(text):
-            before = text[last:mt.start()]
-            if before:
-                toks += self._encode_segment(before, not after_special)
-            toks.append(self.special_tokens[mt.group(0)])
-            last, after_special = mt.end(), True
-        rem = text[last:]
-        if rem:
-            toks += self._encode_segment(rem, not after_special)
-        return toks
-
-    def decode_token(self, tid: int) -> str:
-        if 0 <= tid < len(self.vocab) and self.vocab[tid]:
-            return self.vocab[tid].replace("▁", " ")
-        return f"<unk:{tid}>"
+        b = text.encode("utf-8", "surrogatepass")
+        n = ctypes.c_int()
+        cap = len(b) + 2  # at most one id per UTF-16 unit, plus <bos> and the leading '▁'
+        ids = np.empty(cap, np.int32)
+        rc = self._lib.gg_tokenizer_encode(self._h, b, len(b), ids.ctypes.data_as(ctypes.c_void_p), cap,
+                                           ctypes.byref(n))
+        if rc != 0 or n.value > cap:
+            raise RuntimeError(f"gg_tokenizer_encode failed ({rc})")
+        return ids[:n.value].tolist()
 
     def decode_tokens(self, ids) -> str:
-        return "".join(self.decode_token(int(t)) for t in ids)
+        a = np.ascontiguousarray(np.asarray(list(ids), dtype=np.int32))
+        ln = ctypes.c_size_t()
+        self._lib.gg_tokenizer_decode(self._h, a.ctypes.data_as(ctypes.c_void_p), a.size, None, 0, ctypes.byref(ln))
+        buf = ctypes.create_string_buffer(ln.value)
+        self._lib.gg_tokenizer_decode(self._h, a.ctypes.data_as(ctypes.c_void_p), a.size, buf, ln.value,
+                                      ctypes.byref(ln))
+        return buf.raw[:ln.value].decode("utf-8")
+
+    def decode_token(self, tid: int) -> str:
+        return self.decode_tokens([tid])
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self._lib.gg_tokenizer_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    __del__ = close
