@@ -201,203 +201,260 @@ __global__ void __launch_bounds__(PF_THREADS)
 
 // Causal attention, split over key ranges. A work item is (a block of 32 query rows, a range
 // of 128 keys): the rows are QT = 32/G consecutive tokens times the G query heads that share
-// one KV head, so each K/V row loaded into shared memory serves all of them. Scores are
-// register-tiled (thread: 2 rows x 4 keys), then P.V (thread: 4 rows x 8 dims). An item
-// leaves unnormalised partial results (running max m, sum l, output o) that pf_attn_merge
-// combines with the usual online-softmax rescaling.
+// one KV head, so each K/V row serves all of them. An item leaves unnormalised partial results
+// (running max m, sum l, output o) that pf_attn_merge combines with the usual online-softmax
+// rescaling.
 constexpr int PA_ROWS = 32;
-constexpr int PA_KB = 64;                      // keys per shared-memory block
 constexpr int PA_KC = 128;                     // keys per work item
-constexpr int PA_KSTR = PF_HD + 4;             // K row stride (floats): float4-aligned, conflict-free
 constexpr int PA_PART = PA_ROWS * PF_HD + 2 * PA_ROWS;  // floats per item: o, then m, then l
-constexpr int PA_SMEM = (PA_ROWS * PF_HD + PA_KB * PA_KSTR + PA_KB * PF_HD + PA_KB * PA_ROWS + PA_ROWS) * 4;
 
-// Rows of a 64-key block of K and V (PF_HD cache elements each) into f32 shared memory (row r
-// at ks + r * kstride, vs + r * PF_HD): 16-byte async copies from an f32 cache; from a bf16
-// cache, every 16-byte load of the block is issued before the first one is widened and stored.
-template <bool KV16>
-GG_DEV void kv_block_to_smem(float* ks, int kstride, float* vs, const kv_t<KV16>* kg, const kv_t<KV16>* vg,
-                             long long sstride, int nrows) {
-  if constexpr (KV16) {
-    constexpr int PER = PF_HD / 8;                  // 16-byte chunks per row
-    constexpr int IT = PA_KB * PER / PF_THREADS;    // chunks per thread per matrix
-    uint4 wk[IT], wv[IT];
+// The work item runs on the tensor cores: mma.sync m16n8k16 with bf16 operands and f32
+// accumulation. Every f32 operand is split into bf16 hi + lo (hi + lo = x to ~2^-16) and each
+// product is the sum of three MMAs (hi*hi + hi*lo + lo*hi), which keeps the scores and outputs
+// within ~1e-5 of f32.
+//   warp w: query rows 16*(w>>1).. (one m16 tile), output dims 128*(w&1).. ; both warps of a row
+//   tile compute the tile's scores (16 rows x 32 keys per block), so the probabilities never
+//   leave registers: the score accumulators are re-packed as the A operand of P.V.
+// K and V blocks of 32 keys are converted to swizzled bf16 hi/lo tiles in shared memory (16-byte
+// chunk c of row r stored at chunk c ^ (r & 7), so ldmatrix reads 8 rows without bank conflicts).
+constexpr int TA_KB = 32;                          // keys per shared-memory block
+constexpr int TA_THREADS = 128;
+constexpr int TA_TILE = PF_HD * 2;                 // bytes of one bf16 row of 256 dims
+constexpr int TA_SMEM = (PA_ROWS * 2 + TA_KB * 4) * TA_TILE;  // Q hi/lo, K hi/lo, V hi/lo
+
+GG_DEV uint32_t ta_off(int r, int col) {  // byte offset of bf16 element (r, col) in a swizzled tile
+  return (uint32_t)(r * TA_TILE + ((((col >> 3) ^ (r & 7)) & 31) << 4) + (col & 7) * 2);
+}
+GG_DEV void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+GG_DEV void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+GG_DEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Eight f32 -> one 16-byte chunk of bf16 hi and one of bf16 lo (lo = x - hi, rounded).
+GG_DEV void split8(const float* f, uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
 #pragma unroll
-    for (int k = 0; k < IT; k++) {
-      const int idx = threadIdx.x + k * PF_THREADS, r = idx / PER, c8 = idx % PER;
-      if (r < nrows) {
-        wk[k] = __ldg(reinterpret_cast<const uint4*>(kg + r * sstride + 8 * c8));
-        wv[k] = __ldg(reinterpret_cast<const uint4*>(vg + r * sstride + 8 * c8));
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < IT; k++) {
-      const int idx = threadIdx.x + k * PF_THREADS, r = idx / PER, c8 = idx % PER;
-      if (r < nrows) {
-        float f[8];
-        bf16x8_widen(wk[k], f);
-        float4* d = reinterpret_cast<float4*>(ks + r * kstride + 8 * c8);
-        d[0] = make_float4(f[0], f[1], f[2], f[3]);
-        d[1] = make_float4(f[4], f[5], f[6], f[7]);
-        bf16x8_widen(wv[k], f);
-        d = reinterpret_cast<float4*>(vs + r * PF_HD + 8 * c8);
-        d[0] = make_float4(f[0], f[1], f[2], f[3]);
-        d[1] = make_float4(f[4], f[5], f[6], f[7]);
-      }
-    }
-  } else {
-    constexpr int PER = PF_HD / 4;
-    for (int idx = threadIdx.x; idx < nrows * PER; idx += PF_THREADS) {
-      const int r = idx / PER, c4 = idx % PER;
-      cp_async16(ks + r * kstride + 4 * c4, kg + r * sstride + 4 * c4);
-      cp_async16(vs + r * PF_HD + 4 * c4, vg + r * sstride + 4 * c4);
-    }
+  for (int i = 0; i < 4; i++) {
+    const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * i]), h1 = __float2bfloat16_rn(f[2 * i + 1]);
+    const __nv_bfloat16 l0 = __float2bfloat16_rn(f[2 * i] - __bfloat162float(h0));
+    const __nv_bfloat16 l1 = __float2bfloat16_rn(f[2 * i + 1] - __bfloat162float(h1));
+    h[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+    l[i] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
   }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+GG_DEV uint32_t pack2(float a, float b) {  // a in the low half (lower column)
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
+         ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
 }
 
 template <bool KV16>
-__global__ void __launch_bounds__(PF_THREADS)
-    pf_attn_part_kernel(const float* __restrict__ q, const kv_t<KV16>* __restrict__ kc,
-                        const kv_t<KV16>* __restrict__ vc, int T,
-                        int p0, int NQH, int NKH, float scale, int window, int maxc, float* __restrict__ part) {
+__global__ void __launch_bounds__(TA_THREADS, 1)
+    pf_attn_tc_kernel(const float* __restrict__ q, const kv_t<KV16>* __restrict__ kc, const kv_t<KV16>* __restrict__ vc,
+                      int T, int p0, int NQH, int NKH, float scale, int window, int maxc, float* __restrict__ part) {
   pdl_trigger();
   pdl_wait();  // before touching any buffer shared with the other kernels of the chain
-  extern __shared__ __align__(16) float sm[];
-  float* qs = sm;                         // [ROWS][HD]
-  float* ks = qs + PA_ROWS * PF_HD;       // [KB][KSTR]
-  float* vs = ks + PA_KB * PA_KSTR;       // [KB][HD]
-  float* ps = vs + PA_KB * PF_HD;         // [KB][ROWS]  probabilities, key-major
-  float* al = ps + PA_KB * PA_ROWS;       // [ROWS] rescale factors of this block
+  extern __shared__ __align__(128) uint8_t ta_smem[];
+  uint8_t* qh = ta_smem;
+  uint8_t* ql = qh + PA_ROWS * TA_TILE;
+  uint8_t* kh = ql + PA_ROWS * TA_TILE;
+  uint8_t* kl = kh + TA_KB * TA_TILE;
+  uint8_t* vh = kl + TA_KB * TA_TILE;
+  uint8_t* vl = vh + TA_KB * TA_TILE;
   const int G = NQH / NKH, QT = PA_ROWS / G;
   const int c = blockIdx.x, b = blockIdx.y, kvh = blockIdx.z;
   const int t0 = b * QT, nq = min(QT, T - t0);
-  const int kmax = p0 + t0 + nq - 1;  // last key any row of this block needs
+  const int kmax = p0 + t0 + nq - 1;
   const int k_begin = c * PA_KC;
   if (k_begin > kmax) return;
   const int k_end = min(k_begin + PA_KC, kmax + 1);
-  // sliding window: key range of the block's first row; ranges wholly below it are not needed
   const int klo0 = window > 0 ? max(0, p0 + t0 + 1 - window) : 0;
   if (k_end <= klo0) return;
   const int QD = NQH * PF_HD, KVD = NKH * PF_HD;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  // rows r = token * G + g  ->  query head kvh * G + g of token t0 + token
-  for (int idx = tid; idx < PA_ROWS * (PF_HD / 4); idx += PF_THREADS) {
-    const int r = idx / (PF_HD / 4), d4 = idx % (PF_HD / 4);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // query rows r = token * G + g -> head kvh * G + g of token t0 + token, as bf16 hi/lo
+  for (int i = tid; i < PA_ROWS * (PF_HD / 8); i += TA_THREADS) {
+    const int r = i / (PF_HD / 8), c8 = i % (PF_HD / 8);
     const int tok = r / G, hq = kvh * G + r % G;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (tok < nq) v = reinterpret_cast<const float4*>(q + (long long)(t0 + tok) * QD + hq * PF_HD)[d4];
-    reinterpret_cast<float4*>(qs + r * PF_HD)[d4] = v;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (tok < nq) {
+      const float4* src = reinterpret_cast<const float4*>(q + (long long)(t0 + tok) * QD + hq * PF_HD + 8 * c8);
+      const float4 a = src[0], bq = src[1];
+      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = bq.x; f[5] = bq.y; f[6] = bq.z; f[7] = bq.w;
+    }
+    uint4 hi, lo;
+    split8(f, hi, lo);
+    *reinterpret_cast<uint4*>(qh + ta_off(r, 8 * c8)) = hi;
+    *reinterpret_cast<uint4*>(ql + ta_off(r, 8 * c8)) = lo;
   }
-  // score tile of this thread: rows 2*qg, 2*qg+1; keys kg + 16*u
-  const int kg = tid & 15, qg = tid >> 4;
-  const int r0 = 2 * qg, r1 = r0 + 1;
-  const int pos0 = p0 + t0 + r0 / G, pos1 = p0 + t0 + r1 / G;
-  const int lo0 = window > 0 ? max(0, pos0 + 1 - window) : 0, lo1 = window > 0 ? max(0, pos1 + 1 - window) : 0;
-  float m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
-  // output tile of this thread: rows 4*warp..+3; dims 4*dg..+3 and 128+4*dg..+3
-  const int dg = tid & 31;
-  float o[4][8];
+  const int rt = warp >> 1, dh = warp & 1;  // row tile, dim half
+  const int g = lane >> 2, tq = lane & 3;   // mma fragment coordinates
+  const int ra = 16 * rt + g, rb = ra + 8;  // this thread's two rows
+  const int pos_a = p0 + t0 + ra / G, pos_b = p0 + t0 + rb / G;
+  const bool va = ra / G < nq, vb = rb / G < nq;
+  const int lo_a = window > 0 ? max(0, pos_a + 1 - window) : 0, lo_b = window > 0 ? max(0, pos_b + 1 - window) : 0;
+  float m_a = -1e30f, m_b = -1e30f, l_a = 0.f, l_b = 0.f;
+  float o[16][4];
 #pragma unroll
-  for (int i = 0; i < 4; i++)
-#pragma unroll
-    for (int j = 0; j < 8; j++) o[i][j] = 0.f;
+  for (int n = 0; n < 16; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
-  for (int j0 = k_begin; j0 < k_end; j0 += PA_KB) {
-    const int nk = min(PA_KB, k_end - j0);
-    __syncthreads();
-    kv_block_to_smem<KV16>(ks, PA_KSTR, vs, kc + (long long)j0 * KVD + kvh * PF_HD,
-                           vc + (long long)j0 * KVD + kvh * PF_HD, KVD, nk);
-    cp_async_wait_all();
-    __syncthreads();
-    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-    const float4* qa = reinterpret_cast<const float4*>(qs + r0 * PF_HD);
-    const float4* qb = reinterpret_cast<const float4*>(qs + r1 * PF_HD);
+  for (int j0 = k_begin; j0 < k_end; j0 += TA_KB) {
+    const int nk = min(TA_KB, k_end - j0);
+    __syncthreads();  // the previous block's tiles are no longer read (and Q is written)
+    // K and V rows j0.. as bf16 hi/lo tiles; rows past nk are zero
 #pragma unroll 4
-    for (int d4 = 0; d4 < PF_HD / 4; d4++) {
-      const float4 x0 = qa[d4], x1 = qb[d4];
+    for (int i = tid; i < TA_KB * (PF_HD / 8); i += TA_THREADS) {
+      const int r = i / (PF_HD / 8), c8 = i % (PF_HD / 8);
+      float fk[8], fv[8];
+      if (r < nk) {
+        const long long e = (long long)(j0 + r) * KVD + kvh * PF_HD + 8 * c8;
+        if constexpr (KV16) {
+          bf16x8_widen(__ldg(reinterpret_cast<const uint4*>(kc + e)), fk);
+          bf16x8_widen(__ldg(reinterpret_cast<const uint4*>(vc + e)), fv);
+        } else {
+          const float4* ks4 = reinterpret_cast<const float4*>(kc + e);
+          const float4* vs4 = reinterpret_cast<const float4*>(vc + e);
+          const float4 k0 = ks4[0], k1 = ks4[1], v0 = vs4[0], v1 = vs4[1];
+          fk[0] = k0.x; fk[1] = k0.y; fk[2] = k0.z; fk[3] = k0.w; fk[4] = k1.x; fk[5] = k1.y; fk[6] = k1.z; fk[7] = k1.w;
+          fv[0] = v0.x; fv[1] = v0.y; fv[2] = v0.z; fv[3] = v0.w; fv[4] = v1.x; fv[5] = v1.y; fv[6] = v1.z; fv[7] = v1.w;
+        }
+      } else {
 #pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const float4 kv = reinterpret_cast<const float4*>(ks + (kg + 16 * u) * PA_KSTR)[d4];
-        sa[u] = fmaf(x0.x, kv.x, sa[u]); sa[u] = fmaf(x0.y, kv.y, sa[u]);
-        sa[u] = fmaf(x0.z, kv.z, sa[u]); sa[u] = fmaf(x0.w, kv.w, sa[u]);
-        sb[u] = fmaf(x1.x, kv.x, sb[u]); sb[u] = fmaf(x1.y, kv.y, sb[u]);
-        sb[u] = fmaf(x1.z, kv.z, sb[u]); sb[u] = fmaf(x1.w, kv.w, sb[u]);
+        for (int u = 0; u < 8; u++) fk[u] = fv[u] = 0.f;
       }
-    }
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const int key = j0 + kg + 16 * u;
-      const bool in = kg + 16 * u < nk;
-      sa[u] = (in && key <= pos0 && key >= lo0) ? sa[u] * scale : -INFINITY;
-      sb[u] = (in && key <= pos1 && key >= lo1) ? sb[u] * scale : -INFINITY;
-      mx0 = fmaxf(mx0, sa[u]);
-      mx1 = fmaxf(mx1, sb[u]);
-    }
-#pragma unroll
-    for (int off = 1; off < 16; off <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-    }
-    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-    float e0s = 0.f, e1s = 0.f;
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      const float e0 = sa[u] == -INFINITY ? 0.f : expf(sa[u] - n0);
-      const float e1 = sb[u] == -INFINITY ? 0.f : expf(sb[u] - n1);
-      ps[(kg + 16 * u) * PA_ROWS + r0] = e0;
-      ps[(kg + 16 * u) * PA_ROWS + r1] = e1;
-      e0s += e0;
-      e1s += e1;
-    }
-#pragma unroll
-    for (int off = 1; off < 16; off <<= 1) {
-      e0s += __shfl_xor_sync(0xffffffffu, e0s, off);
-      e1s += __shfl_xor_sync(0xffffffffu, e1s, off);
-    }
-    const float a0 = expf(m0 - n0), a1 = expf(m1 - n1);
-    l0 = l0 * a0 + e0s;
-    l1 = l1 * a1 + e1s;
-    m0 = n0;
-    m1 = n1;
-    if (kg == 0) {
-      al[r0] = a0;
-      al[r1] = a1;
+      uint4 hi, lo;
+      split8(fk, hi, lo);
+      *reinterpret_cast<uint4*>(kh + ta_off(r, 8 * c8)) = hi;
+      *reinterpret_cast<uint4*>(kl + ta_off(r, 8 * c8)) = lo;
+      split8(fv, hi, lo);
+      *reinterpret_cast<uint4*>(vh + ta_off(r, 8 * c8)) = hi;
+      *reinterpret_cast<uint4*>(vl + ta_off(r, 8 * c8)) = lo;
     }
     __syncthreads();
-    float av[4];
+    // S = Q K^T for this warp's 16 rows x 32 keys (4 n-tiles of 8 keys)
+    float sacc[4][4];
 #pragma unroll
-    for (int i = 0; i < 4; i++) av[i] = al[4 * warp + i];
+    for (int n = 0; n < 4; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+    const int arow = 16 * rt + (lane & 15), acol = 8 * (lane >> 4);              // A (Q) ldmatrix lanes
+    const int brow = (lane & 7) + 8 * (lane >> 4), bcol = 8 * ((lane >> 3) & 1);  // B (K) ldmatrix lanes
+#pragma unroll 4
+    for (int ks = 0; ks < PF_HD / 16; ks++) {
+      uint32_t ah[4], al[4], bh[2][4], bl[2][4];
+      ldsm_x4(smem_u32(qh + ta_off(arow, 16 * ks + acol)), ah);
+      ldsm_x4(smem_u32(ql + ta_off(arow, 16 * ks + acol)), al);
 #pragma unroll
-    for (int i = 0; i < 4; i++)
+      for (int np = 0; np < 2; np++) {
+        ldsm_x4(smem_u32(kh + ta_off(16 * np + brow, 16 * ks + bcol)), bh[np]);
+        ldsm_x4(smem_u32(kl + ta_off(16 * np + brow, 16 * ks + bcol)), bl[np]);
+      }
+      // the three products rotate over the four accumulators, so consecutive MMAs are independent
 #pragma unroll
-      for (int j = 0; j < 8; j++) o[i][j] *= av[i];
-    for (int j = 0; j < nk; j++) {
-      const float4 pr = reinterpret_cast<const float4*>(ps + j * PA_ROWS)[warp];
-      const float4 va = reinterpret_cast<const float4*>(vs + j * PF_HD)[dg];
-      const float4 vb = reinterpret_cast<const float4*>(vs + j * PF_HD + 128)[dg];
-      const float pv[4] = {pr.x, pr.y, pr.z, pr.w};
+      for (int n = 0; n < 4; n++) mma_bf16(sacc[n], ah, bh[n >> 1][2 * (n & 1)], bh[n >> 1][2 * (n & 1) + 1]);
+#pragma unroll
+      for (int n = 0; n < 4; n++) mma_bf16(sacc[n], ah, bl[n >> 1][2 * (n & 1)], bl[n >> 1][2 * (n & 1) + 1]);
+#pragma unroll
+      for (int n = 0; n < 4; n++) mma_bf16(sacc[n], al, bh[n >> 1][2 * (n & 1)], bh[n >> 1][2 * (n & 1) + 1]);
+    }
+    // causal / window / range mask, scale, and the online softmax of rows ra (d0, d1) and rb (d2, d3)
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 4; n++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int key = j0 + 8 * n + 2 * tq + e;
+        const bool in = key < j0 + nk;
+        sacc[n][e] = (in && va && key <= pos_a && key >= lo_a) ? sacc[n][e] * scale : -INFINITY;
+        sacc[n][2 + e] = (in && vb && key <= pos_b && key >= lo_b) ? sacc[n][2 + e] * scale : -INFINITY;
+        mx_a = fmaxf(mx_a, sacc[n][e]);
+        mx_b = fmaxf(mx_b, sacc[n][2 + e]);
+      }
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+    const float nm_a = fmaxf(m_a, mx_a), nm_b = fmaxf(m_b, mx_b);
+    const float al_a = expf(m_a - nm_a), al_b = expf(m_b - nm_b);
+    m_a = nm_a;
+    m_b = nm_b;
+    float ps_a = 0.f, ps_b = 0.f;
+#pragma unroll
+    for (int n = 0; n < 4; n++)
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        sacc[n][e] = sacc[n][e] == -INFINITY ? 0.f : expf(sacc[n][e] - nm_a);
+        sacc[n][2 + e] = sacc[n][2 + e] == -INFINITY ? 0.f : expf(sacc[n][2 + e] - nm_b);
+        ps_a += sacc[n][e];
+        ps_b += sacc[n][2 + e];
+      }
+    l_a = l_a * al_a + ps_a;  // this thread's columns; the quad is summed at the end
+    l_b = l_b * al_b + ps_b;
+#pragma unroll
+    for (int n = 0; n < 16; n++) {
+      o[n][0] *= al_a;
+      o[n][1] *= al_a;
+      o[n][2] *= al_b;
+      o[n][3] *= al_b;
+    }
+    // O += P V: P (16 rows x 32 keys) from the score registers as bf16 hi/lo A fragments
+    const int vrow = (lane & 7) + 8 * ((lane >> 3) & 1), vcol = 8 * (lane >> 4);  // V ldmatrix.trans lanes
+#pragma unroll
+    for (int kk = 0; kk < 2; kk++) {
+      float pf[8] = {sacc[2 * kk][0], sacc[2 * kk][1], sacc[2 * kk][2], sacc[2 * kk][3],
+                     sacc[2 * kk + 1][0], sacc[2 * kk + 1][1], sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]};
+      uint32_t ph[4], pl[4];
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        o[i][0] = fmaf(pv[i], va.x, o[i][0]); o[i][1] = fmaf(pv[i], va.y, o[i][1]);
-        o[i][2] = fmaf(pv[i], va.z, o[i][2]); o[i][3] = fmaf(pv[i], va.w, o[i][3]);
-        o[i][4] = fmaf(pv[i], vb.x, o[i][4]); o[i][5] = fmaf(pv[i], vb.y, o[i][5]);
-        o[i][6] = fmaf(pv[i], vb.z, o[i][6]); o[i][7] = fmaf(pv[i], vb.w, o[i][7]);
+        // A fragment order: (row g, keys 2t..), (row g+8, keys 2t..), (row g, keys 2t+8..), (row g+8, keys 2t+8..)
+        const float x0 = pf[(i & 1) * 2 + (i >> 1) * 4], x1 = pf[(i & 1) * 2 + (i >> 1) * 4 + 1];
+        ph[i] = pack2(x0, x1);
+        const float h0 = __uint_as_float((ph[i] & 0xffffu) << 16), h1 = __uint_as_float(ph[i] & 0xffff0000u);
+        pl[i] = pack2(x0 - h0, x1 - h1);
+      }
+#pragma unroll
+      for (int np = 0; np < 8; np += 2) {  // dims 128*dh + 16*np .. (two pairs of n-tiles at a time)
+        uint32_t bh[2][4], bl[2][4];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+          const int dcol = 128 * dh + 16 * (np + u) + vcol;
+          ldsm_x4_t(smem_u32(vh + ta_off(16 * kk + vrow, dcol)), bh[u]);
+          ldsm_x4_t(smem_u32(vl + ta_off(16 * kk + vrow, dcol)), bl[u]);
+        }
+#pragma unroll
+        for (int n = 0; n < 4; n++) mma_bf16(o[2 * np + n], ph, bh[n >> 1][2 * (n & 1)], bh[n >> 1][2 * (n & 1) + 1]);
+#pragma unroll
+        for (int n = 0; n < 4; n++) mma_bf16(o[2 * np + n], ph, bl[n >> 1][2 * (n & 1)], bl[n >> 1][2 * (n & 1) + 1]);
+#pragma unroll
+        for (int n = 0; n < 4; n++) mma_bf16(o[2 * np + n], pl, bh[n >> 1][2 * (n & 1)], bh[n >> 1][2 * (n & 1) + 1]);
       }
     }
   }
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
   float* dst = part + ((size_t)(kvh * gridDim.y + b) * maxc + c) * PA_PART;
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    float* row = dst + (4 * warp + i) * PF_HD;
-    reinterpret_cast<float4*>(row)[dg] = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
-    reinterpret_cast<float4*>(row + 128)[dg] = make_float4(o[i][4], o[i][5], o[i][6], o[i][7]);
+  for (int n = 0; n < 16; n++) {
+    const int d = 128 * dh + 8 * n + 2 * tq;
+    *reinterpret_cast<float2*>(dst + ra * PF_HD + d) = make_float2(o[n][0], o[n][1]);
+    *reinterpret_cast<float2*>(dst + rb * PF_HD + d) = make_float2(o[n][2], o[n][3]);
   }
-  if (kg == 0) {
-    dst[PA_ROWS * PF_HD + r0] = m0;
-    dst[PA_ROWS * PF_HD + r1] = m1;
-    dst[PA_ROWS * PF_HD + PA_ROWS + r0] = l0;
-    dst[PA_ROWS * PF_HD + PA_ROWS + r1] = l1;
+  if (dh == 0 && tq == 0) {
+    dst[PA_ROWS * PF_HD + ra] = m_a;
+    dst[PA_ROWS * PF_HD + rb] = m_b;
+    dst[PA_ROWS * PF_HD + PA_ROWS + ra] = l_a;
+    dst[PA_ROWS * PF_HD + PA_ROWS + rb] = l_b;
   }
 }
 
@@ -754,9 +811,9 @@ cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv
   if (r != cudaSuccess) return r;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    r = cudaFuncSetAttribute(pf_attn_part_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
+    r = cudaFuncSetAttribute(pf_attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM);
     if (r == cudaSuccess)
-      r = cudaFuncSetAttribute(pf_attn_part_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PA_SMEM);
+      r = cudaFuncSetAttribute(pf_attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM);
     if (r != cudaSuccess) return r;
     attr_set[dev] = true;
   }
@@ -766,10 +823,10 @@ cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv
   if (maxc > 16) return cudaErrorInvalidValue;  // merge weights hold 16 key ranges (2048 positions)
   const dim3 grid(maxc, nb, NKH);
   if (kv16)
-    r = launch_pdl(pf_attn_part_kernel<true>, grid, dim3(PF_THREADS), PA_SMEM, s, q, (const __nv_bfloat16*)kc,
+    r = launch_pdl(pf_attn_tc_kernel<true>, grid, dim3(TA_THREADS), TA_SMEM, s, q, (const __nv_bfloat16*)kc,
                    (const __nv_bfloat16*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
   else
-    r = launch_pdl(pf_attn_part_kernel<false>, grid, dim3(PF_THREADS), PA_SMEM, s, q, (const float*)kc,
+    r = launch_pdl(pf_attn_tc_kernel<false>, grid, dim3(TA_THREADS), TA_SMEM, s, q, (const float*)kc,
                    (const float*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
   if (r != cudaSuccess) return r;
   return launch_pdl(pf_attn_merge_kernel, dim3(nb, NKH), dim3(PF_THREADS), 0, s, (const float*)part, T, p0, NQH, NKH,
