@@ -557,8 +557,9 @@ cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo,
   a.timeout_ns = timeout_ns;
   if (T > 64 && w.dense) {  // prompt chunks: dequantised weights, copies and MMAs only
     a.wt = w.dense;
-    // 256-row tiles halve the weight-tile reads, but only wide matrices have tiles to spare
-    const bool wide = T > 128 && (long long)((T + 255) / 256) * (w.M / 128) * splits >= 148;
+    // 256-row tiles halve the weight-tile reads, but only matrices wide enough to fill two waves
+    // of 256-row tiles have tiles to spare (one and a half waves lose more than the reads save)
+    const bool wide = T > 128 && (long long)((T + 255) / 256) * (w.M / 128) * splits >= 2 * 148;
     return wide ? launch_dense<256>(a, w.M / 128, splits, s) : launch_dense<128>(a, w.M / 128, splits, s);
   }
   return T <= 64 ? launch_nt<64>(w, a, splits, s) : launch_nt<128>(w, a, splits, s);

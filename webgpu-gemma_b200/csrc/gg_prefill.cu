@@ -464,45 +464,51 @@ __global__ void __launch_bounds__(PF_THREADS)
                          uint8_t* thi, uint8_t* tlo) {
   pdl_trigger();
   pdl_wait();  // before touching any buffer shared with the other kernels of the chain
-  __shared__ float wgt[16][PA_ROWS];
-  __shared__ float inv[PA_ROWS];
+  __shared__ float wm[16][PA_ROWS], wl[16][PA_ROWS];  // (max, sum) of every key range and row
   const int G = NQH / NKH, QT = PA_ROWS / G;
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int t0 = b * QT, nq = min(QT, T - t0);
   const int nch = min(maxc, (p0 + t0 + nq - 1) / PA_KC + 1);
   const int c0 = window > 0 ? max(0, p0 + t0 + 1 - window) / PA_KC : 0;  // as in the part kernel
-  const float* base = part + ((size_t)(kvh * gridDim.x + b) * maxc) * PA_PART;
-  if (threadIdx.x < PA_ROWS) {
-    const int r = threadIdx.x;
-    float M = -1e30f;
-    for (int c = c0; c < nch; c++) M = fmaxf(M, base[(size_t)c * PA_PART + PA_ROWS * PF_HD + r]);
-    float L = 0.f;
-    for (int c = c0; c < nch; c++) {
-      const float* pc = base + (size_t)c * PA_PART + PA_ROWS * PF_HD;
-      const float w = expf(pc[r] - M);
-      wgt[c][r] = w;
-      L += pc[PA_ROWS + r] * w;
-    }
-    inv[r] = 1.0f / L;
+  const int nc = nch - c0;
+  const float* base = part + ((size_t)(kvh * gridDim.x + b) * maxc + c0) * PA_PART;
+  for (int i = threadIdx.x; i < nc * PA_ROWS; i += PF_THREADS) {  // every pair in one round of loads
+    const float* pc = base + (size_t)(i / PA_ROWS) * PA_PART + PA_ROWS * PF_HD + i % PA_ROWS;
+    wm[i / PA_ROWS][i % PA_ROWS] = pc[0];
+    wl[i / PA_ROWS][i % PA_ROWS] = pc[PA_ROWS];
   }
   __syncthreads();
-  const int QD = NQH * PF_HD;
-  for (int idx = threadIdx.x; idx < PA_ROWS * (PF_HD / 8); idx += PF_THREADS) {
-    const int r = idx / (PF_HD / 8), c8 = idx % (PF_HD / 8);
-    const int tok = r / G, hq = kvh * G + r % G;
-    if (tok >= nq) continue;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int c = c0; c < nch; c++) {
-      const float* src = base + (size_t)c * PA_PART + r * PF_HD + 8 * c8;
-      const float4 a = reinterpret_cast<const float4*>(src)[0], bq = reinterpret_cast<const float4*>(src)[1];
-      const float w = wgt[c][r];
-      v[0] = fmaf(a.x, w, v[0]); v[1] = fmaf(a.y, w, v[1]); v[2] = fmaf(a.z, w, v[2]); v[3] = fmaf(a.w, w, v[3]);
-      v[4] = fmaf(bq.x, w, v[4]); v[5] = fmaf(bq.y, w, v[5]); v[6] = fmaf(bq.z, w, v[6]); v[7] = fmaf(bq.w, w, v[7]);
+  // thread: row r, 8 dims of this CTA's quarter of the head (blockIdx.z)
+  const int r = threadIdx.x / 8, c8 = 8 * blockIdx.z + threadIdx.x % 8;
+  const int tok = r / G, hq = kvh * G + r % G;
+  if (tok >= nq) return;
+  float M = -1e30f;
+  for (int i = 0; i < nc; i++) M = fmaxf(M, wm[i][r]);
+  float L = 0.f, v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  constexpr int MB = 4;  // key ranges whose outputs are loaded together
+  for (int i0 = 0; i0 < nc; i0 += MB) {
+    float4 va[MB], vb[MB];
+#pragma unroll
+    for (int k = 0; k < MB; k++) {
+      if (i0 + k < nc) {
+        const float4* src = reinterpret_cast<const float4*>(base + (size_t)(i0 + k) * PA_PART + r * PF_HD + 8 * c8);
+        va[k] = src[0];
+        vb[k] = src[1];
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 8; j++) v[j] *= inv[r];
-    xtile_put8(thi, tlo, QD / 64, t0 + tok, hq * PF_HD + 8 * c8, v);
+    for (int k = 0; k < MB; k++) {
+      if (i0 + k >= nc) break;
+      const float w = expf(wm[i0 + k][r] - M);
+      L = fmaf(wl[i0 + k][r], w, L);
+      v[0] = fmaf(va[k].x, w, v[0]); v[1] = fmaf(va[k].y, w, v[1]); v[2] = fmaf(va[k].z, w, v[2]); v[3] = fmaf(va[k].w, w, v[3]);
+      v[4] = fmaf(vb[k].x, w, v[4]); v[5] = fmaf(vb[k].y, w, v[5]); v[6] = fmaf(vb[k].z, w, v[6]); v[7] = fmaf(vb[k].w, w, v[7]);
+    }
   }
+  const float inv = 1.0f / L;
+#pragma unroll
+  for (int j = 0; j < 8; j++) v[j] *= inv;
+  xtile_put8(thi, tlo, NQH * PF_HD / 64, t0 + tok, hq * PF_HD + 8 * c8, v);
 }
 
 // Decode attention for a batch of sequences: row b has one query token (NQH = 4 heads sharing
@@ -829,8 +835,9 @@ cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv
     r = launch_pdl(pf_attn_tc_kernel<false>, grid, dim3(TA_THREADS), TA_SMEM, s, q, (const float*)kc,
                    (const float*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
   if (r != cudaSuccess) return r;
-  return launch_pdl(pf_attn_merge_kernel, dim3(nb, NKH), dim3(PF_THREADS), 0, s, (const float*)part, T, p0, NQH, NKH,
-                    window, maxc, thi, tlo);
+  static_assert(PA_ROWS * 8 == PF_THREADS, "merge: one thread per (row, 8 dims) of a quarter head");
+  return launch_pdl(pf_attn_merge_kernel, dim3(nb, NKH, PF_HD / 64), dim3(PF_THREADS), 0, s, (const float*)part, T, p0,
+                    NQH, NKH, window, maxc, thi, tlo);
 }
 
 size_t bd_attention_part_floats(int max_rows, int ctx) {
