@@ -944,34 +944,43 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st, Smem& S) {
   __shared__ uint32_t cid[256];
   if (tid < 256) cid[tid] = idx;
   __syncthreads();
+  if (T == 0.0f) {
+    if (tid == 0) result = (int)cid[sl[0]];
+    __syncthreads();
+    return result;
+  }
+  // engine.ts:881-901, JS numbers are doubles; probs is a Float32Array. The element-wise terms
+  // (exp, the division by the sum) are computed by one thread each; every running sum is taken
+  // by one thread in index order, as the reference does, so the result is the same bit for bit.
+  __shared__ float probs[256];
+  __shared__ double share[256];
+  __shared__ double sum_all;
+  const double temp = (double)T, top_p = (double)st->top_p;
+  if (tid < 256) probs[tid] = (float)exp((sv[tid] - sv[0]) / temp);
+  __syncthreads();
   if (tid == 0) {
-    int pick;
-    if (T == 0.0f) {
-      pick = 0;
-    } else {
-      // engine.ts:881-901, JS numbers are doubles; probs is a Float32Array
-      const double temp = (double)T, top_p = (double)st->top_p;
-      __shared__ float probs[256];
-      double mx = sv[0], sum = 0.0;
-      for (int i = 0; i < 256; i++) {
-        probs[i] = (float)exp((sv[i] - mx) / temp);
-        sum += (double)probs[i];
-      }
-      double cum = 0.0;
-      int cutoff = 256;
-      for (int i = 0; i < 256; i++) {
-        cum += (double)probs[i] / sum;
-        if (cum >= top_p) { cutoff = i + 1; break; }
-      }
-      double sub = 0.0;
-      for (int i = 0; i < cutoff; i++) sub += (double)probs[i];
-      double u = st->uniforms ? st->uniforms[0] : st->uniform;
-      double r = u * sub;
-      pick = cutoff - 1;
-      for (int i = 0; i < cutoff; i++) {
-        r -= (double)probs[i];
-        if (r <= 0) { pick = i; break; }
-      }
+    double sum = 0.0;
+    for (int i = 0; i < 256; i++) sum += (double)probs[i];
+    sum_all = sum;
+  }
+  __syncthreads();
+  if (tid < 256) share[tid] = (double)probs[tid] / sum_all;
+  __syncthreads();
+  if (tid == 0) {
+    double cum = 0.0;
+    int cutoff = 256;
+    for (int i = 0; i < 256; i++) {
+      cum += share[i];
+      if (cum >= top_p) { cutoff = i + 1; break; }
+    }
+    double sub = 0.0;
+    for (int i = 0; i < cutoff; i++) sub += (double)probs[i];
+    double u = st->uniforms ? st->uniforms[0] : st->uniform;
+    double r = u * sub;
+    int pick = cutoff - 1;
+    for (int i = 0; i < cutoff; i++) {
+      r -= (double)probs[i];
+      if (r <= 0) { pick = i; break; }
     }
     result = (int)cid[sl[pick]];
   }
