@@ -432,6 +432,27 @@ def run_profile_prefill():
     eng.close()
 
 
+def run_profile_batch(steps: int = 4, ctx: int = 2048):
+    """Launch sequence for an ncu launch list of the batched decode step: the 1B model, 64 KV
+    slots of `ctx` positions, 64 rows at position 384 (random tokens), 2 warm-up steps then
+    `steps` sampled steps (T 0.7, top-p 0.9, rep 1.2)."""
+    from gemma_b200 import synth
+    from gemma_b200.native import engine_from_tensors
+    shape = synth.SHAPES["1b"]
+    cfg = shape.config()
+    cfg.context_length = ctx
+    B = CFG4_SEQS
+    eng = engine_from_tensors(cfg, synth.make_tensors(shape, SEED), max_seqs=B)
+    toks = np.arange(B) + 100
+    pos = np.full(B, 384)
+    samples = [CFG4_SAMPLE] * B
+    u = np.random.default_rng(0).random((steps, B))
+    eng.decode_batch(np.arange(B), toks, pos, 2, samples, u[:2])
+    eng.decode_batch(np.arange(B), toks, pos, steps, samples, u)
+    print(json.dumps({"profile_batch": "ok", "ms_per_step": round(eng.last_device_ms() / steps, 4)}))
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -456,6 +477,10 @@ def main():
     ap.add_argument("--cfg2-shapes", default="", help="comma-separated subset of qkv,o,gate_up,down,lm_head")
     ap.add_argument("--cfg2-batches", default="1,8,64")
     ap.add_argument("--cfg2-reps", type=int, default=10)
+    ap.add_argument("--profile-batch", action="store_true",
+                    help="a few batched decode steps (64 rows at position 384), for an ncu launch list")
+    ap.add_argument("--profile-ctx", type=int, default=2048,
+                    help="with --profile-batch: context length of the KV slots (smaller = smaller capture)")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="two 512-token batched prefills of the 1B model, for an ncu launch list")
     args = ap.parse_args()
@@ -470,6 +495,8 @@ def main():
                         [int(x) for x in args.cfg2_batches.split(",")])
     if args.profile_prefill:
         return run_profile_prefill()
+    if args.profile_batch:
+        return run_profile_batch(ctx=args.profile_ctx)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
