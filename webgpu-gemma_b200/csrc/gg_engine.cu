@@ -597,7 +597,9 @@ static void set_sampling(GGState& s, const gg_sample* sp, double u) {
 static int pick_splits(int tiles, int KS, int slots);
 
 static int gemm_tiles(int T, int M) { return (T <= 64 ? 1 : (T + 127) / 128) * (M / 128); }
-static int gemm_slots(const gg_engine* e, int T) { return e->sm_count * (T <= 64 ? 2 : 1); }
+// CTA slots of the GEMM that gg_gemm_q8 picks for T rows: the Q8 kernel (T <= 8, or no dense
+// copy) fits two CTAs per SM, the dense kernel one.
+static int gemm_slots(const gg_engine* e, int T) { return e->sm_count * (T <= 8 || !e->gemm_ok ? 2 : 1); }
 
 // Batched prefill of ids already in e->d_ids: chunks of up to GG_PF_CHUNK tokens, each layer
 // as four tensor-core GEMMs over the chunk's rows and the kernels of gg_prefill.cu between them.

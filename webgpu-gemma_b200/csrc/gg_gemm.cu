@@ -289,7 +289,7 @@ template <int NT>
 struct DenseCfg {
   static constexpr int B_BYTES = NT * 128;
   static constexpr int STAGE = GD_A_STAGE + 2 * B_BYTES;
-  static constexpr int S = NT == 256 ? 2 : 3;
+  static constexpr int S = NT == 256 ? 2 : (NT == 64 ? 4 : 3);
   static constexpr int SMEM = 1024 + S * STAGE + 128;
   static constexpr int TMEM_COLS = NT == 256 ? 512 : 256;  // two accumulators of NT columns
 };
@@ -555,8 +555,9 @@ cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo,
   if ((long long)(splits - 1) * a.slabs_per_split >= a.KS) return cudaErrorInvalidValue;  // an empty split
   a.err = err;
   a.timeout_ns = timeout_ns;
-  if (T > 64 && w.dense) {  // prompt chunks: dequantised weights, copies and MMAs only
+  if (T > 8 && w.dense) {  // dequantised weights, copies and MMAs only (4 B per weight read)
     a.wt = w.dense;
+    if (T <= 64) return launch_dense<64>(a, w.M / 128, splits, s);
     // 256-row tiles halve the weight-tile reads, but only matrices wide enough to fill two waves
     // of 256-row tiles have tiles to spare (one and a half waves lose more than the reads save)
     const bool wide = T > 128 && (long long)((T + 255) / 256) * (w.M / 128) * splits >= 2 * 148;
