@@ -75,12 +75,15 @@ __global__ void __launch_bounds__(1024)
                       const float* rin, float* rout, const float* __restrict__ w_norm, uint8_t* thi, uint8_t* tlo,
                       int H, float eps) {
   pdl_trigger();
-  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   __shared__ float red[32];
   __shared__ float tot[2];
   const int t = blockIdx.x, k = threadIdx.x, nq = H >> 2;
   const bool ok = k < nq;
   const long long base = (long long)t * H + 4 * k;
+  // the norm weights are constant: fetched before waiting for the previous kernel
+  const float4 wp = (ok && part) ? __ldg(reinterpret_cast<const float4*>(w_post) + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 wn = (ok && w_norm) ? __ldg(reinterpret_cast<const float4*>(w_norm) + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   float r[4] = {0.f, 0.f, 0.f, 0.f};
   if (ok) {
     const float4 ri = *reinterpret_cast<const float4*>(rin + base);
@@ -101,23 +104,27 @@ __global__ void __launch_bounds__(1024)
   if (part) {
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     if (ok) {
-      float4 acc = *reinterpret_cast<const float4*>(part + base);
-      int z = 1;
-      for (; z + 1 < splits; z += 2) {
-        const float4 a = *reinterpret_cast<const float4*>(part + (long long)z * plane + base);
-        const float4 c = *reinterpret_cast<const float4*>(part + (long long)(z + 1) * plane + base);
-        acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
-        acc.x += c.x; acc.y += c.y; acc.z += c.z; acc.w += c.w;
-      }
-      for (; z < splits; z++) {
-        const float4 a = *reinterpret_cast<const float4*>(part + (long long)z * plane + base);
-        acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+      // split planes summed in plane order; up to eight loads in flight at a time
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int z0 = 0; z0 < splits; z0 += 8) {
+        float4 a[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          if (z0 + u < splits) a[u] = *reinterpret_cast<const float4*>(part + (long long)(z0 + u) * plane + base);
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          if (z0 + u >= splits) break;
+          if (z0 + u == 0) {
+            acc = a[0];
+          } else {
+            acc.x += a[u].x; acc.y += a[u].y; acc.z += a[u].z; acc.w += a[u].w;
+          }
+        }
       }
       v[0] = acc.x; v[1] = acc.y; v[2] = acc.z; v[3] = acc.w;
     }
     const float rms = sqrtf(bsum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3], 0) / (float)H + eps);
     if (ok) {
-      const float4 wp = *reinterpret_cast<const float4*>(w_post + 4 * k);
       const float wv[4] = {wp.x, wp.y, wp.z, wp.w};
 #pragma unroll
       for (int j = 0; j < 4; j++) r[j] = r[j] + v[j] * wv[j] / rms;
@@ -128,7 +135,6 @@ __global__ void __launch_bounds__(1024)
   if (!w_norm) return;
   const float rms2 = sqrtf(bsum(r[0] * r[0] + r[1] * r[1] + r[2] * r[2] + r[3] * r[3], 1) / (float)H + eps);
   // two quads per tile chunk of 8: the even thread gathers its neighbour's quad
-  const float4 wn = ok ? *reinterpret_cast<const float4*>(w_norm + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
   float x[4] = {r[0] * wn.x / rms2, r[1] * wn.y / rms2, r[2] * wn.z / rms2, r[3] * wn.w / rms2};
   float y[4];
 #pragma unroll
@@ -148,41 +154,53 @@ __global__ void __launch_bounds__(PF_THREADS)
                  float* __restrict__ q_out, kv_t<KV16>* __restrict__ kc, kv_t<KV16>* __restrict__ vc,
                  const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride) {
   pdl_trigger();
-  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   constexpr int NJ = PF_HD / 32;
-  const int t = blockIdx.x, pos = BATCH ? pos_arr[t] : p0 + t;
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int QD = NQH * PF_HD, KVD = NKH * PF_HD, W = QD + 2 * KVD;
+  const long long base = (long long)t * W;
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
+  const int pos = BATCH ? pos_arr[t] : p0 + t;
   if (BATCH) {
     kc += (size_t)seq_arr[t] * seq_stride;
     vc += (size_t)seq_arr[t] * seq_stride;
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int QD = NQH * PF_HD, KVD = NKH * PF_HD, W = QD + 2 * KVD;
-  const long long base = (long long)t * W;
   for (int h = warp; h < NQH + NKH; h += PF_THREADS / 32) {
-    // the head's NJ elements of every split plane: NJ loads in flight per plane, planes in order
+    // norm weights, RoPE table and the head's elements of every split plane issued together
+    // (two planes in flight), the planes summed in plane order
+    const float* nw = h < NQH ? q_norm : k_norm;
+    float nwv[NJ];
+    float2 cr[NJ / 2];  // (cos, sin) of pos * freq_i, i = lane + 32 j
+#pragma unroll
+    for (int j = 0; j < NJ; j++) nwv[j] = __ldg(nw + lane + 32 * j);
+#pragma unroll
+    for (int j = 0; j < NJ / 2; j++) cr[j] = rope[(size_t)pos * (PF_HD / 2) + lane + 32 * j];
     const long long ob = base + h * PF_HD + lane;
     float v[NJ];
 #pragma unroll
     for (int j = 0; j < NJ; j++) v[j] = part[ob + 32 * j];
-    for (int z = 1; z < splits; z++) {
-      float a[NJ];
+    for (int z = 1; z < splits; z += 2) {
+      float a[NJ], b2[NJ];
 #pragma unroll
-      for (int j = 0; j < NJ; j++) a[j] = part[(long long)z * plane + ob + 32 * j];
+      for (int j = 0; j < NJ; j++) {
+        a[j] = part[(long long)z * plane + ob + 32 * j];
+        b2[j] = z + 1 < splits ? part[(long long)(z + 1) * plane + ob + 32 * j] : 0.f;
+      }
 #pragma unroll
-      for (int j = 0; j < NJ; j++) v[j] += a[j];
+      for (int j = 0; j < NJ; j++) {
+        v[j] += a[j];
+        if (z + 1 < splits) v[j] += b2[j];
+      }
     }
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < NJ; j++) ss += v[j] * v[j];
     const float rms = sqrtf(warp_sum(ss) / (float)PF_HD + eps);
-    const float* nw = h < NQH ? q_norm : k_norm;
 #pragma unroll
-    for (int j = 0; j < NJ; j++) v[j] = v[j] * nw[lane + 32 * j] / rms;
+    for (int j = 0; j < NJ; j++) v[j] = v[j] * nwv[j] / rms;
 #pragma unroll
     for (int j = 0; j < NJ / 2; j++) {
-      const int i = lane + 32 * j;
-      const float2 cr = rope[(size_t)pos * (PF_HD / 2) + i];  // (cos, sin) of pos * freq_i
-      const float cs = cr.x, sn = cr.y;
+      const float cs = cr[j].x, sn = cr[j].y;
       const float x0 = v[j], x1 = v[j + NJ / 2];
       v[j] = x0 * cs - x1 * sn;
       v[j + NJ / 2] = x0 * sn + x1 * cs;
