@@ -1034,7 +1034,7 @@ __global__ void gg_sum_splits_kernel(const float* __restrict__ p, int splits, lo
 // at least 3 K slabs each). Tiles of up to 64 rows run two CTAs per SM.
 static int pick_splits(int tiles, int KS, int slots) {
   int s = 1;
-  while (s < 16 && tiles * (s + 1) <= slots && KS / (s + 1) >= 3) s++;
+  while (s < 16 && tiles * (s + 1) <= slots && KS / (s + 1) >= 2) s++;  // at least two K slabs per split
   while (s > 1 && (long long)(s - 1) * ((KS + s - 1) / s) >= KS) s--;
   return s;
 }
