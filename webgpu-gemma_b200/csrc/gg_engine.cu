@@ -1058,6 +1058,19 @@ extern "C" int gg_linear(gg_engine* e, int which, int layer, const float* x, int
   if (which < 4 && (layer < 0 || layer >= e->cfg.num_layers)) return fail(e, GG_E_ARG, "layer %d out of range", layer);
   const GGQ8Map& w = which == 4 ? e->lm_map : e->qmaps[(size_t)layer * 4 + which];
   const int M = w.M, K = w.K, T = batch;
+  if (T == 1) {  // a single row: the CUDA-core matvec over the device rows
+    const uint8_t* rows[5] = {which < 4 ? e->wqkv[layer] : nullptr, which < 4 ? e->wo[layer] : nullptr,
+                              which < 4 ? e->wgu[layer] : nullptr, which < 4 ? e->wdown[layer] : nullptr, e->embd};
+    const int rs[5] = {e->md.rs_h, e->md.rs_q, e->md.rs_h, e->md.rs_i, e->md.rs_h};
+    GG_TRY(grow(e, (void**)&e->lin_x, &e->lin_x_cap, sizeof(float) * (size_t)K));
+    GG_TRY(grow(e, (void**)&e->lin_y, &e->lin_y_cap, sizeof(float) * (size_t)M));
+    GG_CUDA(e, cudaMemcpyAsync(e->lin_x, x, sizeof(float) * (size_t)K, cudaMemcpyHostToDevice, e->stream));
+    GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
+    GG_CUDA(e, gg_matvec_q8(rows[which], rs[which], M, K, e->lin_x, e->lin_y, e->sm_count, e->stream));
+    GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
+    GG_CUDA(e, cudaMemcpyAsync(y, e->lin_y, sizeof(float) * (size_t)M, cudaMemcpyDeviceToHost, e->stream));
+    return finish(e, nullptr);
+  }
   const int splits = pick_splits(gemm_tiles(T, M), K / 64, gemm_slots(e, T));
   const size_t tb = gg_xtiles_bytes(T, K);
   GG_TRY(grow(e, (void**)&e->lin_x, &e->lin_x_cap, sizeof(float) * (size_t)T * K));

@@ -15,6 +15,7 @@
 // reference's linearQ8 shader (src/shaders.ts:92-151) for batched rows (prefill, batches).
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "gg_gemm.h"
@@ -415,6 +416,70 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const Gemm
   }
 }
 
+// ---------------------------------------------------------------------------- one row
+// y[m] = sum_b d[m][b] * (q[m][32b..32b+31] . x[32b..]) for a single activation row: the
+// reference's linearQ8 (shaders.ts:92-151) at batch 1, read straight from the device rows. A
+// warp per weight row; lane l takes the row's 16-byte chunks l, l + 32, ... (16 int8 weights,
+// exact int8 -> f32 by the 2^23 magic-number trick, 16 FMAs, times the block scale). x sits in
+// shared memory permuted so that the warp's four float4 reads of a step are each contiguous
+// (quad i of chunk c at [i][c]): no bank conflicts.
+constexpr int MV_THREADS = 256;
+// R rows per warp at a time (their loads in flight together, x read once for all R): R = 4 when
+// the matrix has rows enough for a CTA per SM that way, else 1.
+template <int R>
+__global__ void __launch_bounds__(MV_THREADS) gg_matvec_q8_kernel(const uint8_t* __restrict__ rows, int rs, int M,
+                                                                int K, const float* __restrict__ x,
+                                                                float* __restrict__ y) {
+  pdl_trigger();
+  extern __shared__ float4 xq[];  // [4][K / 16]
+  const int nch = K / 16;
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
+  for (int qd = threadIdx.x; qd < K / 4; qd += MV_THREADS)
+    xq[(qd & 3) * nch + (qd >> 2)] = reinterpret_cast<const float4*>(x)[qd];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ngroups = (M + R - 1) / R;
+  for (int gi = blockIdx.x * (MV_THREADS / 32) + warp; gi < ngroups; gi += gridDim.x * (MV_THREADS / 32)) {
+    const int m0 = gi * R;
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) acc[r] = 0.f;
+#pragma unroll(R == 1 ? 2 : 1)
+    for (int c = lane; c < nch; c += 32) {
+      uint4 w[R];
+      float d[R];
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        const uint8_t* row = rows + (size_t)min(m0 + r, M - 1) * rs;
+        w[r] = ldg_nc16(row + 16 * c);
+        d[r] = __half2float(__ushort_as_half((unsigned short)ldg_nc_u16(row + K + 2 * (c >> 1))));
+      }
+      float sum[R];
+#pragma unroll
+      for (int r = 0; r < R; r++) sum[r] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float4 xv = xq[i * nch + c];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          const uint32_t wx = (i == 0 ? w[r].x : i == 1 ? w[r].y : i == 2 ? w[r].z : w[r].w) ^ 0x80808080u;
+          sum[r] = fmaf(q8_at(wx, 0), xv.x, sum[r]);
+          sum[r] = fmaf(q8_at(wx, 1), xv.y, sum[r]);
+          sum[r] = fmaf(q8_at(wx, 2), xv.z, sum[r]);
+          sum[r] = fmaf(q8_at(wx, 3), xv.w, sum[r]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < R; r++) acc[r] = fmaf(sum[r], d[r], acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const float v = warp_sum(acc[r]);
+      if (lane == 0 && m0 + r < M) y[m0 + r] = v;
+    }
+  }
+}
+
 // Tiled Q8_0 copy -> dense (hi, lo) operand tiles: one CTA per 128 x 64 slab, one thread per
 // Q8_0 block (same dequantisation as the GEMM's dequantising warps).
 __global__ void __launch_bounds__(256) gg_dense_tile_kernel(const uint8_t* __restrict__ q8tiles, uint8_t* __restrict__ dense) {
@@ -564,4 +629,30 @@ cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo,
     return wide ? launch_dense<256>(a, w.M / 128, splits, s) : launch_dense<128>(a, w.M / 128, splits, s);
   }
   return T <= 64 ? launch_nt<64>(w, a, splits, s) : launch_nt<128>(w, a, splits, s);
+}
+
+cudaError_t gg_matvec_q8(const uint8_t* rows, int rs, int M, int K, const float* x, float* y, int sms,
+                         cudaStream_t s) {
+  if (M <= 0 || K <= 0 || K % 64 || K > 16384 || rs < K + K / 16) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)K * 4;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t r = cudaGetDevice(&dev);
+  if (r != cudaSuccess) return r;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    r = cudaFuncSetAttribute(gg::gg_matvec_q8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(gg::gg_matvec_q8_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    if (r != cudaSuccess) return r;
+    attr_set[dev] = true;
+  }
+  constexpr int WARPS = gg::MV_THREADS / 32;
+  const int cap = sms * 8;  // CTAs: eight per SM of 8 warps
+  if ((M + 4 * WARPS - 1) / (4 * WARPS) >= sms) {  // four rows per warp still fill every SM
+    const int grid = std::min((M + 4 * WARPS - 1) / (4 * WARPS), cap);
+    return gg::launch_pdl(gg::gg_matvec_q8_kernel<4>, dim3(grid), dim3(gg::MV_THREADS), smem, s, rows, rs, M, K, x, y);
+  }
+  const int grid = std::min((M + WARPS - 1) / WARPS, cap);
+  return gg::launch_pdl(gg::gg_matvec_q8_kernel<1>, dim3(grid), dim3(gg::MV_THREADS), smem, s, rows, rs, M, K, x, y);
 }

@@ -37,6 +37,12 @@ size_t gg_xtiles_bytes(int T, int K);
 // x [T][K] f32 -> tile arrays (rows T..round256(T)-1 zero).
 cudaError_t gg_xtiles_from_f32(const float* x, int T, int K, uint8_t* xhi, uint8_t* xlo, cudaStream_t s);
 
+// One activation row: y[m] = row m of a Q8_0 matrix in the device row format (stride rs bytes)
+// times x (K floats), f32 accumulation on the CUDA cores (the tensor-core tiles do not pay at
+// batch 1). K % 64 == 0, K <= 16384.
+cudaError_t gg_matvec_q8(const uint8_t* rows, int rs, int M, int K, const float* x, float* y, int sms,
+                         cudaStream_t s);
+
 // Y (+ split * split_stride) [t][m] with row stride ldy; K is cut into `splits` slices whose
 // partial results land in consecutive split planes (the caller sums them).
 cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo, int T, float* y, long long ldy,
