@@ -218,12 +218,12 @@ __global__ void __launch_bounds__(PF_THREADS)
 }
 
 // Causal attention, split over key ranges. A work item is (a block of 32 query rows, a range
-// of 128 keys): the rows are QT = 32/G consecutive tokens times the G query heads that share
+// of 64 keys): the rows are QT = 32/G consecutive tokens times the G query heads that share
 // one KV head, so each K/V row serves all of them. An item leaves unnormalised partial results
 // (running max m, sum l, output o) that pf_attn_merge combines with the usual online-softmax
 // rescaling.
 constexpr int PA_ROWS = 32;
-constexpr int PA_KC = 128;                     // keys per work item
+constexpr int PA_KC = 64;                      // keys per work item (two CTAs per SM fill the GPU)
 constexpr int PA_PART = PA_ROWS * PF_HD + 2 * PA_ROWS;  // floats per item: o, then m, then l
 
 // The work item runs on the tensor cores: mma.sync m16n8k16 with bf16 operands and f32
@@ -482,7 +482,7 @@ __global__ void __launch_bounds__(PF_THREADS)
                          uint8_t* thi, uint8_t* tlo) {
   pdl_trigger();
   pdl_wait();  // before touching any buffer shared with the other kernels of the chain
-  __shared__ float wm[16][PA_ROWS], wl[16][PA_ROWS];  // (max, sum) of every key range and row
+  __shared__ float wm[32][PA_ROWS], wl[32][PA_ROWS];  // (max, sum) of every key range and row
   const int G = NQH / NKH, QT = PA_ROWS / G;
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int t0 = b * QT, nq = min(QT, T - t0);
@@ -844,7 +844,7 @@ cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv
   const int QT = PA_ROWS / G;
   const int nb = (T + QT - 1) / QT;
   const int maxc = (p0 + T - 1) / PA_KC + 1;
-  if (maxc > 16) return cudaErrorInvalidValue;  // merge weights hold 16 key ranges (2048 positions)
+  if (maxc > 32) return cudaErrorInvalidValue;  // merge weights hold 32 key ranges (2048 positions)
   const dim3 grid(maxc, nb, NKH);
   if (kv16)
     r = launch_pdl(pf_attn_tc_kernel<true>, grid, dim3(TA_THREADS), TA_SMEM, s, q, (const __nv_bfloat16*)kc,
