@@ -230,13 +230,15 @@ constexpr int PA_PART = PA_ROWS * PF_HD + 2 * PA_ROWS;  // floats per item: o, t
 // accumulation. Every f32 operand is split into bf16 hi + lo (hi + lo = x to ~2^-16) and each
 // product is the sum of three MMAs (hi*hi + hi*lo + lo*hi), which keeps the scores and outputs
 // within ~1e-5 of f32.
-//   warp w: query rows 16*(w>>1).. (one m16 tile), output dims 128*(w&1).. ; both warps of a row
-//   tile compute the tile's scores (16 rows x 32 keys per block), so the probabilities never
-//   leave registers: the score accumulators are re-packed as the A operand of P.V.
+//   warp w: query rows 16*((w>>1)&1).. (one m16 tile), output dims 128*(w&1).., keys
+//   16*(w>>2)..+15 of every 32-key block; both dim halves compute the scores of their rows and
+//   keys, so the probabilities never leave registers (the score accumulators are re-packed as
+//   the A operand of P.V). The two key halves keep their own softmax statistics and are merged
+//   through shared memory at the end.
 // K and V blocks of 32 keys are converted to swizzled bf16 hi/lo tiles in shared memory (16-byte
 // chunk c of row r stored at chunk c ^ (r & 7), so ldmatrix reads 8 rows without bank conflicts).
 constexpr int TA_KB = 32;                          // keys per shared-memory block
-constexpr int TA_THREADS = 128;
+constexpr int TA_THREADS = 256;                   // 8 warps: row tile x dim half x key half
 constexpr int TA_TILE = PF_HD * 2;                 // bytes of one bf16 row of 256 dims
 constexpr int TA_SMEM = (PA_ROWS * 2 + TA_KB * 4) * TA_TILE;  // Q hi/lo, K hi/lo, V hi/lo
 
@@ -278,7 +280,7 @@ GG_DEV uint32_t pack2(float a, float b) {  // a in the low half (lower column)
 }
 
 template <bool KV16>
-__global__ void __launch_bounds__(TA_THREADS, 1)
+__global__ void __launch_bounds__(TA_THREADS, 2)
     pf_attn_tc_kernel(const float* __restrict__ q, const kv_t<KV16>* __restrict__ kc, const kv_t<KV16>* __restrict__ vc,
                       int T, int p0, int NQH, int NKH, float scale, int window, int maxc, float* __restrict__ part) {
   pdl_trigger();
@@ -316,7 +318,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     *reinterpret_cast<uint4*>(qh + ta_off(r, 8 * c8)) = hi;
     *reinterpret_cast<uint4*>(ql + ta_off(r, 8 * c8)) = lo;
   }
-  const int rt = warp >> 1, dh = warp & 1;  // row tile, dim half
+  const int rt = (warp >> 1) & 1, dh = warp & 1, kh2 = warp >> 2;  // row tile, dim half, key half
   const int g = lane >> 2, tq = lane & 3;   // mma fragment coordinates
   const int ra = 16 * rt + g, rb = ra + 8;  // this thread's two rows
   const int pos_a = p0 + t0 + ra / G, pos_b = p0 + t0 + rb / G;
@@ -360,37 +362,34 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       *reinterpret_cast<uint4*>(vl + ta_off(r, 8 * c8)) = lo;
     }
     __syncthreads();
-    // S = Q K^T for this warp's 16 rows x 32 keys (4 n-tiles of 8 keys)
-    float sacc[4][4];
+    // S = Q K^T for this warp's 16 rows x 16 keys (2 n-tiles of 8 keys: keys 16*kh2 ..)
+    float sacc[2][4];
 #pragma unroll
-    for (int n = 0; n < 4; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+    for (int n = 0; n < 2; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
     const int arow = 16 * rt + (lane & 15), acol = 8 * (lane >> 4);              // A (Q) ldmatrix lanes
     const int brow = (lane & 7) + 8 * (lane >> 4), bcol = 8 * ((lane >> 3) & 1);  // B (K) ldmatrix lanes
 #pragma unroll 4
     for (int ks = 0; ks < PF_HD / 16; ks++) {
-      uint32_t ah[4], al[4], bh[2][4], bl[2][4];
+      uint32_t ah[4], al[4], bh[4], bl[4];
       ldsm_x4(smem_u32(qh + ta_off(arow, 16 * ks + acol)), ah);
       ldsm_x4(smem_u32(ql + ta_off(arow, 16 * ks + acol)), al);
+      ldsm_x4(smem_u32(kh + ta_off(16 * kh2 + brow, 16 * ks + bcol)), bh);
+      ldsm_x4(smem_u32(kl + ta_off(16 * kh2 + brow, 16 * ks + bcol)), bl);
+      // the three products alternate over the two accumulators
 #pragma unroll
-      for (int np = 0; np < 2; np++) {
-        ldsm_x4(smem_u32(kh + ta_off(16 * np + brow, 16 * ks + bcol)), bh[np]);
-        ldsm_x4(smem_u32(kl + ta_off(16 * np + brow, 16 * ks + bcol)), bl[np]);
-      }
-      // the three products rotate over the four accumulators, so consecutive MMAs are independent
+      for (int n = 0; n < 2; n++) mma_bf16(sacc[n], ah, bh[2 * n], bh[2 * n + 1]);
 #pragma unroll
-      for (int n = 0; n < 4; n++) mma_bf16(sacc[n], ah, bh[n >> 1][2 * (n & 1)], bh[n >> 1][2 * (n & 1) + 1]);
+      for (int n = 0; n < 2; n++) mma_bf16(sacc[n], ah, bl[2 * n], bl[2 * n + 1]);
 #pragma unroll
-      for (int n = 0; n < 4; n++) mma_bf16(sacc[n], ah, bl[n >> 1][2 * (n & 1)], bl[n >> 1][2 * (n & 1) + 1]);
-#pragma unroll
-      for (int n = 0; n < 4; n++) mma_bf16(sacc[n], al, bh[n >> 1][2 * (n & 1)], bh[n >> 1][2 * (n & 1) + 1]);
+      for (int n = 0; n < 2; n++) mma_bf16(sacc[n], al, bh[2 * n], bh[2 * n + 1]);
     }
     // causal / window / range mask, scale, and the online softmax of rows ra (d0, d1) and rb (d2, d3)
     float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
-    for (int n = 0; n < 4; n++)
+    for (int n = 0; n < 2; n++)
 #pragma unroll
       for (int e = 0; e < 2; e++) {
-        const int key = j0 + 8 * n + 2 * tq + e;
+        const int key = j0 + 16 * kh2 + 8 * n + 2 * tq + e;
         const bool in = key < j0 + nk;
         sacc[n][e] = (in && va && key <= pos_a && key >= lo_a) ? sacc[n][e] * scale : -INFINITY;
         sacc[n][2 + e] = (in && vb && key <= pos_b && key >= lo_b) ? sacc[n][2 + e] * scale : -INFINITY;
@@ -407,7 +406,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     m_b = nm_b;
     float ps_a = 0.f, ps_b = 0.f;
 #pragma unroll
-    for (int n = 0; n < 4; n++)
+    for (int n = 0; n < 2; n++)
 #pragma unroll
       for (int e = 0; e < 2; e++) {
         sacc[n][e] = sacc[n][e] == -INFINITY ? 0.f : expf(sacc[n][e] - nm_a);
@@ -424,12 +423,11 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       o[n][2] *= al_b;
       o[n][3] *= al_b;
     }
-    // O += P V: P (16 rows x 32 keys) from the score registers as bf16 hi/lo A fragments
+    // O += P V: P (16 rows x this warp's 16 keys) from the score registers as bf16 hi/lo A fragments
     const int vrow = (lane & 7) + 8 * ((lane >> 3) & 1), vcol = 8 * (lane >> 4);  // V ldmatrix.trans lanes
-#pragma unroll
-    for (int kk = 0; kk < 2; kk++) {
-      float pf[8] = {sacc[2 * kk][0], sacc[2 * kk][1], sacc[2 * kk][2], sacc[2 * kk][3],
-                     sacc[2 * kk + 1][0], sacc[2 * kk + 1][1], sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]};
+    {
+      const int kk = kh2;
+      float pf[8] = {sacc[0][0], sacc[0][1], sacc[0][2], sacc[0][3], sacc[1][0], sacc[1][1], sacc[1][2], sacc[1][3]};
       uint32_t ph[4], pl[4];
 #pragma unroll
       for (int i = 0; i < 4; i++) {
@@ -461,6 +459,35 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
   l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  // merge the key halves: the upper-half warp leaves (m, l, o) in shared memory (the K/V tiles
+  // are free now) and the lower-half warp of the same rows and dims folds them in
+  __syncthreads();
+  float* xo = reinterpret_cast<float*>(kh) + ((rt * 2 + dh) * 32 + lane) * 68;  // 64 o + 4 stats per lane
+  if (kh2 == 1) {
+#pragma unroll
+    for (int n = 0; n < 16; n++)
+      *reinterpret_cast<float4*>(xo + 4 * n) = make_float4(o[n][0], o[n][1], o[n][2], o[n][3]);
+    *reinterpret_cast<float4*>(xo + 64) = make_float4(m_a, m_b, l_a, l_b);
+  }
+  __syncthreads();
+  if (kh2 == 1) return;
+  {
+    const float4 st = *reinterpret_cast<const float4*>(xo + 64);
+    const float nm_a = fmaxf(m_a, st.x), nm_b = fmaxf(m_b, st.y);
+    const float s0a = expf(m_a - nm_a), s1a = expf(st.x - nm_a), s0b = expf(m_b - nm_b), s1b = expf(st.y - nm_b);
+#pragma unroll
+    for (int n = 0; n < 16; n++) {
+      const float4 u = *reinterpret_cast<const float4*>(xo + 4 * n);
+      o[n][0] = o[n][0] * s0a + u.x * s1a;
+      o[n][1] = o[n][1] * s0a + u.y * s1a;
+      o[n][2] = o[n][2] * s0b + u.z * s1b;
+      o[n][3] = o[n][3] * s0b + u.w * s1b;
+    }
+    l_a = l_a * s0a + st.z * s1a;
+    l_b = l_b * s0b + st.w * s1b;
+    m_a = nm_a;
+    m_b = nm_b;
+  }
   float* dst = part + ((size_t)(kvh * gridDim.y + b) * maxc + c) * PA_PART;
 #pragma unroll
   for (int n = 0; n < 16; n++) {
