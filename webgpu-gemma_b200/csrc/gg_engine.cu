@@ -129,6 +129,7 @@ struct gg_engine {
   float* pf_att = nullptr;  // attention partials per key range
   uint8_t* pf_tiles = nullptr;
   size_t pf_tiles_half = 0;
+  uint8_t* pf_kvsplit = nullptr;  // bf16 hi / lo copies of the K and V rows a chunk attends to
   // batched decode: one token for each of up to bd_max sequences per step
   int bd_max = 0;
   float* bd_logits = nullptr;            // [bd_max][V]
@@ -491,6 +492,7 @@ extern "C" int gg_finalize(gg_engine* e) {
     GG_TRY(dalloc(e, &e->pf_y, 4 * yfl));
     GG_TRY(dalloc(e, &e->pf_att, 4 * pf_attention_part_floats((int)TC, m.CTX, m.NQH, m.NKH)));
     GG_TRY(dalloc(e, &e->pf_tiles, 2 * e->pf_tiles_half));
+    GG_TRY(dalloc(e, &e->pf_kvsplit, pf_kv_split_bytes(m.CTX, m.KV)));
   }
   GG_TRY(dalloc(e, &m.t_qkv, 8 * (size_t)(m.Q + 2 * m.KV)));
   GG_TRY(dalloc(e, &m.t_ml, 8 * (size_t)m.max_splits * m.NQH * 2));
@@ -630,7 +632,7 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
       GG_CUDA(e, pf_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, T, p0, m.NQH, m.NKH, m.HD, m.eps,
                                   e->pf_q, kc, vc, m.kv_es == 2, s));
       GG_CUDA(e, pf_attention(e->pf_q, kc, vc, m.kv_es == 2, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, w.window,
-                              e->pf_att, thi, tlo, s));
+                              e->pf_att, e->pf_kvsplit, m.CTX, thi, tlo, s));
       sp = pick_splits(gemm_tiles(T, m.H), m.Q / 64, gemm_slots(e, T));
       plane = (long long)T * m.H;
       GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));

@@ -279,10 +279,42 @@ GG_DEV uint32_t pack2(float a, float b) {  // a in the low half (lower column)
          ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
 }
 
+// K and V rows [r0, r1) of a layer's cache -> bf16 hi / lo copies (row-major [row][KVD]), once per
+// layer and chunk, so the attention CTAs that read a row all copy ready operand halves.
 template <bool KV16>
+__global__ void __launch_bounds__(256)
+    pf_kv_split_kernel(const kv_t<KV16>* __restrict__ kc, const kv_t<KV16>* __restrict__ vc, int r0, int r1, int KVD,
+                       uint16_t* __restrict__ khi, uint16_t* __restrict__ klo, uint16_t* __restrict__ vhi,
+                       uint16_t* __restrict__ vlo) {
+  pdl_trigger();
+  pdl_wait();  // before touching any buffer shared with the other kernels of the chain
+  const long long n8 = (long long)(r1 - r0) * (KVD / 8);
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < n8; i += (long long)gridDim.x * 256) {
+    const long long e = (long long)r0 * KVD + 8 * i;
+    float fk[8], fv[8];
+    if constexpr (KV16) {
+      bf16x8_widen(__ldg(reinterpret_cast<const uint4*>(kc + e)), fk);
+      bf16x8_widen(__ldg(reinterpret_cast<const uint4*>(vc + e)), fv);
+    } else {
+      const float4 k0 = __ldg(reinterpret_cast<const float4*>(kc + e)), k1 = __ldg(reinterpret_cast<const float4*>(kc + e) + 1);
+      const float4 v0 = __ldg(reinterpret_cast<const float4*>(vc + e)), v1 = __ldg(reinterpret_cast<const float4*>(vc + e) + 1);
+      fk[0] = k0.x; fk[1] = k0.y; fk[2] = k0.z; fk[3] = k0.w; fk[4] = k1.x; fk[5] = k1.y; fk[6] = k1.z; fk[7] = k1.w;
+      fv[0] = v0.x; fv[1] = v0.y; fv[2] = v0.z; fv[3] = v0.w; fv[4] = v1.x; fv[5] = v1.y; fv[6] = v1.z; fv[7] = v1.w;
+    }
+    uint4 hi, lo;
+    split8(fk, hi, lo);
+    *reinterpret_cast<uint4*>(khi + e) = hi;
+    *reinterpret_cast<uint4*>(klo + e) = lo;
+    split8(fv, hi, lo);
+    *reinterpret_cast<uint4*>(vhi + e) = hi;
+    *reinterpret_cast<uint4*>(vlo + e) = lo;
+  }
+}
+
 __global__ void __launch_bounds__(TA_THREADS, 2)
-    pf_attn_tc_kernel(const float* __restrict__ q, const kv_t<KV16>* __restrict__ kc, const kv_t<KV16>* __restrict__ vc,
-                      int T, int p0, int NQH, int NKH, float scale, int window, int maxc, float* __restrict__ part) {
+    pf_attn_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict__ khi, const uint16_t* __restrict__ klo,
+                      const uint16_t* __restrict__ vhi, const uint16_t* __restrict__ vlo, int T, int p0, int NQH, int NKH,
+                      float scale, int window, int maxc, float* __restrict__ part) {
   pdl_trigger();
   pdl_wait();  // before touching any buffer shared with the other kernels of the chain
   extern __shared__ __align__(128) uint8_t ta_smem[];
@@ -332,35 +364,26 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
   for (int j0 = k_begin; j0 < k_end; j0 += TA_KB) {
     const int nk = min(TA_KB, k_end - j0);
     __syncthreads();  // the previous block's tiles are no longer read (and Q is written)
-    // K and V rows j0.. as bf16 hi/lo tiles; rows past nk are zero
-#pragma unroll 4
+    // K and V rows j0.. as bf16 hi/lo tiles: 16-byte async copies of the split rows into the
+    // swizzled layout; rows past nk are zero
     for (int i = tid; i < TA_KB * (PF_HD / 8); i += TA_THREADS) {
       const int r = i / (PF_HD / 8), c8 = i % (PF_HD / 8);
-      float fk[8], fv[8];
+      const uint32_t off = ta_off(r, 8 * c8);
       if (r < nk) {
         const long long e = (long long)(j0 + r) * KVD + kvh * PF_HD + 8 * c8;
-        if constexpr (KV16) {
-          bf16x8_widen(__ldg(reinterpret_cast<const uint4*>(kc + e)), fk);
-          bf16x8_widen(__ldg(reinterpret_cast<const uint4*>(vc + e)), fv);
-        } else {
-          const float4* ks4 = reinterpret_cast<const float4*>(kc + e);
-          const float4* vs4 = reinterpret_cast<const float4*>(vc + e);
-          const float4 k0 = ks4[0], k1 = ks4[1], v0 = vs4[0], v1 = vs4[1];
-          fk[0] = k0.x; fk[1] = k0.y; fk[2] = k0.z; fk[3] = k0.w; fk[4] = k1.x; fk[5] = k1.y; fk[6] = k1.z; fk[7] = k1.w;
-          fv[0] = v0.x; fv[1] = v0.y; fv[2] = v0.z; fv[3] = v0.w; fv[4] = v1.x; fv[5] = v1.y; fv[6] = v1.z; fv[7] = v1.w;
-        }
+        cp_async16(kh + off, khi + e);
+        cp_async16(kl + off, klo + e);
+        cp_async16(vh + off, vhi + e);
+        cp_async16(vl + off, vlo + e);
       } else {
-#pragma unroll
-        for (int u = 0; u < 8; u++) fk[u] = fv[u] = 0.f;
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(kh + off) = z;
+        *reinterpret_cast<uint4*>(kl + off) = z;
+        *reinterpret_cast<uint4*>(vh + off) = z;
+        *reinterpret_cast<uint4*>(vl + off) = z;
       }
-      uint4 hi, lo;
-      split8(fk, hi, lo);
-      *reinterpret_cast<uint4*>(kh + ta_off(r, 8 * c8)) = hi;
-      *reinterpret_cast<uint4*>(kl + ta_off(r, 8 * c8)) = lo;
-      split8(fv, hi, lo);
-      *reinterpret_cast<uint4*>(vh + ta_off(r, 8 * c8)) = hi;
-      *reinterpret_cast<uint4*>(vl + ta_off(r, 8 * c8)) = lo;
     }
+    cp_async_wait_all();
     __syncthreads();
     // S = Q K^T for this warp's 16 rows x 16 keys (2 n-tiles of 8 keys: keys 16*kh2 ..)
     float sacc[2][4];
@@ -851,9 +874,12 @@ size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH) {
   return nb * maxc * NKH * PA_PART;
 }
 
+size_t pf_kv_split_bytes(int ctx, int KVD) { return (size_t)4 * ctx * KVD * sizeof(uint16_t); }
+
 cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv16, int T, int p0, int NQH, int NKH,
-                         int HD, float scale, int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
-  if (T <= 0 || HD != PF_HD || NKH <= 0 || NQH % NKH) return cudaErrorInvalidValue;
+                         int HD, float scale, int window, float* part, uint8_t* split, int ctx, uint8_t* thi,
+                         uint8_t* tlo, cudaStream_t s) {
+  if (T <= 0 || HD != PF_HD || NKH <= 0 || NQH % NKH || !split || p0 + T > ctx) return cudaErrorInvalidValue;
   const int G = NQH / NKH;
   if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) return cudaErrorInvalidValue;
   static bool attr_set[64] = {};
@@ -862,9 +888,7 @@ cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv
   if (r != cudaSuccess) return r;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_set[dev]) {
-    r = cudaFuncSetAttribute(pf_attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM);
-    if (r == cudaSuccess)
-      r = cudaFuncSetAttribute(pf_attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM);
+    r = cudaFuncSetAttribute(pf_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM);
     if (r != cudaSuccess) return r;
     attr_set[dev] = true;
   }
@@ -872,15 +896,26 @@ cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv
   const int nb = (T + QT - 1) / QT;
   const int maxc = (p0 + T - 1) / PA_KC + 1;
   if (maxc > 32) return cudaErrorInvalidValue;  // merge weights hold 32 key ranges (2048 positions)
-  const dim3 grid(maxc, nb, NKH);
+  // bf16 hi / lo copies of the rows the chunk can see: [klo, p0 + T)
+  const int KVD = NKH * PF_HD;
+  const int r0 = window > 0 ? max(0, p0 + 1 - window) / PA_KC * PA_KC : 0, r1 = p0 + T;
+  uint16_t* khi = reinterpret_cast<uint16_t*>(split);
+  uint16_t* klo = khi + (size_t)ctx * KVD;
+  uint16_t* vhi = klo + (size_t)ctx * KVD;
+  uint16_t* vlo = vhi + (size_t)ctx * KVD;
+  const long long n8 = (long long)(r1 - r0) * (KVD / 8);
+  const int sblocks = (int)std::min<long long>((n8 + 255) / 256, 148 * 8);
   if (kv16)
-    r = launch_pdl(pf_attn_tc_kernel<true>, grid, dim3(TA_THREADS), TA_SMEM, s, q, (const __nv_bfloat16*)kc,
-                   (const __nv_bfloat16*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
+    r = launch_pdl(pf_kv_split_kernel<true>, dim3(sblocks), dim3(256), 0, s, (const __nv_bfloat16*)kc,
+                   (const __nv_bfloat16*)vc, r0, r1, KVD, khi, klo, vhi, vlo);
   else
-    r = launch_pdl(pf_attn_tc_kernel<false>, grid, dim3(TA_THREADS), TA_SMEM, s, q, (const float*)kc,
-                   (const float*)vc, T, p0, NQH, NKH, scale, window, maxc, part);
+    r = launch_pdl(pf_kv_split_kernel<false>, dim3(sblocks), dim3(256), 0, s, (const float*)kc, (const float*)vc, r0, r1,
+                   KVD, khi, klo, vhi, vlo);
   if (r != cudaSuccess) return r;
-  static_assert(PA_ROWS * 8 == PF_THREADS, "merge: one thread per (row, 8 dims) of a quarter head");
+  r = launch_pdl(pf_attn_tc_kernel, dim3(maxc, nb, NKH), dim3(TA_THREADS), TA_SMEM, s, q, (const uint16_t*)khi,
+                 (const uint16_t*)klo, (const uint16_t*)vhi, (const uint16_t*)vlo, T, p0, NQH, NKH, scale, window, maxc,
+                 part);
+  if (r != cudaSuccess) return r;
   return launch_pdl(pf_attn_merge_kernel, dim3(nb, NKH, PF_HD / 64), dim3(PF_THREADS), 0, s, (const float*)part, T, p0,
                     NQH, NKH, window, maxc, thi, tlo);
 }

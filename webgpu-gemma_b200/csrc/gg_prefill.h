@@ -35,8 +35,12 @@ cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, con
 // of pf_attention_part_floats(T, p0 + T, NQH, NKH) floats (partial results per key range).
 size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH);
 // window > 0: each query at position p sees only keys p-window+1..p (sliding-window layer).
+// `split` is scratch of pf_kv_split_bytes(ctx, NKH * HD) bytes: bf16 hi / lo copies of the rows
+// the chunk attends to, made once per call and read by every attention CTA.
+size_t pf_kv_split_bytes(int ctx, int KVD);
 cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv16, int T, int p0, int NQH, int NKH,
-                         int HD, float scale, int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
+                         int HD, float scale, int window, float* part, uint8_t* split, int ctx, uint8_t* thi,
+                         uint8_t* tlo, cudaStream_t s);
 
 // act[t][i] = gelu_tanh(gu[t][2i]) * gu[t][2i+1] (shaders.ts:153-170, gu = sum of planes) as
 // activation tiles of width I.
