@@ -208,7 +208,17 @@ __global__ void __launch_bounds__(PF_THREADS)
 #pragma unroll
     for (int j = 0; j < NJ; j++) {
       const int i = lane + 32 * j;
-      if (h < NQH) q_out[(long long)t * QD + h * PF_HD + i] = v[j];
+      if (h < NQH) {
+        const long long qi = (long long)t * QD + h * PF_HD + i;
+        if constexpr (BATCH) {
+          q_out[qi] = v[j];
+        } else {  // prompt chunk: q as bf16 hi / lo halves (hi at q_out, lo T * QD elements later)
+          uint16_t* qs = reinterpret_cast<uint16_t*>(q_out);
+          const __nv_bfloat16 hi = __float2bfloat16_rn(v[j]);
+          qs[qi] = __bfloat16_as_ushort(hi);
+          qs[(long long)gridDim.x * QD + qi] = __bfloat16_as_ushort(__float2bfloat16_rn(v[j] - __bfloat162float(hi)));
+        }
+      }
       else kc[(long long)pos * KVD + (h - NQH) * PF_HD + i] = kv_narrow<KV16>(v[j]);
     }
   }
@@ -312,7 +322,8 @@ __global__ void __launch_bounds__(256)
 }
 
 __global__ void __launch_bounds__(TA_THREADS, 2)
-    pf_attn_tc_kernel(const float* __restrict__ q, const uint16_t* __restrict__ khi, const uint16_t* __restrict__ klo,
+    pf_attn_tc_kernel(const uint16_t* __restrict__ qhi, const uint16_t* __restrict__ qlo,
+                      const uint16_t* __restrict__ khi, const uint16_t* __restrict__ klo,
                       const uint16_t* __restrict__ vhi, const uint16_t* __restrict__ vlo, int T, int p0, int NQH, int NKH,
                       float scale, int window, int maxc, float* __restrict__ part) {
   pdl_trigger();
@@ -335,20 +346,21 @@ __global__ void __launch_bounds__(TA_THREADS, 2)
   if (k_end <= klo0) return;
   const int QD = NQH * PF_HD, KVD = NKH * PF_HD;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // query rows r = token * G + g -> head kvh * G + g of token t0 + token, as bf16 hi/lo
+  // query rows r = token * G + g -> head kvh * G + g of token t0 + token: the bf16 hi / lo halves
+  // written by the q/k kernel, copied into the swizzled tiles (their cp.async group completes
+  // with the first K/V block's)
   for (int i = tid; i < PA_ROWS * (PF_HD / 8); i += TA_THREADS) {
     const int r = i / (PF_HD / 8), c8 = i % (PF_HD / 8);
     const int tok = r / G, hq = kvh * G + r % G;
-    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const uint32_t off = ta_off(r, 8 * c8);
     if (tok < nq) {
-      const float4* src = reinterpret_cast<const float4*>(q + (long long)(t0 + tok) * QD + hq * PF_HD + 8 * c8);
-      const float4 a = src[0], bq = src[1];
-      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = bq.x; f[5] = bq.y; f[6] = bq.z; f[7] = bq.w;
+      const long long e = (long long)(t0 + tok) * QD + hq * PF_HD + 8 * c8;
+      cp_async16(qh + off, qhi + e);
+      cp_async16(ql + off, qlo + e);
+    } else {
+      *reinterpret_cast<uint4*>(qh + off) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(ql + off) = make_uint4(0u, 0u, 0u, 0u);
     }
-    uint4 hi, lo;
-    split8(f, hi, lo);
-    *reinterpret_cast<uint4*>(qh + ta_off(r, 8 * c8)) = hi;
-    *reinterpret_cast<uint4*>(ql + ta_off(r, 8 * c8)) = lo;
   }
   const int rt = (warp >> 1) & 1, dh = warp & 1, kh2 = warp >> 2;  // row tile, dim half, key half
   const int g = lane >> 2, tq = lane & 3;   // mma fragment coordinates
@@ -912,7 +924,9 @@ cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv
     r = launch_pdl(pf_kv_split_kernel<false>, dim3(sblocks), dim3(256), 0, s, (const float*)kc, (const float*)vc, r0, r1,
                    KVD, khi, klo, vhi, vlo);
   if (r != cudaSuccess) return r;
-  r = launch_pdl(pf_attn_tc_kernel, dim3(maxc, nb, NKH), dim3(TA_THREADS), TA_SMEM, s, q, (const uint16_t*)khi,
+  const uint16_t* qhi = reinterpret_cast<const uint16_t*>(q);  // hi / lo halves from pf_qk_rope_store
+  const uint16_t* qlo = qhi + (size_t)T * NQH * PF_HD;
+  r = launch_pdl(pf_attn_tc_kernel, dim3(maxc, nb, NKH), dim3(TA_THREADS), TA_SMEM, s, qhi, qlo, (const uint16_t*)khi,
                  (const uint16_t*)klo, (const uint16_t*)vhi, (const uint16_t*)vlo, T, p0, NQH, NKH, scale, window, maxc,
                  part);
   if (r != cudaSuccess) return r;

@@ -24,13 +24,15 @@ cudaError_t pf_addnorm(const float* part, int splits, long long plane, const flo
                        cudaStream_t s);
 
 // Per token: sum the QKV planes, q/k per-head rmsNorm + RoPE at position p0 + t
-// (shaders.ts:420-467), q -> q_out [T][NQH*HD], k and v -> rows p0.. of this layer's cache
-// (f32 elements, or bf16 rounded to nearest even when kv16).
+// (shaders.ts:420-467), q -> q_out as bf16 hi / lo halves ([T][NQH*HD] hi, then [T][NQH*HD] lo,
+// the operand form pf_attention reads), k and v -> rows p0.. of this layer's cache (f32
+// elements, or bf16 rounded to nearest even when kv16).
 cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm,
                              const float* k_norm, const float2* rope, int T, int p0, int NQH, int NKH, int HD, float eps,
                              float* q_out, void* kc, void* vc, bool kv16, cudaStream_t s);
 
-// Causal attention of the T queries at positions p0..p0+T-1 over cache rows 0..p0+t
+// Causal attention of the T queries (q as written by pf_qk_rope_store) at positions
+// p0..p0+T-1 over cache rows 0..p0+t
 // (shaders.ts:229-325), output written as activation tiles of width NQH*HD. `part` is scratch
 // of pf_attention_part_floats(T, p0 + T, NQH, NKH) floats (partial results per key range).
 size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH);
