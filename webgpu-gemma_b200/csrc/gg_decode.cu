@@ -36,10 +36,16 @@ GG_DEV void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
 
 GG_DEV uint32_t make_tag(uint32_t base, int phase) { return 0x80000000u | ((base + (uint32_t)phase) & 0x7fffffffu); }
 
+// Rows [b, e) of M that CTA c of G takes. 32-bit: the host checks grid * rows < 2^31.
 GG_DEV void part(int M, int G, int c, int& b, int& e) {
-  b = (int)((long long)c * M / G);
-  e = (int)((long long)(c + 1) * M / G);
+  b = (int)(((uint32_t)c * (uint32_t)M) / (uint32_t)G);
+  e = (int)(((uint32_t)(c + 1) * (uint32_t)M) / (uint32_t)G);
 }
+
+// This CTA's share of each matvec, computed once per launch (Smem::rows): the range is the same
+// in every layer, and recomputing it after each phase's barrier would put two integer divisions
+// on every hand-over's critical path.
+enum { RG_QKV = 0, RG_H = 2, RG_I = 4, RG_V = 6, RG_N = 8 };
 
 // x operand of the dot products: each 16-element chunk as 24-bit fixed point (shared exponent)
 // split into three byte planes; p0 holds the signed top byte, p1/p2 the unsigned lower bytes.
@@ -63,6 +69,7 @@ struct Smem {
   unsigned long long* keys;
   float* scal;
   int* flag;
+  int* rows;  // [RG_N]: [b, e) of the q/k/v rows, the H rows (O, down), the I gate/up pairs, the V rows
 };
 
 GG_DEV unsigned long long init_lane_key() {
@@ -165,12 +172,10 @@ struct Producer {
   GG_DEV void run() {
     const GGModelDev& m = *x.m;
     const int c = blockIdx.x, G = m.grid;
-    int b, e;
     if (x.mode & GG_RUN_LAYERS) {
       for (int l = 0; l < m.L && ok; l++) {
         const GGLayerW& Lw = m.layers[l];
-        part(m.Q + 2 * m.KV, G, c, b, e);
-        rows(Lw.wqkv, m.rs_h, b, e, m.ph_qkv.rps);
+        rows(Lw.wqkv, m.rs_h, x.S.rows[RG_QKV], x.S.rows[RG_QKV + 1], m.ph_qkv.rps);
         const int rot = (l * x.nsplit) % G, slo = window_lo(Lw, x.pos) / m.pos_per_split;
         for (int s = slo + (c - rot + G) % G; s < x.nsplit && ok; s += G) {
           int p0 = s * m.pos_per_split, pc = min(p0 + m.pos_per_split, x.pos);
@@ -179,17 +184,14 @@ struct Producer {
           size_t off = ((size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + p0) * m.KV) * es;
           issue(m.kcache + off, nb, m.vcache + off, nb, (uint32_t)(m.pos_per_split * m.KV * es));
         }
-        part(m.H, G, c, b, e);
-        rows(Lw.wo, m.rs_q, b, e, m.ph_o.rps);
-        part(m.I, G, c, b, e);
-        rows(Lw.wgu, m.rs_h, 2 * b, 2 * e, 2 * m.pps_gu);
-        part(m.H, G, c, b, e);
-        rows(Lw.wdown, m.rs_i, b, e, m.ph_down.rps);
+        const int hb = x.S.rows[RG_H], he = x.S.rows[RG_H + 1];
+        rows(Lw.wo, m.rs_q, hb, he, m.ph_o.rps);
+        rows(Lw.wgu, m.rs_h, 2 * x.S.rows[RG_I], 2 * x.S.rows[RG_I + 1], 2 * m.pps_gu);
+        rows(Lw.wdown, m.rs_i, hb, he, m.ph_down.rps);
       }
     }
     if ((x.mode & GG_RUN_LM) && ok) {
-      part(m.V, G, c, b, e);
-      rows(m.embd, m.rs_h, b, e, m.ph_lm.rps);
+      rows(m.embd, m.rs_h, x.S.rows[RG_V], x.S.rows[RG_V + 1], m.ph_lm.rps);
     }
     // Drain: wait until every copy issued into the ring has landed before the CTA may exit.
     SpinCtl drain = x.sc;
@@ -520,8 +522,7 @@ struct Consumer {
     }
     cbar();
     trace(l * 6 + 0, 1);
-    int b, e;
-    part(m.Q + 2 * m.KV, m.grid, blockIdx.x, b, e);
+    const int b = x.S.rows[RG_QKV], e = x.S.rows[RG_QKV + 1];
     rows_dispatch(P, m.ph_qkv, b, e, m.H, m.rs_h, EPI_TAG, m.t_qkv, make_tag(x.tagbase, l * PH_PER_LAYER + 0));
   }
 
@@ -741,8 +742,7 @@ struct Consumer {
     planes_tagged(P, m.t_att, make_tag(x.tagbase, l * PH_PER_LAYER + 2), m.Q);
     cbar();
     trace(l * 6 + 3, 1);
-    int b, e;
-    part(m.H, m.grid, blockIdx.x, b, e);
+    const int b = x.S.rows[RG_H], e = x.S.rows[RG_H + 1];
     rows_dispatch(P, m.ph_o, b, e, m.Q, m.rs_q, EPI_TAG, m.t_proj, make_tag(x.tagbase, l * PH_PER_LAYER + 3));
   }
 
@@ -755,8 +755,7 @@ struct Consumer {
                     Lw.ffn_norm, blockIdx.x == 0 ? m.dbg_residual : nullptr, nullptr);
     cbar();
     trace(l * 6 + 4, 1);
-    int b, e;
-    part(m.I, m.grid, blockIdx.x, b, e);
+    const int b = x.S.rows[RG_I], e = x.S.rows[RG_I + 1];
     const uint32_t tag = make_tag(x.tagbase, l * PH_PER_LAYER + 4);
     // gate_i and up_i are adjacent rows: with 8 lanes per row and 2 rows per lane, one lane
     // holds both sums of a pair and applies GeGLU itself (shaders.ts:153-170).
@@ -785,8 +784,7 @@ struct Consumer {
     planes_tagged(P, m.t_act, make_tag(x.tagbase, l * PH_PER_LAYER + 4), m.I);
     cbar();
     trace(l * 6 + 5, 1);
-    int b, e;
-    part(m.H, m.grid, blockIdx.x, b, e);
+    const int b = x.S.rows[RG_H], e = x.S.rows[RG_H + 1];
     rows_dispatch(P, m.ph_down, b, e, m.I, m.rs_i, EPI_TAG, m.t_down, make_tag(x.tagbase, l * PH_PER_LAYER + 5));
   }
 
@@ -822,8 +820,7 @@ struct Consumer {
       plane_quad(P, k, ok, xv);
     }
     cbar();
-    int b, e;
-    part(m.V, m.grid, blockIdx.x, b, e);
+    const int b = x.S.rows[RG_V], e = x.S.rows[RG_V + 1];
     rows_dispatch(P, m.ph_lm, b, e, m.H, m.rs_h, EPI_LOGIT, nullptr, 0);
     cbar();
     const unsigned long long ik = init_lane_key();
@@ -1025,6 +1022,7 @@ GG_DEV void decode_body(const GGModelDev* __restrict__ mp, GGState* __restrict__
   x.S.rcnt = reinterpret_cast<int*>(p); p += 4 * 256;
   x.S.scal = reinterpret_cast<float*>(p); p += 4 * 256;  // 4 rotating csum slots of up to 64
   x.S.flag = reinterpret_cast<int*>(p); p += 16;
+  x.S.rows = reinterpret_cast<int*>(p); p += 4 * RG_N;
 
   const bool bad = x.token < 0 || x.token >= m.V || x.pos < 0 || x.pos >= m.CTX || x.seq < 0 || x.seq >= m.max_seqs;
   if (bad) {
@@ -1040,6 +1038,10 @@ GG_DEV void decode_body(const GGModelDev* __restrict__ mp, GGState* __restrict__
       mbar_init(&x.S.empty[i], NCW);
     }
     mbar_fence_init();
+    part(m.Q + 2 * m.KV, m.grid, blockIdx.x, x.S.rows[RG_QKV], x.S.rows[RG_QKV + 1]);
+    part(m.H, m.grid, blockIdx.x, x.S.rows[RG_H], x.S.rows[RG_H + 1]);
+    part(m.I, m.grid, blockIdx.x, x.S.rows[RG_I], x.S.rows[RG_I + 1]);
+    part(m.V, m.grid, blockIdx.x, x.S.rows[RG_V], x.S.rows[RG_V + 1]);
   }
   __syncthreads();
 

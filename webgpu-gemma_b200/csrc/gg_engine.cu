@@ -266,6 +266,9 @@ static int schedule(gg_engine* e) {
   // gate/up pairs each), so no CTA carries an extra row into every hand-over; measured faster
   // than one CTA per SM (148) on B200.
   m.grid = std::min(e->sm_count, 128);
+  // the decode kernel splits rows as c * M / grid in 32-bit arithmetic
+  if ((long long)m.grid * std::max({m.V, m.Q + 2 * m.KV, m.H, m.I}) >= (1ll << 31))
+    return fail(e, GG_E_ARG, "vocabulary or layer too large for the decode kernel's row split");
   m.stage_bytes = 20480;
   if (m.rs_i > m.stage_bytes || m.rs_q > m.stage_bytes || 4 * m.rs_h > m.stage_bytes)
     return fail(e, GG_E_ARG, "rows too wide for a %d-byte ring stage", m.stage_bytes);
@@ -307,7 +310,7 @@ static int schedule(gg_engine* e) {
   m.tmp_floats = m.Q + 2 * m.KV;
   // keep in step with the carve at the top of gg_decode_kernel
   size_t other = 8 * 256 + (size_t)(3 * m.xs0 + m.xs0 / 4) + (size_t)(3 * m.xs1 + m.xs1 / 4) + 8 * (size_t)m.H +
-                 4 * (size_t)m.tmp_floats + 4 * 1024 + 4 * 256 + 4 * 256 + 16;
+                 4 * (size_t)m.tmp_floats + 4 * 1024 + 4 * 256 + 4 * 256 + 16 + 32;
   cudaFuncAttributes fa;
   GG_CUDA(e, cudaFuncGetAttributes(&fa, decode_fn(m)));
   int optin = 0;
