@@ -65,7 +65,7 @@ def measured_peaks() -> tuple[float, str]:
 
 # ncu capture of the same kernel on this workload (its summary is kept under profiles/):
 # dram bytes read + written per launch, or None before a capture exists.
-NCU_TRAFFIC_PER_LAUNCH = 1103105280 + 4954624  # 1B model, one launch at position 641 (grid 128)
+NCU_TRAFFIC_PER_LAUNCH = 1103156224 + 4640000  # 1B model, one launch at position 641 (grid 128, 5-stage ring)
 
 
 class ClockSampler:
