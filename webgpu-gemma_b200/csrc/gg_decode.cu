@@ -626,24 +626,35 @@ struct Consumer {
         f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
       }
     };
+    // Every position of the split reads a valid row (positions outside [pv, np) read row pv
+    // instead and get weight 0), so the eight dot products, their warp sums and the P.V loads
+    // carry no per-position branch and overlap. Each warp sum keeps the butterfly order, and a
+    // masked position adds an exact zero, so the results equal a loop over the valid rows only.
+    const float scale = m.attn_scale;
     for (int h = warp; h < NQH; h += NCW) {
       const int kvh = h * NKH / NQH;
       float qv[8];
       row8(nullptr, t + h * HD, false, qv);
       float sc[GG_POS_PER_SPLIT];
+#pragma unroll
+      for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+        const int pp = (p >= pv && p < np) ? p : pv;
+        float kf[8];
+        row8(Kst + (size_t)pp * KV + kvh * HD, t + Q + kvh * HD, p0 + pp < x.pos, kf);
+        float d = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) d = fmaf(qv[j], kf[j], d);
+        sc[p] = d;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int p = 0; p < GG_POS_PER_SPLIT; p++) sc[p] += __shfl_xor_sync(0xffffffffu, sc[p], o);
       float mx = -1e30f;
 #pragma unroll
       for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-        sc[p] = 0.f;
-        if (p >= pv && p < np) {
-          float kf[8];
-          row8(Kst + (size_t)p * KV + kvh * HD, t + Q + kvh * HD, p0 + p < x.pos, kf);
-          float d = 0.f;
-#pragma unroll
-          for (int j = 0; j < 8; j++) d = fmaf(qv[j], kf[j], d);
-          sc[p] = warp_sum(d) * m.attn_scale;
-          mx = fmaxf(mx, sc[p]);
-        }
+        sc[p] *= scale;
+        if (p >= pv && p < np) mx = fmaxf(mx, sc[p]);
       }
       float sum = 0.f;
 #pragma unroll
@@ -654,12 +665,11 @@ struct Consumer {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-        if (p >= pv && p < np) {
-          float vf[8];
-          row8(Vst + (size_t)p * KV + kvh * HD, t + Q + KV + kvh * HD, p0 + p < x.pos, vf);
+        const int pp = (p >= pv && p < np) ? p : pv;
+        float vf[8];
+        row8(Vst + (size_t)pp * KV + kvh * HD, t + Q + KV + kvh * HD, p0 + pp < x.pos, vf);
 #pragma unroll
-          for (int j = 0; j < 8; j++) acc[j] = fmaf(sc[p], vf[j], acc[j]);
-        }
+        for (int j = 0; j < 8; j++) acc[j] = fmaf(sc[p], vf[j], acc[j]);
       }
 #pragma unroll
       for (int j = 0; j < 8; j++) tag_store(m.t_o + (size_t)s * Q + h * HD + 8 * lane + j, acc[j], tag);
