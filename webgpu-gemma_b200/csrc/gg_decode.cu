@@ -306,22 +306,29 @@ struct Consumer {
 
   // NV sums over the consumer threads with one barrier; every consumer thread gets the same
   // totals (same summation order everywhere). Scratch slots rotate, so no second barrier.
+  // Only warps 0..nw-1 hold data: the others (whose values are all zero) only take part in
+  // the barrier and leave v as it is; skipping their zero terms leaves every total unchanged.
   template <int NV>
-  GG_DEV void csum(float* v) {
+  GG_DEV void csum(float* v, int nw) {
     float* s = x.S.scal + (cslot & 3) * (16 * NV);
     cslot++;
+    if (warp < nw) {
 #pragma unroll
-    for (int k = 0; k < NV; k++) {
-      const float t = warp_sum(v[k]);
-      if (lane == 0) s[16 * k + warp] = t;
+      for (int k = 0; k < NV; k++) {
+        const float t = warp_sum(v[k]);
+        if (lane == 0) s[16 * k + warp] = t;
+      }
     }
     cbar();
+    if (warp < nw) {
 #pragma unroll
-    for (int k = 0; k < NV; k++) {
-      float t = 0.f;
+      for (int k = 0; k < NV; k++) {
+        float t = 0.f;
 #pragma unroll
-      for (int w = 0; w < NCW; w++) t += s[16 * k + w];
-      v[k] = t;
+        for (int w = 0; w < NCW; w++)
+          if (w < nw) t += s[16 * k + w];
+        v[k] = t;
+      }
     }
   }
 
@@ -370,7 +377,7 @@ struct Consumer {
   GG_DEV void add_norm_planes(const XPlanes& P, const uint64_t* src, uint32_t tag, const float* wa,
                               const float* base, float* out, const float* wb, float* dbg_out, float* dbg_x) {
     const GGModelDev& m = *x.m;
-    const int nq = m.H >> 2, k = tid;
+    const int nq = m.H >> 2, k = tid, nw = (nq + 31) >> 5;
     const bool ok = k < nq;
     float4 fa = make_float4(0.f, 0.f, 0.f, 0.f), fb = fa, fbase = fa;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -391,7 +398,8 @@ struct Consumer {
       s[2] += bv[j] * vw;
       s[3] += vw * vw;
     }
-    csum<4>(s);
+    csum<4>(s, nw);
+    if (warp >= nw) return;  // no element quads in this warp: nothing to normalise or store
     const float r1 = sqrtf(s[0] / (float)m.H + m.eps);
     const float ss_out = s[1] + 2.f * s[2] / r1 + s[3] / (r1 * r1);
     const float r2 = sqrtf(ss_out / (float)m.H + m.eps);
@@ -415,7 +423,7 @@ struct Consumer {
     const GGModelDev& m = *x.m;
     const uint8_t* row = m.embd + (size_t)x.token * m.rs_h;
     const float sq = sqrtf((float)m.H);
-    const int nq = m.H >> 2, k = tid;
+    const int nq = m.H >> 2, k = tid, nw = (nq + 31) >> 5;
     const bool ok = k < nq;
     float o[4] = {0.f, 0.f, 0.f, 0.f};
     float4 fb = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -433,7 +441,8 @@ struct Consumer {
       }
       reinterpret_cast<float4*>(x.S.hid)[k] = make_float4(o[0], o[1], o[2], o[3]);
     }
-    csum<1>(s);
+    csum<1>(s, nw);
+    if (warp >= nw) return;
     const float r = sqrtf(s[0] / (float)m.H + m.eps);
     const float wbv[4] = {fb.x, fb.y, fb.z, fb.w};
     float xv[4];
@@ -807,7 +816,7 @@ struct Consumer {
                       x.S.res, x.S.hid, m.out_norm, blockIdx.x == 0 ? m.dbg_hidden : nullptr,
                       blockIdx.x == 0 ? m.dbg_normed : nullptr);
     } else {  // LM head on the hidden state a previous launch left behind
-      const int nq = m.H >> 2, k = tid;
+      const int nq = m.H >> 2, k = tid, nw = (nq + 31) >> 5;
       const bool ok = k < nq;
       float h[4] = {0.f, 0.f, 0.f, 0.f};
       float4 fw = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -820,14 +829,16 @@ struct Consumer {
         for (int j = 0; j < 4; j++) s[0] += h[j] * h[j];
         reinterpret_cast<float4*>(x.S.hid)[k] = f;
       }
-      csum<1>(s);
-      const float r = sqrtf(s[0] / (float)m.H + m.eps);
-      const float wv[4] = {fw.x, fw.y, fw.z, fw.w};
-      float xv[4];
+      csum<1>(s, nw);
+      if (warp < nw) {
+        const float r = sqrtf(s[0] / (float)m.H + m.eps);
+        const float wv[4] = {fw.x, fw.y, fw.z, fw.w};
+        float xv[4];
 #pragma unroll
-      for (int j = 0; j < 4; j++) xv[j] = h[j] * wv[j] / r;
-      if (ok && blockIdx.x == 0) reinterpret_cast<float4*>(m.dbg_normed)[k] = make_float4(xv[0], xv[1], xv[2], xv[3]);
-      plane_quad(P, k, ok, xv);
+        for (int j = 0; j < 4; j++) xv[j] = h[j] * wv[j] / r;
+        if (ok && blockIdx.x == 0) reinterpret_cast<float4*>(m.dbg_normed)[k] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+        plane_quad(P, k, ok, xv);
+      }
     }
     cbar();
     const int b = x.S.rows[RG_V], e = x.S.rows[RG_V + 1];
