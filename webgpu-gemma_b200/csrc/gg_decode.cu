@@ -31,6 +31,7 @@ namespace gg {
 constexpr int NCW = GG_NCW;
 constexpr int NCT = GG_NCT;
 constexpr int PH_PER_LAYER = 6;
+constexpr uint32_t NS = GG_RING_STAGES;  // ring slots (GGModelDev::nstages holds the same value)
 
 GG_DEV void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
 
@@ -151,8 +152,8 @@ struct Producer {
 
   GG_DEV void issue(const void* s0, uint32_t b0, const void* s1, uint32_t b1, uint32_t off1) {
     const GGModelDev& m = *x.m;
-    int slot = x.idx % m.nstages;
-    uint32_t use = x.idx / m.nstages;
+    int slot = x.idx % NS;
+    uint32_t use = x.idx / NS;
     if (use > 0 && ok) ok = mbar_wait(&x.S.empty[slot], (use - 1) & 1, x.sc);
     if (!ok) return;
     uint8_t* dst = x.S.ring + (size_t)slot * m.stage_bytes;
@@ -195,10 +196,10 @@ struct Producer {
     }
     // Drain: wait until every copy issued into the ring has landed before the CTA may exit.
     SpinCtl drain = x.sc;
-    uint32_t n = x.idx < (uint32_t)m.nstages ? x.idx : (uint32_t)m.nstages;
+    uint32_t n = x.idx < NS ? x.idx : NS;
     for (uint32_t k = x.idx - n; k < x.idx; k++) {
-      int slot = k % m.nstages;
-      uint32_t par = (k / m.nstages) & 1;
+      int slot = k % NS;
+      uint32_t par = (k / NS) & 1;
       uint64_t t0 = global_timer_ns();
       while (!mbar_try_wait(&x.S.full[slot], par)) {
         if (global_timer_ns() - t0 > drain.timeout_ns) { atomicOr(drain.err, GG_ERR_WAIT_MBAR); break; }
@@ -223,11 +224,11 @@ struct Consumer {
 
   GG_DEV uint8_t* stage_acquire() {
     const GGModelDev& m = *x.m;
-    int slot = x.idx % m.nstages;
+    int slot = x.idx % NS;
     if (!dead) {
       const bool tr = (x.mode & GG_TRACE) && tid == 0;
       const uint64_t t0 = tr ? global_timer_ns() : 0;
-      bool ok = mbar_wait(&x.S.full[slot], (x.idx / m.nstages) & 1, x.sc);
+      bool ok = mbar_wait(&x.S.full[slot], (x.idx / NS) & 1, x.sc);
       dead = !__all_sync(0xffffffffu, ok);
       if (tr) ring_wait_ns += global_timer_ns() - t0;
       if (tr && blockIdx.x == 0 && x.idx < 480) {  // stage acquire times of warp 0 (CTA 0)
@@ -239,7 +240,7 @@ struct Consumer {
   }
   GG_DEV void stage_release() {
     __syncwarp();
-    if (lane == 0 && !dead) mbar_arrive(&x.S.empty[x.idx % x.m->nstages]);
+    if (lane == 0 && !dead) mbar_arrive(&x.S.empty[x.idx % NS]);
     x.idx++;
   }
 
@@ -842,7 +843,10 @@ struct Consumer {
     }
     cbar();
     const int b = x.S.rows[RG_V], e = x.S.rows[RG_V + 1];
-    rows_dispatch(P, m.ph_lm, b, e, m.H, m.rs_h, EPI_LOGIT, nullptr, 0);
+    // Two rows per 8-lane group: each load of the x planes serves both rows' dot products,
+    // halving the LM head's shared-memory reads of the planes (each row's sum is unchanged).
+    if (m.ph_lm.gs == 8 && m.ph_lm.r == 2) rows_phase<8, 2>(P, b, e, m.ph_lm.rps, m.H, m.rs_h, 1, EPI_LOGIT, nullptr, 0);
+    else rows_dispatch(P, m.ph_lm, b, e, m.H, m.rs_h, EPI_LOGIT, nullptr, 0);
     cbar();
     const unsigned long long ik = init_lane_key();
     for (int i = tid; i < 256; i += NCT)
@@ -1025,9 +1029,9 @@ GG_DEV void decode_body(const GGModelDev* __restrict__ mp, GGState* __restrict__
   x.idx = 0;
   // carve shared memory (sizes: GGModelDev::smem_bytes, computed by the host the same way)
   uint8_t* p = smem;
-  x.S.ring = p; p += (size_t)m.nstages * m.stage_bytes;
-  x.S.full = reinterpret_cast<uint64_t*>(p); p += 8 * m.nstages;
-  x.S.empty = reinterpret_cast<uint64_t*>(p); p += 8 * m.nstages;
+  x.S.ring = p; p += (size_t)NS * m.stage_bytes;
+  x.S.full = reinterpret_cast<uint64_t*>(p); p += 8 * NS;
+  x.S.empty = reinterpret_cast<uint64_t*>(p); p += 8 * NS;
   x.S.keys = reinterpret_cast<unsigned long long*>(p); p += 8 * 256;
   const int xsz[2] = {m.xs0, m.xs1};
   for (int b = 0; b < 2; b++) {
@@ -1054,7 +1058,7 @@ GG_DEV void decode_body(const GGModelDev* __restrict__ mp, GGState* __restrict__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < m.nstages; i++) {
+    for (int i = 0; i < (int)NS; i++) {
       mbar_init(&x.S.full[i], 1);
       mbar_init(&x.S.empty[i], NCW);
     }

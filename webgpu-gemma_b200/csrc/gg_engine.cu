@@ -295,7 +295,7 @@ static int schedule(gg_engine* e) {
   m.ph_qkv = pick(m.Q + 2 * m.KV, m.H, m.rs_h, true, 1);
   m.ph_o = pick(m.H, m.Q, m.rs_q, true, 1);
   m.ph_down = pick(m.H, m.I, m.rs_i, true, 1);
-  m.ph_lm = pick(m.V, m.H, m.rs_h, false, 1);
+  m.ph_lm = pick(m.V, m.H, m.rs_h, false, 2);  // two rows per lane group (1.150 -> 1.134 ms per token)
   if (m.pps_gu < 4 || m.rs_i > m.stage_bytes) return fail(e, GG_E_ARG, "rows too wide for a %d-byte ring stage", m.stage_bytes);
   if (m.H / 4 > GG_NCT) return fail(e, GG_E_ARG, "hidden_size above %d", 4 * GG_NCT);
   if (m.HD != GG_HEAD_DIM) return fail(e, GG_E_ARG, "head_dim must be %d (Gemma 3)", GG_HEAD_DIM);
@@ -316,13 +316,14 @@ static int schedule(gg_engine* e) {
   int optin = 0;
   GG_CUDA(e, cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->device));
   long avail = (long)optin - (long)fa.sharedSizeBytes - (long)other;
-  // Five stages: enough for the largest per-CTA share of a phase that must be resident at once
-  // (the 1B down projection: 5 stages). A deeper ring buys no bandwidth and takes shared memory
-  // from L1: at 5 stages the kernel fits the 164 KB shared-memory carveout (L1 92 KB instead of
-  // 28 KB at 8 stages). Measured on the 1B model: 8 / 7 / 6 / 5 / 4 / 3 stages = 1.209 / 1.202 /
-  // 1.195 / 1.187 / 1.273 / 1.358 ms per token.
-  int ns = (int)std::min<long>(5, avail / (m.stage_bytes + 16));
-  if (ns < 2) return fail(e, GG_E_ARG, "not enough shared memory for the weight ring (%ld bytes left)", avail);
+  // GG_RING_STAGES (five): enough for the largest per-CTA share of a phase that must be
+  // resident at once (the 1B down projection: 5 stages). A deeper ring buys no bandwidth and
+  // takes shared memory from L1: at 5 stages the kernel fits the 164 KB shared-memory carveout
+  // (L1 92 KB instead of 28 KB at 8 stages). Measured on the 1B model: 8 / 7 / 6 / 5 / 4 / 3
+  // stages = 1.209 / 1.202 / 1.195 / 1.187 / 1.273 / 1.358 ms per token.
+  const int ns = GG_RING_STAGES;
+  if (avail / (m.stage_bytes + 16) < ns)
+    return fail(e, GG_E_ARG, "not enough shared memory for the %d-stage weight ring (%ld bytes left)", ns, avail);
   m.nstages = ns;
   m.smem_bytes = (int)(other + (size_t)ns * (m.stage_bytes + 16));
   GG_CUDA(e, cudaFuncSetAttribute(decode_fn(m), cudaFuncAttributeMaxDynamicSharedMemorySize, m.smem_bytes));

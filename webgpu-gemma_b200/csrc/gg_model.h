@@ -16,6 +16,8 @@
 #define GG_NCT (GG_NCW * 32)          // consumer threads
 #define GG_HEAD_DIM 256                // Gemma 3 head size (compile-time for the attention phase)
 #define GG_POS_PER_SPLIT 8             // KV positions per attention split
+#define GG_RING_STAGES 5               // decode kernel's weight ring depth (compile-time: the ring
+                                       // index math runs in every warp at every stage)
 #define GG_TRACE_PHASES 512            // phases traced per CTA by GG_TRACE launches (4 stamps each)
 
 static inline int gg_row_stride(int K) { return ((K + (K / 32) * 2) + 15) / 16 * 16; }
