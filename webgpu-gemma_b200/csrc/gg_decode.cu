@@ -311,25 +311,27 @@ struct Consumer {
   // the barrier and leave v as it is; skipping their zero terms leaves every total unchanged.
   template <int NV>
   GG_DEV void csum(float* v, int nw) {
-    float* s = x.S.scal + (cslot & 3) * (16 * NV);
+    // slot layout [warp][4]: a warp's NV (<= 4) partials are one 16-byte store and load
+    static_assert(NV <= 4, "at most four sums per call");
+    float4* s = reinterpret_cast<float4*>(x.S.scal) + (cslot & 3) * 16;
     cslot++;
     if (warp < nw) {
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < NV; k++) {
-        const float t = warp_sum(v[k]);
-        if (lane == 0) s[16 * k + warp] = t;
-      }
+      for (int k = 0; k < NV; k++) t[k] = warp_sum(v[k]);
+      if (lane == 0) s[warp] = make_float4(t[0], t[1], t[2], t[3]);
     }
     cbar();
     if (warp < nw) {
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < NV; k++) {
-        float t = 0.f;
+      for (int w = 0; w < NCW; w++)
+        if (w < nw) {
+          const float4 f = s[w];
+          t[0] += f.x; t[1] += f.y; t[2] += f.z; t[3] += f.w;
+        }
 #pragma unroll
-        for (int w = 0; w < NCW; w++)
-          if (w < nw) t += s[16 * k + w];
-        v[k] = t;
-      }
+      for (int k = 0; k < NV; k++) v[k] = t[k];
     }
   }
 
@@ -345,15 +347,14 @@ struct Consumer {
     if (!ok) return;
     const int e = max((int)((__float_as_uint(mx) >> 23) & 255) - 126, -100);
     const float s = __int_as_float((127 + 23 - e) << 23);
-    uint32_t b0 = 0, b1 = 0, b2 = 0;
+    uint32_t X[4];
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      int X = __float2int_rn(v[j] * s);
-      X = min(max(X, -8388607), 8388607);
-      b0 |= (uint32_t)((X >> 16) & 255) << (8 * j);
-      b1 |= (uint32_t)((X >> 8) & 255) << (8 * j);
-      b2 |= (uint32_t)(X & 255) << (8 * j);
-    }
+    for (int j = 0; j < 4; j++) X[j] = (uint32_t)min(max(__float2int_rn(v[j] * s), -8388607), 8388607);
+    // byte b of X[j] goes to byte j of plane 2 - b (b = 0, 1, 2: the 24-bit two's complement)
+    const uint32_t lo01 = __byte_perm(X[0], X[1], 0x5140), lo23 = __byte_perm(X[2], X[3], 0x5140);
+    const uint32_t hi01 = __byte_perm(X[0], X[1], 0x0062), hi23 = __byte_perm(X[2], X[3], 0x0062);
+    const uint32_t b2 = __byte_perm(lo01, lo23, 0x5410), b1 = __byte_perm(lo01, lo23, 0x7632);
+    const uint32_t b0 = __byte_perm(hi01, hi23, 0x5410);
     reinterpret_cast<uint32_t*>(P.p0)[k] = b0;
     reinterpret_cast<uint32_t*>(P.p1)[k] = b1;
     reinterpret_cast<uint32_t*>(P.p2)[k] = b2;
