@@ -53,6 +53,11 @@ class GemmaEngine:
             self._mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
         parsed = gguf.parse(memoryview(self._mm))
         gguf.update_config_from_gguf(parsed, self.config, context_length)
+        # The reference keeps vocab_size at 262,144, the size of every Gemma 3 GGUF; taking it from
+        # the embedding's row count gives the same value for those and also loads other sizes.
+        embd = next((t for t in parsed.tensors if t.name == "token_embd.weight"), None)
+        if embd is not None and len(embd.dims) == 2:
+            self.config.vocab_size = int(embd.dims[1])
         # options beyond the reference's: KV element type, Gemma 3's sliding window + local theta
         self.config.kv_dtype = kv_dtype
         if spec:
