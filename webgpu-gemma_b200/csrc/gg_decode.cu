@@ -305,8 +305,8 @@ struct Consumer {
     v[3] = __uint_as_float((uint32_t)w3);
   }
 
-  // NV sums over the consumer threads with one barrier; every consumer thread gets the same
-  // totals (same summation order everywhere). Scratch slots rotate, so no second barrier.
+  // NV sums over the consumer threads with one barrier; every thread of warps 0..nw-1 gets the
+  // same totals (same summation order everywhere). Scratch slots rotate, so no second barrier.
   // Only warps 0..nw-1 hold data: the others (whose values are all zero) only take part in
   // the barrier and leave v as it is; skipping their zero terms leaves every total unchanged.
   template <int NV>
@@ -1046,7 +1046,7 @@ GG_DEV void decode_body(const GGModelDev* __restrict__ mp, GGState* __restrict__
   x.S.tmp = reinterpret_cast<float*>(p); p += 4 * (size_t)m.tmp_floats;
   x.S.red = reinterpret_cast<float*>(p); p += 4 * 1024;
   x.S.rcnt = reinterpret_cast<int*>(p); p += 4 * 256;
-  x.S.scal = reinterpret_cast<float*>(p); p += 4 * 256;  // 4 rotating csum slots of up to 64
+  x.S.scal = reinterpret_cast<float*>(p); p += 4 * 256;  // 4 rotating csum slots of 16 warps x float4
   x.S.flag = reinterpret_cast<int*>(p); p += 16;
   x.S.rows = reinterpret_cast<int*>(p); p += 4 * RG_N;
 
