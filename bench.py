@@ -155,12 +155,17 @@ def dist_setup(n_gpus: int):
     return rank, local, world, None, None
 
 
-def cpu_oracle_rate(tensors, cfg, n_tokens: int, prompt_len: int = 4):
-    """Decode tok/s of the CPU restatement on a bounded sample; returns (tok/s, threads, sample)."""
+def cpu_oracle_rate(tensors, cfg, n_tokens: int, prompt_len: int = 4, threads: int | None = None):
+    """Decode tok/s of the CPU restatement on a bounded sample, on every host core (threads=None)
+    or on `threads` threads; returns (tok/s, threads, sample)."""
     from oracle import oracle
     from gemma_b200 import synth
 
-    threads = oracle.use_all_host_cores()
+    if threads is None:
+        threads = oracle.use_all_host_cores()
+    else:
+        oracle.lib().or_set_threads(int(threads))
+        threads = int(oracle.lib().or_get_threads())
     m = oracle.OracleModel.from_tensors(cfg, tensors)
     prompt = synth.make_prompt(SEED, prompt_len, cfg.vocab_size)
     for i, t in enumerate(prompt):
@@ -575,6 +580,7 @@ def main():
     achieved = algo / per_launch_s / 1e9
     peak, peak_kind = measured_peaks()
     cpu_v, cpu_threads, cpu_sample = cpu_oracle_rate(tensors, cfg, args.cpu_tokens)
+    cpu_v1, _, cpu_sample1 = cpu_oracle_rate(tensors, cfg, min(args.cpu_tokens, 2), prompt_len=1, threads=1)
     ttft_p50 = statistics.median(ttft_wall)
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -590,7 +596,7 @@ def main():
                      "peak_kind": peak_kind, "kernel": "gg_decode_kernel",
                      "algo_bytes_per_launch": int(algo)},
         "cpu_baseline": {"value": round(cpu_v, 3), "unit": UNIT, "cores": cpu_threads, "kind": "port",
-                         "sample": cpu_sample},
+                         "sample": cpu_sample, "value_1_thread": round(cpu_v1, 3), "sample_1_thread": cpu_sample1},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": STATE_H2D_BYTES,
                 "d2h_bytes_per_step": STATE_D2H_BYTES},
         "gpu_launches": args.steps,
