@@ -127,7 +127,7 @@ int gg_reset_kv(gg_engine* eng, int seq);
  * 2 split combine, 3 O projection, 4 gate/up, 5 down), phase 6*L = LM head; event 0 = enter,
  * 1 = inputs arrived, 2 = done. gg_read_trace copies the first n stamps. */
 int gg_set_trace(gg_engine* eng, int on);
-/* Number of CTAs (one per SM) of the persistent step kernel. */
+/* Number of CTAs of the persistent step kernel (at most one per SM; 128 on a B200). */
 int gg_grid(gg_engine* eng, int* out);
 int gg_read_trace(gg_engine* eng, uint64_t* out, int n);
 
