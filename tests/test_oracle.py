@@ -252,3 +252,36 @@ def test_oracle_sliding_window_semantics():
     assert (run(dataclasses.replace(cfg, sliding_window=64)) == base).all()
     assert (run(dataclasses.replace(cfg, sliding_window=4, swa_period=1)) == base).all()
     assert not (run(dataclasses.replace(cfg, sliding_window=4)) == base).all()
+
+
+def test_sampler_known_answers(oracle_mod):
+    """Hand-computed cases of engine.ts:862-901, independent of both restatements."""
+    from oracle import oracle_np
+    vocab = 1024
+    ids = np.arange(256, dtype=np.uint32) + 500
+    low = np.float32(-1e30)  # candidates that contribute exp(-inf) = 0
+
+    def both(vals, T, top_p, rep, seen, u):
+        a = oracle_mod.sample(vals, ids, T, top_p, rep, list(seen), u, vocab)
+        b = oracle_np.sample(vals, ids, T, top_p, rep, set(seen), u)
+        assert a == b
+        return a
+
+    # repetition penalty: a seen positive logit is divided (2.0 / 1.25 = 1.6 < 1.9) ...
+    v = np.full(256, low, np.float32)
+    v[0], v[1] = 2.0, 1.9
+    assert both(v, 0.0, 0.9, 1.0, [], 0.0) == 500           # no penalty: greedy fast path
+    assert both(v, 0.0, 0.9, 1.25, [500], 0.0) == 501       # penalised: the other candidate wins
+    # ... and a seen negative logit is multiplied (-1.0 * 1.25 = -1.25 < -1.1)
+    v[0], v[1] = -1.0, -1.1
+    assert both(v, 0.0, 0.9, 1.25, [500], 0.0) == 501
+    # ties keep lane order (the sort is stable)
+    v[0], v[1] = 0.5, 0.5
+    assert both(v, 0.0, 0.9, 1.5, [700], 0.0) == 500
+    # top-p: probs 1, 1/2, 1/4 (T = 1), shares 4/7, 2/7, 1/7; top_p 0.8 keeps two (4/7 < 0.8 <= 6/7)
+    v = np.full(256, low, np.float32)
+    v[0], v[1], v[2] = 0.0, np.float32(np.log(0.5)), np.float32(np.log(0.25))
+    assert both(v, 1.0, 0.8, 1.0, [], 0.6) == 500            # r = 0.6 * 1.5 = 0.9; 0.9 - 1 <= 0
+    assert both(v, 1.0, 0.8, 1.0, [], 0.7) == 501            # r = 1.05; 1.05 - 1 > 0; 0.05 - 0.5 <= 0
+    assert both(v, 1.0, 0.8, 1.0, [], 0.999999) == 501       # the third candidate is cut off
+    assert both(v, 1.0, 1.0, 1.0, [], 0.999999) == 502       # top_p 1 keeps all three
