@@ -285,3 +285,46 @@ def test_sampler_known_answers(oracle_mod):
     assert both(v, 1.0, 0.8, 1.0, [], 0.7) == 501            # r = 1.05; 1.05 - 1 > 0; 0.05 - 0.5 <= 0
     assert both(v, 1.0, 0.8, 1.0, [], 0.999999) == 501       # the third candidate is cut off
     assert both(v, 1.0, 1.0, 1.0, [], 0.999999) == 502       # top_p 1 keeps all three
+
+
+def test_ops_known_answers(oracle_mod):
+    """Each op against its formula evaluated in float64 (shaders.ts; see the op's reference lines)."""
+    rng = np.random.default_rng(21)
+    n = 640
+    x = rng.standard_normal(n).astype(np.float32)
+    w = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    res = rng.standard_normal(n).astype(np.float32)
+    x64, w64 = x.astype(np.float64), w.astype(np.float64)
+    rms = np.sqrt(np.mean(x64 * x64) + 1e-6)
+    # rmsNorm is x * w / rms (shaders.ts:25-56): zero weights give zeros (not Gemma's (1 + w))
+    assert rel_l2(oracle_mod.rmsnorm(x, w), x64 * w64 / rms) < 1e-6
+    assert (oracle_mod.rmsnorm(x, np.zeros(n, np.float32)) == 0).all()
+    # fusedNormAdd: res + x * w / rms(x) (shaders.ts:386-418)
+    assert rel_l2(oracle_mod.fused_norm_add(x, w, res), res + x64 * w64 / rms) < 1e-6
+    # GeGLU with the argument clamp at +-15 (shaders.ts:153-170)
+    g = np.array([0.0, 1.0, -1.0, 20.0, -20.0], np.float32)
+    u = np.array([3.0, 2.0, 2.0, 0.5, 0.5], np.float32)
+    t = np.clip(0.7978845608028654 * g * (1 + 0.044715 * g.astype(np.float64) ** 2), -15, 15)
+    want = 0.5 * g * (1 + np.tanh(t)) * u
+    got = oracle_mod.gelu_mul(g, u).astype(np.float64)
+    assert np.allclose(got, want, rtol=1e-6, atol=1e-12)
+    assert got[3] == pytest.approx(10.0, rel=1e-6) and abs(got[4]) < 1e-9
+    # per-head norm + RoPE (shaders.ts:420-467): position 0 is the norm alone; at pos p the pair
+    # (i, i + 128) turns by p * theta^(-2i/256)
+    hd = 256
+    d = rng.standard_normal(hd).astype(np.float32)
+    wn = (rng.standard_normal(hd) * 0.1 + 1.0).astype(np.float32)
+    d64 = d.astype(np.float64)
+    normed = d64 * wn.astype(np.float64) / np.sqrt(np.mean(d64 * d64) + 1e-6)
+    assert rel_l2(oracle_mod.fused_norm_rope(d, wn, 1, hd, 1e-6, 0, 1e6), normed) < 1e-6
+    pos, theta = 37, 1e4
+    ang = pos * theta ** (-2.0 * np.arange(hd // 2) / hd)
+    a0, a1 = normed[:hd // 2], normed[hd // 2:]
+    rot = np.concatenate([a0 * np.cos(ang) - a1 * np.sin(ang), a0 * np.sin(ang) + a1 * np.cos(ang)])
+    assert rel_l2(oracle_mod.fused_norm_rope(d, wn, 1, hd, 1e-6, pos, theta), rot) < 1e-5
+    # attention over one key returns that key's value row for every head (softmax of one score)
+    q = rng.standard_normal(4 * hd).astype(np.float32)
+    kc = rng.standard_normal((1, hd)).astype(np.float32)
+    vc = rng.standard_normal((1, hd)).astype(np.float32)
+    out = oracle_mod.attention(q, kc, vc, 4, 1, hd, 1, 0.0625).reshape(4, hd)
+    assert (out == vc[0]).all()
