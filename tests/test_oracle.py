@@ -328,3 +328,25 @@ def test_ops_known_answers(oracle_mod):
     vc = rng.standard_normal((1, hd)).astype(np.float32)
     out = oracle_mod.attention(q, kc, vc, 4, 1, hd, 1, 0.0625).reshape(4, hd)
     assert (out == vc[0]).all()
+
+
+def test_linear_q8_and_embedding_known_answers(oracle_mod):
+    """linearQ8 (shaders.ts:92-151): y[m] = sum over blocks of (sum_j q * x) * d; embedding
+    (shaders.ts:2-23): h = q * d * sqrt(H). Small integers and power-of-two scales keep every
+    step exact, so the expected values are exact."""
+    def block(d_f16_bits, q):
+        return np.concatenate([np.array([d_f16_bits & 255, d_f16_bits >> 8], np.uint8),
+                               np.asarray(q, np.int8).view(np.uint8)])
+    n, m = 64, 2                        # two rows of two blocks each
+    q = np.arange(-16, 16, dtype=np.int8)
+    raw = np.concatenate([block(0x3C00, q), block(0x4000, -q),        # row 0: d = 1, then d = 2
+                          block(0x3800, np.ones(32)), block(0x3400, 2 * np.ones(32))])  # row 1: 0.5, 0.25
+    packed = oracle_mod.pack_q8_0(raw)
+    x = np.concatenate([np.ones(32), np.arange(32)]).astype(np.float32)
+    y = oracle_mod.linear_q8(x, packed, m, n)
+    want0 = q.astype(np.int64).sum() * 1.0 + (-q.astype(np.int64) * np.arange(32)).sum() * 2.0
+    want1 = 32 * 0.5 + 2 * np.arange(32).sum() * 0.25
+    assert y.tolist() == [float(want0), float(want1)]
+    # embedding row 1 of a [2][64] table: h = q * d * sqrt(64) = q * d * 8
+    h = oracle_mod.embedding(packed, n, 1)
+    assert h.tolist() == [0.5 * 8.0] * 32 + [2 * 0.25 * 8.0] * 32
