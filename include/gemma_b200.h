@@ -55,12 +55,13 @@ typedef struct {
   int32_t sliding_window;
 } gg_config;
 
-/* Sampling options of one step: GenerateOptions (src/types.ts:65-78). */
+/* Sampling options of one step: GenerateOptions (src/types.ts:65-78). Doubles, as the
+ * reference's sampler computes in JS numbers (engine.ts:868-899): 0.7, 0.9 and 1.2 reach the
+ * kernel without an f32 rounding. */
 typedef struct {
-  float temperature; /* 0 = greedy */
-  float top_p;
-  float rep_penalty; /* 1.0 = none */
-  float pad_;
+  double temperature; /* 0 = greedy */
+  double top_p;
+  double rep_penalty; /* 1.0 = none */
 } gg_sample;
 
 /* Replaces initWebGPU + createWorkBuffers (engine.ts:124-138, 402-448): binds the engine
@@ -115,6 +116,14 @@ int gg_get_kv(gg_engine* eng, int seq, int layer, int pos, int which, float* out
  * 6 residual, 7 final-normed hidden, 8 logits. */
 int gg_debug_read(gg_engine* eng, int which, float* out, int n);
 
+/* Parity aid for the weight upload (packQ8_0ForGPU + f16ToF32, gguf.ts:95-149): the n = K
+ * values of row `row` of one Q8_0 matrix as the device holds it, dequantised as f32(q) *
+ * f32(d) -- the exact products every kernel multiplies. which: 0 fused Q|K|V, 1 O, 2 gate/up
+ * (gate_i at row 2i, up_i at 2i+1), 3 down, 4 token_embd / tied LM head (layer ignored).
+ * copy: 0 the row format the decode kernel streams, 1 the tiled copy the tensor-core GEMM
+ * reads (GG_E_STATE when the model's shapes give it none). */
+int gg_dequant_row(gg_engine* eng, int which, int layer, int row, int copy, float* out, int n);
+
 /* Repetition-penalty set of `seq` (allTokens, engine.ts:989-994): reset / add ids. */
 int gg_seen_reset(gg_engine* eng, int seq);
 int gg_seen_add(gg_engine* eng, int seq, const int32_t* ids, int n);
@@ -163,8 +172,9 @@ int gg_last_device_ms(gg_engine* eng, float* ms);
 /* dispose (engine.ts:1039-1077). */
 int gg_destroy(gg_engine* eng);
 
-/* Message of the engine's last failure ("" if none). eng = NULL gives the last failure of a
- * call without an engine (gg_create, gg_sample_logits_noalloc). */
+/* Message of the engine's last failure ("" if none). eng = NULL gives the calling thread's last
+ * failure of a call without an engine (gg_create, gg_sample_logits_noalloc); that message is
+ * kept per thread and stays valid until the same thread's next such failure. */
 const char* gg_last_error(const gg_engine* eng);
 
 /* Sampling from logits the caller already holds on the GPU, with no memory allocation.
@@ -180,14 +190,16 @@ const char* gg_last_error(const gg_engine* eng);
  *               repetition penalty (tokens generated this turn); NULL = no tokens
  *   sp, uniform sampling parameters and the draw, as for gg_sample_last
  *   out_token   device pointer, receives the sampled token
- *   stream      a cudaStream_t, or NULL for the default stream
+ *   stream      a cudaStream_t of the current device (another device's stream is rejected
+ *               with GG_E_ARG), or NULL for the default stream
  * Asynchronous: *out_token is written when the stream reaches the kernel. Its scratch is one
  * static 256 KiB device array (held by every GPU that loads this library until the process
- * exits). The first call on a device looks up that array's device address, so make it before
- * any stream capture on that device. All calls on a device share the array: calls that can
- * run at the same time on the GPU (different streams, or threads without ordering) race and
- * must be serialised by the caller. Errors: GG_E_ARG / GG_E_CUDA, message from
- * gg_last_error(NULL). */
+ * exits). The first call on a device -- and the first in a new context on it, e.g. after
+ * cudaDeviceReset -- looks up that array's device address, so make it before any stream
+ * capture on that device. All calls on a device share the array: calls that can run at the
+ * same time on the GPU (different streams, or threads without ordering) race and must be
+ * serialised by the caller. Errors: GG_E_ARG / GG_E_CUDA, message from gg_last_error(NULL),
+ * which is kept per calling thread. */
 int gg_sample_logits_noalloc(const float* logits, int vocab, const uint32_t* seen_bits, const gg_sample* sp,
                              double uniform, int32_t* out_token, void* stream);
 

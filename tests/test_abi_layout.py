@@ -15,7 +15,7 @@ from conftest import ROOT
 CONFIG_FIELDS = ["hidden_size", "q_dim", "kv_dim", "num_q_heads", "num_kv_heads", "head_dim",
                  "intermediate_size", "vocab_size", "num_layers", "context_length", "rms_norm_eps",
                  "rope_theta_global", "rope_theta_swa", "swa_period", "max_seqs", "flags", "sliding_window"]
-SAMPLE_FIELDS = ["temperature", "top_p", "rep_penalty", "pad_"]
+SAMPLE_FIELDS = ["temperature", "top_p", "rep_penalty"]
 CONSTANTS = ["GG_OK", "GG_E_ARG", "GG_E_CUDA", "GG_E_STATE", "GG_E_DEVICE", "GG_E_NOMEM",
              "GG_FLAG_SERIAL_PREFILL", "GG_FLAG_KV_BF16"]
 

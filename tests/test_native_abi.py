@@ -63,7 +63,7 @@ def test_bad_config_rejected(lib):
 def test_noalloc_sampler_rejects_oversize_vocab(lib):
     """The size check comes before any CUDA call, so it runs without a GPU."""
     from gemma_b200.native import GGSample
-    s = GGSample(0.0, 0.9, 1.0, 0.0)
+    s = GGSample(0.0, 0.9, 1.0)
     out = ctypes.c_int32()
     rc = lib.gg_sample_logits_noalloc(ctypes.c_void_p(16), 524289, None, ctypes.byref(s), 0.0,
                                       ctypes.byref(out), None)

@@ -108,18 +108,66 @@ def test_topk256_and_argmax_rules(oracle_mod):
     # lane 3 holds the max twice (indices 3 and 259): first index wins inside a lane
     lg[3] = 2.0
     lg[259] = 2.0
-    # lane 1 holds an equal max at a larger index: lower lane wins across lanes
+    # lane 1 holds an equal max at a larger index. Across lanes the shader's tree (strides 128,
+    # 64, ..., 1, the lower slot kept on a tie) prefers the smallest bit-reversed lane index:
+    # bitrev8(1) = 128 < bitrev8(3) = 192, so lane 1 wins here
     lg[257] = 2.0
     lg[10] = np.nan  # NaN is never selected
     v, i = oracle_mod.topk256(lg)
     assert i[3] == 3 and i[1] == 257 and v[3] == 2.0
-    assert oracle_mod.argmax(lg) == 257  # lane 1 < lane 3
+    assert oracle_mod.argmax(lg) == 257
     assert oracle_np.argmax(lg) == 257
     # values at or below the -1e30 init never replace it (strict '>' from (-1e30, 0))
     lg2 = np.full(512, -1e30, np.float32)
     v2, i2 = oracle_mod.topk256(lg2)
     assert (i2 == 0).all() and (v2 == np.float32(-1e30)).all()
     assert oracle_mod.argmax(lg2) == 0
+
+
+def bitrev8(x: int) -> int:
+    return int(f"{x:08b}"[::-1], 2)
+
+
+def tree_argmax(lg) -> int:
+    """src/shaders.ts:327-361 written as plain loops: lane maxima with strict '>', then the
+    stride-halving tree that keeps the lower slot on a tie."""
+    m, ix = [np.float32(-1e30)] * 256, [0] * 256
+    for i, v in enumerate(np.asarray(lg, np.float32)):
+        if v > m[i % 256]:
+            m[i % 256], ix[i % 256] = v, i
+    stride = 128
+    while stride:
+        for t in range(stride):
+            if m[t + stride] > m[t]:
+                m[t], ix[t] = m[t + stride], ix[t + stride]
+        stride >>= 1
+    return ix[0]
+
+
+@pytest.mark.parametrize("lanes,winner", [((1, 2), 2), ((3, 5), 5), ((2, 1), 2), ((0, 128), 0),
+                                          ((128, 64), 128), ((255, 127), 127), ((6, 10, 12), 12)])
+def test_argmax_tie_across_lanes_follows_the_tree(oracle_mod, lanes, winner):
+    """Equal maxima in several lanes: the reference's tree reduce returns the lane with the
+    smallest bit-reversed index (lanes 1 and 2 tied -> lane 2), not the lowest lane."""
+    from oracle import oracle_np
+    lg = np.full(1024, -3.0, np.float32)
+    for k, lane in enumerate(lanes):
+        lg[lane + 256 * (k % 4)] = 1.5
+    want = [lane + 256 * (k % 4) for k, lane in enumerate(lanes) if lane == winner][0]
+    assert min(lanes, key=bitrev8) == winner
+    assert tree_argmax(lg) == want
+    assert oracle_mod.argmax(lg) == want
+    assert oracle_np.argmax(lg) == want
+
+
+def test_argmax_signed_zeros_tie(oracle_mod):
+    """-0 and +0 compare equal under '>': inside a lane the first index keeps the maximum."""
+    lg = np.full(512, -1.0, np.float32)
+    lg[7] = np.float32(-0.0)
+    lg[263] = np.float32(0.0)
+    v, i = oracle_mod.topk256(lg)
+    assert i[7] == 7
+    assert oracle_mod.argmax(lg) == tree_argmax(lg) == 7
 
 
 def test_sampler_rules(oracle_mod):

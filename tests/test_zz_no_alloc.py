@@ -45,7 +45,7 @@ class NoAlloc:
         if seen_ids is not None:
             seen = torch.from_numpy(_bits(seen_ids, vocab).view(np.int32)).to("cuda:0")
         torch.cuda.synchronize()
-        s = GGSample(temperature, top_p, rep, 0.0)
+        s = GGSample(temperature, top_p, rep)
         rc = self.lib.gg_sample_logits_noalloc(ctypes.c_void_p(lg.data_ptr()), vocab,
                                                ctypes.c_void_p(seen.data_ptr()) if seen is not None else None,
                                                ctypes.byref(s), float(uniform),
@@ -101,7 +101,7 @@ def test_noalloc_large_vocab_then_small_matches():
     noalloc = NoAlloc()
     rng = np.random.default_rng(11)
     big = (rng.standard_normal(262144) * 2).astype(np.float32)
-    big[123456] = big[1000] = np.float32(9.5)  # tie across lanes: the lower lane wins
+    big[123456] = big[1000] = np.float32(9.5)  # tie across lanes 64 and 232: lane 64 wins
     vals, ids = oracle_np.topk256(big)
     for T, top_p, rep, u in [(0.0, 0.9, 1.0, 0.0), (0.8, 0.9, 1.0, 0.3)]:
         want = oracle_np.sample(vals, ids, T, top_p, rep, set(), u)
@@ -113,3 +113,54 @@ def test_noalloc_large_vocab_then_small_matches():
     ref = eng.sample_last(0)
     assert noalloc(eng.logits()) == ref
     eng.close()
+
+
+@pytest.mark.parametrize("lanes", [(1, 2), (3, 5), (2, 1), (128, 64), (255, 127), (6, 10, 12), (0, 17, 34)])
+def test_noalloc_greedy_ties_follow_the_reference_tree(lanes):
+    """Equal maxima in several lanes of a 262,144-entry vocabulary: the greedy pick must be the
+    reference's argmax tree result (smallest bit-reversed lane, shaders.ts:327-361), as the
+    C oracle computes it, not the lowest lane. -0 and +0 tie inside a lane."""
+    from oracle import oracle
+    noalloc = NoAlloc()
+    rng = np.random.default_rng(sum(lanes))
+    lg = (rng.standard_normal(262144) * 0.5).astype(np.float32)
+    for k, lane in enumerate(lanes):
+        lg[lane + 256 * (100 + 37 * k)] = np.float32(7.25)
+    want = oracle.argmax(lg)
+    assert lg[want] == np.float32(7.25)
+    assert noalloc(lg) == want
+    z = np.full(4096, -1.0, np.float32)
+    z[9], z[9 + 256 * 3] = np.float32(-0.0), np.float32(0.0)
+    assert noalloc(z) == oracle.argmax(z) == 9
+
+
+def test_noalloc_allocates_no_device_memory():
+    """After one warm-up call, further calls leave the device's free memory unchanged."""
+    import torch
+    noalloc = NoAlloc()
+    rng = np.random.default_rng(5)
+    lg = (rng.standard_normal(262144)).astype(np.float32)
+    dev = torch.from_numpy(lg).to("cuda:0")
+    seen = torch.zeros(262144 // 32, dtype=torch.int32, device="cuda:0")
+    from gemma_b200.native import GGSample
+    s = GGSample(0.8, 0.9, 1.2)
+    torch.cuda.synchronize()
+    rc = noalloc.lib.gg_sample_logits_noalloc(ctypes.c_void_p(dev.data_ptr()), 262144, ctypes.c_void_p(seen.data_ptr()),
+                                              ctypes.byref(s), 0.4, ctypes.c_void_p(noalloc.out.data_ptr()), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    toks = []
+    for i in range(8):
+        rc = noalloc.lib.gg_sample_logits_noalloc(ctypes.c_void_p(dev.data_ptr()), 262144,
+                                                  ctypes.c_void_p(seen.data_ptr()), ctypes.byref(s), 0.1 * i,
+                                                  ctypes.c_void_p(noalloc.out.data_ptr()), None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        toks.append(int(noalloc.out.item()))
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    from oracle import oracle
+    vals, ids = oracle.topk256(lg)
+    for i, t in enumerate(toks):
+        assert t == oracle.sample(vals, ids, 0.8, 0.9, 1.2, [], 0.1 * i, 262144)

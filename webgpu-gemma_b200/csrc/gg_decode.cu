@@ -461,6 +461,7 @@ struct Consumer {
     } else {
       x.m->logits[row] = v;
       if (!isnan(v)) {  // topk256 lane rule: strict '>' from (-1e30, 0), first index wins
+        if (v == 0.0f) v = 0.0f;  // -0 and +0 compare equal under '>': key them alike
         unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - (uint32_t)row);
         atomicMax(&x.S.keys[row & 255], k);
       }
@@ -909,12 +910,15 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st, Smem& S) {
     val = f32_from_order_key((uint32_t)(k >> 32));
     idx = 0xffffffffu - (uint32_t)k;
   }
-  const float T = st->temperature, rep = st->rep_penalty;
-  if (T == 0.0f && rep <= 1.0f) {
-    // argmax (shaders.ts:327-361): max value, ties -> lowest lane
+  const double T = st->temperature, rep = st->rep_penalty;
+  if (T == 0.0 && rep <= 1.0) {
+    // argmax (shaders.ts:327-361): the largest lane maximum. The shader's tree keeps the lower
+    // slot on a tie at every stride (128, 64, ..., 1), so bit 0 of the lane is decided last and
+    // weighs most: among equal maxima the lane with the smallest bit-reversed 8-bit index wins
+    // (lanes 1 and 2 tied: lane 2). The low word keys that order for the max below.
     __shared__ unsigned long long wk[8];
     unsigned long long key = 0;
-    if (tid < 256) key = ((unsigned long long)f32_order_key(val) << 32) | (uint32_t)(255 - tid);
+    if (tid < 256) key = ((unsigned long long)f32_order_key(val) << 32) | (uint32_t)(255u - (__brev((uint32_t)tid) >> 24));
     if (tid < 256) {
       for (int o = 16; o > 0; o >>= 1) {
         unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
@@ -926,8 +930,7 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st, Smem& S) {
     if (tid == 0) {
       unsigned long long best = wk[0];
       for (int w = 1; w < 8; w++) best = wk[w] > best ? wk[w] : best;
-      int lane = 255 - (int)(uint32_t)(best & 0xffffffffu);
-      result = lane;
+      result = (int)(__brev(255u - (uint32_t)(best & 0xffffffffu)) >> 24);  // back from bit-reversed order
     }
     __syncthreads();
     int lane = result;
@@ -940,8 +943,8 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st, Smem& S) {
   if (tid < 256) {
     double v = (double)val;
     const uint8_t* seen = m.seen + (size_t)seq * m.seen_stride;
-    if (rep > 1.0f && st->seen_count > 0 && idx < (uint32_t)m.V && (seen[idx >> 3] >> (idx & 7)) & 1)
-      v = v > 0 ? v / (double)rep : v * (double)rep;
+    if (rep > 1.0 && st->seen_count > 0 && idx < (uint32_t)m.V && (seen[idx >> 3] >> (idx & 7)) & 1)
+      v = v > 0 ? v / rep : v * rep;
     sv[tid] = v;
     sl[tid] = tid;
   }
@@ -967,7 +970,7 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st, Smem& S) {
   __shared__ uint32_t cid[256];
   if (tid < 256) cid[tid] = idx;
   __syncthreads();
-  if (T == 0.0f) {
+  if (T == 0.0) {
     if (tid == 0) result = (int)cid[sl[0]];
     __syncthreads();
     return result;
@@ -978,7 +981,7 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st, Smem& S) {
   __shared__ float probs[256];
   __shared__ double share[256];
   __shared__ double sum_all;
-  const double temp = (double)T, top_p = (double)st->top_p;
+  const double temp = T, top_p = st->top_p;
   if (tid < 256) probs[tid] = (float)exp((sv[tid] - sv[0]) / temp);
   __syncthreads();
   if (tid == 0) {
@@ -1249,6 +1252,8 @@ cudaError_t gg_batch_sample(const float* logits, int B, int V, const int32_t* se
 // logits the caller already holds on the device. Its scratch (per-CTA lane maxima and an
 // end-of-launch ticket) lives in a static device array, so a call allocates no memory.
 
+#include <cuda.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -1272,7 +1277,7 @@ static __device__ __align__(256) unsigned long long g_sample_scratch[SL_SCRATCH_
 
 __global__ void __launch_bounds__(SL_THREADS)
     gg_sample_logits_kernel(const float* __restrict__ logits, int V, const uint32_t* __restrict__ seen_bits,
-                            float temperature, float top_p, float rep_penalty, double uniform,
+                            double temperature, double top_p, double rep_penalty, double uniform,
                             int32_t* __restrict__ out_token, unsigned long long* __restrict__ scratch) {
   __shared__ int is_last;
   __shared__ GGModelDev sm;
@@ -1337,7 +1342,39 @@ namespace {
 
 constexpr int SL_MAX_DEVICES = 64;
 std::mutex g_sl_mu;
-unsigned long long* g_sl_scratch[SL_MAX_DEVICES] = {};  // device address of the array, per device
+// Device address of the array per device, with the id of the context it was looked up in: a
+// context that replaced that one (after cudaDeviceReset, or another context made current) has
+// its own copy of the array at a possibly different address, so the lookup is redone there.
+struct SlSlot {
+  unsigned long long ctx_id = 0;
+  unsigned long long* addr = nullptr;
+};
+SlSlot g_sl_scratch[SL_MAX_DEVICES];
+
+typedef CUresult (*PfnCtxGetCurrent)(CUcontext*);
+typedef CUresult (*PfnCtxGetId)(CUcontext, unsigned long long*);
+
+// Unique id (for the life of the process) of the calling thread's current context, or 0.
+unsigned long long current_ctx_id() {
+  static PfnCtxGetCurrent get_cur = nullptr;
+  static PfnCtxGetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<PfnCtxGetCurrent>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PfnCtxGetId>(f);
+  });
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (!get_cur || !get_id || get_cur(&c) != CUDA_SUCCESS || !c || get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 int sl_fail(int code, const char* fmt, ...) {
   char buf[320];
@@ -1363,22 +1400,33 @@ extern "C" int gg_sample_logits_noalloc(const float* logits, int vocab, const ui
   cudaError_t r = cudaGetDevice(&dev);
   if (r != cudaSuccess) return sl_fail(GG_E_CUDA, "gg_sample_logits_noalloc: cudaGetDevice: %s", cudaGetErrorString(r));
   if (dev < 0 || dev >= SL_MAX_DEVICES) return sl_fail(GG_E_ARG, "gg_sample_logits_noalloc: device %d >= %d", dev, SL_MAX_DEVICES);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (s) {  // the kernel and the memset run on the current device: the stream must belong to it
+    int sdev = -1;
+    r = cudaStreamGetDevice(s, &sdev);
+    if (r != cudaSuccess) return sl_fail(GG_E_ARG, "gg_sample_logits_noalloc: cudaStreamGetDevice: %s", cudaGetErrorString(r));
+    if (sdev != dev)
+      return sl_fail(GG_E_ARG, "gg_sample_logits_noalloc: stream belongs to device %d, the current device is %d", sdev, dev);
+  }
   unsigned long long* scratch = nullptr;
   {
-    // First call on a device: look up the array's device address with that device current.
-    // The host-side name g_sample_scratch is not a device address and is never passed to a kernel.
+    // First call on a device (or in a new context on it): look up the array's device address
+    // with that device current. The host-side name g_sample_scratch is not a device address and
+    // is never passed to a kernel.
     std::lock_guard<std::mutex> g(g_sl_mu);
-    if (!g_sl_scratch[dev]) {
+    SlSlot& slot = g_sl_scratch[dev];
+    const unsigned long long ctx = current_ctx_id();  // 0 before the runtime made a context current
+    if (!slot.addr || ctx == 0 || slot.ctx_id != ctx) {
       void* p = nullptr;
-      r = cudaGetSymbolAddress(&p, g_sample_scratch);
+      r = cudaGetSymbolAddress(&p, g_sample_scratch);  // also makes the primary context current
       if (r != cudaSuccess || !p)
         return sl_fail(GG_E_CUDA, "gg_sample_logits_noalloc: cudaGetSymbolAddress on device %d: %s", dev,
                        cudaGetErrorString(r));
-      g_sl_scratch[dev] = static_cast<unsigned long long*>(p);
+      slot.addr = static_cast<unsigned long long*>(p);
+      slot.ctx_id = current_ctx_id();
     }
-    scratch = g_sl_scratch[dev];
+    scratch = slot.addr;
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   r = cudaMemsetAsync(scratch, 0, sizeof(unsigned long long), s);  // the ticket starts at zero
   if (r != cudaSuccess) return sl_fail(GG_E_CUDA, "gg_sample_logits_noalloc: clearing the ticket: %s", cudaGetErrorString(r));
   const int grid = (vocab + SL_ROWS_PER_CTA - 1) / SL_ROWS_PER_CTA;

@@ -150,9 +150,12 @@ static_assert(sizeof(GGSampleDev) == sizeof(gg_sample), "gg_sample layout");
 
 constexpr int GG_PF_CHUNK = 512;  // prompt tokens per batched-prefill chunk
 
-static std::string g_create_err;
+// Failures of calls that have no engine (gg_create, gg_sample_logits_noalloc) land here, one
+// message per calling thread (as errno): threads that fail at the same time do not overwrite
+// each other's message, and the pointer gg_last_error(NULL) returns stays valid until the same
+// thread's next failure.
+static thread_local std::string g_create_err;
 
-// Failures of calls that have no engine (gg_create, gg_sample_logits_noalloc) land here.
 void gg_set_engineless_error(const char* msg) { g_create_err = msg; }
 
 static int fail(gg_engine* e, int code, const char* fmt, ...) {
@@ -591,7 +594,7 @@ static GGState base_inputs(gg_engine* e, int seq, int mode) {
   s.seq = seq;
   s.mode = mode;
   s.timeout_ns = e->timeout_ns;
-  s.rep_penalty = 1.0f;
+  s.rep_penalty = 1.0;
   if (e->trace_on) s.mode |= GG_TRACE;
   return s;
 }
@@ -867,7 +870,7 @@ extern "C" int gg_decode(gg_engine* e, int seq, int32_t token, int pos, int n, c
   s.token = token;
   s.pos = pos;
   set_sampling(s, sp, 0.0);
-  const bool greedy = !sp || sp->temperature == 0.0f;
+  const bool greedy = !sp || sp->temperature == 0.0;
   if (!greedy) {
     if (!uniforms) return fail(e, GG_E_ARG, "uniforms required when temperature > 0");
     if (e->unif_cap < n) {
@@ -930,6 +933,55 @@ extern "C" int gg_get_kv(gg_engine* e, int seq, int layer, int pos, int which, f
 __global__ void gg_untag_kernel(const uint64_t* src, float* dst, int n) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) dst[i] = __uint_as_float((uint32_t)src[i]);
+}
+
+// One weight row dequantised from what the device holds: f32(int8 q) * f32(f16 d), the exact
+// values every matvec and GEMM of this library multiplies (the reference's packQ8_0ForGPU +
+// f16ToF32, src/gguf.ts:95-149, and the shader's q * d). tiled = 0 reads the row format, 1 the
+// GEMM's tiled copy (row r of 128-row tile r / 128, 64-column slabs).
+__global__ void gg_dequant_row_kernel(const uint8_t* __restrict__ base, int K, int tiled, int r, float* __restrict__ out) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= K) return;
+  const uint8_t *qp, *dp;
+  if (!tiled) {
+    qp = base + k;
+    dp = base + K + 2 * (k >> 5);
+  } else {
+    const uint8_t* t = base + ((size_t)(r >> 7) * (K / 64) + (k >> 6)) * GG_Q8_TILE_BYTES;
+    qp = t + (r & 127) * 64 + (k & 63);
+    dp = t + 128 * 64 + (r & 127) * 4 + ((k >> 5) & 1) * 2;
+  }
+  out[k] = (float)(int8_t)*qp * __half2float(*reinterpret_cast<const __half*>(dp));
+}
+
+extern "C" int gg_dequant_row(gg_engine* e, int which, int layer, int row, int copy, float* out, int n) {
+  GG_TRY(ready(e, 0));
+  const GGModelDev& m = e->md;
+  if (!out || which < 0 || which > 4 || copy < 0 || copy > 1) return fail(e, GG_E_ARG, "bad matrix %d or copy %d", which, copy);
+  if (which < 4 && (layer < 0 || layer >= m.L)) return fail(e, GG_E_ARG, "layer %d outside 0..%d", layer, m.L - 1);
+  const int M[5] = {m.Q + 2 * m.KV, m.H, 2 * m.I, m.H, m.V}, K[5] = {m.H, m.Q, m.H, m.I, m.H};
+  const int rs[5] = {m.rs_h, m.rs_q, m.rs_h, m.rs_i, m.rs_h};
+  if (row < 0 || row >= M[which]) return fail(e, GG_E_ARG, "row %d outside 0..%d", row, M[which] - 1);
+  if (n != K[which]) return fail(e, GG_E_ARG, "n=%d, the row has %d values", n, K[which]);
+  const uint8_t* base;
+  if (copy == 0) {
+    const uint8_t* rows[4] = {e->wqkv[layer < 0 ? 0 : layer], e->wo[layer < 0 ? 0 : layer], e->wgu[layer < 0 ? 0 : layer],
+                              e->wdown[layer < 0 ? 0 : layer]};
+    base = (which == 4 ? e->embd : rows[which]) + (size_t)row * rs[which];
+  } else {
+    if (!e->gemm_ok) return fail(e, GG_E_STATE, "this model has no tiled copy (shapes not multiples of 128 x 64)");
+    base = (which == 4 ? e->lm_map : e->qmaps[(size_t)layer * 4 + which]).tiles;
+  }
+  float* tmp = nullptr;
+  GG_CUDA(e, cudaMalloc(&tmp, 4 * (size_t)n));
+  gg_dequant_row_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(base, n, copy, row, tmp);
+  cudaError_t r = cudaGetLastError();
+  if (r == cudaSuccess) r = cudaMemcpyAsync(out, tmp, 4 * (size_t)n, cudaMemcpyDeviceToHost, e->stream);
+  cudaError_t r2 = cudaStreamSynchronize(e->stream);
+  cudaFree(tmp);
+  if (r == cudaSuccess) r = r2;
+  if (r != cudaSuccess) return fail(e, GG_E_CUDA, "dequant row: %s", cudaGetErrorString(r));
+  return GG_OK;
 }
 
 extern "C" int gg_debug_read(gg_engine* e, int which, float* out, int n) {

@@ -96,7 +96,7 @@ enum : int {
 // chain of launches; the device advances token/pos/prefill_ids/uniforms/step_index itself.
 // Sampling parameters of one sequence (the C-ABI's gg_sample).
 struct GGSampleDev {
-  float temperature, top_p, rep_penalty, pad_;
+  double temperature, top_p, rep_penalty;
 };
 
 struct GGState {
@@ -104,8 +104,9 @@ struct GGState {
   int32_t pos;     // its position
   int32_t seq;     // KV slot
   int32_t mode;    // GG_RUN_* bits
-  float temperature, top_p, rep_penalty;
+  double temperature, top_p, rep_penalty;
   int32_t step_index;        // incremented per sampled token
+  int32_t pad0_;
   double uniform;            // the draw replacing Math.random() when `uniforms` is null
   const double* uniforms;    // per-step draws, advanced by one per sampled token
   uint64_t timeout_ns;       // bounded-wait limit

@@ -19,7 +19,7 @@ GG_OK, GG_E_ARG, GG_E_CUDA, GG_E_STATE, GG_E_DEVICE, GG_E_NOMEM = 0, -1, -2, -3,
 # Bytes a gg_step call moves: the host-written prefix of GGState (token, pos, sampling options,
 # ... up to `epoch`, csrc/gg_model.h) host->device, and its device-owned tail (out_token,
 # error, ...) device->host.
-STATE_H2D_BYTES = 80
+STATE_H2D_BYTES = 96
 STATE_D2H_BYTES = 32
 
 # Every symbol the header declares, with (restype, argtypes).
@@ -37,6 +37,7 @@ SIGNATURES = {
     "gg_get_hidden": (_I, [_P, _P]),
     "gg_get_kv": (_I, [_P, _I, _I, _I, _I, _P]),
     "gg_debug_read": (_I, [_P, _I, _P, _I]),
+    "gg_dequant_row": (_I, [_P, _I, _I, _I, _I, _P, _I]),
     "gg_seen_reset": (_I, [_P, _I]),
     "gg_seen_add": (_I, [_P, _I, _I32P, _I]),
     "gg_reset_kv": (_I, [_P, _I]),
@@ -64,8 +65,7 @@ GG_FLAG_SERIAL_PREFILL = 1  # prefill one token per launch (the reference's orde
 
 
 class GGSample(ctypes.Structure):
-    _fields_ = [("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("rep_penalty", ctypes.c_float),
-                ("pad_", ctypes.c_float)]
+    _fields_ = [("temperature", ctypes.c_double), ("top_p", ctypes.c_double), ("rep_penalty", ctypes.c_double)]
 
 
 class GemmaB200Error(RuntimeError):
@@ -131,7 +131,7 @@ class NativeEngine:
 
     @staticmethod
     def _sample(temperature: float, top_p: float, rep: float) -> GGSample:
-        return GGSample(float(temperature), float(top_p), float(rep), 0.0)
+        return GGSample(float(temperature), float(top_p), float(rep))
 
     def sample_last(self, seq: int = 0, temperature=0.0, top_p=0.9, rep=1.0, uniform=0.0) -> int:
         out = ctypes.c_int32()
@@ -183,6 +183,15 @@ class NativeEngine:
         self._check(self.lib.gg_debug_read(self.h, self.DEBUG_BUFFERS.index(which), out.ctypes.data_as(_P), n))
         return out
 
+    def dequant_row(self, which: int, layer: int, row: int, copy: int = 0) -> np.ndarray:
+        """Row `row` of matrix `which` (0 qkv, 1 o, 2 gate/up interleaved, 3 down, 4 embedding)
+        dequantised from the device's copy (0 row format, 1 the GEMM's tiled copy)."""
+        c = self.cfg
+        k = {0: c.hidden_size, 1: c.q_dim, 2: c.hidden_size, 3: c.intermediate_size, 4: c.hidden_size}[which]
+        out = np.empty(k, np.float32)
+        self._check(self.lib.gg_dequant_row(self.h, which, layer, row, copy, out.ctypes.data_as(_P), k))
+        return out
+
     def seen_reset(self, seq: int = 0):
         self._check(self.lib.gg_seen_reset(self.h, seq))
 
@@ -214,7 +223,7 @@ class NativeEngine:
         tokens = np.ascontiguousarray(tokens, np.int32)
         pos = np.ascontiguousarray(pos, np.int32)
         n = seqs.size
-        sp = (GGSample * n)(*[GGSample(float(t), float(p), float(r), 0.0) for (t, p, r) in samples])
+        sp = (GGSample * n)(*[GGSample(float(t), float(p), float(r)) for (t, p, r) in samples])
         u = np.ascontiguousarray(np.asarray(uniforms, np.float64).reshape(steps, n))
         out = np.empty((steps, n), np.int32)
         self._check(self.lib.gg_decode_batch(self.h, n, seqs.ctypes.data_as(_P), tokens.ctypes.data_as(_P),
