@@ -14,7 +14,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 OUT = os.path.join(HERE, "gemma_b200", "libgemma_b200.so")
-SOURCES = ["gg_engine.cu", "gg_decode.cu", "gg_gemm.cu", "gg_prefill.cu", "gg_tokenizer.cpp"]
+SOURCES = ["gg_engine.cu", "gg_step.cu", "gg_decode.cu", "gg_gemm.cu", "gg_prefill.cu", "gg_tokenizer.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
          "-Xcompiler", "-fPIC", "-shared", "--expt-relaxed-constexpr", "-I", INCLUDE]

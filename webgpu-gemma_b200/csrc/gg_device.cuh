@@ -23,6 +23,25 @@ enum : uint32_t {
 
 GG_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// Shared-memory accesses by 32-bit shared-window address (ld/st.shared): the hot loops read
+// planes and ring stages through these, never through generic pointers.
+GG_DEV uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+GG_DEV float ldsf(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+GG_DEV float lds_half(uint32_t a) {  // an f16 value, widened
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return __half2float(__ushort_as_half(v));
+}
+GG_DEV void sts32(uint32_t a, uint32_t v) { asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory"); }
+
 GG_DEV uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -87,6 +106,12 @@ GG_DEV uint64_t tag_load(const uint64_t* p) {
   return w;
 }
 
+// Two consecutive words (16-byte aligned) with one load at gpu scope (served by L2: always sees
+// the latest store of another SM).
+GG_DEV void ld2_relaxed(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 struct SpinCtl {
   uint32_t* err;        // global error word (GGState::error)
   uint64_t timeout_ns;  // give up after this long
@@ -125,10 +150,13 @@ GG_DEV float tag_wait(const uint64_t* p, uint32_t tag, const SpinCtl& sc) {
 
 // Bounded wait on an mbarrier phase. Returns false (and sets err) on timeout.
 GG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const SpinCtl& sc) {
-  // Fast path without reading the clock; the timed loop below bounds the wait.
+  // Fast path without reading the clock; the timed loop below bounds the wait. Not unrolled:
+  // every copy of a wait loop costs instruction-cache space on the critical path.
+#pragma unroll 1
   for (int it = 0; it < 64; ++it)
     if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+#pragma unroll 1
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 15u) == 0) {

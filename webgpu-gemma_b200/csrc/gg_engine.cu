@@ -23,13 +23,14 @@
 #include "gg_prefill.h"
 
 namespace gg {
-extern "C" __global__ void gg_decode_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
-extern "C" __global__ void gg_decode_kernel_kv16(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
+extern "C" __global__ void gg_step_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
+extern "C" __global__ void gg_step_kernel_kv16(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
 }
 
 // The persistent step kernel built for the engine's KV element type.
 using DecodeFn = void (*)(const GGModelDev*, GGState*);
-static DecodeFn decode_fn(const GGModelDev& m) { return m.kv_es == 2 ? gg::gg_decode_kernel_kv16 : gg::gg_decode_kernel; }
+static DecodeFn decode_fn(const GGModelDev& m) { return m.kv_es == 2 ? gg::gg_step_kernel_kv16 : gg::gg_step_kernel; }
+constexpr int GG_STEP_THREADS = (GG_STEP_NCW + 1) * 32;
 
 // ------------------------------------------------------------------------------ utility kernels
 
@@ -264,76 +265,87 @@ extern "C" int gg_create(const gg_config* cfg, int device, gg_engine** out) {
 
 static int schedule(gg_engine* e) {
   GGModelDev& m = e->md;
-  const gg_config& c = e->cfg;
-  // 128 CTAs divide the model's row counts evenly (1B: 12 q/k/v rows, 9 O and down rows, 54
-  // gate/up pairs each), so no CTA carries an extra row into every hand-over; measured faster
-  // than one CTA per SM (148) on B200.
+  // 128 CTAs split the 1B model's row sets into whole quads of near-equal size (3 q/k/v quads,
+  // 2-3 quads of O and down rows, 13-14 quads of gate/up pairs, 512 quads of LM-head rows) and
+  // need one hand-over fewer CTA than one per SM; measured faster than 148 on B200.
   m.grid = std::min(e->sm_count, 128);
-  // the decode kernel splits rows as c * M / grid in 32-bit arithmetic
-  if ((long long)m.grid * std::max({m.V, m.Q + 2 * m.KV, m.H, m.I}) >= (1ll << 31))
-    return fail(e, GG_E_ARG, "vocabulary or layer too large for the decode kernel's row split");
-  m.stage_bytes = 20480;
-  if (m.rs_i > m.stage_bytes || m.rs_q > m.stage_bytes || 4 * m.rs_h > m.stage_bytes)
-    return fail(e, GG_E_ARG, "rows too wide for a %d-byte ring stage", m.stage_bytes);
-  m.pps_gu = (m.stage_bytes / (2 * m.rs_h)) / 4 * 4;  // whole 4-pair warp units
-  // lanes per row and K-slices: 8 lanes per row when a stage holds 4+ rows, else 16, else 32;
-  // K-slices give every consumer warp a unit on the short phases.
-  auto pick = [&](int M, int K, int rs, bool split, int r) {
-    GGPhaseCfg p{};
-    const int cap = m.stage_bytes / rs;
-    p.gs = cap >= 4 * r ? 8 : 16;
-    p.r = r;
-    const int ur = (32 / p.gs) * r;
-    p.rps = (cap / ur) * ur;
-    if (p.rps < 1) { p.gs = 16; p.r = 1; p.rps = (cap / 2) * 2; }
-    const int nch = K / 16;
-    const int rows = (M + m.grid - 1) / m.grid;
-    const int units = (rows + ur - 1) / ur;
-    p.ks = 1;
-    if (split)
-      for (int ks = 2; ks <= 16; ks++)
-        if (nch % ks == 0 && (nch / ks) % p.gs == 0 && units * ks <= GG_NCW && rows * ks <= 1024) p.ks = ks;
-    return p;
-  };
-  m.ph_qkv = pick(m.Q + 2 * m.KV, m.H, m.rs_h, true, 1);
-  m.ph_o = pick(m.H, m.Q, m.rs_q, true, 1);
-  m.ph_down = pick(m.H, m.I, m.rs_i, true, 1);
-  m.ph_lm = pick(m.V, m.H, m.rs_h, false, 2);  // two rows per lane group (1.150 -> 1.134 ms per token)
-  if (m.pps_gu < 4 || m.rs_i > m.stage_bytes) return fail(e, GG_E_ARG, "rows too wide for a %d-byte ring stage", m.stage_bytes);
-  if (m.H / 4 > GG_NCT) return fail(e, GG_E_ARG, "hidden_size above %d", 4 * GG_NCT);
+  const int G = m.grid;
+  // the step kernel splits quads as c * nq / G in 32-bit arithmetic
+  if ((long long)(G + 1) * (m.V / 4 + 1) >= (1ll << 31)) return fail(e, GG_E_ARG, "vocabulary too large for the step kernel's row split");
   if (m.HD != GG_HEAD_DIM) return fail(e, GG_E_ARG, "head_dim must be %d (Gemma 3)", GG_HEAD_DIM);
+  if (m.H / 4 > 32 * GG_STEP_NCW) return fail(e, GG_E_ARG, "hidden_size above %d", 128 * GG_STEP_NCW);
+  if (m.I / 4 > 4 * 32 * GG_STEP_NCW || m.Q / 4 > 4 * 32 * GG_STEP_NCW)
+    return fail(e, GG_E_ARG, "intermediate_size and q_dim must be at most %d", 512 * GG_STEP_NCW);
+  const int SB = GG_STEP_STAGE_BYTES;
+  if (m.rs_i > SB || m.rs_q > SB || 2 * m.rs_h > SB) return fail(e, GG_E_ARG, "rows too wide for a %d-byte ring stage", SB);
+  m.stage_bytes = SB;
+  m.rps_h = SB / m.rs_h;
+  m.rps_q = SB / m.rs_q;
+  m.rps_i = SB / m.rs_i;
+  m.rps_gu = (SB / m.rs_h) & ~1;
+  const auto slot = [&](int nq) { return 4 * ((nq + G - 1) / G); };
+  m.sl_qkv = slot((m.Q + 2 * m.KV) / 4);
+  m.sl_h = slot(m.H / 4);
+  m.sl_i = slot(m.I / 4);
+  m.lm_rows = slot(m.V / 4);
+  // the q/k/v, O and down rows of a CTA are computed one per consumer warp
+  if (m.sl_qkv > GG_STEP_NCW || m.sl_h > GG_STEP_NCW)
+    return fail(e, GG_E_ARG, "the step kernel needs at most %d q/k/v and hidden rows per CTA (grid %d)", GG_STEP_NCW, G);
+  // rows of one phase per CTA: at most one per consumer warp and ring stage group (matvec)
   m.pos_per_split = GG_POS_PER_SPLIT;
-  if (2 * GG_POS_PER_SPLIT * m.KV * 4 > m.stage_bytes) return fail(e, GG_E_ARG, "kv_dim too large for a ring stage");
+  if (2 * GG_POS_PER_SPLIT * m.KV * 4 > SB) return fail(e, GG_E_ARG, "kv_dim too large for a ring stage");
   m.max_splits = (m.CTX + m.pos_per_split - 1) / m.pos_per_split;
+  if ((m.max_splits + G - 1) / G > GG_STEP_NCW / m.NQH)
+    return fail(e, GG_E_ARG, "context too long for the step kernel's %d attention splits per CTA", GG_STEP_NCW / m.NQH);
+  m.att_slot = m.NQH * (m.HD + 4);
+  // the small phases (q/k/v, O, down rows of a CTA) keep all their ring stages resident at once
+  {
+    const int rq = SB / m.rs_h, ro = SB / m.rs_q, rd = SB / m.rs_i;
+    const int nst = std::max({(m.sl_qkv + std::min(rq, m.sl_qkv) - 1) / std::min(rq, m.sl_qkv),
+                              (m.sl_h + std::min(ro, m.sl_h) - 1) / std::min(ro, m.sl_h),
+                              (m.sl_h + std::min(rd, m.sl_h) - 1) / std::min(rd, m.sl_h)});
+    if (nst >= GG_STEP_STAGES) return fail(e, GG_E_ARG, "rows too wide: a phase needs %d ring stages at once", nst);
+  }
   m.dims_per_comb = 8;
-  if (m.HD % m.dims_per_comb) return fail(e, GG_E_ARG, "head_dim must be a multiple of 8");
-  m.ncomb = m.Q / m.dims_per_comb;
+  m.ncomb = m.Q / 8;
   m.xs0 = (m.H + 63) / 64 * 64;
   m.xs1 = (std::max(m.Q, m.I) + 63) / 64 * 64;
   m.tmp_floats = m.Q + 2 * m.KV;
-  // keep in step with the carve at the top of gg_decode_kernel
-  size_t other = 8 * 256 + (size_t)(3 * m.xs0 + m.xs0 / 4) + (size_t)(3 * m.xs1 + m.xs1 / 4) + 8 * (size_t)m.H +
-                 4 * (size_t)m.tmp_floats + 4 * 1024 + 4 * 256 + 4 * 256 + 16 + 32;
+  m.nstages = GG_STEP_STAGES;
+  // keep in step with the carve at the top of step_body (gg_step.cu)
+  // shared-memory layout of the step kernel (carved the same way at the top of step_body)
+  {
+    size_t off = (size_t)GG_STEP_STAGES * SB + 16 * (size_t)GG_STEP_STAGES;  // ring + full/empty mbarriers
+    const auto take = [&](size_t bytes) {
+      const size_t o = off;
+      off = (off + bytes + 15) / 16 * 16;
+      return (int)o;
+    };
+    const size_t xb_bytes = (size_t)3 * m.xs1 + m.xs1 / 4;
+    m.sm_xa = take((size_t)3 * m.xs0 + m.xs0 / 4);
+    m.sm_xb = take(xb_bytes);
+    // q | k | v (attention) and the LM-head logits reuse the O / down planes when they fit
+    m.sm_tmp = 4 * (size_t)m.tmp_floats <= xb_bytes ? m.sm_xb : take(4 * (size_t)m.tmp_floats);
+    m.sm_lmv = 4 * (size_t)m.lm_rows <= xb_bytes ? m.sm_xb : take(4 * (size_t)m.lm_rows);
+    m.sm_hid = take(4 * (size_t)m.H);
+    m.sm_res = take(4 * (size_t)m.H);
+    m.sm_scal = take(16 * 4 * GG_STEP_NCW);
+    m.sm_red = take(4 * 16 * GG_STEP_NCW);
+    m.sm_flag = take(16);
+    m.sm_rows = take(32);
+    m.smem_bytes = (int)off;
+  }
   cudaFuncAttributes fa;
   GG_CUDA(e, cudaFuncGetAttributes(&fa, decode_fn(m)));
   int optin = 0;
   GG_CUDA(e, cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, e->device));
-  long avail = (long)optin - (long)fa.sharedSizeBytes - (long)other;
-  // GG_RING_STAGES (five): enough for the largest per-CTA share of a phase that must be
-  // resident at once (the 1B down projection: 5 stages). A deeper ring buys no bandwidth and
-  // takes shared memory from L1: at 5 stages the kernel fits the 164 KB shared-memory carveout
-  // (L1 92 KB instead of 28 KB at 8 stages). Measured on the 1B model: 8 / 7 / 6 / 5 / 4 / 3
-  // stages = 1.209 / 1.202 / 1.195 / 1.187 / 1.273 / 1.358 ms per token.
-  const int ns = GG_RING_STAGES;
-  if (avail / (m.stage_bytes + 16) < ns)
-    return fail(e, GG_E_ARG, "not enough shared memory for the %d-stage weight ring (%ld bytes left)", ns, avail);
-  m.nstages = ns;
-  m.smem_bytes = (int)(other + (size_t)ns * (m.stage_bytes + 16));
+  if ((long)m.smem_bytes + (long)fa.sharedSizeBytes > (long)optin)
+    return fail(e, GG_E_ARG, "step kernel needs %d + %d bytes of shared memory, the device offers %d", m.smem_bytes,
+                (int)fa.sharedSizeBytes, optin);
   GG_CUDA(e, cudaFuncSetAttribute(decode_fn(m), cudaFuncAttributeMaxDynamicSharedMemorySize, m.smem_bytes));
   int nb = 0;
-  GG_CUDA(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, decode_fn(m), GG_NTHREADS, m.smem_bytes));
-  if (nb < 1) return fail(e, GG_E_CUDA, "decode kernel cannot be resident (smem %d)", m.smem_bytes);
-  (void)c;
+  GG_CUDA(e, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, decode_fn(m), GG_STEP_THREADS, m.smem_bytes));
+  if (nb < 1) return fail(e, GG_E_CUDA, "step kernel cannot be resident (smem %d)", m.smem_bytes);
   return GG_OK;
 }
 
@@ -506,13 +518,13 @@ extern "C" int gg_finalize(gg_engine* e) {
     GG_TRY(dalloc(e, &e->pf_tiles, 2 * e->pf_tiles_half));
     GG_TRY(dalloc(e, &e->pf_kvsplit, pf_kv_split_bytes(m.CTX, m.KV)));
   }
-  GG_TRY(dalloc(e, &m.t_qkv, 8 * (size_t)(m.Q + 2 * m.KV)));
-  GG_TRY(dalloc(e, &m.t_ml, 8 * (size_t)m.max_splits * m.NQH * 2));
-  GG_TRY(dalloc(e, &m.t_o, 8 * (size_t)m.max_splits * m.Q));
+  // exchange buffers of the step kernel (tagged words; one slot per CTA, or per attention split)
+  GG_TRY(dalloc(e, &m.t_qkv, 8 * (size_t)m.grid * m.sl_qkv));
+  GG_TRY(dalloc(e, &m.t_o, 8 * (size_t)m.max_splits * m.att_slot));
   GG_TRY(dalloc(e, &m.t_att, 8 * (size_t)m.Q));
-  GG_TRY(dalloc(e, &m.t_proj, 8 * (size_t)m.H));
-  GG_TRY(dalloc(e, &m.t_act, 8 * (size_t)m.I));
-  GG_TRY(dalloc(e, &m.t_down, 8 * (size_t)m.H));
+  GG_TRY(dalloc(e, &m.t_proj, 8 * (size_t)m.grid * m.sl_h));
+  GG_TRY(dalloc(e, &m.t_act, 8 * (size_t)m.grid * m.sl_i));
+  GG_TRY(dalloc(e, &m.t_down, 8 * (size_t)m.grid * m.sl_h));
   GG_TRY(dalloc(e, &m.logits, 4 * (size_t)m.V));
   GG_TRY(dalloc(e, &m.lane_keys, 8 * 256));
   GG_TRY(dalloc(e, &m.dbg_hidden, 4 * (size_t)m.H));
@@ -560,7 +572,7 @@ static int put_inputs(gg_engine* e, const GGState& in) {
 static int launch(gg_engine* e) {
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(e->md.grid);
-  lc.blockDim = dim3(GG_NTHREADS);
+  lc.blockDim = dim3(GG_STEP_THREADS);
   lc.dynamicSmemBytes = e->md.smem_bytes;
   lc.stream = e->stream;
   cudaLaunchAttribute at[1];
@@ -930,9 +942,20 @@ extern "C" int gg_get_kv(gg_engine* e, int seq, int layer, int pos, int which, f
   return GG_OK;
 }
 
-__global__ void gg_untag_kernel(const uint64_t* src, float* dst, int n) {
+// Element i of a tagged exchange buffer, to f32. sl > 0: the buffer holds one slot of sl words
+// per CTA, and quad q = i / 4 of the nq quads lives in the slot of the CTA that owns it (the
+// step kernel's quad partition q in [c * nq / G, (c + 1) * nq / G)).
+__global__ void gg_untag_kernel(const uint64_t* src, float* dst, int n, int nq, int G, int sl) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) dst[i] = __uint_as_float((uint32_t)src[i]);
+  if (i >= n) return;
+  size_t w = (size_t)i;
+  if (sl > 0) {
+    const uint32_t q = (uint32_t)i >> 2;
+    const uint32_t c = ((q + 1u) * (uint32_t)G - 1u) / (uint32_t)nq;
+    const uint32_t qb = (c * (uint32_t)nq) / (uint32_t)G;
+    w = (size_t)c * sl + 4 * (q - qb) + (i & 3);
+  }
+  dst[i] = __uint_as_float((uint32_t)src[w]);
 }
 
 // One weight row dequantised from what the device holds: f32(int8 q) * f32(f16 d), the exact
@@ -997,7 +1020,9 @@ extern "C" int gg_debug_read(gg_engine* e, int which, float* out, int n) {
   if (which < 5) {
     float* tmp = nullptr;
     GG_CUDA(e, cudaMalloc(&tmp, 4 * (size_t)n));
-    gg_untag_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(tagged[which], tmp, n);
+    const int nq[5] = {(m.Q + 2 * m.KV) / 4, m.Q / 4, m.H / 4, m.I / 4, m.H / 4};
+    const int sl[5] = {m.sl_qkv, 0, m.sl_h, m.sl_i, m.sl_h};
+    gg_untag_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(tagged[which], tmp, n, nq[which], m.grid, sl[which]);
     cudaError_t r = cudaMemcpyAsync(out, tmp, 4 * (size_t)n, cudaMemcpyDeviceToHost, e->stream);
     cudaStreamSynchronize(e->stream);
     cudaFree(tmp);

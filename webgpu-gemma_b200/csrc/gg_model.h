@@ -11,14 +11,12 @@
 #include <stddef.h>
 
 #define GG_MAX_LAYERS 64
-#define GG_NCW 15                     // consumer warps per CTA (16 warps: 4 per SM sub-partition)
-#define GG_NTHREADS ((GG_NCW + 1) * 32)  // + one producer warp
-#define GG_NCT (GG_NCW * 32)          // consumer threads
 #define GG_HEAD_DIM 256                // Gemma 3 head size (compile-time for the attention phase)
 #define GG_POS_PER_SPLIT 8             // KV positions per attention split
-#define GG_RING_STAGES 5               // decode kernel's weight ring depth (compile-time: the ring
-                                       // index math runs in every warp at every stage)
 #define GG_TRACE_PHASES 512            // phases traced per CTA by GG_TRACE launches (4 stamps each)
+#define GG_STEP_NCW 15                 // step kernel: consumer warps per CTA (+ one producer warp: 4 warps per SM sub-partition, 128 registers a thread)
+#define GG_STEP_STAGES 9               // step kernel: weight ring stages
+#define GG_STEP_STAGE_BYTES 20480      // step kernel: bytes per ring stage (16 rows of 1,152 Q8_0 weights)
 
 static inline int gg_row_stride(int K) { return ((K + (K / 32) * 2) + 15) / 16 * 16; }
 
@@ -38,21 +36,13 @@ struct GGLayerW {
   const float2* rope;  // [CTX][HD/2] (cos, sin) of pos * theta^(-2i/HD) for this layer's theta
 };
 
-struct GGPhaseCfg {
-  int gs, r, ks, rps;  // lanes per row, rows per lane, K-slices, rows per ring stage
-};
-
 struct GGModelDev {
   int H, Q, KV, NQH, NKH, HD, I, V, L, CTX;
   float eps, attn_scale;
   int rs_h, rs_q, rs_i;  // row strides (bytes) for K = H, Q, I
   int grid;              // CTAs of the persistent kernel (one per SM)
   int stage_bytes, nstages;
-  // Per matvec phase: lanes per row (gs: 8, 16 or 32), K-slices per row (ks; the slice
-  // partials are summed across warps), whole rows per ring stage (rps, a multiple of 32/gs).
-  GGPhaseCfg ph_qkv, ph_o, ph_down, ph_lm;
-  int pps_gu;               // gate/up row pairs per ring stage (16 lanes per row)
-  int pos_per_split, max_splits, ncomb, dims_per_comb;
+  int pos_per_split, max_splits, ncomb, dims_per_comb;  // attention splits; merge units of 8 dims
   int xs0, xs1;     // x-plane buffer sizes (elements, multiples of 64): xs0 >= H, xs1 >= max(Q, I)
   int tmp_floats;   // attention scratch (q | k | v)
   int smem_bytes;
@@ -62,13 +52,13 @@ struct GGModelDev {
   uint8_t* vcache;
   size_t kv_seq_stride;  // elements per sequence
   // tagged activation exchange (value | tag << 32)
-  uint64_t* t_qkv;  // Q + 2KV
-  uint64_t* t_ml;   // [max_splits][NQH][2]  (running max, sum of exp)
-  uint64_t* t_o;    // [max_splits][Q]
-  uint64_t* t_att;  // Q
-  uint64_t* t_proj; // H
-  uint64_t* t_act;  // I
-  uint64_t* t_down; // H
+  // (each CTA's outputs of a phase in its own slot of sl_* words; see the step kernel)
+  uint64_t* t_qkv;  // [grid][sl_qkv] q | k | v rows
+  uint64_t* t_o;    // [max_splits][att_slot] attention split partials (o, max, sum per head)
+  uint64_t* t_att;  // Q merged attention output (8 dims per merge unit, contiguous)
+  uint64_t* t_proj; // [grid][sl_h] O projection rows
+  uint64_t* t_act;  // [grid][sl_i] GeGLU outputs
+  uint64_t* t_down; // [grid][sl_h] down projection rows
   float* logits;                    // V
   unsigned long long* lane_keys;    // 256 per-lane (value, index) maxima of the LM head
   float* dbg_hidden;    // H: hidden state after the last finished layer (CTA 0 writes)
@@ -81,6 +71,17 @@ struct GGModelDev {
   unsigned long long* trace;  // [grid][GG_TRACE_PHASES][4] globaltimer stamps
   GGLayerW layers[GG_MAX_LAYERS];
   int kv_es;  // bytes per KV cache element: 4 (f32), or 2 (bf16)
+  // Step kernel. Rows per ring stage for K = H, Q, I, and for row pairs of K = H (even); words per
+  // CTA slot of the exchange buffers (whole quads: the CTA's outputs start on a 32-byte sector)
+  // of the Q+2KV, H and I (pair) outputs; words per attention split (NQH x (HD + 4): o, max, sum).
+  int rps_h, rps_q, rps_i, rps_gu;
+  int sl_qkv, sl_h, sl_i;
+  int att_slot;
+  int lm_rows;  // most LM-head rows of one CTA (its logits are staged in shared memory)
+  // Step kernel shared-memory layout: byte offsets from the dynamic shared-memory base (after the
+  // ring and its mbarriers). The attention scratch (q | k | v) and the LM-head logits share the
+  // O / down plane buffer when they fit: none of the three is live while another is.
+  int sm_xa, sm_xb, sm_hid, sm_res, sm_tmp, sm_lmv, sm_scal, sm_red, sm_flag, sm_rows;
 };
 
 // Launch-mode bits.

@@ -1,0 +1,1055 @@
+// gg_step.cu -- the batch-1 Gemma 3 token step as one persistent sm_100a kernel.
+//
+// One CTA per SM (cooperative launch), 16 consumer warps and one producer warp. The producer's
+// lane 0 walks the whole token's weight schedule -- per layer this CTA's rows of Wqkv, the KV rows
+// of its attention splits, its rows of Wo, Wgu and Wdown, then its LM-head rows -- and streams
+// them with cp.async.bulk into a ring of 16 KB shared-memory stages completing on mbarriers. It
+// only ever waits for free stages, so weight streaming runs ahead across phase and layer
+// boundaries while the consumers wait for activations.
+//
+// Between phases the CTAs exchange activations as tagged 64-bit words (f32 value | tag << 32,
+// the tag naming the launch and phase), so each word is its own ready flag. A CTA's outputs of a
+// phase occupy its own slot of whole 32-byte sectors: producers never share a sector, and a
+// consumer loads every word it needs with 16-byte loads that are all in flight before it checks
+// any tag.
+//
+// Phases per layer (reference: src/engine.ts:766-795):
+//   0  post-ffw norm + residual of the previous layer, attention rmsNorm, fused QKV matvec
+//                                                      (shaders.ts:25-56, 92-151, 386-418)
+//   1  q/k per-head norm + RoPE, KV store, attention splits of 8 positions (shaders.ts:209-325, 420-467)
+//   2  merge of the splits (online softmax): one warp per 8 output dimensions
+//   3  O projection                                               (shaders.ts:92-151)
+//   4  post-attn norm + residual, ffn rmsNorm, gate/up + GeGLU    (shaders.ts:153-170, 386-418)
+//   5  down projection                                            (shaders.ts:92-151)
+// then the final norm, the tied LM head with per-lane maxima (engine.ts:797-821, shaders.ts:327-384)
+// and the sampler in the last CTA to finish (engine.ts:823-901).
+//
+// Matvec arithmetic: x is held as 24-bit fixed point per 16-element chunk in three byte planes
+// (one exponent per chunk); q . x is three exact int32 dp4a sums per chunk, recombined in f32 and
+// scaled by the chunk exponent and the Q8_0 block scale. A warp computes one row (two for the
+// gate/up pairs and the LM head) with its lanes over the row's chunks.
+//
+// Code size is kept small on purpose: one dot-product routine per row count serves every matvec
+// phase, so the per-layer loop stays resident in the SM's instruction cache.
+#include "gg_device.cuh"
+#include "gg_model.h"
+#include "gg_sample.cuh"
+
+namespace gg {
+namespace step {
+
+constexpr int NCW = GG_STEP_NCW;
+constexpr int NCT = NCW * 32;
+constexpr int NTH = NCT + 32;
+constexpr uint32_t NS = GG_STEP_STAGES;
+constexpr int PH = 6;  // phases (tags) per layer
+
+#define GG_NOINLINE __device__ __noinline__
+
+GG_DEV void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
+
+GG_DEV uint32_t make_tag(uint32_t base, int phase) { return 0x80000000u | ((base + (uint32_t)phase) & 0x7fffffffu); }
+
+// Quad partition: quads [qpart(c), qpart(c + 1)) of nq go to CTA c of G (32-bit: the host checks
+// G * nq < 2^31), and the CTA that owns quad q.
+GG_DEV int qpart(int nq, int G, int c) { return (int)(((uint32_t)c * (uint32_t)nq) / (uint32_t)G); }
+GG_DEV int qowner(int nq, int G, int q) { return (int)((((uint32_t)q + 1u) * (uint32_t)G - 1u) / (uint32_t)nq); }
+// Word offset of element quad q in a slot layout (CTA c's words start at c * sl).
+GG_DEV int slot_word(int nq, int G, int sl, int q) {
+  const int c = qowner(nq, G, q);
+  return c * sl + 4 * (q - qpart(nq, G, c));
+}
+
+// The planes of one x vector, as shared-window addresses.
+struct XPlanes {
+  uint32_t p0;   // signed top byte of each element's 24-bit fixed point value
+  uint32_t p1;   // middle byte (unsigned)
+  uint32_t p2;   // low byte (unsigned)
+  uint32_t inv;  // f32 2^(e - 23) per 16-element chunk
+};
+
+enum { RG_QKV = 0, RG_H = 2, RG_I = 4, RG_V = 6, RG_N = 8 };  // this CTA's [begin, end) rows / pairs
+
+struct Smem {
+  uint8_t* ring;
+  uint64_t* full;
+  uint64_t* empty;
+  float* lmv;   // this CTA's LM-head logits (rows [RG_V, RG_V + 1))
+  XPlanes xa;   // H-wide inputs: QKV, gate/up, LM head
+  XPlanes xb;   // Q- and I-wide inputs: O, down
+  float* hid;   // residual stream (identical in every CTA)
+  float* res;   // residual after the attention block
+  float* tmp;   // q | k | v of the current token
+  float4* scal;
+  float* red;   // [16 rows][NCW slices] partial sums of the small matvecs
+  int* flag;
+  int* rows;
+};
+
+// Per-launch constants, held in shared memory (filled by thread 0 at the start): keeping them out
+// of registers leaves the hot loops free of register spills.
+struct Ctx {
+  const GGModelDev* m;
+  GGState* st;
+  Smem S;
+  SpinCtl sc;
+  int mode, token, pos, seq, nsplit;
+  uint32_t tagbase;
+};
+
+// Rows per ring stage of a phase whose n rows (n <= NCW) are computed one per warp.
+GG_DEV int shared_rps(int rps_max, int n) { return max(min(rps_max, n), 1); }
+
+GG_DEV int window_lo(const GGLayerW& Lw, int pos) { return (Lw.window > 0 && pos + 1 > Lw.window) ? pos + 1 - Lw.window : 0; }
+
+// First split of this CTA in layer l (splits s >= slo with s - slo = (c - rot) mod G).
+GG_DEV int first_split(const GGModelDev& m, int l, int pos, int nsplit, int c) {
+  const int G = m.grid, rot = (l * nsplit) % G;
+  return window_lo(m.layers[l], pos) / m.pos_per_split + (c - rot + G) % G;
+}
+
+// ---------------------------------------------------------------------------------- producer
+
+template <bool KV16>
+struct Producer {
+  Ctx& x;
+  uint64_t pol;
+  bool ok = true;
+  uint32_t idx = 0;  // ring position
+
+  GG_DEV void issue(const void* s0, uint32_t b0, const void* s1, uint32_t b1, uint32_t off1) {
+    const int slot = idx % NS;
+    const uint32_t use = idx / NS;
+    if (use > 0 && ok) ok = mbar_wait(&x.S.empty[slot], (use - 1) & 1, x.sc);
+    if (!ok) return;
+    uint8_t* dst = x.S.ring + (size_t)slot * GG_STEP_STAGE_BYTES;
+    mbar_arrive_expect_tx(&x.S.full[slot], b0 + b1);
+    if (b0) bulk_g2s(dst, s0, b0, &x.S.full[slot], pol);
+    if (b1) bulk_g2s(dst + off1, s1, b1, &x.S.full[slot], pol);
+    idx++;
+  }
+  GG_DEV void rows(const uint8_t* W, int rs, int rb, int re, int rps) {
+    for (int r = rb; r < re && ok; r += rps) issue(W + (size_t)r * rs, (uint32_t)(min(rps, re - r) * rs), nullptr, 0, 0);
+  }
+  GG_DEV void run() {
+    const GGModelDev& m = *x.m;
+    const int c = blockIdx.x, G = m.grid;
+    const int* R = x.S.rows;
+    if (x.mode & GG_RUN_LAYERS) {
+      for (int l = 0; l < m.L && ok; l++) {
+        const GGLayerW& Lw = m.layers[l];
+        rows(Lw.wqkv, m.rs_h, R[RG_QKV], R[RG_QKV + 1], shared_rps(m.rps_h, R[RG_QKV + 1] - R[RG_QKV]));
+        for (int s = first_split(m, l, x.pos, x.nsplit, c); s < x.nsplit && ok; s += G) {
+          const int p0 = s * m.pos_per_split, pc = min(p0 + m.pos_per_split, x.pos);
+          constexpr int es = KV16 ? 2 : 4;
+          const uint32_t nb = pc > p0 ? (uint32_t)((pc - p0) * m.KV * es) : 0u;
+          const size_t off = ((size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + p0) * m.KV) * es;
+          issue(m.kcache + off, nb, m.vcache + off, nb, (uint32_t)(m.pos_per_split * m.KV * es));
+        }
+        rows(Lw.wo, m.rs_q, R[RG_H], R[RG_H + 1], shared_rps(m.rps_q, R[RG_H + 1] - R[RG_H]));
+        rows(Lw.wgu, m.rs_h, 2 * R[RG_I], 2 * R[RG_I + 1], m.rps_gu);
+        rows(Lw.wdown, m.rs_i, R[RG_H], R[RG_H + 1], shared_rps(m.rps_i, R[RG_H + 1] - R[RG_H]));
+      }
+    }
+    if ((x.mode & GG_RUN_LM) && ok) rows(m.embd, m.rs_h, R[RG_V], R[RG_V + 1], m.rps_gu);
+    // Drain: every copy issued into the ring must land before the CTA may exit.
+    const uint32_t n = idx < NS ? idx : NS;
+    for (uint32_t k = idx - n; k < idx; k++) {
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(&x.S.full[k % NS], (k / NS) & 1)) {
+        if (global_timer_ns() - t0 > x.sc.timeout_ns) { atomicOr(x.sc.err, GG_ERR_WAIT_MBAR); break; }
+      }
+    }
+  }
+};
+
+// The slow path of a tagged-word wait (one copy, out of line): re-poll the four words at p until
+// all carry `tag`. Bounded: on timeout (or an error raised elsewhere) the values read as 0 and
+// the error word is set.
+GG_NOINLINE void poll4(const uint64_t* p, uint32_t tag, const SpinCtl sc, float* v) {
+  uint64_t w0, w1, w2, w3;
+  bool a = false, b = false;
+  uint64_t t0 = 0;
+#pragma unroll 1
+  for (uint32_t it = 0; !(a && b); ++it) {
+    if (!a) {
+      ld2_relaxed(p, w0, w1);
+      a = (uint32_t)(w0 >> 32) == tag && (uint32_t)(w1 >> 32) == tag;
+    }
+    if (!b) {
+      ld2_relaxed(p + 2, w2, w3);
+      b = (uint32_t)(w2 >> 32) == tag && (uint32_t)(w3 >> 32) == tag;
+    }
+    if (it == 512) t0 = global_timer_ns();  // the first 512 polls read no clock
+    if (it > 512 && (it & 31u) == 0) {
+      const uint64_t dt = global_timer_ns() - t0;
+      if (dt > GG_QUIET_SPIN_NS && (*(volatile uint32_t*)sc.err || dt > sc.timeout_ns)) {
+        if (dt > sc.timeout_ns) atomicOr(sc.err, GG_ERR_WAIT_FLAG);
+        w0 = w1 = w2 = w3 = 0;
+        break;
+      }
+    }
+  }
+  v[0] = __uint_as_float((uint32_t)w0);
+  v[1] = __uint_as_float((uint32_t)w1);
+  v[2] = __uint_as_float((uint32_t)w2);
+  v[3] = __uint_as_float((uint32_t)w3);
+}
+
+// ---------------------------------------------------------------------------------- dot products
+
+// q . x over one Q8_0 row of K inputs held in shared memory (K int8 quants, then K/32 f16 scales):
+// lane l takes the 16-element chunks l, l + 32, ...; each chunk is three exact dp4a sums against
+// the byte planes of x, recombined in f32 and scaled by the chunk's 2^(e-23) and the block scale.
+// Every lane receives the row total.
+GG_DEV float dot_row(uint32_t row, int K, const XPlanes P) {
+  const int lane = threadIdx.x & 31, nch = K >> 4;
+  float acc = 0.f;
+#pragma unroll 2
+  for (int c = lane; c < nch; c += 32) {
+    const uint4 a0 = lds128(P.p0 + 16 * c);
+    const uint4 a1 = lds128(P.p1 + 16 * c);
+    const uint4 a2 = lds128(P.p2 + 16 * c);
+    const uint4 w = lds128(row + 16 * c);
+    const float sc = lds_half(row + K + 2 * (c >> 1)) * ldsf(P.inv + 4 * c);
+    int s0 = dp4a_ss((int)w.x, (int)a0.x, 0);
+    s0 = dp4a_ss((int)w.y, (int)a0.y, s0);
+    s0 = dp4a_ss((int)w.z, (int)a0.z, s0);
+    s0 = dp4a_ss((int)w.w, (int)a0.w, s0);
+    int s1 = dp4a_su((int)w.x, (int)a1.x, 0);
+    s1 = dp4a_su((int)w.y, (int)a1.y, s1);
+    s1 = dp4a_su((int)w.z, (int)a1.z, s1);
+    s1 = dp4a_su((int)w.w, (int)a1.w, s1);
+    int s2 = dp4a_su((int)w.x, (int)a2.x, 0);
+    s2 = dp4a_su((int)w.y, (int)a2.y, s2);
+    s2 = dp4a_su((int)w.z, (int)a2.z, s2);
+    s2 = dp4a_su((int)w.w, (int)a2.w, s2);
+    acc = fmaf(fmaf((float)s0, 65536.f, (float)(s1 * 256 + s2)), sc, acc);
+  }
+  return warp_sum(acc);
+}
+
+// Four rows (addresses r[0..3], equal width K) over the chunks [c0, c1): lane l takes chunks
+// c0 + l, c0 + l + 32, ...; each load of the x planes serves all four rows. Every lane receives
+// the four slice totals.
+GG_DEV float4 dot_rows4(const uint32_t (&r)[4], int K, int c0, int c1, const XPlanes& P) {
+  const int lane = threadIdx.x & 31;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int c = c0 + lane; c < c1; c += 32) {
+    const uint4 a0 = lds128(P.p0 + 16 * c);
+    const uint4 a1 = lds128(P.p1 + 16 * c);
+    const uint4 a2 = lds128(P.p2 + 16 * c);
+    const float is = ldsf(P.inv + 4 * c);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint4 w = lds128(r[k] + 16 * c);
+      const float sc = lds_half(r[k] + K + 2 * (c >> 1)) * is;
+      int s0 = dp4a_ss((int)w.x, (int)a0.x, 0);
+      s0 = dp4a_ss((int)w.y, (int)a0.y, s0);
+      s0 = dp4a_ss((int)w.z, (int)a0.z, s0);
+      s0 = dp4a_ss((int)w.w, (int)a0.w, s0);
+      int s1 = dp4a_su((int)w.x, (int)a1.x, 0);
+      s1 = dp4a_su((int)w.y, (int)a1.y, s1);
+      s1 = dp4a_su((int)w.z, (int)a1.z, s1);
+      s1 = dp4a_su((int)w.w, (int)a1.w, s1);
+      int s2 = dp4a_su((int)w.x, (int)a2.x, 0);
+      s2 = dp4a_su((int)w.y, (int)a2.y, s2);
+      s2 = dp4a_su((int)w.z, (int)a2.z, s2);
+      s2 = dp4a_su((int)w.w, (int)a2.w, s2);
+      acc[k] = fmaf(fmaf((float)s0, 65536.f, (float)(s1 * 256 + s2)), sc, acc[k]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int k = 0; k < 4; k++) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], o);
+  return make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// Row pairs by lane groups: the 8 lanes of group g (lane / 8) compute rows (ra, ra + rs) over the
+// chunks c = lane % 8, lane % 8 + 8, ...; the pair totals end up in every lane of the group.
+GG_DEV float2 dot_pair8(uint32_t ra, int rs, int K, const XPlanes& P) {
+  const int gl = threadIdx.x & 7, nch = K >> 4;
+  const uint32_t rb = ra + rs;
+  float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 2
+  for (int c = gl; c < nch; c += 8) {
+    const uint4 a0 = lds128(P.p0 + 16 * c);
+    const uint4 a1 = lds128(P.p1 + 16 * c);
+    const uint4 a2 = lds128(P.p2 + 16 * c);
+    const float is = ldsf(P.inv + 4 * c);
+    const uint4 wa = lds128(ra + 16 * c);
+    const uint4 wb = lds128(rb + 16 * c);
+    const float sa = lds_half(ra + K + 2 * (c >> 1)) * is;
+    const float sb = lds_half(rb + K + 2 * (c >> 1)) * is;
+    int x0 = dp4a_ss((int)wa.x, (int)a0.x, 0), y0 = dp4a_ss((int)wb.x, (int)a0.x, 0);
+    x0 = dp4a_ss((int)wa.y, (int)a0.y, x0); y0 = dp4a_ss((int)wb.y, (int)a0.y, y0);
+    x0 = dp4a_ss((int)wa.z, (int)a0.z, x0); y0 = dp4a_ss((int)wb.z, (int)a0.z, y0);
+    x0 = dp4a_ss((int)wa.w, (int)a0.w, x0); y0 = dp4a_ss((int)wb.w, (int)a0.w, y0);
+    int x1 = dp4a_su((int)wa.x, (int)a1.x, 0), y1 = dp4a_su((int)wb.x, (int)a1.x, 0);
+    x1 = dp4a_su((int)wa.y, (int)a1.y, x1); y1 = dp4a_su((int)wb.y, (int)a1.y, y1);
+    x1 = dp4a_su((int)wa.z, (int)a1.z, x1); y1 = dp4a_su((int)wb.z, (int)a1.z, y1);
+    x1 = dp4a_su((int)wa.w, (int)a1.w, x1); y1 = dp4a_su((int)wb.w, (int)a1.w, y1);
+    int x2 = dp4a_su((int)wa.x, (int)a2.x, 0), y2 = dp4a_su((int)wb.x, (int)a2.x, 0);
+    x2 = dp4a_su((int)wa.y, (int)a2.y, x2); y2 = dp4a_su((int)wb.y, (int)a2.y, y2);
+    x2 = dp4a_su((int)wa.z, (int)a2.z, x2); y2 = dp4a_su((int)wb.z, (int)a2.z, y2);
+    x2 = dp4a_su((int)wa.w, (int)a2.w, x2); y2 = dp4a_su((int)wb.w, (int)a2.w, y2);
+    acc0 = fmaf(fmaf((float)x0, 65536.f, (float)(x1 * 256 + x2)), sa, acc0);
+    acc1 = fmaf(fmaf((float)y0, 65536.f, (float)(y1 * 256 + y2)), sb, acc1);
+  }
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) {
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, o);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, o);
+  }
+  return make_float2(acc0, acc1);
+}
+
+// ---------------------------------------------------------------------------------- consumers
+
+template <bool KV16>
+struct Consumer {
+  Ctx& x;
+  int tid, lane, warp;
+  // Once a ring wait gives up, this warp stops waiting on and releasing slots, so the producer
+  // can never refill a slot whose copy might still be landing; it drains and exits.
+  bool dead = false;
+  int cslot = 0;
+  uint32_t idx = 0;  // ring position
+
+  // Every warp walks the ring in the producer's order and waits for and releases every stage,
+  // whether or not it computes on it: a slot's mbarrier phases are then never more than one use
+  // apart for any warp, which is what the parity waits require.
+  GG_DEV uint8_t* stage_wait() { return stage_wait_ahead(0); }
+  // Wait for the stage k places after the next one to release (k < NS).
+  GG_DEV uint8_t* stage_wait_ahead(int k) {
+    const uint32_t i = idx + (uint32_t)k;
+    const int slot = i % NS;
+    if (!dead) dead = !__all_sync(0xffffffffu, mbar_wait(&x.S.full[slot], (i / NS) & 1, x.sc));
+    return x.S.ring + (size_t)slot * GG_STEP_STAGE_BYTES;
+  }
+  GG_DEV void stage_done() {
+    __syncwarp();
+    if (lane == 0 && !dead) mbar_arrive(&x.S.empty[idx % NS]);
+    idx++;
+  }
+
+  // Trace stamps (GG_TRACE launches): globaltimer of event ev (0 enter, 1 inputs ready, 2 done)
+  // of phase ph: trace[(cta * GG_TRACE_PHASES + ph) * 4 + ev].
+  GG_DEV void trace(int ph, int ev) {
+    if (!(x.mode & GG_TRACE)) return;
+    if (ev == 2) cbar();  // "done" = every warp of the CTA finished the phase
+    if (tid == 0 && ph < GG_TRACE_PHASES)
+      x.m->trace[((size_t)blockIdx.x * GG_TRACE_PHASES + ph) * 4 + ev] = global_timer_ns();
+  }
+
+  // Poll until the four tagged words w (loaded from p) all carry `tag`; bounded. On timeout (or
+  // an error raised elsewhere) the values read as 0 and the error word is set.
+  GG_DEV void settle4(const uint64_t* p, uint32_t tag, uint64_t (&w)[4], float* v) {
+    const bool ready = (uint32_t)(w[0] >> 32) == tag && (uint32_t)(w[1] >> 32) == tag &&
+                       (uint32_t)(w[2] >> 32) == tag && (uint32_t)(w[3] >> 32) == tag;
+    if (ready) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) v[j] = __uint_as_float((uint32_t)w[j]);
+    } else {
+      poll4(p, tag, x.sc, v);
+    }
+  }
+  GG_DEV void issue4(const uint64_t* p, uint64_t (&w)[4]) {
+    ld2_relaxed(p, w[0], w[1]);
+    ld2_relaxed(p + 2, w[2], w[3]);
+  }
+
+  // NV sums over the consumer threads with one barrier; warps 0..nw-1 hold data and receive the
+  // totals (same summation order everywhere); the other warps only take part in the barrier.
+  template <int NV>
+  GG_DEV void csum(float* v, int nw) {
+    static_assert(NV <= 4, "at most four sums per call");
+    float4* s = x.S.scal + (cslot & 3) * NCW;
+    cslot++;
+    if (warp < nw) {
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < NV; k++) t[k] = warp_sum(v[k]);
+      if (lane == 0) s[warp] = make_float4(t[0], t[1], t[2], t[3]);
+    }
+    cbar();
+    if (warp < nw) {
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int w = 0; w < nw; w++) {
+        const float4 f = s[w];
+        t[0] += f.x; t[1] += f.y; t[2] += f.z; t[3] += f.w;
+      }
+#pragma unroll
+      for (int k = 0; k < NV; k++) v[k] = t[k];
+    }
+  }
+
+  // One element quad (4 consecutive values) of the planes, by the thread owning quad k. The four
+  // quads of a 16-element chunk sit on four consecutive lanes and share the chunk maximum by
+  // shuffles, so every lane of the warp must call this (ok = false: no quad).
+  // Chunk exponent e: max|x| < 2^e; X = round(x * 2^(23-e)) in (-2^23, 2^23), X = 65536*p0 + 256*p1 + p2.
+  GG_DEV void plane_quad(const XPlanes& P, int k, bool ok, const float* v) {
+    float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (!ok) return;
+    const int e = max((int)((__float_as_uint(mx) >> 23) & 255) - 126, -100);
+    const float s = __int_as_float((127 + 23 - e) << 23);
+    uint32_t X[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) X[j] = (uint32_t)min(max(__float2int_rn(v[j] * s), -8388607), 8388607);
+    // byte b of X[j] goes to byte j of plane 2 - b (b = 0, 1, 2: the 24-bit two's complement)
+    const uint32_t lo01 = __byte_perm(X[0], X[1], 0x5140), lo23 = __byte_perm(X[2], X[3], 0x5140);
+    const uint32_t hi01 = __byte_perm(X[0], X[1], 0x0062), hi23 = __byte_perm(X[2], X[3], 0x0062);
+    sts32(P.p0 + 4 * k, __byte_perm(hi01, hi23, 0x5410));
+    sts32(P.p1 + 4 * k, __byte_perm(lo01, lo23, 0x7632));
+    sts32(P.p2 + 4 * k, __byte_perm(lo01, lo23, 0x5410));
+    if ((k & 3) == 0) sts32(P.inv + 4 * (k >> 2), (uint32_t)((127 - 23 + e) << 23));
+  }
+
+  // Planes of nq element quads held in a slot layout (sl words per CTA slot) or contiguously
+  // (sl = 0), without normalisation: the inputs of the O and down projections. Every load of a
+  // thread (at most four quads) is in flight before any tag is checked.
+  GG_DEV void planes_gather(const XPlanes& P, const uint64_t* src, int nq, int sl, uint32_t tag) {
+    const int G = x.m->grid;
+    for (int base = 0; base < nq; base += 2 * NCT) {  // two quads per thread in flight
+      uint64_t w[2][4];
+      const uint64_t* pk[2];
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const int q = base + tid + k * NCT;
+        pk[k] = src + (sl ? slot_word(nq, G, sl, q) : 4 * q);
+        if (q < nq) issue4(pk[k], w[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        const int q = base + tid + k * NCT;
+        if (base + k * NCT >= nq) break;  // uniform over the CTA
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (q < nq) settle4(pk[k], tag, w[k], v);
+        plane_quad(P, q, q < nq, v);
+      }
+    }
+  }
+
+  // out = base + v * wa / r1 with r1 = rms(v) (shaders.ts:386-418; v = the tagged words of a
+  // slot layout), then the planes of out * wb / r2 with r2 = rms(out) (shaders.ts:25-56). One
+  // barrier: the sums of v^2, base^2, base*v*wa and (v*wa)^2 give both norms. Thread t owns
+  // element quad t; the weights are fetched before the wait.
+  GG_DEV void add_norm_planes(const XPlanes& P, const uint64_t* src, uint32_t tag, const float* wa, const float* base,
+                              float* out, const float* wb, float* dbg_out, float* dbg_x) {
+    const GGModelDev& m = *x.m;
+    const int nq = m.H >> 2, k = tid, nw = (nq + 31) >> 5;
+    const bool ok = k < nq;
+    float4 fa = make_float4(0.f, 0.f, 0.f, 0.f), fb = fa, fbase = fa;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+      const uint64_t* p = src + slot_word(nq, m.grid, m.sl_h, k);
+      uint64_t w[4];
+      issue4(p, w);
+      fa = __ldg(reinterpret_cast<const float4*>(wa) + k);
+      fb = __ldg(reinterpret_cast<const float4*>(wb) + k);
+      fbase = reinterpret_cast<const float4*>(base)[k];
+      settle4(p, tag, w, v);
+    }
+    const float wav[4] = {fa.x, fa.y, fa.z, fa.w}, wbv[4] = {fb.x, fb.y, fb.z, fb.w};
+    const float bv[4] = {fbase.x, fbase.y, fbase.z, fbase.w};
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float vw = v[j] * wav[j];
+      s[0] += v[j] * v[j];
+      s[1] += bv[j] * bv[j];
+      s[2] += bv[j] * vw;
+      s[3] += vw * vw;
+    }
+    csum<4>(s, nw);
+    if (warp >= nw) return;
+    // one square root and one division per norm (x * w / rms as x * w * (1 / rms))
+    const float invh = 1.0f / (float)m.H;
+    const float i1 = 1.0f / sqrtf(s[0] * invh + m.eps);
+    const float i2 = 1.0f / sqrtf((s[1] + 2.f * s[2] * i1 + s[3] * (i1 * i1)) * invh + m.eps);
+    float o[4], xv[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      o[j] = bv[j] + v[j] * wav[j] * i1;
+      xv[j] = o[j] * wbv[j] * i2;
+    }
+    if (ok) {
+      reinterpret_cast<float4*>(out)[k] = make_float4(o[0], o[1], o[2], o[3]);
+      if (dbg_out) reinterpret_cast<float4*>(dbg_out)[k] = make_float4(o[0], o[1], o[2], o[3]);
+      if (dbg_x) reinterpret_cast<float4*>(dbg_x)[k] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+    }
+    plane_quad(P, k, ok, xv);
+  }
+
+  // x = rmsNorm(h) * wb for a hidden state h already in hand (thread t: quad t), as planes.
+  GG_DEV void norm_planes(const XPlanes& P, const float* h, bool ok, const float* wb, float* dbg_x) {
+    const GGModelDev& m = *x.m;
+    const int k = tid, nw = ((m.H >> 2) + 31) >> 5;
+    float4 fb = make_float4(0.f, 0.f, 0.f, 0.f);
+    float s[1] = {0.f};
+    if (ok) {
+      fb = __ldg(reinterpret_cast<const float4*>(wb) + k);
+#pragma unroll
+      for (int j = 0; j < 4; j++) s[0] += h[j] * h[j];
+    }
+    csum<1>(s, nw);
+    if (warp >= nw) return;
+    const float ir = 1.0f / sqrtf(s[0] * (1.0f / (float)m.H) + m.eps);
+    const float wbv[4] = {fb.x, fb.y, fb.z, fb.w};
+    float xv[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) xv[j] = h[j] * wbv[j] * ir;
+    if (ok && dbg_x) reinterpret_cast<float4*>(dbg_x)[k] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+    plane_quad(P, k, ok, xv);
+  }
+
+  // shaders.ts:2-23: h[i] = q * d * sqrt(H), evaluated left to right in f32; then the planes of
+  // rmsNorm(h) * wb.
+  GG_DEV void embed_planes(const XPlanes& P, const float* wb) {
+    const GGModelDev& m = *x.m;
+    const uint8_t* row = m.embd + (size_t)x.token * m.rs_h;
+    const float sq = sqrtf((float)m.H);
+    const int k = tid;
+    const bool ok = k < (m.H >> 2);
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+      const float d = __half2float(*reinterpret_cast<const __half*>(row + m.H + 2 * ((4 * k) >> 5)));
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        float vv = (float)(int8_t)row[4 * k + j] * d;
+        o[j] = vv * sq;
+      }
+      reinterpret_cast<float4*>(x.S.hid)[k] = make_float4(o[0], o[1], o[2], o[3]);
+    }
+    norm_planes(P, o, ok, wb, nullptr);
+  }
+
+  // The CTA's n rows (n <= 16) of a phase, in nst ring stages of d = shared_rps(rps_max, n) rows
+  // (all resident at once: the host checks nst < NS). Work units are (group of four rows, K
+  // slice): warp w takes group w / S and slice w % S, S = NCW / groups, so the four rows share
+  // every load of the x planes. The slice totals meet in shared memory; thread r < n sums them in
+  // slice order and passes the row total to epi(r, value). Every consumer warp must call this
+  // (it holds a CTA barrier).
+  template <class Epi>
+  GG_DEV void matvec(const XPlanes& P, int n, int rps_max, int K, int rs, Epi epi) {
+    const int d = shared_rps(rps_max, n), nst = (n + d - 1) / d;
+    const int ng = (n + 3) >> 2, S = NCW / ng, nch = K >> 4;
+    const int g = warp / S, sl = warp % S;
+    for (int k = 0; k < nst; k++) stage_wait_ahead(k);
+    float* red = x.S.red;  // [row][slice]
+    if (g < ng) {
+      uint32_t ra[4];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int r = min(4 * g + k, n - 1);  // rows past n repeat the last row; their sums are dropped
+        ra[k] = smem_u32(x.S.ring) + (uint32_t)(((idx + (uint32_t)(r / d)) % NS) * GG_STEP_STAGE_BYTES + (r % d) * rs);
+      }
+      const float4 v = dot_rows4(ra, K, sl * nch / S, (sl + 1) * nch / S, P);
+      if (lane == 0) {
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+          if (4 * g + k < n) red[(4 * g + k) * S + sl] = vv[k];
+      }
+    }
+    for (int k = 0; k < nst; k++) stage_done();
+    cbar();
+    if (tid < n) {
+      float t = 0.f;
+      for (int k = 0; k < S; k++) t += red[tid * S + k];
+      epi(tid, t);
+    }
+  }
+
+  // Row pairs (2j, 2j + 1), rps / 2 pairs per ring stage, in units of four pairs: unit n goes to
+  // warp n % NCW, whose four 8-lane groups take one pair each; the group's first lane passes the
+  // pair to epi(j, row 2j, row 2j + 1).
+  template <class Epi>
+  GG_DEV void matvec_pairs(const XPlanes& P, int npairs, int rps, int K, int rs, Epi epi) {
+    const int pps = rps >> 1, g = lane >> 3;
+    int unit = 0;
+    for (int j0 = 0; j0 < npairs; j0 += pps) {
+      const uint8_t* stg = stage_wait();
+      const int j1 = min(j0 + pps, npairs);
+      for (int u = j0; u < j1; u += 4, unit++) {
+        if (unit % NCW != warp) continue;
+        const int j = u + g;
+        const float2 v = dot_pair8(smem_u32(stg) + (uint32_t)(2 * (min(j, j1 - 1) - j0) * rs), rs, K, P);
+        if ((lane & 7) == 0 && j < j1) epi(j, v.x, v.y);
+      }
+      stage_done();
+    }
+  }
+
+  GG_DEV void phase_qkv(int l) {
+    const GGModelDev& m = *x.m;
+    if (l == 0) {
+      embed_planes(x.S.xa, m.layers[0].attn_norm);
+    } else {  // hidden = residual + post_ffw_norm(down) (engine.ts:794), attention rmsNorm (768)
+      add_norm_planes(x.S.xa, m.t_down, make_tag(x.tagbase, (l - 1) * PH + 5), m.layers[l - 1].post_ffw_norm, x.S.res,
+                      x.S.hid, m.layers[l].attn_norm, blockIdx.x == 0 ? m.dbg_hidden : nullptr, nullptr);
+    }
+    cbar();
+    trace(l * PH + 0, 1);
+    uint64_t* out = m.t_qkv + (size_t)blockIdx.x * m.sl_qkv;
+    const uint32_t tag = make_tag(x.tagbase, l * PH + 0);
+    const int n = x.S.rows[RG_QKV + 1] - x.S.rows[RG_QKV];
+    matvec(x.S.xa, n, m.rps_h, m.H, m.rs_h, [&](int r, float v) { tag_store(out + r, v, tag); });
+  }
+
+  // q/k per-head RMSNorm + RoPE (shaders.ts:420-467), the KV store (shaders.ts:209-227) and this
+  // CTA's attention splits (shaders.ts:229-325) with local softmax statistics.
+  GG_DEV void phase_attn(int l) {
+    const GGModelDev& m = *x.m;
+    const GGLayerW& Lw = m.layers[l];
+    const int G = m.grid, s0 = first_split(m, l, x.pos, x.nsplit, blockIdx.x);
+    if (s0 >= x.nsplit) return;
+    const int HD = m.HD, NQH = m.NQH, NKH = m.NKH, Q = m.Q, KV = m.KV;
+    constexpr int NJ = GG_HEAD_DIM / 32;
+    float* t = x.S.tmp;  // q [Q] | k [KV] | v [KV]
+    const uint32_t tagA = make_tag(x.tagbase, l * PH + 0);
+    // gather q | k | v into shared memory (every thread at most one quad in flight per 512)
+    const int nq = (Q + 2 * KV) >> 2;
+    for (int base = 0; base < nq; base += NCT) {
+      const int q = base + tid;
+      if (q < nq) {
+        const uint64_t* p = m.t_qkv + slot_word(nq, G, m.sl_qkv, q);
+        uint64_t w[4];
+        float v[4];
+        issue4(p, w);
+        settle4(p, tagA, w, v);
+        reinterpret_cast<float4*>(t)[q] = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
+    cbar();
+    // per-head norm + RoPE: one warp per q or k head; lane l holds elements l + 32j, so the
+    // RoPE pair (i, i + HD/2) is in one lane
+    for (int h = warp; h < NQH + NKH; h += NCW) {
+      const float* nw = h < NQH ? Lw.q_norm : Lw.k_norm;
+      float* hp = t + h * HD;
+      float v[NJ];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        v[j] = hp[lane + 32 * j];
+        ss += v[j] * v[j];
+      }
+      const float ir = 1.0f / sqrtf(warp_sum(ss) * (1.0f / (float)HD) + m.eps);
+#pragma unroll
+      for (int j = 0; j < NJ; j++) v[j] = v[j] * __ldg(nw + lane + 32 * j) * ir;
+#pragma unroll
+      for (int j = 0; j < NJ / 2; j++) {
+        const float2 cr = __ldg(Lw.rope + (size_t)x.pos * (HD / 2) + lane + 32 * j);  // (cos, sin)
+        const float x0 = v[j], x1 = v[j + NJ / 2];
+        v[j] = x0 * cr.x - x1 * cr.y;
+        v[j + NJ / 2] = x0 * cr.y + x1 * cr.x;
+      }
+      if (KV16 && h >= NQH) {  // bf16 cache: attention reads the stored (rounded) k
+#pragma unroll
+        for (int j = 0; j < NJ; j++) v[j] = bf16_rne(v[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < NJ; j++) hp[lane + 32 * j] = v[j];
+    }
+    if (KV16) {  // the stored (rounded) v as well
+      for (int i = tid; i < KV; i += NCT) t[Q + KV + i] = bf16_rne(t[Q + KV + i]);
+    }
+    cbar();
+    trace(l * PH + 1, 1);
+    // the CTA whose splits include the new position stores its k and v
+    if ((x.pos / m.pos_per_split - s0) % G == 0 && x.pos / m.pos_per_split >= s0) {
+      using KT = kv_t<KV16>;
+      const size_t off = (size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + x.pos) * KV;
+      KT* kc = reinterpret_cast<KT*>(m.kcache);
+      KT* vc = reinterpret_cast<KT*>(m.vcache);
+      for (int i = tid; i < KV; i += NCT) {
+        kc[off + i] = kv_narrow<KV16>(t[Q + i]);
+        vc[off + i] = kv_narrow<KV16>(t[Q + KV + i]);
+      }
+    }
+    const uint32_t tag = make_tag(x.tagbase, l * PH + 1);
+    const int plo = window_lo(Lw, x.pos);
+    // split k of this CTA is handled by warps NQH*k .. NQH*k + NQH - 1 (one per query head);
+    // every warp acquires and releases every stage
+    int k = 0;
+    for (int s = s0; s < x.nsplit; s += G, k++) {
+      const uint8_t* stg = stage_wait();
+      if (warp / NQH == k) attn_split(s, plo, stg, warp % NQH, tag);
+      stage_done();
+    }
+  }
+
+  // One split of PPS positions for query head h (one warp): K rows at the start of the stage, V
+  // rows after PPS K rows; the current position's k and v come from the scratch vector.
+  // Output: the split's unnormalised o (256 values), its max and its sum of exp, into the split's
+  // slot of the exchange buffer.
+  __device__ __noinline__ void attn_split(int s, int plo, const uint8_t* stg, int h, uint32_t tag) {
+    using KT = kv_t<KV16>;
+    const GGModelDev& m = *x.m;
+    const int Q = m.Q, KV = m.KV, HD = m.HD, NQH = m.NQH, NKH = m.NKH, PPS = m.pos_per_split;
+    static_assert(GG_HEAD_DIM == 8 * 32, "a lane holds 8 dims of a head");
+    const float* t = x.S.tmp;
+    const int p0 = s * PPS, p1 = min(p0 + PPS, x.pos + 1), np = p1 - p0;
+    const int pv = max(plo - p0, 0);  // positions before pv are outside the window
+    const KT* Kst = reinterpret_cast<const KT*>(stg);
+    const KT* Vst = reinterpret_cast<const KT*>(stg + (size_t)PPS * KV * sizeof(KT));
+    const auto row8 = [&](const KT* st_row, const float* cur_row, bool cached, float* f) {
+      if (cached && KV16) {
+        bf16x8_widen(*reinterpret_cast<const uint4*>(st_row + 8 * lane), f);
+      } else {
+        if (cached) cur_row = reinterpret_cast<const float*>(st_row);
+        const float4 a = reinterpret_cast<const float4*>(cur_row + 8 * lane)[0];
+        const float4 b = reinterpret_cast<const float4*>(cur_row + 8 * lane)[1];
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+      }
+    };
+    const int kvh = h * NKH / NQH;
+    float qv[8];
+    row8(nullptr, t + h * HD, false, qv);
+    // Every position reads a valid row (positions outside [pv, np) read row pv and weigh zero),
+    // so the dot products and their warp sums carry no per-position branch.
+    float sc[GG_POS_PER_SPLIT];
+#pragma unroll
+    for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+      const int pp = (p >= pv && p < np) ? p : pv;
+      float kf[8];
+      row8(Kst + (size_t)pp * KV + kvh * HD, t + Q + kvh * HD, p0 + pp < x.pos, kf);
+      float d = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) d = fmaf(qv[j], kf[j], d);
+      sc[p] = d;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int p = 0; p < GG_POS_PER_SPLIT; p++) sc[p] += __shfl_xor_sync(0xffffffffu, sc[p], o);
+    float mx = -1e30f;
+#pragma unroll
+    for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+      sc[p] *= m.attn_scale;
+      if (p >= pv && p < np) mx = fmaxf(mx, sc[p]);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+      sc[p] = (p >= pv && p < np) ? expf(sc[p] - mx) : 0.f;
+      sum += sc[p];
+    }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
+      const int pp = (p >= pv && p < np) ? p : pv;
+      float vf[8];
+      row8(Vst + (size_t)pp * KV + kvh * HD, t + Q + KV + kvh * HD, p0 + pp < x.pos, vf);
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[j] = fmaf(sc[p], vf[j], acc[j]);
+    }
+    uint64_t* o = m.t_o + (size_t)s * m.att_slot + (size_t)h * (HD + 4);
+#pragma unroll
+    for (int j = 0; j < 8; j++) tag_store(o + 8 * lane + j, acc[j], tag);
+    if (lane == 0) {  // the split's header quad: max, sum of exp, two zero words (one 16-byte pair each)
+      tag_store(o + HD, mx, tag);
+      tag_store(o + HD + 1, sum, tag);
+      tag_store(o + HD + 2, 0.f, tag);
+      tag_store(o + HD + 3, 0.f, tag);
+    }
+  }
+
+  // Merge of the attention splits (online softmax) for 8 output dimensions per unit: warp 0 of
+  // the unit's CTA, lanes over splits, every load of a batch in flight before any check.
+  GG_DEV void phase_combine(int l) {
+    const GGModelDev& m = *x.m;
+    const int HD = m.HD, ncomb = m.Q >> 3;
+    const uint32_t tagB = make_tag(x.tagbase, l * PH + 1);
+    const uint32_t tagC = make_tag(x.tagbase, l * PH + 2);
+    const int slo = window_lo(m.layers[l], x.pos) / m.pos_per_split;
+    if (warp == 0) {
+      for (int u = blockIdx.x; u < ncomb; u += m.grid) {
+        const int d0 = 8 * u, h = d0 / HD, dh = d0 % HD;
+        float mx = -INFINITY, lsum = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int sb = slo; sb < x.nsplit; sb += 32) {  // one split per lane in flight
+          const int s = sb + lane;
+          if (s < x.nsplit) {
+            const uint64_t* pb = m.t_o + (size_t)s * m.att_slot + (size_t)h * (HD + 4);
+            uint64_t wml[4], wo0[4], wo1[4];
+            issue4(pb + HD, wml);
+            issue4(pb + dh, wo0);
+            issue4(pb + dh + 4, wo1);
+            float fml[4], f0[4], f1[4];
+            settle4(pb + HD, tagB, wml, fml);
+            settle4(pb + dh, tagB, wo0, f0);
+            settle4(pb + dh + 4, tagB, wo1, f1);
+            const float nm = fmaxf(mx, fml[0]);
+            const float a = (mx == -INFINITY) ? 0.f : expf(mx - nm);
+            const float b = expf(fml[0] - nm);
+            lsum = fmaf(b, fml[1], lsum * a);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              acc[j] = fmaf(b, f0[j], acc[j] * a);
+              acc[4 + j] = fmaf(b, f1[j], acc[4 + j] * a);
+            }
+            mx = nm;
+          }
+        }
+        const float gm = warp_max(mx);
+        const float f = (mx == -INFINITY) ? 0.f : expf(mx - gm);
+        lsum = warp_sum(lsum * f);
+        float res = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const float a = warp_sum(acc[j] * f);
+          if (lane == j) res = a;
+        }
+        if (lane < 8) tag_store(m.t_att + d0 + lane, res / lsum, tagC);
+      }
+    }
+    cbar();  // the other warps wait here instead of polling the merged words
+  }
+
+  GG_DEV void phase_o(int l) {
+    const GGModelDev& m = *x.m;
+    planes_gather(x.S.xb, m.t_att, m.Q >> 2, 0, make_tag(x.tagbase, l * PH + 2));
+    cbar();
+    trace(l * PH + 3, 1);
+    uint64_t* out = m.t_proj + (size_t)blockIdx.x * m.sl_h;
+    const uint32_t tag = make_tag(x.tagbase, l * PH + 3);
+    const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
+    matvec(x.S.xb, n, m.rps_q, m.Q, m.rs_q, [&](int r, float v) { tag_store(out + r, v, tag); });
+  }
+
+  GG_DEV void phase_ffn_up(int l) {
+    const GGModelDev& m = *x.m;
+    const GGLayerW& Lw = m.layers[l];
+    // residual = hidden + post_attention_norm(proj) (engine.ts:785), then ffn rmsNorm (786)
+    add_norm_planes(x.S.xa, m.t_proj, make_tag(x.tagbase, l * PH + 3), Lw.post_attn_norm, x.S.hid, x.S.res,
+                    Lw.ffn_norm, blockIdx.x == 0 ? m.dbg_residual : nullptr, nullptr);
+    cbar();
+    trace(l * PH + 4, 1);
+    uint64_t* out = m.t_act + (size_t)blockIdx.x * m.sl_i;
+    const uint32_t tag = make_tag(x.tagbase, l * PH + 4);
+    const int n = x.S.rows[RG_I + 1] - x.S.rows[RG_I];
+    // gate_i and up_i are adjacent rows (2i, 2i + 1): GeGLU on the pair (shaders.ts:153-170)
+    matvec_pairs(x.S.xa, n, m.rps_gu, m.H, m.rs_h,
+                 [&](int j, float g, float u) { tag_store(out + j, gelu_tanh(g) * u, tag); });
+  }
+
+  GG_DEV void phase_down(int l) {
+    const GGModelDev& m = *x.m;
+    planes_gather(x.S.xb, m.t_act, m.I >> 2, m.sl_i, make_tag(x.tagbase, l * PH + 4));
+    cbar();
+    trace(l * PH + 5, 1);
+    uint64_t* out = m.t_down + (size_t)blockIdx.x * m.sl_h;
+    const uint32_t tag = make_tag(x.tagbase, l * PH + 5);
+    const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
+    matvec(x.S.xb, n, m.rps_i, m.I, m.rs_i, [&](int r, float v) { tag_store(out + r, v, tag); });
+  }
+
+  GG_DEV void phase_lm() {
+    const GGModelDev& m = *x.m;
+    if (x.mode & GG_RUN_LAYERS) {  // hidden = residual + post_ffw_norm(down), final rmsNorm (engine.ts:797-801)
+      add_norm_planes(x.S.xa, m.t_down, make_tag(x.tagbase, (m.L - 1) * PH + 5), m.layers[m.L - 1].post_ffw_norm,
+                      x.S.res, x.S.hid, m.out_norm, blockIdx.x == 0 ? m.dbg_hidden : nullptr,
+                      blockIdx.x == 0 ? m.dbg_normed : nullptr);
+    } else {  // LM head on the hidden state a previous launch left behind
+      const bool ok = tid < (m.H >> 2);
+      float h[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ok) {
+        const float4 f = reinterpret_cast<const float4*>(m.dbg_hidden)[tid];
+        h[0] = f.x; h[1] = f.y; h[2] = f.z; h[3] = f.w;
+        reinterpret_cast<float4*>(x.S.hid)[tid] = f;
+      }
+      norm_planes(x.S.xa, h, ok, m.out_norm, blockIdx.x == 0 ? m.dbg_normed : nullptr);
+    }
+    cbar();
+    const int rb = x.S.rows[RG_V], re = x.S.rows[RG_V + 1];
+    float* lg = x.S.lmv;  // this CTA's logits, row rb + i at i
+    float2* gl = reinterpret_cast<float2*>(m.logits + rb);
+    matvec_pairs(x.S.xa, (re - rb) >> 1, m.rps_gu, m.H, m.rs_h, [&](int j, float a, float b) {
+      reinterpret_cast<float2*>(lg)[j] = make_float2(a, b);
+      gl[j] = make_float2(a, b);
+    });
+    cbar();
+    // topk256 lanes (shaders.ts:363-384): lane t keeps the largest logit among rows = t (mod 256)
+    // with strict '>' from (-1e30, 0), so the first index wins a tie; NaN is never taken and -0
+    // is keyed as +0. One thread per lane scans this CTA's rows of that lane in index order.
+    if (tid < 256) {
+      const unsigned long long ik = init_lane_key();
+      unsigned long long best = ik;
+      for (int r = rb + ((tid - rb) & 255); r < re; r += 256) {
+        float v = lg[r - rb];
+        if (!isnan(v)) {
+          if (v == 0.0f) v = 0.0f;
+          const unsigned long long k = ((unsigned long long)f32_order_key(v) << 32) | (0xffffffffu - (uint32_t)r);
+          best = k > best ? k : best;
+        }
+      }
+      if (best != ik) atomicMax(&m.lane_keys[tid], best);
+    }
+  }
+
+  GG_DEV void run() {
+    const GGModelDev& m = *x.m;
+    if (x.mode & GG_RUN_LAYERS) {
+      for (int l = 0; l < m.L; l++) {
+        trace(l * PH + 0, 0);
+        phase_qkv(l);
+        trace(l * PH + 0, 2);
+        trace(l * PH + 1, 0);
+        phase_attn(l);
+        trace(l * PH + 1, 2);
+        trace(l * PH + 2, 0);
+        phase_combine(l);
+        trace(l * PH + 2, 2);
+        trace(l * PH + 3, 0);
+        phase_o(l);
+        trace(l * PH + 3, 2);
+        trace(l * PH + 4, 0);
+        phase_ffn_up(l);
+        trace(l * PH + 4, 2);
+        trace(l * PH + 5, 0);
+        phase_down(l);
+        trace(l * PH + 5, 2);
+      }
+      if (!(x.mode & GG_RUN_LM)) {  // leave the hidden state for a later LM-head launch
+        add_norm_planes(x.S.xa, m.t_down, make_tag(x.tagbase, (m.L - 1) * PH + 5), m.layers[m.L - 1].post_ffw_norm,
+                        x.S.res, x.S.hid, m.out_norm, blockIdx.x == 0 ? m.dbg_hidden : nullptr, nullptr);
+      }
+    }
+    if (x.mode & GG_RUN_LM) {
+      trace(m.L * PH, 0);
+      phase_lm();
+      trace(m.L * PH, 2);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------- kernel
+
+template <bool KV16>
+GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ Ctx x;
+  const GGModelDev& m = *mp;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+  x.m = mp;
+  x.st = st;
+  x.mode = st->mode;
+  x.token = st->token;
+  x.pos = st->pos;
+  x.seq = st->seq;
+  x.tagbase = st->epoch;
+  x.sc.err = &st->error;
+  x.sc.timeout_ns = st->timeout_ns;
+  // carve shared memory (offsets and GGModelDev::smem_bytes computed by the host)
+  x.S.ring = smem;
+  x.S.full = reinterpret_cast<uint64_t*>(smem + (size_t)NS * GG_STEP_STAGE_BYTES);
+  x.S.empty = x.S.full + NS;
+  XPlanes* xp[2] = {&x.S.xa, &x.S.xb};
+  const int xsz[2] = {m.xs0, m.xs1}, xoff[2] = {m.sm_xa, m.sm_xb};
+  for (int b = 0; b < 2; b++) {
+    const uint32_t a = smem_u32(smem + xoff[b]);
+    xp[b]->p0 = a;
+    xp[b]->p1 = a + xsz[b];
+    xp[b]->p2 = a + 2 * xsz[b];
+    xp[b]->inv = a + 3 * xsz[b];
+  }
+  x.S.hid = reinterpret_cast<float*>(smem + m.sm_hid);
+  x.S.res = reinterpret_cast<float*>(smem + m.sm_res);
+  x.S.tmp = reinterpret_cast<float*>(smem + m.sm_tmp);
+  x.S.lmv = reinterpret_cast<float*>(smem + m.sm_lmv);
+  x.S.scal = reinterpret_cast<float4*>(smem + m.sm_scal);
+  x.S.red = reinterpret_cast<float*>(smem + m.sm_red);
+  x.S.flag = reinterpret_cast<int*>(smem + m.sm_flag);
+  x.S.rows = reinterpret_cast<int*>(smem + m.sm_rows);
+
+  const bool bad = x.token < 0 || x.token >= m.V || x.pos < 0 || x.pos >= m.CTX || x.seq < 0 || x.seq >= m.max_seqs;
+  if (bad) {
+    if (blockIdx.x == 0) atomicOr(&st->error, GG_ERR_BAD_INPUT);
+    x.mode = 0;
+  }
+  x.nsplit = (x.pos + m.pos_per_split) / m.pos_per_split;  // ceil((pos + 1) / PPS)
+    for (int i = 0; i < (int)NS; i++) {
+      mbar_init(&x.S.full[i], 1);
+      mbar_init(&x.S.empty[i], NCW);
+    }
+    mbar_fence_init();
+    const int c = blockIdx.x, G = m.grid;
+    const int nq[4] = {(m.Q + 2 * m.KV) >> 2, m.H >> 2, m.I >> 2, m.V >> 2};
+    for (int k = 0; k < 4; k++) {
+      x.S.rows[2 * k] = 4 * qpart(nq[k], G, c);
+      x.S.rows[2 * k + 1] = 4 * qpart(nq[k], G, c + 1);
+    }
+  }
+  __syncthreads();
+
+  if (warp == NCW) {
+    if (lane == 0) {
+      Producer<KV16> pr{x, l2_policy_evict_first()};
+      pr.run();
+    }
+  } else {
+    Consumer<KV16> cs{x, (int)threadIdx.x, lane, warp};
+    cs.run();
+  }
+  __syncthreads();
+
+  // End of launch: the last CTA to arrive runs the sampler and hands the state on.
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t t = atomicAdd(&st->done, 1u);
+    *x.S.flag = (t == (uint32_t)m.grid - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!*x.S.flag) return;
+  __threadfence();
+  int tok = -1;
+  if (x.mode & GG_RUN_SAMPLE) tok = sample_token(m, st);
+  __syncthreads();
+  if (threadIdx.x < 256) m.lane_keys[threadIdx.x] = init_lane_key();
+  if (threadIdx.x == 0) {
+    st->epoch = st->epoch + (uint32_t)(m.L * PH + 1);
+    st->done = 0;
+    if (x.mode & GG_RUN_SAMPLE) {
+      st->out_token = tok;
+      if (tok >= 0 && tok < m.V) {
+        uint8_t* seen = m.seen + (size_t)x.seq * m.seen_stride;
+        seen[tok >> 3] |= (uint8_t)(1u << (tok & 7));
+        st->seen_count = st->seen_count + 1;
+        if (m.seen_cnt) m.seen_cnt[x.seq] += 1;
+      }
+      if (st->token_ring && st->ring_len > 0) st->token_ring[st->step_index % st->ring_len] = tok;
+      st->step_index = st->step_index + 1;
+      if (st->uniforms) st->uniforms = st->uniforms + 1;
+      st->token = tok;
+      st->pos = x.pos + 1;
+    } else if (x.mode & GG_PREFILL_ADVANCE) {
+      if (st->prefill_left > 0) {
+        st->token = *st->prefill_ids;
+        st->prefill_ids = st->prefill_ids + 1;
+        st->prefill_left = st->prefill_left - 1;
+      }
+      st->pos = x.pos + 1;
+    }
+  }
+}
+
+}  // namespace step
+
+extern "C" __global__ void __launch_bounds__(step::NTH, 1)
+    gg_step_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
+  step::step_body<false>(mp, st);
+}
+
+// The same kernel for a bf16 KV cache (GG_FLAG_KV_BF16).
+extern "C" __global__ void __launch_bounds__(step::NTH, 1)
+    gg_step_kernel_kv16(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
+  step::step_body<true>(mp, st);
+}
+
+}  // namespace gg
