@@ -63,9 +63,15 @@ def measured_peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-# ncu capture of the same kernel on this workload (its summary is kept under profiles/):
-# dram bytes read + written per launch, or None before a capture exists.
-NCU_TRAFFIC_PER_LAUNCH = 1103156224 + 4640000  # 1B model, one launch at position 641 (grid 128, 5-stage ring)
+# ncu capture of the step kernel on this workload (summary under profiles/): dram bytes read +
+# written by one launch at position NCU_TRAFFIC_POS. The line reports it moved to the mean timed
+# position by the KV bytes per position (the weights are the same every token).
+NCU_TRAFFIC_PER_LAUNCH = 1103156224 + 4640000
+NCU_TRAFFIC_POS = 641
+
+
+def traffic_at(pos: float) -> int:
+    return int(NCU_TRAFFIC_PER_LAUNCH + KV_BYTES_PER_POS * (pos - NCU_TRAFFIC_POS))
 
 
 class ClockSampler:
@@ -155,9 +161,13 @@ def dist_setup(n_gpus: int):
     return rank, local, world, None, None
 
 
-def cpu_oracle_rate(tensors, cfg, n_tokens: int, prompt_len: int = 4, threads: int | None = None):
+def cpu_oracle_rate(tensors, cfg, n_tokens: int, prompt_len: int = 4, threads: int | None = None,
+                    start_pos: int = PROMPT_LEN):
     """Decode tok/s of the CPU restatement on a bounded sample, on every host core (threads=None)
-    or on `threads` threads; returns (tok/s, threads, sample)."""
+    or on `threads` threads; returns (tok/s, threads, sample). The decode runs at the GPU arm's
+    positions (from start_pos = 512): a short prompt fills the first cache rows and the rows up to
+    start_pos stay empty, so each token reads as many KV rows as the GPU arm's tokens do without
+    a CPU prefill of 512 tokens."""
     from oracle import oracle
     from gemma_b200 import synth
 
@@ -171,7 +181,7 @@ def cpu_oracle_rate(tensors, cfg, n_tokens: int, prompt_len: int = 4, threads: i
     for i, t in enumerate(prompt):
         m.forward(int(t), i)
     tok = oracle.argmax(m.logits())
-    pos = prompt_len
+    pos = max(start_pos, prompt_len)
     t0 = time.perf_counter()
     for _ in range(n_tokens):
         m.forward(tok, pos)
@@ -179,8 +189,10 @@ def cpu_oracle_rate(tensors, cfg, n_tokens: int, prompt_len: int = 4, threads: i
         pos += 1
     dt = time.perf_counter() - t0
     m.close()
+    p0 = max(start_pos, prompt_len)
     sample = (f"1B synthetic (seed 1), {prompt_len}-token prompt then {n_tokens} greedy decode tokens at positions "
-              f"{prompt_len}..{prompt_len + n_tokens - 1}, full LM head + argmax per token, {threads} OpenMP threads")
+              f"{p0}..{p0 + n_tokens - 1} (the GPU arm's positions; cache rows {prompt_len}..{p0 - 1} left empty), "
+              f"full LM head + argmax per token, {threads} OpenMP threads")
     return n_tokens / dt, threads, sample
 
 
@@ -198,8 +210,10 @@ def run_reference(args):
     prompt = synth.make_prompt(SEED, 4, cfg.vocab_size)
     for i, t in enumerate(prompt):
         m.forward(int(t), i)
-    tok, pos = oracle.argmax(m.logits()), len(prompt)
-    lo = len(prompt)
+    # decode at the GPU arm's positions (512..767); the cache rows between the 4-token prompt and
+    # position 512 stay empty, so every token reads as many KV rows as the GPU arm's tokens do
+    tok, pos = oracle.argmax(m.logits()), PROMPT_LEN
+    lo = PROMPT_LEN
 
     def one(tok, pos):  # one decode token; positions cycle over a 256-token window like our arm
         m.forward(tok, pos)
@@ -215,7 +229,8 @@ def run_reference(args):
     dt = time.perf_counter() - t0
     v = args.steps / dt
     sample = (f"one greedy decode token per step of the 1B synthetic model (seed 1) with LM head + argmax, "
-              f"positions cycling over {lo}..{lo + DECODE_LEN - 1} after a 4-token prompt, {threads} OpenMP threads")
+              f"positions cycling over {lo}..{lo + DECODE_LEN - 1} (the GPU arm's positions; cache rows 4..{lo - 1} "
+              f"left empty after a 4-token prompt), {threads} OpenMP threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * dt / args.steps, 3),
@@ -276,7 +291,7 @@ def run_profile():
     """Launch sequence for ncu on the bench's own workload: the 1B model, decode launches at
     positions 640..643 (the mean position of the timed decode, 512..767), so each launch reads
     the weights plus 641..644 KV rows per layer. The KV rows hold zeros instead of a prompt's
-    keys; the bytes moved are the same. Capture with -k regex:gg_decode_kernel -s 1 -c 1..3."""
+    keys; the bytes moved are the same. Capture with -k regex:gg_step_kernel -s 1 -c 1..3."""
     from gemma_b200 import synth
     from gemma_b200.native import engine_from_tensors
     shape = synth.SHAPES["1b"]
@@ -581,6 +596,13 @@ def main():
     peak, peak_kind = measured_peaks()
     cpu_v, cpu_threads, cpu_sample = cpu_oracle_rate(tensors, cfg, args.cpu_tokens)
     cpu_v1, _, cpu_sample1 = cpu_oracle_rate(tensors, cfg, min(args.cpu_tokens, 2), prompt_len=1, threads=1)
+    # the timed tokens against the oracle's greedy tokens of this workload (tests/golden/cfg1_1b.npz)
+    fixture = os.path.join(ROOT, "tests", "golden", "cfg1_1b.npz")
+    match = None
+    if os.path.exists(fixture):
+        want = np.load(fixture)["tokens"]
+        got = np.concatenate([np.array([first])] + [np.asarray(t) for t in toks])[:len(want)]
+        match = bool(np.array_equal(got, want[:len(got)]))
     ttft_p50 = statistics.median(ttft_wall)
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -592,8 +614,11 @@ def main():
                    "replicas": world, "l2": "no flush: each step streams 1.06 GB of weights (> 126 MB L2)"},
         "ttft_ms_p50": round(ttft_p50, 3), "ttft_device_ms_p50": round(statistics.median(ttft_dev), 3),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": NCU_TRAFFIC_PER_LAUNCH,
-                     "peak_kind": peak_kind, "kernel": "gg_decode_kernel",
+                     "frac": round(achieved / peak, 4),
+                     "traffic": traffic_at(sum(positions) / len(positions)),
+                     "traffic_source": f"ncu dram bytes of one launch at position {NCU_TRAFFIC_POS}, moved to the mean "
+                                       f"timed position by {KV_BYTES_PER_POS} KV bytes per position",
+                     "peak_kind": peak_kind, "kernel": "gg_step_kernel",
                      "algo_bytes_per_launch": int(algo)},
         "cpu_baseline": {"value": round(cpu_v, 3), "unit": UNIT, "cores": cpu_threads, "kind": "port",
                          "sample": cpu_sample, "value_1_thread": round(cpu_v1, 3), "sample_1_thread": cpu_sample1},
@@ -603,6 +628,7 @@ def main():
         "clocks": clk.summary(),
         "vs_baseline_source": "reference README.md:17 (59.8 tok/s, Mac Mini M4 Pro, Chrome 134)",
         "first_token": int(first),
+        "tokens_match_oracle_fixture": match,
     }
     print(json.dumps(out))
     eng.close()

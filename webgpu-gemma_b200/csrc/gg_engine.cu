@@ -304,10 +304,13 @@ static int schedule(gg_engine* e) {
     const int nst = std::max({(m.sl_qkv + std::min(rq, m.sl_qkv) - 1) / std::min(rq, m.sl_qkv),
                               (m.sl_h + std::min(ro, m.sl_h) - 1) / std::min(ro, m.sl_h),
                               (m.sl_h + std::min(rd, m.sl_h) - 1) / std::min(rd, m.sl_h)});
-    if (nst >= GG_STEP_STAGES) return fail(e, GG_E_ARG, "rows too wide: a phase needs %d ring stages at once", nst);
+    const int nst_gu = (m.sl_i + m.rps_gu / 2 - 1) / (m.rps_gu / 2);  // gate/up stages (one waiting warp each)
+    if (nst >= GG_STEP_STAGES || nst_gu >= GG_STEP_STAGES || nst_gu > GG_STEP_NCW)
+      return fail(e, GG_E_ARG, "rows too wide: a phase needs %d ring stages at once", std::max(nst, nst_gu));
   }
   m.dims_per_comb = 8;
   m.ncomb = m.Q / 8;
+  if (m.ncomb > G) return fail(e, GG_E_ARG, "q_dim / 8 = %d attention merge units exceed the grid (%d)", m.ncomb, G);
   m.xs0 = (m.H + 63) / 64 * 64;
   m.xs1 = (std::max(m.Q, m.I) + 63) / 64 * 64;
   m.tmp_floats = m.Q + 2 * m.KV;

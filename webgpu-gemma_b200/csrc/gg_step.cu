@@ -97,8 +97,10 @@ struct Ctx {
   uint32_t tagbase;
 };
 
-// Rows per ring stage of a phase whose n rows (n <= NCW) are computed one per warp.
+// Rows per ring stage of a phase whose n rows (n <= NCW) are computed one per warp, and the
+// number of such stages.
 GG_DEV int shared_rps(int rps_max, int n) { return max(min(rps_max, n), 1); }
+GG_DEV int shared_nst(int rps_max, int n) { const int d = shared_rps(rps_max, n); return (n + d - 1) / d; }
 
 GG_DEV int window_lo(const GGLayerW& Lw, int pos) { return (Lw.window > 0 && pos + 1 > Lw.window) ? pos + 1 - Lw.window : 0; }
 
@@ -163,37 +165,42 @@ struct Producer {
   }
 };
 
-// The slow path of a tagged-word wait (one copy, out of line): re-poll the four words at p until
-// all carry `tag`. Bounded: on timeout (or an error raised elsewhere) the values read as 0 and
-// the error word is set.
-GG_NOINLINE void poll4(const uint64_t* p, uint32_t tag, const SpinCtl sc, float* v) {
-  uint64_t w0, w1, w2, w3;
-  bool a = false, b = false;
-  uint64_t t0 = 0;
-#pragma unroll 1
-  for (uint32_t it = 0; !(a && b); ++it) {
-    if (!a) {
-      ld2_relaxed(p, w0, w1);
-      a = (uint32_t)(w0 >> 32) == tag && (uint32_t)(w1 >> 32) == tag;
-    }
-    if (!b) {
-      ld2_relaxed(p + 2, w2, w3);
-      b = (uint32_t)(w2 >> 32) == tag && (uint32_t)(w3 >> 32) == tag;
-    }
-    if (it == 512) t0 = global_timer_ns();  // the first 512 polls read no clock
-    if (it > 512 && (it & 31u) == 0) {
-      const uint64_t dt = global_timer_ns() - t0;
-      if (dt > GG_QUIET_SPIN_NS && (*(volatile uint32_t*)sc.err || dt > sc.timeout_ns)) {
-        if (dt > sc.timeout_ns) atomicOr(sc.err, GG_ERR_WAIT_FLAG);
-        w0 = w1 = w2 = w3 = 0;
-        break;
-      }
-    }
+// Deadline of a tagged-word wait, checked every 32 passes after the first 512 (which read no
+// clock): after GG_QUIET_SPIN_NS the wait gives up once an error is raised elsewhere, and after
+// the timeout it raises GG_ERR_WAIT_FLAG itself.
+GG_NOINLINE bool spin_gave_up(const SpinCtl sc, uint64_t t0) {
+  const uint64_t dt = global_timer_ns() - t0;
+  if (dt <= GG_QUIET_SPIN_NS) return false;
+  if (dt > sc.timeout_ns) {
+    atomicOr(sc.err, GG_ERR_WAIT_FLAG);
+    return true;
   }
-  v[0] = __uint_as_float((uint32_t)w0);
-  v[1] = __uint_as_float((uint32_t)w1);
-  v[2] = __uint_as_float((uint32_t)w2);
-  v[3] = __uint_as_float((uint32_t)w3);
+  return *(volatile uint32_t*)sc.err != 0;
+}
+
+struct SpinClock {
+  uint32_t it = 0;
+  uint64_t t0 = 0;
+  GG_DEV bool expired(const SpinCtl& sc) {
+    ++it;
+    if (it == 512) t0 = global_timer_ns();
+    if (it <= 512 || (it & 31u)) return false;
+    return spin_gave_up(sc, t0);
+  }
+};
+
+GG_DEV bool quad_ready(const uint64_t (&w)[4], uint32_t tag) {
+  return (uint32_t)(w[0] >> 32) == tag && (uint32_t)(w[1] >> 32) == tag && (uint32_t)(w[2] >> 32) == tag &&
+         (uint32_t)(w[3] >> 32) == tag;
+}
+// A quad that takes part in a warp wait without a load: four tagged zeros.
+GG_DEV void quad_idle(uint64_t (&w)[4], uint32_t tag) {
+#pragma unroll
+  for (int j = 0; j < 4; j++) w[j] = (uint64_t)tag << 32;
+}
+GG_DEV void quad_vals(const uint64_t (&w)[4], float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; j++) v[j] = __uint_as_float((uint32_t)w[j]);
 }
 
 // ---------------------------------------------------------------------------------- dot products
@@ -318,9 +325,15 @@ struct Consumer {
   int cslot = 0;
   uint32_t idx = 0;  // ring position
 
-  // Every warp walks the ring in the producer's order and waits for and releases every stage,
-  // whether or not it computes on it: a slot's mbarrier phases are then never more than one use
-  // apart for any warp, which is what the parity waits require.
+  // Ring protocol. Every warp walks the ring in the producer's order (idx). A slot is waited on
+  // for use u only after its use u - 1 has been consumed and released, so a parity wait can never
+  // mistake use u - 1 for use u.
+  // * Gated phases (all stages resident at once: q/k/v, O, gate/up, down): warp k waits for stage
+  //   k of the phase before a CTA barrier, every warp reads the stages after it, and once every
+  //   warp is past a later barrier thread 0 releases them all (release_all).
+  // * Attention KV: the warps of split k wait for stage k and release it themselves.
+  // * Streaming phase (LM head): every warp waits for and releases every stage (stage_wait,
+  //   stage_done), computing on the stages it owns.
   GG_DEV uint8_t* stage_wait() { return stage_wait_ahead(0); }
   // Wait for the stage k places after the next one to release (k < NS).
   GG_DEV uint8_t* stage_wait_ahead(int k) {
@@ -334,6 +347,18 @@ struct Consumer {
     if (lane == 0 && !dead) mbar_arrive(&x.S.empty[idx % NS]);
     idx++;
   }
+  // Gated phase, before its CTA barrier: warp k (< nst) waits for stage k of the phase.
+  GG_DEV void gate(int nst) {
+    if (warp < nst) stage_wait_ahead(warp);
+  }
+  // Gated phase, after a CTA barrier that every use of its nst stages precedes: release them
+  // (NCW arrivals each, by one thread). After an error nothing is released: the producer's waits
+  // then run out instead of refilling a slot whose copy may still be landing.
+  GG_DEV void release_all(int nst) {
+    if (tid == 0 && !dead && !*(volatile uint32_t*)x.sc.err)
+      for (int k = 0; k < nst; k++) mbar_arrive_cnt(&x.S.empty[(idx + (uint32_t)k) % NS], NCW);
+    idx += (uint32_t)nst;
+  }
 
   // Trace stamps (GG_TRACE launches): globaltimer of event ev (0 enter, 1 inputs ready, 2 done)
   // of phase ph: trace[(cta * GG_TRACE_PHASES + ph) * 4 + ev].
@@ -344,16 +369,27 @@ struct Consumer {
       x.m->trace[((size_t)blockIdx.x * GG_TRACE_PHASES + ph) * 4 + ev] = global_timer_ns();
   }
 
-  // Poll until the four tagged words w (loaded from p) all carry `tag`; bounded. On timeout (or
-  // an error raised elsewhere) the values read as 0 and the error word is set.
-  GG_DEV void settle4(const uint64_t* p, uint32_t tag, uint64_t (&w)[4], float* v) {
-    const bool ready = (uint32_t)(w[0] >> 32) == tag && (uint32_t)(w[1] >> 32) == tag &&
-                       (uint32_t)(w[2] >> 32) == tag && (uint32_t)(w[3] >> 32) == tag;
-    if (ready) {
+  // Warp-uniform wait for NQ quads per lane, first loaded by issue4 (or quad_idle): each pass
+  // re-reads every quad of the warp that does not carry `tag` yet, all in flight together, and the
+  // warp leaves together once every quad does. No lane spins alone while the rest of its warp
+  // waits at a reconvergence point. Bounded (SpinClock); after giving up the values read 0.
+  template <int NQ>
+  GG_DEV void settle_warp(const uint64_t* const (&p)[NQ], uint32_t tag, uint64_t (&w)[NQ][4]) {
+    SpinClock clk;
+#pragma unroll 1
+    for (;;) {
+      bool ok = true;
 #pragma unroll
-      for (int j = 0; j < 4; j++) v[j] = __uint_as_float((uint32_t)w[j]);
-    } else {
-      poll4(p, tag, x.sc, v);
+      for (int k = 0; k < NQ; k++) ok = ok && quad_ready(w[k], tag);
+      if (__all_sync(0xffffffffu, ok)) return;
+#pragma unroll
+      for (int k = 0; k < NQ; k++)
+        if (!quad_ready(w[k], tag)) issue4(p[k], w[k]);
+      if (__any_sync(0xffffffffu, clk.expired(x.sc))) {
+#pragma unroll
+        for (int k = 0; k < NQ; k++) quad_idle(w[k], tag);
+        return;
+      }
     }
   }
   GG_DEV void issue4(const uint64_t* p, uint64_t (&w)[4]) {
@@ -420,15 +456,19 @@ struct Consumer {
 #pragma unroll
       for (int k = 0; k < 2; k++) {
         const int q = base + tid + k * NCT;
-        pk[k] = src + (sl ? slot_word(nq, G, sl, q) : 4 * q);
-        if (q < nq) issue4(pk[k], w[k]);
+        pk[k] = q < nq ? src + (sl ? slot_word(nq, G, sl, q) : 4 * q) : src;
+        if (q < nq)
+          issue4(pk[k], w[k]);
+        else
+          quad_idle(w[k], tag);
       }
+      settle_warp<2>(pk, tag, w);
 #pragma unroll
       for (int k = 0; k < 2; k++) {
         const int q = base + tid + k * NCT;
         if (base + k * NCT >= nq) break;  // uniform over the CTA
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (q < nq) settle4(pk[k], tag, w[k], v);
+        float v[4];
+        quad_vals(w[k], v);
         plane_quad(P, q, q < nq, v);
       }
     }
@@ -444,16 +484,19 @@ struct Consumer {
     const int nq = m.H >> 2, k = tid, nw = (nq + 31) >> 5;
     const bool ok = k < nq;
     float4 fa = make_float4(0.f, 0.f, 0.f, 0.f), fb = fa, fbase = fa;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    float v[4];
+    const uint64_t* p[1] = {src + slot_word(nq, m.grid, m.sl_h, ok ? k : 0)};
+    uint64_t w[1][4];
     if (ok) {
-      const uint64_t* p = src + slot_word(nq, m.grid, m.sl_h, k);
-      uint64_t w[4];
-      issue4(p, w);
+      issue4(p[0], w[0]);
       fa = __ldg(reinterpret_cast<const float4*>(wa) + k);
       fb = __ldg(reinterpret_cast<const float4*>(wb) + k);
       fbase = reinterpret_cast<const float4*>(base)[k];
-      settle4(p, tag, w, v);
+    } else {
+      quad_idle(w[0], tag);
     }
+    settle_warp<1>(p, tag, w);
+    quad_vals(w[0], v);
     const float wav[4] = {fa.x, fa.y, fa.z, fa.w}, wbv[4] = {fb.x, fb.y, fb.z, fb.w};
     const float bv[4] = {fbase.x, fbase.y, fbase.z, fbase.w};
     float s[4] = {0.f, 0.f, 0.f, 0.f};
@@ -529,17 +572,15 @@ struct Consumer {
   }
 
   // The CTA's n rows (n <= 16) of a phase, in nst ring stages of d = shared_rps(rps_max, n) rows
-  // (all resident at once: the host checks nst < NS). Work units are (group of four rows, K
+  // (all resident at once: the host checks nst < NS; the caller gated them before its barrier). Work units are (group of four rows, K
   // slice): warp w takes group w / S and slice w % S, S = NCW / groups, so the four rows share
   // every load of the x planes. The slice totals meet in shared memory; thread r < n sums them in
-  // slice order and passes the row total to epi(r, value). Every consumer warp must call this
-  // (it holds a CTA barrier).
-  template <class Epi>
-  GG_DEV void matvec(const XPlanes& P, int n, int rps_max, int K, int rs, Epi epi) {
+  // slice order and stores the row total as tagged word out[r]. Every consumer warp must call
+  // this (it holds a CTA barrier).
+  GG_DEV void matvec(const XPlanes& P, int n, int rps_max, int K, int rs, uint64_t* out, uint32_t tag) {
     const int d = shared_rps(rps_max, n), nst = (n + d - 1) / d;
     const int ng = (n + 3) >> 2, S = NCW / ng, nch = K >> 4;
     const int g = warp / S, sl = warp % S;
-    for (int k = 0; k < nst; k++) stage_wait_ahead(k);
     float* red = x.S.red;  // [row][slice]
     if (g < ng) {
       uint32_t ra[4];
@@ -556,24 +597,26 @@ struct Consumer {
           if (4 * g + k < n) red[(4 * g + k) * S + sl] = vv[k];
       }
     }
-    for (int k = 0; k < nst; k++) stage_done();
     cbar();
+    release_all(nst);
     if (tid < n) {
       float t = 0.f;
       for (int k = 0; k < S; k++) t += red[tid * S + k];
-      epi(tid, t);
+      tag_store(out + tid, t, tag);
     }
   }
 
   // Row pairs (2j, 2j + 1), rps / 2 pairs per ring stage, in units of four pairs: unit n goes to
   // warp n % NCW, whose four 8-lane groups take one pair each; the group's first lane passes the
   // pair to epi(j, row 2j, row 2j + 1).
+  // gated: the stages are resident and were gated by the caller (who releases them after a
+  // barrier); otherwise they stream in and every warp waits for and releases each.
   template <class Epi>
-  GG_DEV void matvec_pairs(const XPlanes& P, int npairs, int rps, int K, int rs, Epi epi) {
+  GG_DEV void matvec_pairs(const XPlanes& P, int npairs, int rps, int K, int rs, bool gated, Epi epi) {
     const int pps = rps >> 1, g = lane >> 3;
     int unit = 0;
-    for (int j0 = 0; j0 < npairs; j0 += pps) {
-      const uint8_t* stg = stage_wait();
+    for (int j0 = 0, k = 0; j0 < npairs; j0 += pps, k++) {
+      const uint8_t* stg = gated ? x.S.ring + (size_t)((idx + (uint32_t)k) % NS) * GG_STEP_STAGE_BYTES : stage_wait();
       const int j1 = min(j0 + pps, npairs);
       for (int u = j0; u < j1; u += 4, unit++) {
         if (unit % NCW != warp) continue;
@@ -581,7 +624,7 @@ struct Consumer {
         const float2 v = dot_pair8(smem_u32(stg) + (uint32_t)(2 * (min(j, j1 - 1) - j0) * rs), rs, K, P);
         if ((lane & 7) == 0 && j < j1) epi(j, v.x, v.y);
       }
-      stage_done();
+      if (!gated) stage_done();
     }
   }
 
@@ -593,12 +636,13 @@ struct Consumer {
       add_norm_planes(x.S.xa, m.t_down, make_tag(x.tagbase, (l - 1) * PH + 5), m.layers[l - 1].post_ffw_norm, x.S.res,
                       x.S.hid, m.layers[l].attn_norm, blockIdx.x == 0 ? m.dbg_hidden : nullptr, nullptr);
     }
+    const int n = x.S.rows[RG_QKV + 1] - x.S.rows[RG_QKV];
+    gate(shared_nst(m.rps_h, n));
     cbar();
     trace(l * PH + 0, 1);
     uint64_t* out = m.t_qkv + (size_t)blockIdx.x * m.sl_qkv;
     const uint32_t tag = make_tag(x.tagbase, l * PH + 0);
-    const int n = x.S.rows[RG_QKV + 1] - x.S.rows[RG_QKV];
-    matvec(x.S.xa, n, m.rps_h, m.H, m.rs_h, [&](int r, float v) { tag_store(out + r, v, tag); });
+    matvec(x.S.xa, n, m.rps_h, m.H, m.rs_h, out, tag);
   }
 
   // q/k per-head RMSNorm + RoPE (shaders.ts:420-467), the KV store (shaders.ts:209-227) and this
@@ -607,56 +651,59 @@ struct Consumer {
     const GGModelDev& m = *x.m;
     const GGLayerW& Lw = m.layers[l];
     const int G = m.grid, s0 = first_split(m, l, x.pos, x.nsplit, blockIdx.x);
+    const int att_nst = s0 < x.nsplit ? (x.nsplit - 1 - s0) / G + 1 : 0;  // this CTA's splits (KV stages)
     if (s0 >= x.nsplit) return;
     const int HD = m.HD, NQH = m.NQH, NKH = m.NKH, Q = m.Q, KV = m.KV;
-    constexpr int NJ = GG_HEAD_DIM / 32;
     float* t = x.S.tmp;  // q [Q] | k [KV] | v [KV]
     const uint32_t tagA = make_tag(x.tagbase, l * PH + 0);
-    // gather q | k | v into shared memory (every thread at most one quad in flight per 512)
+    // One warp per q, k or v head. Lane l takes quads l and l + 32 of its head (elements 4l..4l+3
+    // and HD/2 + 4l..): the RoPE pairs (i, i + HD/2) sit in one lane, and the norm weights and the
+    // RoPE row are fetched in the same round trip as the head's values.
+    static_assert(GG_HEAD_DIM == 256, "two quads per lane cover a head");
     const int nq = (Q + 2 * KV) >> 2;
-    for (int base = 0; base < nq; base += NCT) {
-      const int q = base + tid;
-      if (q < nq) {
-        const uint64_t* p = m.t_qkv + slot_word(nq, G, m.sl_qkv, q);
-        uint64_t w[4];
-        float v[4];
-        issue4(p, w);
-        settle4(p, tagA, w, v);
-        reinterpret_cast<float4*>(t)[q] = make_float4(v[0], v[1], v[2], v[3]);
+    for (int h = warp; h < NQH + 2 * NKH; h += NCW) {
+      const bool normed = h < NQH + NKH;  // q and k heads; v is stored as is
+      const int q0 = h * (HD / 4) + lane, q1 = q0 + HD / 8;
+      const uint64_t* pq[2] = {m.t_qkv + slot_word(nq, G, m.sl_qkv, q0), m.t_qkv + slot_word(nq, G, m.sl_qkv, q1)};
+      uint64_t w[2][4];
+      issue4(pq[0], w[0]);
+      issue4(pq[1], w[1]);
+      float4 n0 = make_float4(1.f, 1.f, 1.f, 1.f), n1 = n0, c0 = make_float4(1.f, 0.f, 1.f, 0.f), c1 = c0;
+      if (normed) {
+        const float4* nw = reinterpret_cast<const float4*>(h < NQH ? Lw.q_norm : Lw.k_norm);
+        n0 = __ldg(nw + lane);
+        n1 = __ldg(nw + lane + HD / 8);
+        const float4* cr = reinterpret_cast<const float4*>(Lw.rope + (size_t)x.pos * (HD / 2) + 4 * lane);  // (cos, sin) x 4
+        c0 = __ldg(cr);
+        c1 = __ldg(cr + 1);
       }
-    }
-    cbar();
-    // per-head norm + RoPE: one warp per q or k head; lane l holds elements l + 32j, so the
-    // RoPE pair (i, i + HD/2) is in one lane
-    for (int h = warp; h < NQH + NKH; h += NCW) {
-      const float* nw = h < NQH ? Lw.q_norm : Lw.k_norm;
-      float* hp = t + h * HD;
-      float v[NJ];
-      float ss = 0.f;
+      settle_warp<2>(pq, tagA, w);
+      float a[4], b[4];
+      quad_vals(w[0], a);
+      quad_vals(w[1], b);
+      if (normed) {
+        float ss = 0.f;
 #pragma unroll
-      for (int j = 0; j < NJ; j++) {
-        v[j] = hp[lane + 32 * j];
-        ss += v[j] * v[j];
+        for (int j = 0; j < 4; j++) ss += a[j] * a[j] + b[j] * b[j];
+        const float ir = 1.0f / sqrtf(warp_sum(ss) * (1.0f / (float)HD) + m.eps);
+        const float na[4] = {n0.x, n0.y, n0.z, n0.w}, nb[4] = {n1.x, n1.y, n1.z, n1.w};
+        const float cs[4] = {c0.x, c0.z, c1.x, c1.z}, sn[4] = {c0.y, c0.w, c1.y, c1.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float x0 = a[j] * na[j] * ir, x1 = b[j] * nb[j] * ir;
+          a[j] = x0 * cs[j] - x1 * sn[j];
+          b[j] = x0 * sn[j] + x1 * cs[j];
+        }
       }
-      const float ir = 1.0f / sqrtf(warp_sum(ss) * (1.0f / (float)HD) + m.eps);
+      if (KV16 && h >= NQH) {  // bf16 cache: attention reads the stored (rounded) k and v
 #pragma unroll
-      for (int j = 0; j < NJ; j++) v[j] = v[j] * __ldg(nw + lane + 32 * j) * ir;
-#pragma unroll
-      for (int j = 0; j < NJ / 2; j++) {
-        const float2 cr = __ldg(Lw.rope + (size_t)x.pos * (HD / 2) + lane + 32 * j);  // (cos, sin)
-        const float x0 = v[j], x1 = v[j + NJ / 2];
-        v[j] = x0 * cr.x - x1 * cr.y;
-        v[j + NJ / 2] = x0 * cr.y + x1 * cr.x;
+        for (int j = 0; j < 4; j++) {
+          a[j] = bf16_rne(a[j]);
+          b[j] = bf16_rne(b[j]);
+        }
       }
-      if (KV16 && h >= NQH) {  // bf16 cache: attention reads the stored (rounded) k
-#pragma unroll
-        for (int j = 0; j < NJ; j++) v[j] = bf16_rne(v[j]);
-      }
-#pragma unroll
-      for (int j = 0; j < NJ; j++) hp[lane + 32 * j] = v[j];
-    }
-    if (KV16) {  // the stored (rounded) v as well
-      for (int i = tid; i < KV; i += NCT) t[Q + KV + i] = bf16_rne(t[Q + KV + i]);
+      reinterpret_cast<float4*>(t)[q0] = make_float4(a[0], a[1], a[2], a[3]);
+      reinterpret_cast<float4*>(t)[q1] = make_float4(b[0], b[1], b[2], b[3]);
     }
     cbar();
     trace(l * PH + 1, 1);
@@ -673,14 +720,18 @@ struct Consumer {
     }
     const uint32_t tag = make_tag(x.tagbase, l * PH + 1);
     const int plo = window_lo(Lw, x.pos);
-    // split k of this CTA is handled by warps NQH*k .. NQH*k + NQH - 1 (one per query head);
-    // every warp acquires and releases every stage
-    int k = 0;
-    for (int s = s0; s < x.nsplit; s += G, k++) {
-      const uint8_t* stg = stage_wait();
-      if (warp / NQH == k) attn_split(s, plo, stg, warp % NQH, tag);
-      stage_done();
+    // Split k of this CTA is handled by warps NQH*k .. NQH*k + NQH - 1 (one per query head), which
+    // wait for its KV stage themselves and release it when done: NCW arrivals in all, the first
+    // warp giving those of the warps that do not read it. Every later ring wait follows the
+    // merge's CTA barrier, which these arrivals precede.
+    const int k = warp / NQH;
+    if (k < att_nst) {
+      attn_split(s0 + k * G, plo, stage_wait_ahead(k), warp % NQH, tag);
+      __syncwarp();
+      if (lane == 0 && !dead && !*(volatile uint32_t*)x.sc.err)
+        mbar_arrive_cnt(&x.S.empty[(idx + (uint32_t)k) % NS], warp % NQH == 0 ? (uint32_t)(NCW - NQH + 1) : 1u);
     }
+    idx += (uint32_t)att_nst;
   }
 
   // One split of PPS positions for query head h (one warp): K rows at the start of the stage, V
@@ -760,66 +811,93 @@ struct Consumer {
     }
   }
 
-  // Merge of the attention splits (online softmax) for 8 output dimensions per unit: warp 0 of
-  // the unit's CTA, lanes over splits, every load of a batch in flight before any check.
+  // Merge of the attention splits (online softmax) for 8 output dimensions per unit. The unit's
+  // splits are spread over W = ceil(splits / 32) warps, one split per lane, every load in flight
+  // before any check; each warp merges its lanes, and warp 0 merges the W warp results from
+  // shared memory in warp order and stores the unit's outputs.
   GG_DEV void phase_combine(int l) {
     const GGModelDev& m = *x.m;
     const int HD = m.HD, ncomb = m.Q >> 3;
     const uint32_t tagB = make_tag(x.tagbase, l * PH + 1);
     const uint32_t tagC = make_tag(x.tagbase, l * PH + 2);
     const int slo = window_lo(m.layers[l], x.pos) / m.pos_per_split;
-    if (warp == 0) {
-      for (int u = blockIdx.x; u < ncomb; u += m.grid) {
-        const int d0 = 8 * u, h = d0 / HD, dh = d0 % HD;
-        float mx = -INFINITY, lsum = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int sb = slo; sb < x.nsplit; sb += 32) {  // one split per lane in flight
-          const int s = sb + lane;
-          if (s < x.nsplit) {
-            const uint64_t* pb = m.t_o + (size_t)s * m.att_slot + (size_t)h * (HD + 4);
-            uint64_t wml[4], wo0[4], wo1[4];
-            issue4(pb + HD, wml);
-            issue4(pb + dh, wo0);
-            issue4(pb + dh + 4, wo1);
-            float fml[4], f0[4], f1[4];
-            settle4(pb + HD, tagB, wml, fml);
-            settle4(pb + dh, tagB, wo0, f0);
-            settle4(pb + dh + 4, tagB, wo1, f1);
-            const float nm = fmaxf(mx, fml[0]);
-            const float a = (mx == -INFINITY) ? 0.f : expf(mx - nm);
-            const float b = expf(fml[0] - nm);
-            lsum = fmaf(b, fml[1], lsum * a);
+    const int ns = x.nsplit - slo, W = min((ns + 31) >> 5, NCW);
+    float* part = x.S.red;  // [warp][10]: max, sum, 8 outputs
+    const int u = blockIdx.x;
+    const bool have = u < ncomb;  // one unit per CTA (the host checks Q / 8 <= grid)
+    const int d0 = 8 * u, h = d0 / HD, dh = d0 % HD;
+    if (have && warp < W) {
+      float mx = -INFINITY, lsum = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int sb = slo + warp * 32; sb < x.nsplit; sb += 32 * W) {  // uniform over the warp
+        const int s = sb + lane;
+        const bool act = s < x.nsplit;
+        const uint64_t* pb = m.t_o + (size_t)(act ? s : sb) * m.att_slot + (size_t)h * (HD + 4);
+        const uint64_t* pq[3] = {pb + HD, pb + dh, pb + dh + 4};
+        uint64_t w[3][4];
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-              acc[j] = fmaf(b, f0[j], acc[j] * a);
-              acc[4 + j] = fmaf(b, f1[j], acc[4 + j] * a);
-            }
-            mx = nm;
-          }
+        for (int k = 0; k < 3; k++) {
+          if (act)
+            issue4(pq[k], w[k]);
+          else
+            quad_idle(w[k], tagB);
         }
-        const float gm = warp_max(mx);
-        const float f = (mx == -INFINITY) ? 0.f : expf(mx - gm);
-        lsum = warp_sum(lsum * f);
-        float res = 0.f;
+        settle_warp<3>(pq, tagB, w);
+        if (!act) continue;
+        float fml[4], f0[4], f1[4];
+        quad_vals(w[0], fml);
+        quad_vals(w[1], f0);
+        quad_vals(w[2], f1);
+        const float nm = fmaxf(mx, fml[0]);
+        const float a = (mx == -INFINITY) ? 0.f : expf(mx - nm);
+        const float b = expf(fml[0] - nm);
+        lsum = fmaf(b, fml[1], lsum * a);
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          const float a = warp_sum(acc[j] * f);
-          if (lane == j) res = a;
+        for (int j = 0; j < 4; j++) {
+          acc[j] = fmaf(b, f0[j], acc[j] * a);
+          acc[4 + j] = fmaf(b, f1[j], acc[4 + j] * a);
         }
-        if (lane < 8) tag_store(m.t_att + d0 + lane, res / lsum, tagC);
+        mx = nm;
       }
+      const float gm = warp_max(mx);
+      const float f = (mx == -INFINITY) ? 0.f : expf(mx - gm);
+      lsum = warp_sum(lsum * f);
+      float res = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float a = warp_sum(acc[j] * f);
+        if (lane == j) res = a;
+      }
+      if (lane == 0) {
+        part[warp * 10] = gm;
+        part[warp * 10 + 1] = lsum;
+      }
+      if (lane < 8) part[warp * 10 + 2 + lane] = res;
     }
     cbar();  // the other warps wait here instead of polling the merged words
+    if (have && warp == 0) {
+      float gm = -INFINITY;
+      for (int w = 0; w < W; w++) gm = fmaxf(gm, part[w * 10]);
+      float lsum = 0.f, o = 0.f;
+      for (int w = 0; w < W; w++) {
+        const float wm = part[w * 10];
+        const float f = (wm == -INFINITY) ? 0.f : expf(wm - gm);
+        lsum = fmaf(f, part[w * 10 + 1], lsum);
+        if (lane < 8) o = fmaf(f, part[w * 10 + 2 + lane], o);
+      }
+      if (lane < 8) tag_store(m.t_att + d0 + lane, o / lsum, tagC);
+    }
   }
 
   GG_DEV void phase_o(int l) {
     const GGModelDev& m = *x.m;
     planes_gather(x.S.xb, m.t_att, m.Q >> 2, 0, make_tag(x.tagbase, l * PH + 2));
+    const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
+    gate(shared_nst(m.rps_q, n));
     cbar();
     trace(l * PH + 3, 1);
     uint64_t* out = m.t_proj + (size_t)blockIdx.x * m.sl_h;
     const uint32_t tag = make_tag(x.tagbase, l * PH + 3);
-    const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
-    matvec(x.S.xb, n, m.rps_q, m.Q, m.rs_q, [&](int r, float v) { tag_store(out + r, v, tag); });
+    matvec(x.S.xb, n, m.rps_q, m.Q, m.rs_q, out, tag);
   }
 
   GG_DEV void phase_ffn_up(int l) {
@@ -828,25 +906,30 @@ struct Consumer {
     // residual = hidden + post_attention_norm(proj) (engine.ts:785), then ffn rmsNorm (786)
     add_norm_planes(x.S.xa, m.t_proj, make_tag(x.tagbase, l * PH + 3), Lw.post_attn_norm, x.S.hid, x.S.res,
                     Lw.ffn_norm, blockIdx.x == 0 ? m.dbg_residual : nullptr, nullptr);
+    const int n = x.S.rows[RG_I + 1] - x.S.rows[RG_I];
+    const int nst = (n + (m.rps_gu >> 1) - 1) / (m.rps_gu >> 1);
+    gate(nst);
     cbar();
     trace(l * PH + 4, 1);
     uint64_t* out = m.t_act + (size_t)blockIdx.x * m.sl_i;
     const uint32_t tag = make_tag(x.tagbase, l * PH + 4);
-    const int n = x.S.rows[RG_I + 1] - x.S.rows[RG_I];
     // gate_i and up_i are adjacent rows (2i, 2i + 1): GeGLU on the pair (shaders.ts:153-170)
-    matvec_pairs(x.S.xa, n, m.rps_gu, m.H, m.rs_h,
+    matvec_pairs(x.S.xa, n, m.rps_gu, m.H, m.rs_h, true,
                  [&](int j, float g, float u) { tag_store(out + j, gelu_tanh(g) * u, tag); });
+    cbar();
+    release_all(nst);
   }
 
   GG_DEV void phase_down(int l) {
     const GGModelDev& m = *x.m;
     planes_gather(x.S.xb, m.t_act, m.I >> 2, m.sl_i, make_tag(x.tagbase, l * PH + 4));
+    const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
+    gate(shared_nst(m.rps_i, n));
     cbar();
     trace(l * PH + 5, 1);
     uint64_t* out = m.t_down + (size_t)blockIdx.x * m.sl_h;
     const uint32_t tag = make_tag(x.tagbase, l * PH + 5);
-    const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
-    matvec(x.S.xb, n, m.rps_i, m.I, m.rs_i, [&](int r, float v) { tag_store(out + r, v, tag); });
+    matvec(x.S.xb, n, m.rps_i, m.I, m.rs_i, out, tag);
   }
 
   GG_DEV void phase_lm() {
@@ -869,7 +952,7 @@ struct Consumer {
     const int rb = x.S.rows[RG_V], re = x.S.rows[RG_V + 1];
     float* lg = x.S.lmv;  // this CTA's logits, row rb + i at i
     float2* gl = reinterpret_cast<float2*>(m.logits + rb);
-    matvec_pairs(x.S.xa, (re - rb) >> 1, m.rps_gu, m.H, m.rs_h, [&](int j, float a, float b) {
+    matvec_pairs(x.S.xa, (re - rb) >> 1, m.rps_gu, m.H, m.rs_h, false, [&](int j, float a, float b) {
       reinterpret_cast<float2*>(lg)[j] = make_float2(a, b);
       gl[j] = make_float2(a, b);
     });
