@@ -336,6 +336,7 @@ static int schedule(gg_engine* e) {
     m.sm_red = take(4 * 16 * GG_STEP_NCW);
     m.sm_flag = take(16);
     m.sm_rows = take(32);
+    m.sm_model = take(GG_MODEL_BYTES(m.L));
     m.smem_bytes = (int)off;
   }
   cudaFuncAttributes fa;

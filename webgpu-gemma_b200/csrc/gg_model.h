@@ -69,7 +69,6 @@ struct GGModelDev {
   int32_t* seen_cnt;    // [max_seqs] tokens added to each slot's seen set since its last reset
   int max_seqs;
   unsigned long long* trace;  // [grid][GG_TRACE_PHASES][4] globaltimer stamps
-  GGLayerW layers[GG_MAX_LAYERS];
   int kv_es;  // bytes per KV cache element: 4 (f32), or 2 (bf16)
   // Step kernel. Rows per ring stage for K = H, Q, I, and for row pairs of K = H (even); words per
   // CTA slot of the exchange buffers (whole quads: the CTA's outputs start on a 32-byte sector)
@@ -82,7 +81,13 @@ struct GGModelDev {
   // ring and its mbarriers). The attention scratch (q | k | v) and the LM-head logits share the
   // O / down plane buffer when they fit: none of the three is live while another is.
   int sm_xa, sm_xb, sm_hid, sm_res, sm_tmp, sm_lmv, sm_scal, sm_red, sm_flag, sm_rows;
+  // The step kernel keeps a copy of this descriptor up to layers[L - 1] in shared memory at
+  // sm_model (GG_MODEL_BYTES(L) bytes), so its parameter reads never wait on L2.
+  int sm_model;
+  GGLayerW layers[GG_MAX_LAYERS];  // last member: a copy of the first L entries is a valid prefix
 };
+
+#define GG_MODEL_BYTES(L) (offsetof(GGModelDev, layers) + (size_t)(L) * sizeof(GGLayerW))
 
 // Launch-mode bits.
 enum : int {

@@ -446,15 +446,16 @@ struct Consumer {
   }
 
   // Planes of nq element quads held in a slot layout (sl words per CTA slot) or contiguously
-  // (sl = 0), without normalisation: the inputs of the O and down projections. Every load of a
-  // thread (at most four quads) is in flight before any tag is checked.
+  // (sl = 0), without normalisation: the inputs of the O and down projections. QPT quads per
+  // thread are in flight before any tag is checked (one round trip when nq <= QPT * NCT).
+  template <int QPT>
   GG_DEV void planes_gather(const XPlanes& P, const uint64_t* src, int nq, int sl, uint32_t tag) {
     const int G = x.m->grid;
-    for (int base = 0; base < nq; base += 2 * NCT) {  // two quads per thread in flight
-      uint64_t w[2][4];
-      const uint64_t* pk[2];
+    for (int base = 0; base < nq; base += QPT * NCT) {
+      uint64_t w[QPT][4];
+      const uint64_t* pk[QPT];
 #pragma unroll
-      for (int k = 0; k < 2; k++) {
+      for (int k = 0; k < QPT; k++) {
         const int q = base + tid + k * NCT;
         pk[k] = q < nq ? src + (sl ? slot_word(nq, G, sl, q) : 4 * q) : src;
         if (q < nq)
@@ -462,9 +463,9 @@ struct Consumer {
         else
           quad_idle(w[k], tag);
       }
-      settle_warp<2>(pk, tag, w);
+      settle_warp<QPT>(pk, tag, w);
 #pragma unroll
-      for (int k = 0; k < 2; k++) {
+      for (int k = 0; k < QPT; k++) {
         const int q = base + tid + k * NCT;
         if (base + k * NCT >= nq) break;  // uniform over the CTA
         float v[4];
@@ -734,75 +735,109 @@ struct Consumer {
     idx += (uint32_t)att_nst;
   }
 
-  // One split of PPS positions for query head h (one warp): K rows at the start of the stage, V
-  // rows after PPS K rows; the current position's k and v come from the scratch vector.
-  // Output: the split's unnormalised o (256 values), its max and its sum of exp, into the split's
-  // slot of the exchange buffer.
+  // One split of PPS = 8 positions for query head h (one warp): K rows at the start of the stage,
+  // V rows after PPS K rows; the current position's k and v come from the scratch vector.
+  // Scores: lane (p, j) = (lane / 4, lane % 4) takes position p over head dims [64j, 64j + 64)
+  // (its 16-byte chunks rotated by 2j + p % 2, so the eight lanes of a quarter warp read eight
+  // different bank groups), and
+  // two shuffles finish the dot product: all eight positions are scored at once. Softmax over the
+  // positions inside the window by three shuffle levels; then lane l accumulates dims 8l..8l+7 of
+  // the weighted V rows. Output: the split's unnormalised o (256 values), its max and its sum of
+  // exp, into the split's slot of the exchange buffer.
   __device__ __noinline__ void attn_split(int s, int plo, const uint8_t* stg, int h, uint32_t tag) {
     using KT = kv_t<KV16>;
     const GGModelDev& m = *x.m;
-    const int Q = m.Q, KV = m.KV, HD = m.HD, NQH = m.NQH, NKH = m.NKH, PPS = m.pos_per_split;
-    static_assert(GG_HEAD_DIM == 8 * 32, "a lane holds 8 dims of a head");
+    const int Q = m.Q, KV = m.KV, HD = m.HD, NQH = m.NQH, NKH = m.NKH;
+    static_assert(GG_HEAD_DIM == 256 && GG_POS_PER_SPLIT == 8, "lanes are 8 positions x 4 quarters of a head");
+    constexpr int PPS = GG_POS_PER_SPLIT;
     const float* t = x.S.tmp;
-    const int p0 = s * PPS, p1 = min(p0 + PPS, x.pos + 1), np = p1 - p0;
-    const int pv = max(plo - p0, 0);  // positions before pv are outside the window
-    const KT* Kst = reinterpret_cast<const KT*>(stg);
-    const KT* Vst = reinterpret_cast<const KT*>(stg + (size_t)PPS * KV * sizeof(KT));
-    const auto row8 = [&](const KT* st_row, const float* cur_row, bool cached, float* f) {
-      if (cached && KV16) {
-        bf16x8_widen(*reinterpret_cast<const uint4*>(st_row + 8 * lane), f);
-      } else {
-        if (cached) cur_row = reinterpret_cast<const float*>(st_row);
-        const float4 a = reinterpret_cast<const float4*>(cur_row + 8 * lane)[0];
-        const float4 b = reinterpret_cast<const float4*>(cur_row + 8 * lane)[1];
-        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    const int p0 = s * PPS, np = min(p0 + PPS, x.pos + 1) - p0;
+    const int pv = max(plo - p0, 0);  // positions before pv are outside the window (pv < np)
+    const int kvh = h * NKH / NQH;
+    const KT* Kst = reinterpret_cast<const KT*>(stg) + kvh * HD;
+    const KT* Vst = reinterpret_cast<const KT*>(stg + (size_t)PPS * KV * sizeof(KT)) + kvh * HD;
+    const float* qh = t + h * HD;
+    const float* kcur = t + Q + kvh * HD;
+    const float* vcur = t + Q + KV + kvh * HD;
+    // ---- scores (every lane reads a row of the split: positions outside [pv, np) read row pv)
+    const int p = lane >> 2, j = lane & 3, rot = 2 * j + (p & 1);
+    const bool valid = p >= pv && p < np;
+    const int pk = valid ? p : pv;
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    const auto dot_f32 = [&](const float* kr) {  // kr: the row's quarter j
+#pragma unroll 4
+      for (int i = 0; i < 16; i++) {
+        const int r = (i + rot) & 15;
+        const float4 k4 = reinterpret_cast<const float4*>(kr)[r];
+        const float4 q4 = reinterpret_cast<const float4*>(qh + 64 * j)[r];
+        d[0] = fmaf(q4.x, k4.x, d[0]);
+        d[1] = fmaf(q4.y, k4.y, d[1]);
+        d[2] = fmaf(q4.z, k4.z, d[2]);
+        d[3] = fmaf(q4.w, k4.w, d[3]);
       }
     };
-    const int kvh = h * NKH / NQH;
-    float qv[8];
-    row8(nullptr, t + h * HD, false, qv);
-    // Every position reads a valid row (positions outside [pv, np) read row pv and weigh zero),
-    // so the dot products and their warp sums carry no per-position branch.
-    float sc[GG_POS_PER_SPLIT];
-#pragma unroll
-    for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-      const int pp = (p >= pv && p < np) ? p : pv;
-      float kf[8];
-      row8(Kst + (size_t)pp * KV + kvh * HD, t + Q + kvh * HD, p0 + pp < x.pos, kf);
-      float d = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; j++) d = fmaf(qv[j], kf[j], d);
-      sc[p] = d;
+    if (p0 + pk < x.pos) {
+      if constexpr (KV16) {
+        const KT* kr = Kst + (size_t)pk * KV + 64 * j;
+#pragma unroll 4
+        for (int i = 0; i < 8; i++) {
+          const int r = (i + rot) & 7;
+          float kf[8];
+          bf16x8_widen(reinterpret_cast<const uint4*>(kr)[r], kf);
+          const float4 qa = reinterpret_cast<const float4*>(qh + 64 * j)[2 * r];
+          const float4 qb = reinterpret_cast<const float4*>(qh + 64 * j)[2 * r + 1];
+          d[0] = fmaf(qa.x, kf[0], d[0]);
+          d[1] = fmaf(qa.y, kf[1], d[1]);
+          d[2] = fmaf(qa.z, kf[2], d[2]);
+          d[3] = fmaf(qa.w, kf[3], d[3]);
+          d[0] = fmaf(qb.x, kf[4], d[0]);
+          d[1] = fmaf(qb.y, kf[5], d[1]);
+          d[2] = fmaf(qb.z, kf[6], d[2]);
+          d[3] = fmaf(qb.w, kf[7], d[3]);
+        }
+      } else {
+        dot_f32(reinterpret_cast<const float*>(Kst + (size_t)pk * KV) + 64 * j);
+      }
+    } else {
+      dot_f32(kcur + 64 * j);
     }
+    float sc = (d[0] + d[1]) + (d[2] + d[3]);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+    sc *= m.attn_scale;
+    float mx = valid ? sc : -INFINITY;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
+    for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float e = valid ? __expf(sc - mx) : 0.f;
+    float sum = e;
 #pragma unroll
-      for (int p = 0; p < GG_POS_PER_SPLIT; p++) sc[p] += __shfl_xor_sync(0xffffffffu, sc[p], o);
-    float mx = -1e30f;
-#pragma unroll
-    for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-      sc[p] *= m.attn_scale;
-      if (p >= pv && p < np) mx = fmaxf(mx, sc[p]);
-    }
-    float sum = 0.f;
-#pragma unroll
-    for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-      sc[p] = (p >= pv && p < np) ? expf(sc[p] - mx) : 0.f;
-      sum += sc[p];
-    }
+    for (int o = 4; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    // ---- o = sum_p e_p v_p (invalid positions weigh 0 and read row pv)
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int p = 0; p < GG_POS_PER_SPLIT; p++) {
-      const int pp = (p >= pv && p < np) ? p : pv;
+    for (int q = 0; q < PPS; q++) {
+      const float w = __shfl_sync(0xffffffffu, e, 4 * q);
+      const int pq = (q >= pv && q < np) ? q : pv;
       float vf[8];
-      row8(Vst + (size_t)pp * KV + kvh * HD, t + Q + KV + kvh * HD, p0 + pp < x.pos, vf);
+      if (p0 + pq < x.pos && KV16) {
+        bf16x8_widen(*reinterpret_cast<const uint4*>(Vst + (size_t)pq * KV + 8 * lane), vf);
+      } else {
+        // lanes 4..7 of each quarter warp load their two 16-byte halves in the other order, so the
+        // quarter's first loads cover all eight bank groups
+        const float* vr = p0 + pq < x.pos ? reinterpret_cast<const float*>(Vst + (size_t)pq * KV) : vcur;
+        const int sw = (lane >> 2) & 1;
+        const float4 u = reinterpret_cast<const float4*>(vr + 8 * lane)[sw];
+        const float4 v = reinterpret_cast<const float4*>(vr + 8 * lane)[sw ^ 1];
+        const float4 a = sw ? v : u, b = sw ? u : v;
+        vf[0] = a.x; vf[1] = a.y; vf[2] = a.z; vf[3] = a.w;
+        vf[4] = b.x; vf[5] = b.y; vf[6] = b.z; vf[7] = b.w;
+      }
 #pragma unroll
-      for (int j = 0; j < 8; j++) acc[j] = fmaf(sc[p], vf[j], acc[j]);
+      for (int jj = 0; jj < 8; jj++) acc[jj] = fmaf(w, vf[jj], acc[jj]);
     }
     uint64_t* o = m.t_o + (size_t)s * m.att_slot + (size_t)h * (HD + 4);
 #pragma unroll
-    for (int j = 0; j < 8; j++) tag_store(o + 8 * lane + j, acc[j], tag);
+    for (int jj = 0; jj < 8; jj++) tag_store(o + 8 * lane + jj, acc[jj], tag);
     if (lane == 0) {  // the split's header quad: max, sum of exp, two zero words (one 16-byte pair each)
       tag_store(o + HD, mx, tag);
       tag_store(o + HD + 1, sum, tag);
@@ -890,7 +925,7 @@ struct Consumer {
 
   GG_DEV void phase_o(int l) {
     const GGModelDev& m = *x.m;
-    planes_gather(x.S.xb, m.t_att, m.Q >> 2, 0, make_tag(x.tagbase, l * PH + 2));
+    planes_gather<1>(x.S.xb, m.t_att, m.Q >> 2, 0, make_tag(x.tagbase, l * PH + 2));
     const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
     gate(shared_nst(m.rps_q, n));
     cbar();
@@ -922,7 +957,7 @@ struct Consumer {
 
   GG_DEV void phase_down(int l) {
     const GGModelDev& m = *x.m;
-    planes_gather(x.S.xb, m.t_act, m.I >> 2, m.sl_i, make_tag(x.tagbase, l * PH + 4));
+    planes_gather<4>(x.S.xb, m.t_act, m.I >> 2, m.sl_i, make_tag(x.tagbase, l * PH + 4));
     const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
     gate(shared_nst(m.rps_i, n));
     cbar();
@@ -1019,8 +1054,16 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
   __shared__ Ctx x;
   const GGModelDev& m = *mp;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the descriptor's copy in shared memory (its size is a multiple of 8 bytes)
+  GGModelDev* msm = reinterpret_cast<GGModelDev*>(smem + m.sm_model);
+  {
+    const int nw = (int)(GG_MODEL_BYTES(m.L) / 8);
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(mp);
+    uint64_t* dst = reinterpret_cast<uint64_t*>(msm);
+    for (int i = threadIdx.x; i < nw; i += blockDim.x) dst[i] = src[i];
+  }
   if (threadIdx.x == 0) {
-  x.m = mp;
+  x.m = msm;
   x.st = st;
   x.mode = st->mode;
   x.token = st->token;
