@@ -91,7 +91,8 @@ __global__ void __launch_bounds__(512)
   }
   __threadfence_block();
   __syncthreads();
-  const int tok = sample_token(sm, &ss);
+  __shared__ SampleScratch sscr;
+  const int tok = sample_token(sm, &ss, sscr);
   if (t == 0) {
     out[b] = tok;
     if (tok >= 0 && tok < V) {
@@ -197,7 +198,8 @@ __global__ void __launch_bounds__(SL_THREADS)
   }
   __threadfence_block();
   __syncthreads();
-  const int tok = sample_token(sm, &ss);
+  __shared__ SampleScratch sscr;
+  const int tok = sample_token(sm, &ss, sscr);
   if (t == 0) *out_token = tok;
 }
 

@@ -56,6 +56,27 @@ __global__ void gg_f16_to_f32_kernel(const uint16_t* __restrict__ src, float* __
   if (i < n) dst[i] = __half2float(__ushort_as_half(src[i]));
 }
 
+// Wo (H rows of the row format, K = Q) -> Q / 8 column slices for the step kernel: slice u,
+// row r = {the 8 quants of columns 8u..8u+7, the f16 scale of their block, 6 zero bytes}.
+__global__ void gg_wo_cols_kernel(const uint8_t* __restrict__ wo, int H, int Q, int rs, uint8_t* __restrict__ out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // u * H + r
+  if (i >= (long long)(Q / 8) * H) return;
+  const int u = (int)(i / H), r = (int)(i % H);
+  const uint8_t* row = wo + (size_t)r * rs;
+  uint32_t w[4];
+  w[0] = *reinterpret_cast<const uint32_t*>(row + 8 * u);
+  w[1] = *reinterpret_cast<const uint32_t*>(row + 8 * u + 4);
+  w[2] = *reinterpret_cast<const uint16_t*>(row + Q + 2 * ((8 * u) / 32));
+  w[3] = 0;
+  *reinterpret_cast<uint4*>(out + 16 * (size_t)i) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Fixed-point accumulators (2^-32 units, two's complement u64) -> f32.
+__global__ void gg_fixed_to_f32_kernel(const unsigned long long* __restrict__ src, float* __restrict__ dst, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = (float)(long long)src[i] * 0x1p-32f;
+}
+
 __global__ void gg_init_keys_kernel(unsigned long long* keys) {
   int i = threadIdx.x;
   if (i < 256) keys[i] = ((unsigned long long)f32_order_key(-1e30f) << 32) | 0xffffffffull;
@@ -94,6 +115,7 @@ struct gg_engine {
   std::vector<void*> allocs;
   // weights
   std::vector<uint8_t*> wqkv, wo, wgu, wdown;
+  std::vector<uint8_t*> wo_cols;  // the step kernel's Wo column slices
   std::vector<float*> norms[6];  // attn_norm, ffn_norm, q_norm, k_norm, post_attn_norm, post_ffw_norm
   uint8_t* embd = nullptr;
   float* out_norm = nullptr;
@@ -311,6 +333,13 @@ static int schedule(gg_engine* e) {
   m.dims_per_comb = 8;
   m.ncomb = m.Q / 8;
   if (m.ncomb > G) return fail(e, GG_E_ARG, "q_dim / 8 = %d attention merge units exceed the grid (%d)", m.ncomb, G);
+  // the merge units apply their 8 columns of Wo: H rows of 16 bytes, all stages resident at once
+  m.wo_rows_per_stage = SB / 16;
+  {
+    const int nst_wo = (m.H + m.wo_rows_per_stage - 1) / m.wo_rows_per_stage;
+    if (nst_wo >= GG_STEP_STAGES || nst_wo > GG_STEP_NCW) return fail(e, GG_E_ARG, "hidden_size too large for the O slices");
+  }
+  m.acc_stride = (m.H + 3) / 4 * 4;
   m.xs0 = (m.H + 63) / 64 * 64;
   m.xs1 = (std::max(m.Q, m.I) + 63) / 64 * 64;
   m.tmp_floats = m.Q + 2 * m.KV;
@@ -461,9 +490,21 @@ extern "C" int gg_finalize(gg_engine* e) {
   GG_TRY(schedule(e));
   m.embd = e->embd;
   m.out_norm = e->out_norm;
+  e->wo_cols.assign(c.num_layers, nullptr);
+  for (int l = 0; l < c.num_layers; l++) {
+    const long long n = (long long)(m.Q / 8) * m.H;
+    GG_TRY(dalloc(e, &e->wo_cols[l], 16 * (size_t)n));
+    gg_wo_cols_kernel<<<(unsigned)((n + 255) / 256), 256, 0, e->stream>>>(e->wo[l], m.H, m.Q, m.rs_q, e->wo_cols[l]);
+    GG_CUDA(e, cudaGetLastError());
+  }
+  GG_TRY(dalloc(e, &m.acc, 8 * (size_t)2 * c.num_layers * m.acc_stride));
+  GG_TRY(dalloc(e, &m.acc_cnt, 4 * (size_t)2 * c.num_layers * 8));
+  GG_CUDA(e, cudaMemsetAsync(m.acc, 0, 8 * (size_t)2 * c.num_layers * m.acc_stride, e->stream));
+  GG_CUDA(e, cudaMemsetAsync(m.acc_cnt, 0, 4 * (size_t)2 * c.num_layers * 8, e->stream));
   for (int l = 0; l < c.num_layers; l++) {
     GGLayerW& w = m.layers[l];
     w.wqkv = e->wqkv[l]; w.wo = e->wo[l]; w.wgu = e->wgu[l]; w.wdown = e->wdown[l];
+    w.wo_cols = e->wo_cols[l];
     w.attn_norm = e->norms[0][l]; w.ffn_norm = e->norms[1][l]; w.q_norm = e->norms[2][l];
     w.k_norm = e->norms[3][l]; w.post_attn_norm = e->norms[4][l]; w.post_ffw_norm = e->norms[5][l];
     // getRopeTheta (types.ts:38-44)
@@ -526,7 +567,6 @@ extern "C" int gg_finalize(gg_engine* e) {
   GG_TRY(dalloc(e, &m.t_qkv, 8 * (size_t)m.grid * m.sl_qkv));
   GG_TRY(dalloc(e, &m.t_o, 8 * (size_t)m.max_splits * m.att_slot));
   GG_TRY(dalloc(e, &m.t_att, 8 * (size_t)m.Q));
-  GG_TRY(dalloc(e, &m.t_proj, 8 * (size_t)m.grid * m.sl_h));
   GG_TRY(dalloc(e, &m.t_act, 8 * (size_t)m.grid * m.sl_i));
   GG_TRY(dalloc(e, &m.t_down, 8 * (size_t)m.grid * m.sl_h));
   GG_TRY(dalloc(e, &m.logits, 4 * (size_t)m.V));
@@ -1014,14 +1054,26 @@ extern "C" int gg_dequant_row(gg_engine* e, int which, int layer, int row, int c
 extern "C" int gg_debug_read(gg_engine* e, int which, float* out, int n) {
   GG_TRY(ready(e, 0));
   const GGModelDev& m = e->md;
-  const uint64_t* tagged[5] = {m.t_qkv, m.t_att, m.t_proj, m.t_act, m.t_down};
+  const uint64_t* tagged[5] = {m.t_qkv, m.t_att, nullptr, m.t_act, m.t_down};
   const int tlen[5] = {m.Q + 2 * m.KV, m.Q, m.H, m.I, m.H};
   const float* plain[4] = {m.dbg_hidden, m.dbg_residual, m.dbg_normed, m.logits};
   const int plen[4] = {m.H, m.H, m.H, m.V};
   if (!out || which < 0 || which > 8) return fail(e, GG_E_ARG, "bad buffer id %d", which);
   int cap = which < 5 ? tlen[which] : plen[which - 5];
   if (n <= 0 || n > cap) return fail(e, GG_E_ARG, "n=%d outside 1..%d", n, cap);
-  if (which < 5) {
+  if (which == 2) {  // O projection: fixed-point sums of the last launch (parity flipped after it)
+    uint32_t par = 0;
+    GG_CUDA(e, cudaMemcpyAsync(&par, &e->d_st->parity, 4, cudaMemcpyDeviceToHost, e->stream));
+    GG_CUDA(e, cudaStreamSynchronize(e->stream));
+    const unsigned long long* src = m.acc + ((size_t)((par ^ 1u) & 1u) * m.L + (m.L - 1)) * m.acc_stride;
+    float* tmp = nullptr;
+    GG_CUDA(e, cudaMalloc(&tmp, 4 * (size_t)n));
+    gg_fixed_to_f32_kernel<<<(n + 255) / 256, 256, 0, e->stream>>>(src, tmp, n);
+    cudaError_t r = cudaMemcpyAsync(out, tmp, 4 * (size_t)n, cudaMemcpyDeviceToHost, e->stream);
+    cudaStreamSynchronize(e->stream);
+    cudaFree(tmp);
+    if (r != cudaSuccess) return fail(e, GG_E_CUDA, "debug read: %s", cudaGetErrorString(r));
+  } else if (which < 5) {
     float* tmp = nullptr;
     GG_CUDA(e, cudaMalloc(&tmp, 4 * (size_t)n));
     const int nq[5] = {(m.Q + 2 * m.KV) / 4, m.Q / 4, m.H / 4, m.I / 4, m.H / 4};

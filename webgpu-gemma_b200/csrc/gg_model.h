@@ -34,6 +34,10 @@ struct GGLayerW {
   float theta;
   int window;  // 0: attend the whole prefix; W: only positions pos-W+1..pos (sliding-window layer)
   const float2* rope;  // [CTX][HD/2] (cos, sin) of pos * theta^(-2i/HD) for this layer's theta
+  // The O projection by column slices for the step kernel: slice u (attention dims 8u..8u+7) is
+  // H rows of 16 bytes {8 int8 quants of those columns, the f16 scale of their Q8_0 block, 6 zero
+  // bytes}, H * 16 bytes per slice.
+  const uint8_t* wo_cols;
 };
 
 struct GGModelDev {
@@ -56,7 +60,6 @@ struct GGModelDev {
   uint64_t* t_qkv;  // [grid][sl_qkv] q | k | v rows
   uint64_t* t_o;    // [max_splits][att_slot] attention split partials (o, max, sum per head)
   uint64_t* t_att;  // Q merged attention output (8 dims per merge unit, contiguous)
-  uint64_t* t_proj; // [grid][sl_h] O projection rows
   uint64_t* t_act;  // [grid][sl_i] GeGLU outputs
   uint64_t* t_down; // [grid][sl_h] down projection rows
   float* logits;                    // V
@@ -81,6 +84,13 @@ struct GGModelDev {
   // ring and its mbarriers). The attention scratch (q | k | v) and the LM-head logits share the
   // O / down plane buffer when they fit: none of the three is live while another is.
   int sm_xa, sm_xb, sm_hid, sm_res, sm_tmp, sm_lmv, sm_scal, sm_red, sm_flag, sm_rows;
+  // K-split reductions of the step kernel (the O projection: every merge unit adds its 8 columns'
+  // products): per launch parity and layer, acc_stride accumulators in 2^-32 fixed point (u64,
+  // exact and order-independent) and one arrival counter (8 words apart).
+  unsigned long long* acc;  // [2][L][acc_stride]
+  unsigned int* acc_cnt;    // [2][L][8]
+  int acc_stride;           // >= H, a multiple of 4
+  int wo_rows_per_stage;    // 16-byte rows of a Wo column slice per ring stage
   // The step kernel keeps a copy of this descriptor up to layers[L - 1] in shared memory at
   // sm_model (GG_MODEL_BYTES(L) bytes), so its parameter reads never wait on L2.
   int sm_model;
@@ -126,5 +136,6 @@ struct GGState {
   uint32_t error;     // GG_ERR_* bits
   int32_t out_token;  // sampled token
   int32_t seen_count; // > 0 once this turn has tokens in the seen set
-  int32_t pad_[3];
+  uint32_t parity;    // accumulator set of the next launch (flipped by the last CTA of each)
+  int32_t pad_[2];
 };

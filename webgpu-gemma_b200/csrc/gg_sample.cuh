@@ -12,11 +12,24 @@ GG_DEV unsigned long long init_lane_key() {
   return ((unsigned long long)f32_order_key(-1e30f) << 32) | 0xffffffffull;
 }
 
+// The sampler's shared-memory workspace. The step kernel carves it from its weight ring, which is
+// idle once the LM head is done; the other kernels declare one.
+struct SampleScratch {
+  double sv[256];
+  double share[256];
+  unsigned long long wk[8];
+  double sum_all;
+  int sl[256];
+  uint32_t cid[256];
+  float probs[256];
+  int result;
+};
+
 // Run by every thread of one CTA (at least 256 threads). engine.ts:823-901.
-GG_DEV int sample_token(const GGModelDev& m, GGState* st) {
-  __shared__ double sv[256];
-  __shared__ int sl[256];
-  __shared__ int result;
+GG_DEV int sample_token(const GGModelDev& m, GGState* st, SampleScratch& S) {
+  double* sv = S.sv;
+  int* sl = S.sl;
+  int& result = S.result;
   const int tid = threadIdx.x;
   const int seq = st->seq;
   float val = 0.f;
@@ -32,7 +45,7 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st) {
     // slot on a tie at every stride (128, 64, ..., 1), so bit 0 of the lane is decided last and
     // weighs most: among equal maxima the lane with the smallest bit-reversed 8-bit index wins
     // (lanes 1 and 2 tied: lane 2). The low word keys that order for the max below.
-    __shared__ unsigned long long wk[8];
+    unsigned long long* wk = S.wk;
     unsigned long long key = 0;
     if (tid < 256) key = ((unsigned long long)f32_order_key(val) << 32) | (uint32_t)(255u - (__brev((uint32_t)tid) >> 24));
     if (tid < 256) {
@@ -83,7 +96,7 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st) {
       __syncthreads();
     }
   }
-  __shared__ uint32_t cid[256];
+  uint32_t* cid = S.cid;
   if (tid < 256) cid[tid] = idx;
   __syncthreads();
   if (T == 0.0) {
@@ -94,9 +107,9 @@ GG_DEV int sample_token(const GGModelDev& m, GGState* st) {
   // engine.ts:881-901, JS numbers are doubles; probs is a Float32Array. The element-wise terms
   // (exp, the division by the sum) are computed by one thread each; every running sum is taken
   // by one thread in index order, as the reference does, so the result is the same bit for bit.
-  __shared__ float probs[256];
-  __shared__ double share[256];
-  __shared__ double sum_all;
+  float* probs = S.probs;
+  double* share = S.share;
+  double& sum_all = S.sum_all;
   const double temp = T, top_p = st->top_p;
   if (tid < 256) probs[tid] = (float)exp((sv[tid] - sv[0]) / temp);
   __syncthreads();

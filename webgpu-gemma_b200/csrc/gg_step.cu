@@ -43,6 +43,7 @@ constexpr int NCT = NCW * 32;
 constexpr int NTH = NCT + 32;
 constexpr uint32_t NS = GG_STEP_STAGES;
 constexpr int PH = 6;  // phases (tags) per layer
+static_assert(sizeof(SampleScratch) <= (size_t)GG_STEP_STAGES * GG_STEP_STAGE_BYTES, "the sampler works in the idle ring");
 
 #define GG_NOINLINE __device__ __noinline__
 
@@ -95,6 +96,7 @@ struct Ctx {
   SpinCtl sc;
   int mode, token, pos, seq, nsplit;
   uint32_t tagbase;
+  uint32_t par;  // accumulator set of this launch (0 or 1)
 };
 
 // Rows per ring stage of a phase whose n rows (n <= NCW) are computed one per warp, and the
@@ -148,7 +150,7 @@ struct Producer {
           const size_t off = ((size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + p0) * m.KV) * es;
           issue(m.kcache + off, nb, m.vcache + off, nb, (uint32_t)(m.pos_per_split * m.KV * es));
         }
-        rows(Lw.wo, m.rs_q, R[RG_H], R[RG_H + 1], shared_rps(m.rps_q, R[RG_H + 1] - R[RG_H]));
+        if (c < m.ncomb) rows(Lw.wo_cols + (size_t)c * m.H * 16, 16, 0, m.H, m.wo_rows_per_stage);
         rows(Lw.wgu, m.rs_h, 2 * R[RG_I], 2 * R[RG_I + 1], m.rps_gu);
         rows(Lw.wdown, m.rs_i, R[RG_H], R[RG_H + 1], shared_rps(m.rps_i, R[RG_H + 1] - R[RG_H]));
       }
@@ -201,6 +203,19 @@ GG_DEV void quad_idle(uint64_t (&w)[4], uint32_t tag) {
 GG_DEV void quad_vals(const uint64_t (&w)[4], float* v) {
 #pragma unroll
   for (int j = 0; j < 4; j++) v[j] = __uint_as_float((uint32_t)w[j]);
+}
+
+// K-split reductions: an f32 partial added into a u64 accumulator in 2^-32 fixed point. Integer
+// addition is exact and associative, so the sum is the same whatever order the CTAs arrive in.
+GG_DEV void acc_add(unsigned long long* p, float v) {
+  const long long q = __float2ll_rn(v * 4294967296.0f);
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)q) : "memory");
+}
+GG_DEV float acc_value(unsigned long long w) { return (float)(long long)w * 0x1p-32f; }
+GG_DEV uint32_t ld_acquire_u32(const unsigned int* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // ---------------------------------------------------------------------------------- dot products
@@ -482,7 +497,7 @@ struct Consumer {
   GG_DEV void add_norm_planes(const XPlanes& P, const uint64_t* src, uint32_t tag, const float* wa, const float* base,
                               float* out, const float* wb, float* dbg_out, float* dbg_x) {
     const GGModelDev& m = *x.m;
-    const int nq = m.H >> 2, k = tid, nw = (nq + 31) >> 5;
+    const int nq = m.H >> 2, k = tid;
     const bool ok = k < nq;
     float4 fa = make_float4(0.f, 0.f, 0.f, 0.f), fb = fa, fbase = fa;
     float v[4];
@@ -498,6 +513,50 @@ struct Consumer {
     }
     settle_warp<1>(p, tag, w);
     quad_vals(w[0], v);
+    add_norm_tail(P, v, fa, fb, fbase, out, dbg_out, dbg_x);
+  }
+
+  // The same on the fixed-point sums of a K-split reduction: every warp first waits until `cnt`
+  // reaches `target` arrivals (each lane polls with acquire semantics, so its loads that follow
+  // see every arrival's additions). Bounded: after giving up the sums read 0.
+  GG_DEV void add_norm_sums(const XPlanes& P, const unsigned long long* acc, const unsigned int* cnt, uint32_t target,
+                            const float* wa, const float* base, float* out, const float* wb, float* dbg_out,
+                            float* dbg_x) {
+    const GGModelDev& m = *x.m;
+    const int nq = m.H >> 2, k = tid;
+    const bool ok = k < nq;
+    float4 fa = make_float4(0.f, 0.f, 0.f, 0.f), fb = fa, fbase = fa;
+    if (ok) {
+      fa = __ldg(reinterpret_cast<const float4*>(wa) + k);
+      fb = __ldg(reinterpret_cast<const float4*>(wb) + k);
+      fbase = reinterpret_cast<const float4*>(base)[k];
+    }
+    bool live = true;
+    {
+      SpinClock clk;
+#pragma unroll 1
+      while (ld_acquire_u32(cnt) < target) {
+        if (__any_sync(0xffffffffu, clk.expired(x.sc))) {
+          live = false;
+          break;
+        }
+      }
+    }
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (ok && live) {
+      uint64_t w[4];
+      issue4(reinterpret_cast<const uint64_t*>(acc) + 4 * k, w);
+#pragma unroll
+      for (int j = 0; j < 4; j++) v[j] = acc_value(w[j]);
+    }
+    add_norm_tail(P, v, fa, fb, fbase, out, dbg_out, dbg_x);
+  }
+
+  GG_DEV void add_norm_tail(const XPlanes& P, const float* v, float4 fa, float4 fb, float4 fbase, float* out,
+                            float* dbg_out, float* dbg_x) {
+    const GGModelDev& m = *x.m;
+    const int nq = m.H >> 2, k = tid, nw = (nq + 31) >> 5;
+    const bool ok = k < nq;
     const float wav[4] = {fa.x, fa.y, fa.z, fa.w}, wbv[4] = {fb.x, fb.y, fb.z, fb.w};
     const float bv[4] = {fbase.x, fbase.y, fbase.z, fbase.w};
     float s[4] = {0.f, 0.f, 0.f, 0.f};
@@ -909,7 +968,9 @@ struct Consumer {
       if (lane < 8) part[warp * 10 + 2 + lane] = res;
     }
     cbar();  // the other warps wait here instead of polling the merged words
-    if (have && warp == 0) {
+    if (!have) return;  // uniform over the CTA
+    float* av = x.S.red + 16 * ((10 * NCW + 15) / 16);  // the unit's 8 merged values, after part[]
+    if (warp == 0) {
       float gm = -INFINITY;
       for (int w = 0; w < W; w++) gm = fmaxf(gm, part[w * 10]);
       float lsum = 0.f, o = 0.f;
@@ -919,28 +980,44 @@ struct Consumer {
         lsum = fmaf(f, part[w * 10 + 1], lsum);
         if (lane < 8) o = fmaf(f, part[w * 10 + 2 + lane], o);
       }
-      if (lane < 8) tag_store(m.t_att + d0 + lane, o / lsum, tagC);
+      if (lane < 8) {
+        av[lane] = o / lsum;
+        tag_store(m.t_att + d0 + lane, o / lsum, tagC);  // kept for gg_debug_read
+      }
     }
-  }
-
-  GG_DEV void phase_o(int l) {
-    const GGModelDev& m = *x.m;
-    planes_gather<1>(x.S.xb, m.t_att, m.Q >> 2, 0, make_tag(x.tagbase, l * PH + 2));
-    const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
-    gate(shared_nst(m.rps_q, n));
+    // O projection by columns (shaders.ts matmul of attn_output, engine.ts:783): this unit adds
+    // Wo[r][d0..d0+7] . o for every row r into the layer's accumulators, then counts itself in.
+    const int wrs = m.wo_rows_per_stage, nst = (m.H + wrs - 1) / wrs;
+    gate(nst);
     cbar();
-    trace(l * PH + 3, 1);
-    uint64_t* out = m.t_proj + (size_t)blockIdx.x * m.sl_h;
-    const uint32_t tag = make_tag(x.tagbase, l * PH + 3);
-    matvec(x.S.xb, n, m.rps_q, m.Q, m.rs_q, out, tag);
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) a[j] = av[j];
+    unsigned long long* acc = m.acc + ((size_t)x.par * m.L + l) * m.acc_stride;
+    const uint32_t ring = smem_u32(x.S.ring);
+    for (int r = tid; r < m.H; r += NCT) {
+      const uint4 w = lds128(ring + ((idx + (uint32_t)(r / wrs)) % NS) * GG_STEP_STAGE_BYTES + (uint32_t)(r % wrs) * 16u);
+      const uint32_t q[2] = {w.x, w.y};
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) sum = fmaf((float)((int)(q[j >> 2] << (24 - 8 * (j & 3))) >> 24), a[j], sum);
+      acc_add(acc + r, sum * __half2float(__ushort_as_half((unsigned short)(w.z & 0xffffu))));
+    }
+    cbar();
+    release_all(nst);
+    if (tid == 0) {
+      __threadfence();
+      atomicAdd(m.acc_cnt + ((size_t)x.par * m.L + l) * 8, 1u);
+    }
   }
 
   GG_DEV void phase_ffn_up(int l) {
     const GGModelDev& m = *x.m;
     const GGLayerW& Lw = m.layers[l];
     // residual = hidden + post_attention_norm(proj) (engine.ts:785), then ffn rmsNorm (786)
-    add_norm_planes(x.S.xa, m.t_proj, make_tag(x.tagbase, l * PH + 3), Lw.post_attn_norm, x.S.hid, x.S.res,
-                    Lw.ffn_norm, blockIdx.x == 0 ? m.dbg_residual : nullptr, nullptr);
+    const size_t ai = (size_t)x.par * m.L + l;
+    add_norm_sums(x.S.xa, m.acc + ai * m.acc_stride, m.acc_cnt + ai * 8, (uint32_t)m.ncomb, Lw.post_attn_norm, x.S.hid,
+                  x.S.res, Lw.ffn_norm, blockIdx.x == 0 ? m.dbg_residual : nullptr, nullptr);
     const int n = x.S.rows[RG_I + 1] - x.S.rows[RG_I];
     const int nst = (n + (m.rps_gu >> 1) - 1) / (m.rps_gu >> 1);
     gate(nst);
@@ -1023,9 +1100,6 @@ struct Consumer {
         trace(l * PH + 2, 0);
         phase_combine(l);
         trace(l * PH + 2, 2);
-        trace(l * PH + 3, 0);
-        phase_o(l);
-        trace(l * PH + 3, 2);
         trace(l * PH + 4, 0);
         phase_ffn_up(l);
         trace(l * PH + 4, 2);
@@ -1070,6 +1144,7 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
   x.pos = st->pos;
   x.seq = st->seq;
   x.tagbase = st->epoch;
+  x.par = st->parity & 1u;
   x.sc.err = &st->error;
   x.sc.timeout_ns = st->timeout_ns;
   // carve shared memory (offsets and GGModelDev::smem_bytes computed by the host)
@@ -1113,6 +1188,13 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
     }
   }
   __syncthreads();
+  {  // zero this CTA's share of the other accumulator set (the next launch's)
+    unsigned long long* a = m.acc + (size_t)(x.par ^ 1u) * m.L * m.acc_stride;
+    const int n = m.L * m.acc_stride, stride = m.grid * (int)blockDim.x;
+    for (int i = blockIdx.x * (int)blockDim.x + (int)threadIdx.x; i < n; i += stride) a[i] = 0ull;
+    unsigned int* cn = m.acc_cnt + (size_t)(x.par ^ 1u) * m.L * 8;
+    for (int i = blockIdx.x * (int)blockDim.x + (int)threadIdx.x; i < m.L * 8; i += stride) cn[i] = 0u;
+  }
 
   if (warp == NCW) {
     if (lane == 0) {
@@ -1135,12 +1217,13 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
   if (!*x.S.flag) return;
   __threadfence();
   int tok = -1;
-  if (x.mode & GG_RUN_SAMPLE) tok = sample_token(m, st);
+  if (x.mode & GG_RUN_SAMPLE) tok = sample_token(m, st, *reinterpret_cast<SampleScratch*>(smem));  // ring is idle
   __syncthreads();
   if (threadIdx.x < 256) m.lane_keys[threadIdx.x] = init_lane_key();
   if (threadIdx.x == 0) {
     st->epoch = st->epoch + (uint32_t)(m.L * PH + 1);
     st->done = 0;
+    st->parity = x.par ^ 1u;
     if (x.mode & GG_RUN_SAMPLE) {
       st->out_token = tok;
       if (tok >= 0 && tok < m.V) {
