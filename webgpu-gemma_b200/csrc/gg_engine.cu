@@ -290,7 +290,9 @@ static int schedule(gg_engine* e) {
   // 128 CTAs split the 1B model's row sets into whole quads of near-equal size (3 q/k/v quads,
   // 2-3 quads of O and down rows, 13-14 quads of gate/up pairs, 512 quads of LM-head rows) and
   // need one hand-over fewer CTA than one per SM; measured faster than 148 on B200.
-  m.grid = std::min(e->sm_count, 128);
+  if (e->sm_count < GG_STEP_GRID)
+    return fail(e, GG_E_ARG, "the step kernel needs %d SMs (device has %d)", GG_STEP_GRID, e->sm_count);
+  m.grid = GG_STEP_GRID;
   const int G = m.grid;
   // the step kernel splits quads as c * nq / G in 32-bit arithmetic
   if ((long long)(G + 1) * (m.V / 4 + 1) >= (1ll << 31)) return fail(e, GG_E_ARG, "vocabulary too large for the step kernel's row split");
@@ -309,6 +311,10 @@ static int schedule(gg_engine* e) {
   m.sl_qkv = slot((m.Q + 2 * m.KV) / 4);
   m.sl_h = slot(m.H / 4);
   m.sl_i = slot(m.I / 4);
+  const auto magic = [](int nq) { return ((1ull << 40) + (unsigned long long)nq - 1) / (unsigned long long)nq; };
+  m.mq_qkv = magic((m.Q + 2 * m.KV) / 4);
+  m.mq_h = magic(m.H / 4);
+  m.mq_i = magic(m.I / 4);
   m.lm_rows = slot(m.V / 4);
   // the q/k/v, O and down rows of a CTA are computed one per consumer warp
   if (m.sl_qkv > GG_STEP_NCW || m.sl_h > GG_STEP_NCW)
@@ -335,10 +341,7 @@ static int schedule(gg_engine* e) {
   if (m.ncomb > G) return fail(e, GG_E_ARG, "q_dim / 8 = %d attention merge units exceed the grid (%d)", m.ncomb, G);
   // the merge units apply their 8 columns of Wo: H rows of 16 bytes, all stages resident at once
   m.wo_rows_per_stage = SB / 16;
-  {
-    const int nst_wo = (m.H + m.wo_rows_per_stage - 1) / m.wo_rows_per_stage;
-    if (nst_wo >= GG_STEP_STAGES || nst_wo > GG_STEP_NCW) return fail(e, GG_E_ARG, "hidden_size too large for the O slices");
-  }
+  if (m.H > m.wo_rows_per_stage) return fail(e, GG_E_ARG, "hidden_size above %d: the O column slice needs one ring stage", m.wo_rows_per_stage);
   m.acc_stride = (m.H + 3) / 4 * 4;
   m.xs0 = (m.H + 63) / 64 * 64;
   m.xs1 = (std::max(m.Q, m.I) + 63) / 64 * 64;

@@ -14,6 +14,8 @@
 #define GG_HEAD_DIM 256                // Gemma 3 head size (compile-time for the attention phase)
 #define GG_POS_PER_SPLIT 8             // KV positions per attention split
 #define GG_TRACE_PHASES 512            // phases traced per CTA by GG_TRACE launches (4 stamps each)
+#define GG_STEP_GRID 128               // step kernel: CTAs (a power of two, one per SM; B200 has 148 SMs)
+#define GG_STEP_LOG2_GRID 7
 #define GG_STEP_NCW 15                 // step kernel: consumer warps per CTA (+ one producer warp: 4 warps per SM sub-partition, 128 registers a thread)
 #define GG_STEP_STAGES 9               // step kernel: weight ring stages
 #define GG_STEP_STAGE_BYTES 20480      // step kernel: bytes per ring stage (16 rows of 1,152 Q8_0 weights)
@@ -78,6 +80,9 @@ struct GGModelDev {
   // of the Q+2KV, H and I (pair) outputs; words per attention split (NQH x (HD + 4): o, max, sum).
   int rps_h, rps_q, rps_i, rps_gu;
   int sl_qkv, sl_h, sl_i;
+  // ceil(2^40 / nq) for the quad counts of those outputs ((Q + 2KV) / 4, H / 4, I / 4): the owner
+  // of quad q is ((q + 1) * G - 1) * mq >> 40 (exact while that product's factors stay below 2^40)
+  unsigned long long mq_qkv, mq_h, mq_i;
   int att_slot;
   int lm_rows;  // most LM-head rows of one CTA (its logits are staged in shared memory)
   // Step kernel shared-memory layout: byte offsets from the dynamic shared-memory base (after the

@@ -53,12 +53,15 @@ GG_DEV uint32_t make_tag(uint32_t base, int phase) { return 0x80000000u | ((base
 
 // Quad partition: quads [qpart(c), qpart(c + 1)) of nq go to CTA c of G (32-bit: the host checks
 // G * nq < 2^31), and the CTA that owns quad q.
-GG_DEV int qpart(int nq, int G, int c) { return (int)(((uint32_t)c * (uint32_t)nq) / (uint32_t)G); }
-GG_DEV int qowner(int nq, int G, int q) { return (int)((((uint32_t)q + 1u) * (uint32_t)G - 1u) / (uint32_t)nq); }
+GG_DEV int qpart(int nq, int c) { return (int)(((uint32_t)c * (uint32_t)nq) >> GG_STEP_LOG2_GRID); }
+// (division by nq as a multiply by mq = ceil(2^40 / nq): n * nq < 2^40 here, so it is exact)
+GG_DEV int qowner(unsigned long long mq, int q) {
+  return (int)(((unsigned long long)(((uint32_t)q + 1u) * (uint32_t)GG_STEP_GRID - 1u) * mq) >> 40);
+}
 // Word offset of element quad q in a slot layout (CTA c's words start at c * sl).
-GG_DEV int slot_word(int nq, int G, int sl, int q) {
-  const int c = qowner(nq, G, q);
-  return c * sl + 4 * (q - qpart(nq, G, c));
+GG_DEV int slot_word(int nq, unsigned long long mq, int sl, int q) {
+  const int c = qowner(mq, q);
+  return c * sl + 4 * (q - qpart(nq, c));
 }
 
 // The planes of one x vector, as shared-window addresses.
@@ -87,6 +90,25 @@ struct Smem {
   int* rows;
 };
 
+// Rows per ring stage of a phase whose n rows (n <= NCW) are computed one per warp, and the
+// number of such stages.
+GG_DEV int shared_rps(int rps_max, int n) { return max(min(rps_max, n), 1); }
+GG_DEV int shared_nst(int rps_max, int n) { const int d = shared_rps(rps_max, n); return (n + d - 1) / d; }
+
+// Work map of a small matvec phase (q/k/v, down) for one consumer warp, fixed for a launch: the
+// ring offsets of its four rows ((stage << 16) | byte offset; rows past n repeat the last row),
+// its 16-element chunk slice [c0, c1), its row group g (0xff: no rows) and slice index sl.
+struct MvWarp {
+  uint32_t roff[4];
+  uint16_t c0, c1;
+  uint8_t g, sl;
+  uint16_t pad;
+};
+struct MvPhase {
+  int n, nst, S;  // rows, ring stages, K slices per row group
+  MvWarp w[GG_STEP_NCW];
+};
+
 // Per-launch constants, held in shared memory (filled by thread 0 at the start): keeping them out
 // of registers leaves the hot loops free of register spills.
 struct Ctx {
@@ -97,19 +119,51 @@ struct Ctx {
   int mode, token, pos, seq, nsplit;
   uint32_t tagbase;
   uint32_t par;  // accumulator set of this launch (0 or 1)
+  MvPhase mv[2];  // matvec maps: 0 q/k/v, 1 down
 };
 
-// Rows per ring stage of a phase whose n rows (n <= NCW) are computed one per warp, and the
-// number of such stages.
-GG_DEV int shared_rps(int rps_max, int n) { return max(min(rps_max, n), 1); }
-GG_DEV int shared_nst(int rps_max, int n) { const int d = shared_rps(rps_max, n); return (n + d - 1) / d; }
+// The matvec map of phase p for warp w (integer divisions, once per launch): the CTA's n rows in
+// stages of d = shared_rps(rps_max, n) rows of rs bytes, K inputs; groups of four rows, each split
+// into S = NCW / groups K slices.
+GG_DEV void mv_map(MvPhase& ph, int w, int n, int rps_max, int K, int rs) {
+  MvWarp& e = ph.w[w];
+  if (n <= 0) {  // a CTA without rows in this phase (narrow models): no stages, every warp idle
+    if (w == 0) {
+      ph.n = 0;
+      ph.nst = 0;
+      ph.S = 1;
+    }
+    e.g = 0xff;
+    e.sl = 0;
+    e.c0 = e.c1 = 0;
+    for (int k = 0; k < 4; k++) e.roff[k] = 0;
+    return;
+  }
+  const int d = shared_rps(rps_max, n), ng = (n + 3) >> 2, S = GG_STEP_NCW / ng, nch = K >> 4;
+  if (w == 0) {
+    ph.n = n;
+    ph.nst = (n + d - 1) / d;
+    ph.S = S;
+  }
+  const int g = w / S, sl = w % S;
+  e.g = g < ng ? (uint8_t)g : (uint8_t)0xff;
+  e.sl = (uint8_t)sl;
+  e.c0 = (uint16_t)(sl * nch / S);
+  e.c1 = (uint16_t)((sl + 1) * nch / S);
+  for (int k = 0; k < 4; k++) {
+    const int r = min(4 * g + k, n - 1);
+    e.roff[k] = ((uint32_t)(r / d) << 16) | (uint32_t)((r % d) * rs);
+  }
+}
+
 
 GG_DEV int window_lo(const GGLayerW& Lw, int pos) { return (Lw.window > 0 && pos + 1 > Lw.window) ? pos + 1 - Lw.window : 0; }
 
 // First split of this CTA in layer l (splits s >= slo with s - slo = (c - rot) mod G).
 GG_DEV int first_split(const GGModelDev& m, int l, int pos, int nsplit, int c) {
-  const int G = m.grid, rot = (l * nsplit) % G;
-  return window_lo(m.layers[l], pos) / m.pos_per_split + (c - rot + G) % G;
+  constexpr int G = GG_STEP_GRID;
+  const int rot = (l * nsplit) & (G - 1);
+  return window_lo(m.layers[l], pos) / GG_POS_PER_SPLIT + ((c - rot + G) & (G - 1));
 }
 
 // ---------------------------------------------------------------------------------- producer
@@ -464,15 +518,14 @@ struct Consumer {
   // (sl = 0), without normalisation: the inputs of the O and down projections. QPT quads per
   // thread are in flight before any tag is checked (one round trip when nq <= QPT * NCT).
   template <int QPT>
-  GG_DEV void planes_gather(const XPlanes& P, const uint64_t* src, int nq, int sl, uint32_t tag) {
-    const int G = x.m->grid;
+  GG_DEV void planes_gather(const XPlanes& P, const uint64_t* src, int nq, unsigned long long mq, int sl, uint32_t tag) {
     for (int base = 0; base < nq; base += QPT * NCT) {
       uint64_t w[QPT][4];
       const uint64_t* pk[QPT];
 #pragma unroll
       for (int k = 0; k < QPT; k++) {
         const int q = base + tid + k * NCT;
-        pk[k] = q < nq ? src + (sl ? slot_word(nq, G, sl, q) : 4 * q) : src;
+        pk[k] = q < nq ? src + (sl ? slot_word(nq, mq, sl, q) : 4 * q) : src;
         if (q < nq)
           issue4(pk[k], w[k]);
         else
@@ -501,7 +554,7 @@ struct Consumer {
     const bool ok = k < nq;
     float4 fa = make_float4(0.f, 0.f, 0.f, 0.f), fb = fa, fbase = fa;
     float v[4];
-    const uint64_t* p[1] = {src + slot_word(nq, m.grid, m.sl_h, ok ? k : 0)};
+    const uint64_t* p[1] = {src + slot_word(nq, m.mq_h, m.sl_h, ok ? k : 0)};
     uint64_t w[1][4];
     if (ok) {
       issue4(p[0], w[0]);
@@ -631,34 +684,34 @@ struct Consumer {
     norm_planes(P, o, ok, wb, nullptr);
   }
 
-  // The CTA's n rows (n <= 16) of a phase, in nst ring stages of d = shared_rps(rps_max, n) rows
-  // (all resident at once: the host checks nst < NS; the caller gated them before its barrier). Work units are (group of four rows, K
-  // slice): warp w takes group w / S and slice w % S, S = NCW / groups, so the four rows share
-  // every load of the x planes. The slice totals meet in shared memory; thread r < n sums them in
+  // The CTA's n rows (n <= 16) of a phase, in the ph.nst ring stages of its map (all resident at
+  // once: the host checks nst < NS; the caller gated them before its barrier). Work units are
+  // (group of four rows, K slice), as mv_map assigns them, so the four rows share every load of
+  // the x planes. The slice totals meet in shared memory; thread r < n sums them in
   // slice order and stores the row total as tagged word out[r]. Every consumer warp must call
   // this (it holds a CTA barrier).
-  GG_DEV void matvec(const XPlanes& P, int n, int rps_max, int K, int rs, uint64_t* out, uint32_t tag) {
-    const int d = shared_rps(rps_max, n), nst = (n + d - 1) / d;
-    const int ng = (n + 3) >> 2, S = NCW / ng, nch = K >> 4;
-    const int g = warp / S, sl = warp % S;
+  GG_DEV void matvec(const XPlanes& P, const MvPhase& ph, int K, uint64_t* out, uint32_t tag) {
+    const MvWarp& e = ph.w[warp];
+    const int n = ph.n, S = ph.S, g = e.g;
     float* red = x.S.red;  // [row][slice]
-    if (g < ng) {
+    if (g != 0xff) {
       uint32_t ra[4];
+      const uint32_t ring = smem_u32(x.S.ring);
 #pragma unroll
-      for (int k = 0; k < 4; k++) {
-        const int r = min(4 * g + k, n - 1);  // rows past n repeat the last row; their sums are dropped
-        ra[k] = smem_u32(x.S.ring) + (uint32_t)(((idx + (uint32_t)(r / d)) % NS) * GG_STEP_STAGE_BYTES + (r % d) * rs);
+      for (int k = 0; k < 4; k++) {  // rows past n repeat the last row; their sums are dropped
+        const uint32_t o = e.roff[k];
+        ra[k] = ring + ((idx + (o >> 16)) % NS) * GG_STEP_STAGE_BYTES + (o & 0xffffu);
       }
-      const float4 v = dot_rows4(ra, K, sl * nch / S, (sl + 1) * nch / S, P);
+      const float4 v = dot_rows4(ra, K, e.c0, e.c1, P);
       if (lane == 0) {
         const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int k = 0; k < 4; k++)
-          if (4 * g + k < n) red[(4 * g + k) * S + sl] = vv[k];
+          if (4 * g + k < n) red[(4 * g + k) * S + e.sl] = vv[k];
       }
     }
     cbar();
-    release_all(nst);
+    release_all(ph.nst);
     if (tid < n) {
       float t = 0.f;
       for (int k = 0; k < S; k++) t += red[tid * S + k];
@@ -696,13 +749,12 @@ struct Consumer {
       add_norm_planes(x.S.xa, m.t_down, make_tag(x.tagbase, (l - 1) * PH + 5), m.layers[l - 1].post_ffw_norm, x.S.res,
                       x.S.hid, m.layers[l].attn_norm, blockIdx.x == 0 ? m.dbg_hidden : nullptr, nullptr);
     }
-    const int n = x.S.rows[RG_QKV + 1] - x.S.rows[RG_QKV];
-    gate(shared_nst(m.rps_h, n));
+    gate(x.mv[0].nst);
     cbar();
     trace(l * PH + 0, 1);
     uint64_t* out = m.t_qkv + (size_t)blockIdx.x * m.sl_qkv;
     const uint32_t tag = make_tag(x.tagbase, l * PH + 0);
-    matvec(x.S.xa, n, m.rps_h, m.H, m.rs_h, out, tag);
+    matvec(x.S.xa, x.mv[0], m.H, out, tag);
   }
 
   // q/k per-head RMSNorm + RoPE (shaders.ts:420-467), the KV store (shaders.ts:209-227) and this
@@ -710,10 +762,12 @@ struct Consumer {
   GG_DEV void phase_attn(int l) {
     const GGModelDev& m = *x.m;
     const GGLayerW& Lw = m.layers[l];
-    const int G = m.grid, s0 = first_split(m, l, x.pos, x.nsplit, blockIdx.x);
-    const int att_nst = s0 < x.nsplit ? (x.nsplit - 1 - s0) / G + 1 : 0;  // this CTA's splits (KV stages)
+    constexpr int G = GG_STEP_GRID;
+    const int s0 = first_split(m, l, x.pos, x.nsplit, blockIdx.x);
+    const int att_nst = s0 < x.nsplit ? ((x.nsplit - 1 - s0) >> GG_STEP_LOG2_GRID) + 1 : 0;  // this CTA's splits (KV stages)
     if (s0 >= x.nsplit) return;
-    const int HD = m.HD, NQH = m.NQH, NKH = m.NKH, Q = m.Q, KV = m.KV;
+    constexpr int HD = GG_HEAD_DIM;
+    const int NQH = m.NQH, NKH = m.NKH, Q = m.Q, KV = m.KV;
     float* t = x.S.tmp;  // q [Q] | k [KV] | v [KV]
     const uint32_t tagA = make_tag(x.tagbase, l * PH + 0);
     // One warp per q, k or v head. Lane l takes quads l and l + 32 of its head (elements 4l..4l+3
@@ -724,7 +778,7 @@ struct Consumer {
     for (int h = warp; h < NQH + 2 * NKH; h += NCW) {
       const bool normed = h < NQH + NKH;  // q and k heads; v is stored as is
       const int q0 = h * (HD / 4) + lane, q1 = q0 + HD / 8;
-      const uint64_t* pq[2] = {m.t_qkv + slot_word(nq, G, m.sl_qkv, q0), m.t_qkv + slot_word(nq, G, m.sl_qkv, q1)};
+      const uint64_t* pq[2] = {m.t_qkv + slot_word(nq, m.mq_qkv, m.sl_qkv, q0), m.t_qkv + slot_word(nq, m.mq_qkv, m.sl_qkv, q1)};
       uint64_t w[2][4];
       issue4(pq[0], w[0]);
       issue4(pq[1], w[1]);
@@ -768,7 +822,7 @@ struct Consumer {
     cbar();
     trace(l * PH + 1, 1);
     // the CTA whose splits include the new position stores its k and v
-    if ((x.pos / m.pos_per_split - s0) % G == 0 && x.pos / m.pos_per_split >= s0) {
+    if ((((x.pos / GG_POS_PER_SPLIT) - s0) & (G - 1)) == 0 && x.pos / GG_POS_PER_SPLIT >= s0) {
       using KT = kv_t<KV16>;
       const size_t off = (size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + x.pos) * KV;
       KT* kc = reinterpret_cast<KT*>(m.kcache);
@@ -806,7 +860,8 @@ struct Consumer {
   __device__ __noinline__ void attn_split(int s, int plo, const uint8_t* stg, int h, uint32_t tag) {
     using KT = kv_t<KV16>;
     const GGModelDev& m = *x.m;
-    const int Q = m.Q, KV = m.KV, HD = m.HD, NQH = m.NQH, NKH = m.NKH;
+    const int Q = m.Q, KV = m.KV, NQH = m.NQH, NKH = m.NKH;
+    constexpr int HD = GG_HEAD_DIM;
     static_assert(GG_HEAD_DIM == 256 && GG_POS_PER_SPLIT == 8, "lanes are 8 positions x 4 quarters of a head");
     constexpr int PPS = GG_POS_PER_SPLIT;
     const float* t = x.S.tmp;
@@ -911,10 +966,11 @@ struct Consumer {
   // shared memory in warp order and stores the unit's outputs.
   GG_DEV void phase_combine(int l) {
     const GGModelDev& m = *x.m;
-    const int HD = m.HD, ncomb = m.Q >> 3;
+    constexpr int HD = GG_HEAD_DIM;
+    const int ncomb = m.Q >> 3;
     const uint32_t tagB = make_tag(x.tagbase, l * PH + 1);
     const uint32_t tagC = make_tag(x.tagbase, l * PH + 2);
-    const int slo = window_lo(m.layers[l], x.pos) / m.pos_per_split;
+    const int slo = window_lo(m.layers[l], x.pos) / GG_POS_PER_SPLIT;
     const int ns = x.nsplit - slo, W = min((ns + 31) >> 5, NCW);
     float* part = x.S.red;  // [warp][10]: max, sum, 8 outputs
     const int u = blockIdx.x;
@@ -987,7 +1043,7 @@ struct Consumer {
     }
     // O projection by columns (shaders.ts matmul of attn_output, engine.ts:783): this unit adds
     // Wo[r][d0..d0+7] . o for every row r into the layer's accumulators, then counts itself in.
-    const int wrs = m.wo_rows_per_stage, nst = (m.H + wrs - 1) / wrs;
+    constexpr int nst = 1;  // the host checks H <= wo_rows_per_stage
     gate(nst);
     cbar();
     float a[8];
@@ -996,7 +1052,7 @@ struct Consumer {
     unsigned long long* acc = m.acc + ((size_t)x.par * m.L + l) * m.acc_stride;
     const uint32_t ring = smem_u32(x.S.ring);
     for (int r = tid; r < m.H; r += NCT) {
-      const uint4 w = lds128(ring + ((idx + (uint32_t)(r / wrs)) % NS) * GG_STEP_STAGE_BYTES + (uint32_t)(r % wrs) * 16u);
+      const uint4 w = lds128(ring + (idx % NS) * GG_STEP_STAGE_BYTES + (uint32_t)r * 16u);
       const uint32_t q[2] = {w.x, w.y};
       float sum = 0.f;
 #pragma unroll
@@ -1034,14 +1090,13 @@ struct Consumer {
 
   GG_DEV void phase_down(int l) {
     const GGModelDev& m = *x.m;
-    planes_gather<4>(x.S.xb, m.t_act, m.I >> 2, m.sl_i, make_tag(x.tagbase, l * PH + 4));
-    const int n = x.S.rows[RG_H + 1] - x.S.rows[RG_H];
-    gate(shared_nst(m.rps_i, n));
+    planes_gather<4>(x.S.xb, m.t_act, m.I >> 2, m.mq_i, m.sl_i, make_tag(x.tagbase, l * PH + 4));
+    gate(x.mv[1].nst);
     cbar();
     trace(l * PH + 5, 1);
     uint64_t* out = m.t_down + (size_t)blockIdx.x * m.sl_h;
     const uint32_t tag = make_tag(x.tagbase, l * PH + 5);
-    matvec(x.S.xb, n, m.rps_i, m.I, m.rs_i, out, tag);
+    matvec(x.S.xb, x.mv[1], m.I, out, tag);
   }
 
   GG_DEV void phase_lm() {
@@ -1174,20 +1229,27 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
     if (blockIdx.x == 0) atomicOr(&st->error, GG_ERR_BAD_INPUT);
     x.mode = 0;
   }
-  x.nsplit = (x.pos + m.pos_per_split) / m.pos_per_split;  // ceil((pos + 1) / PPS)
+  x.nsplit = (x.pos + GG_POS_PER_SPLIT) / GG_POS_PER_SPLIT;  // ceil((pos + 1) / PPS)
     for (int i = 0; i < (int)NS; i++) {
       mbar_init(&x.S.full[i], 1);
       mbar_init(&x.S.empty[i], NCW);
     }
     mbar_fence_init();
-    const int c = blockIdx.x, G = m.grid;
+    const int c = blockIdx.x;
     const int nq[4] = {(m.Q + 2 * m.KV) >> 2, m.H >> 2, m.I >> 2, m.V >> 2};
     for (int k = 0; k < 4; k++) {
-      x.S.rows[2 * k] = 4 * qpart(nq[k], G, c);
-      x.S.rows[2 * k + 1] = 4 * qpart(nq[k], G, c + 1);
+      x.S.rows[2 * k] = 4 * qpart(nq[k], c);
+      x.S.rows[2 * k + 1] = 4 * qpart(nq[k], c + 1);
     }
   }
   __syncthreads();
+  if (threadIdx.x < 2 * NCW) {  // the matvec maps of the q/k/v (0) and down (1) phases
+    const int p = threadIdx.x / NCW, w = threadIdx.x % NCW;
+    if (p == 0)
+      mv_map(x.mv[0], w, x.S.rows[RG_QKV + 1] - x.S.rows[RG_QKV], m.rps_h, m.H, m.rs_h);
+    else
+      mv_map(x.mv[1], w, x.S.rows[RG_H + 1] - x.S.rows[RG_H], m.rps_i, m.I, m.rs_i);
+  }
   {  // zero this CTA's share of the other accumulator set (the next launch's)
     unsigned long long* a = m.acc + (size_t)(x.par ^ 1u) * m.L * m.acc_stride;
     const int n = m.L * m.acc_stride, stride = m.grid * (int)blockDim.x;
@@ -1195,6 +1257,7 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
     unsigned int* cn = m.acc_cnt + (size_t)(x.par ^ 1u) * m.L * 8;
     for (int i = blockIdx.x * (int)blockDim.x + (int)threadIdx.x; i < m.L * 8; i += stride) cn[i] = 0u;
   }
+  __syncthreads();
 
   if (warp == NCW) {
     if (lane == 0) {
