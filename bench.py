@@ -66,7 +66,7 @@ def measured_peaks() -> tuple[float, str]:
 # ncu capture of the step kernel on this workload (summary under profiles/): dram bytes read +
 # written by one launch at position NCU_TRAFFIC_POS. The line reports it moved to the mean timed
 # position by the KV bytes per position (the weights are the same every token).
-NCU_TRAFFIC_PER_LAUNCH = 1103156224 + 4640000
+NCU_TRAFFIC_PER_LAUNCH = 1108814592 + 3782912
 NCU_TRAFFIC_POS = 641
 
 
@@ -259,11 +259,15 @@ def run_trace():
     L, G = cfg.num_layers, eng.grid()
     t = eng.read_trace(G * 512 * 4).astype(np.int64).reshape(G, 512, 4)
     t0 = t[:, 0, 0].min()
-    names = ["qkv", "attn", "combine", "o_proj", "gate_up", "down"]
-    rows = {n: {"wait_us": [], "compute_us": [], "span_us": [], "ring_wait_us": []} for n in names}
+    # phase slots per layer: q/k/v, attention splits, merge + O column slices (the O projection is
+    # summed in the merge phase; slot 3 is unused), gate/up, down
+    names = ["qkv", "attn", "merge_o_proj", None, "gate_up", "down"]
+    rows = {n: {"wait_us": [], "compute_us": [], "span_us": []} for n in names if n}
     prev_done = None
     for l in range(L):
         for k in range(6):
+            if names[k] is None:
+                continue
             ph = t[:, l * 6 + k, :]
             ready, done, enter = ph[:, 1], ph[:, 2], ph[:, 0]
             has = ready > 0
@@ -273,13 +277,11 @@ def run_trace():
                 rows[names[k]]["compute_us"].append(np.median(done[has] - ready[has]) / 1e3)
             if prev_done is not None:
                 rows[names[k]]["span_us"].append((done_max - prev_done) / 1e3)
-                rows[names[k]]["ring_wait_us"].append(float(np.median(ph[:, 3])) / 1e3)
             prev_done = done_max
     out = {n: {kk: round(float(np.mean(v)), 2) if v else None for kk, v in d.items()} for n, d in rows.items()}
     lm = t[:, 6 * L, :]
     out["layers_total_us"] = round(float((t[:, 6 * L - 1, 2].max() - t0) / 1e3), 1)
     out["lm_head_us"] = round(float((lm[:, 2].max() - lm[:, 0].min()) / 1e3), 1)
-    out["lm_head_ring_wait_us"] = round(float(np.median(lm[:, 3])) / 1e3, 1)
     out["step_device_ms"] = round(eng.last_device_ms(), 4)
     print(json.dumps({"trace_per_layer_mean": out,
                       "legend": "span = last CTA done minus previous phase's last CTA done; wait = median CTA inputs "

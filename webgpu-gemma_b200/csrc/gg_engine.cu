@@ -56,19 +56,18 @@ __global__ void gg_f16_to_f32_kernel(const uint16_t* __restrict__ src, float* __
   if (i < n) dst[i] = __half2float(__ushort_as_half(src[i]));
 }
 
-// Wo (H rows of the row format, K = Q) -> Q / 8 column slices for the step kernel: slice u,
-// row r = {the 8 quants of columns 8u..8u+7, the f16 scale of their block, 6 zero bytes}.
+// Wo (H rows of the row format, K = Q) -> Q / 8 column slices for the step kernel: slice u holds
+// the 8 quants of columns 8u..8u+7 of every row (row r at 8r), then the f16 scales of their block
+// (row r at 8H + 2r).
 __global__ void gg_wo_cols_kernel(const uint8_t* __restrict__ wo, int H, int Q, int rs, uint8_t* __restrict__ out) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // u * H + r
   if (i >= (long long)(Q / 8) * H) return;
   const int u = (int)(i / H), r = (int)(i % H);
   const uint8_t* row = wo + (size_t)r * rs;
-  uint32_t w[4];
-  w[0] = *reinterpret_cast<const uint32_t*>(row + 8 * u);
-  w[1] = *reinterpret_cast<const uint32_t*>(row + 8 * u + 4);
-  w[2] = *reinterpret_cast<const uint16_t*>(row + Q + 2 * ((8 * u) / 32));
-  w[3] = 0;
-  *reinterpret_cast<uint4*>(out + 16 * (size_t)i) = make_uint4(w[0], w[1], w[2], w[3]);
+  uint8_t* slice = out + (size_t)u * H * 10;
+  *reinterpret_cast<uint2*>(slice + 8 * (size_t)r) =
+      make_uint2(*reinterpret_cast<const uint32_t*>(row + 8 * u), *reinterpret_cast<const uint32_t*>(row + 8 * u + 4));
+  *reinterpret_cast<uint16_t*>(slice + 8 * (size_t)H + 2 * (size_t)r) = *reinterpret_cast<const uint16_t*>(row + Q + 2 * ((8 * u) / 32));
 }
 
 // Fixed-point accumulators (2^-32 units, two's complement u64) -> f32.
@@ -339,9 +338,10 @@ static int schedule(gg_engine* e) {
   m.dims_per_comb = 8;
   m.ncomb = m.Q / 8;
   if (m.ncomb > G) return fail(e, GG_E_ARG, "q_dim / 8 = %d attention merge units exceed the grid (%d)", m.ncomb, G);
-  // the merge units apply their 8 columns of Wo: H rows of 16 bytes, all stages resident at once
-  m.wo_rows_per_stage = SB / 16;
-  if (m.H > m.wo_rows_per_stage) return fail(e, GG_E_ARG, "hidden_size above %d: the O column slice needs one ring stage", m.wo_rows_per_stage);
+  // the merge units apply their 8 columns of Wo: H rows of 10 bytes in one ring stage
+  m.wo_rows_per_stage = SB / 10;
+  if (m.H > m.wo_rows_per_stage || m.H % 8)
+    return fail(e, GG_E_ARG, "hidden_size must be a multiple of 8 and at most %d (one ring stage of O columns)", m.wo_rows_per_stage);
   m.acc_stride = (m.H + 3) / 4 * 4;
   m.xs0 = (m.H + 63) / 64 * 64;
   m.xs1 = (std::max(m.Q, m.I) + 63) / 64 * 64;
@@ -496,7 +496,7 @@ extern "C" int gg_finalize(gg_engine* e) {
   e->wo_cols.assign(c.num_layers, nullptr);
   for (int l = 0; l < c.num_layers; l++) {
     const long long n = (long long)(m.Q / 8) * m.H;
-    GG_TRY(dalloc(e, &e->wo_cols[l], 16 * (size_t)n));
+    GG_TRY(dalloc(e, &e->wo_cols[l], 10 * (size_t)n));
     gg_wo_cols_kernel<<<(unsigned)((n + 255) / 256), 256, 0, e->stream>>>(e->wo[l], m.H, m.Q, m.rs_q, e->wo_cols[l]);
     GG_CUDA(e, cudaGetLastError());
   }

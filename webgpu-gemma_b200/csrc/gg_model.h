@@ -37,8 +37,8 @@ struct GGLayerW {
   int window;  // 0: attend the whole prefix; W: only positions pos-W+1..pos (sliding-window layer)
   const float2* rope;  // [CTX][HD/2] (cos, sin) of pos * theta^(-2i/HD) for this layer's theta
   // The O projection by column slices for the step kernel: slice u (attention dims 8u..8u+7) is
-  // H rows of 16 bytes {8 int8 quants of those columns, the f16 scale of their Q8_0 block, 6 zero
-  // bytes}, H * 16 bytes per slice.
+  // H x 8 int8 quants (row r at 8r) then the H f16 scales of their Q8_0 block (row r at 8H + 2r),
+  // H * 10 bytes per slice.
   const uint8_t* wo_cols;
 };
 
@@ -95,7 +95,7 @@ struct GGModelDev {
   unsigned long long* acc;  // [2][L][acc_stride]
   unsigned int* acc_cnt;    // [2][L][8]
   int acc_stride;           // >= H, a multiple of 4
-  int wo_rows_per_stage;    // 16-byte rows of a Wo column slice per ring stage
+  int wo_rows_per_stage;    // most rows of a Wo column slice (10 bytes each) that one ring stage holds
   // The step kernel keeps a copy of this descriptor up to layers[L - 1] in shared memory at
   // sm_model (GG_MODEL_BYTES(L) bytes), so its parameter reads never wait on L2.
   int sm_model;

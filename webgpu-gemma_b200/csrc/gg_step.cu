@@ -204,7 +204,7 @@ struct Producer {
           const size_t off = ((size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + p0) * m.KV) * es;
           issue(m.kcache + off, nb, m.vcache + off, nb, (uint32_t)(m.pos_per_split * m.KV * es));
         }
-        if (c < m.ncomb) rows(Lw.wo_cols + (size_t)c * m.H * 16, 16, 0, m.H, m.wo_rows_per_stage);
+        if (c < m.ncomb) issue(Lw.wo_cols + (size_t)c * m.H * 10, (uint32_t)(m.H * 10), nullptr, 0, 0);
         rows(Lw.wgu, m.rs_h, 2 * R[RG_I], 2 * R[RG_I + 1], m.rps_gu);
         rows(Lw.wdown, m.rs_i, R[RG_H], R[RG_H + 1], shared_rps(m.rps_i, R[RG_H + 1] - R[RG_H]));
       }
@@ -1050,14 +1050,14 @@ struct Consumer {
 #pragma unroll
     for (int j = 0; j < 8; j++) a[j] = av[j];
     unsigned long long* acc = m.acc + ((size_t)x.par * m.L + l) * m.acc_stride;
-    const uint32_t ring = smem_u32(x.S.ring);
+    const uint32_t slice = smem_u32(x.S.ring) + (idx % NS) * GG_STEP_STAGE_BYTES;
     for (int r = tid; r < m.H; r += NCT) {
-      const uint4 w = lds128(ring + (idx % NS) * GG_STEP_STAGE_BYTES + (uint32_t)r * 16u);
+      const uint2 w = lds64(slice + 8u * (uint32_t)r);
       const uint32_t q[2] = {w.x, w.y};
       float sum = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; j++) sum = fmaf((float)((int)(q[j >> 2] << (24 - 8 * (j & 3))) >> 24), a[j], sum);
-      acc_add(acc + r, sum * __half2float(__ushort_as_half((unsigned short)(w.z & 0xffffu))));
+      acc_add(acc + r, sum * lds_half(slice + 8u * (uint32_t)m.H + 2u * (uint32_t)r));
     }
     cbar();
     release_all(nst);
