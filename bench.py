@@ -358,7 +358,9 @@ def run_cfg4(args):
     cfg = shape.config()
     if args.kv_bf16:
         cfg.kv_dtype = "bf16"
-    eng = engine_from_tensors(cfg, synth.make_tensors(shape, SEED), device=local, max_seqs=CFG4_SEQS)
+    tensors = synth.make_tensors(shape, SEED)
+    wbytes = weight_bytes(tensors)
+    eng = engine_from_tensors(cfg, tensors, device=local, max_seqs=CFG4_SEQS)
     B, P, N = CFG4_SEQS, CFG4_PROMPT, min(CFG4_TOKENS, args.steps)
     seq_ids = [rank * B + i for i in range(B)]  # global stream ids (Philox streams)
     draws = np.stack([philox_uniforms(SEED, sid, N + 1) for sid in seq_ids], axis=1)  # [N+1][B]
@@ -375,11 +377,24 @@ def run_cfg4(args):
     dev_ms = eng.last_device_ms()
     value, max_ms = aggregate(dev_ms, B * N, dist, f"cuda:{local}")
     if rank == 0:
+        # bytes one step must move: the weights once for all rows, each row's embedding row and KV
+        # rows 0..pos (every row decodes at the same position here), averaged over the timed steps
+        kv_es = 2 if cfg.kv_dtype == "bf16" else 4
+        kv_pos = KV_BYTES_PER_POS * kv_es // 4
+        emb_row = cfg.hidden_size + cfg.hidden_size // 16
+        algo = wbytes + B * emb_row + B * kv_pos * (P + (N - 1) / 2 + 1)
+        peak, peak_kind = measured_peaks()
+        achieved = algo / (max_ms / N / 1000.0) / 1e9
         print(json.dumps({"cfg4": "1B, 64 sequences per GPU, 256-token prompts, 256 sampled tokens (T 0.7, top-p 0.9, rep 1.2)",
                           "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "seqs_per_gpu": B,
                           "tokens_per_seq": N, "ms_per_step": round(max_ms / N, 4), "scaling": "weak",
                           "kv_cache": cfg.kv_dtype,
                           "parallelism": f"dp{world} (independent engines)",
+                          "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                                       "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                                       "algo_bytes_per_step": int(algo),
+                                       "algo": "Q8_0 weights once + per row: embedding row and KV rows 0..pos, "
+                                               "mean over the timed positions"},
                           "first_tokens": [int(t) for t in toks[0, :4]]}))
     eng.close()
     if dist is not None:
