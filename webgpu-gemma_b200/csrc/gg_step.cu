@@ -185,6 +185,7 @@ struct Producer {
     if (b0) bulk_g2s(dst, s0, b0, &x.S.full[slot], pol);
     if (b1) bulk_g2s(dst + off1, s1, b1, &x.S.full[slot], pol);
     idx++;
+    *(volatile uint32_t*)(x.S.flag + 1) = idx;  // stages issued so far (read by the LM head's owners)
   }
   GG_DEV void rows(const uint8_t* W, int rs, int rb, int re, int rps) {
     for (int r = rb; r < re && ok; r += rps) issue(W + (size_t)r * rs, (uint32_t)(min(rps, re - r) * rs), nullptr, 0, 0);
@@ -727,18 +728,41 @@ struct Consumer {
   template <class Epi>
   GG_DEV void matvec_pairs(const XPlanes& P, int npairs, int rps, int K, int rs, bool gated, Epi epi) {
     const int pps = rps >> 1, g = lane >> 3;
-    int unit = 0;
-    for (int j0 = 0, k = 0; j0 < npairs; j0 += pps, k++) {
-      const uint8_t* stg = gated ? x.S.ring + (size_t)((idx + (uint32_t)k) % NS) * GG_STEP_STAGE_BYTES : stage_wait();
+    int unit = 0, k = 0;
+    for (int j0 = 0; j0 < npairs; j0 += pps, k++) {
       const int j1 = min(j0 + pps, npairs);
-      for (int u = j0; u < j1; u += 4, unit++) {
-        if (unit % NCW != warp) continue;
-        const int j = u + g;
+      const int nu = (j1 - j0 + 3) >> 2;  // units in this stage (one per warp: NCW > 1)
+      const int mine = (warp - unit % NCW + NCW) % NCW;  // which of this stage's units is this warp's
+      if (mine < nu) {
+        const uint8_t* stg = gated ? x.S.ring + (size_t)((idx + (uint32_t)k) % NS) * GG_STEP_STAGE_BYTES : owner_wait(k);
+        const int j = j0 + 4 * mine + g;
         const float2 v = dot_pair8(smem_u32(stg) + (uint32_t)(2 * (min(j, j1 - 1) - j0) * rs), rs, K, P);
         if ((lane & 7) == 0 && j < j1) epi(j, v.x, v.y);
+        if (!gated) {  // the stage's owners release it: NCW arrivals in all, the first owner giving the rest
+          __syncwarp();
+          if (lane == 0 && !dead && !*(volatile uint32_t*)x.sc.err)
+            mbar_arrive_cnt(&x.S.empty[(idx + (uint32_t)k) % NS], mine == 0 ? (uint32_t)(NCW - nu + 1) : 1u);
+        }
       }
-      if (!gated) stage_done();
+      unit += nu;
     }
+    if (!gated) idx += (uint32_t)k;
+  }
+
+  // Streamed stage k places after the ring position, waited for only by the warps that compute
+  // on it: first until the producer has issued it (so the slot's previous use was released and
+  // the parity wait below cannot match it), then for its copy. Bounded.
+  GG_DEV const uint8_t* owner_wait(int k) {
+    const uint32_t want = idx + (uint32_t)k + 1u;
+    SpinClock clk;
+#pragma unroll 1
+    while ((int)(*(volatile uint32_t*)(x.S.flag + 1) - want) < 0) {
+      if (__any_sync(0xffffffffu, clk.expired(x.sc))) {
+        dead = true;
+        break;
+      }
+    }
+    return stage_wait_ahead(k);
   }
 
   GG_DEV void phase_qkv(int l) {
@@ -1224,6 +1248,7 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
   x.S.flag = reinterpret_cast<int*>(smem + m.sm_flag);
   x.S.rows = reinterpret_cast<int*>(smem + m.sm_rows);
 
+  x.S.flag[1] = 0;  // stages issued by the producer
   const bool bad = x.token < 0 || x.token >= m.V || x.pos < 0 || x.pos >= m.CTX || x.seq < 0 || x.seq >= m.max_seqs;
   if (bad) {
     if (blockIdx.x == 0) atomicOr(&st->error, GG_ERR_BAD_INPUT);
