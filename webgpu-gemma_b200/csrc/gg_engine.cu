@@ -111,6 +111,10 @@ struct gg_engine {
   GGModelDev* d_md = nullptr;
   GGState* d_st = nullptr;
   GGState* h_st = nullptr;  // pinned
+  // gg_step as one CUDA graph (state in, the token kernel between two events, state out), captured
+  // at the first call: one launch call per token instead of five stream operations.
+  cudaGraphExec_t step_exec = nullptr;
+  int step_graph = 0;  // 0 not tried, 1 ready, -1 unavailable (direct launches)
   std::vector<void*> allocs;
   // weights
   std::vector<uint8_t*> wqkv, wo, wgu, wdown;
@@ -632,11 +636,19 @@ static int launch(gg_engine* e) {
 }
 
 // Read back error/out_token, synchronise, and turn device error bits into a status.
+static int finish_synced(gg_engine* e, int32_t* out_token);
 static int finish(gg_engine* e, int32_t* out_token) {
   GG_CUDA(e, cudaMemcpyAsync(&e->h_st->epoch, &e->d_st->epoch, sizeof(GGState) - offsetof(GGState, epoch),
                              cudaMemcpyDeviceToHost, e->stream));
   GG_CUDA(e, cudaStreamSynchronize(e->stream));
-  cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+  return finish_synced(e, out_token);
+}
+// After the stream has drained the launch and the state copy back: timing, error bits, token.
+static int finish_synced(gg_engine* e, int32_t* out_token) {
+  if (cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1) != cudaSuccess) {
+    e->last_ms = 0.f;
+    cudaGetLastError();  // no pending error left for a later call to pick up
+  }
   uint32_t err = e->h_st->error;
   if (err) {
     cudaMemsetAsync(&e->d_st->error, 0, 4, e->stream);
@@ -902,11 +914,36 @@ extern "C" int gg_step(gg_engine* e, int seq, int32_t token, int pos, const gg_s
   s.token = token;
   s.pos = pos;
   set_sampling(s, sp, uniform);
-  GG_TRY(put_inputs(e, s));
-  GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
-  GG_TRY(launch(e));
-  GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
-  GG_TRY(finish(e, out_token));
+  if (e->step_graph == 0) {  // capture the per-token sequence once; any failure keeps direct launches
+    e->step_graph = -1;
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+      bool ok = cudaMemcpyAsync(e->d_st, e->h_st, offsetof(GGState, epoch), cudaMemcpyHostToDevice, e->stream) == cudaSuccess;
+      // (external event records: plain records in a capture only order the capture, they record nothing)
+      ok = ok && cudaEventRecordWithFlags(e->ev0, e->stream, cudaEventRecordExternal) == cudaSuccess;
+      ok = ok && launch(e) == GG_OK;
+      ok = ok && cudaEventRecordWithFlags(e->ev1, e->stream, cudaEventRecordExternal) == cudaSuccess;
+      ok = ok && cudaMemcpyAsync(&e->h_st->epoch, &e->d_st->epoch, sizeof(GGState) - offsetof(GGState, epoch),
+                                 cudaMemcpyDeviceToHost, e->stream) == cudaSuccess;
+      const bool ended = cudaStreamEndCapture(e->stream, &g) == cudaSuccess;
+      if (ok && ended && g && cudaGraphInstantiate(&e->step_exec, g, 0) == cudaSuccess) e->step_graph = 1;
+      if (g) cudaGraphDestroy(g);
+    }
+    cudaGetLastError();  // a capture that failed leaves no error behind
+    e->err.clear();
+  }
+  *e->h_st = s;
+  if (e->step_graph == 1) {
+    GG_CUDA(e, cudaGraphLaunch(e->step_exec, e->stream));
+    GG_CUDA(e, cudaStreamSynchronize(e->stream));
+    GG_TRY(finish_synced(e, out_token));
+  } else {
+    GG_TRY(put_inputs(e, s));
+    GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
+    GG_TRY(launch(e));
+    GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
+    GG_TRY(finish(e, out_token));
+  }
   e->last_hidden_seq = seq;
   return GG_OK;
 }
@@ -1265,6 +1302,7 @@ extern "C" int gg_destroy(gg_engine* e) {
   if (e->d_unif) cudaFree(e->d_unif);
   if (e->d_ring) cudaFree(e->d_ring);
   if (e->h_ring) cudaFreeHost(e->h_ring);
+  if (e->step_exec) cudaGraphExecDestroy(e->step_exec);
   if (e->h_st) cudaFreeHost(e->h_st);
   if (e->bd_unif) cudaFree(e->bd_unif);
   if (e->bd_out) cudaFree(e->bd_out);
