@@ -23,12 +23,14 @@
 #include "gg_prefill.h"
 
 namespace gg {
-extern "C" __global__ void gg_step_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
-extern "C" __global__ void gg_step_kernel_kv16(const GGModelDev* __restrict__ mp, GGState* __restrict__ st);
+extern "C" __global__ void gg_step_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st, const GGState in,
+                                          int use_in, GGState* host_st);
+extern "C" __global__ void gg_step_kernel_kv16(const GGModelDev* __restrict__ mp, GGState* __restrict__ st,
+                                               const GGState in, int use_in, GGState* host_st);
 }
 
 // The persistent step kernel built for the engine's KV element type.
-using DecodeFn = void (*)(const GGModelDev*, GGState*);
+using DecodeFn = void (*)(const GGModelDev*, GGState*, const GGState, int, GGState*);
 static DecodeFn decode_fn(const GGModelDev& m) { return m.kv_es == 2 ? gg::gg_step_kernel_kv16 : gg::gg_step_kernel; }
 constexpr int GG_STEP_THREADS = (GG_STEP_NCW + 1) * 32;
 
@@ -111,10 +113,6 @@ struct gg_engine {
   GGModelDev* d_md = nullptr;
   GGState* d_st = nullptr;
   GGState* h_st = nullptr;  // pinned
-  // gg_step as one CUDA graph (state in, the token kernel between two events, state out), captured
-  // at the first call: one launch call per token instead of five stream operations.
-  cudaGraphExec_t step_exec = nullptr;
-  int step_graph = 0;  // 0 not tried, 1 ready, -1 unavailable (direct launches)
   std::vector<void*> allocs;
   // weights
   std::vector<uint8_t*> wqkv, wo, wgu, wdown;
@@ -587,7 +585,7 @@ extern "C" int gg_finalize(gg_engine* e) {
   GG_TRY(dalloc(e, &m.trace, 8 * (size_t)m.grid * GG_TRACE_PHASES * 4));
   GG_TRY(dalloc(e, &e->d_md, sizeof(GGModelDev)));
   GG_TRY(dalloc(e, &e->d_st, sizeof(GGState)));
-  GG_CUDA(e, cudaMallocHost(&e->h_st, sizeof(GGState)));
+  GG_CUDA(e, cudaHostAlloc(&e->h_st, sizeof(GGState), cudaHostAllocMapped));  // gg_step's kernel writes its tail here
   memset(e->h_st, 0, sizeof(GGState));
   GG_CUDA(e, cudaMemcpyAsync(e->d_md, &m, sizeof(GGModelDev), cudaMemcpyHostToDevice, e->stream));
   GGState s0{};
@@ -620,7 +618,9 @@ static int put_inputs(gg_engine* e, const GGState& in) {
   return GG_OK;
 }
 
-static int launch(gg_engine* e) {
+// One token-kernel launch. in != nullptr: the host inputs travel as a launch parameter and the
+// last CTA writes the device-owned tail into the mapped pinned state (no copies either way).
+static int launch(gg_engine* e, const GGState* in = nullptr) {
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(e->md.grid);
   lc.blockDim = dim3(GG_STEP_THREADS);
@@ -631,7 +631,9 @@ static int launch(gg_engine* e) {
   at[0].val.cooperative = 1;
   lc.attrs = at;
   lc.numAttrs = 1;
-  GG_CUDA(e, cudaLaunchKernelEx(&lc, decode_fn(e->md), (const GGModelDev*)e->d_md, e->d_st));
+  const GGState in_v = in ? *in : GGState{};
+  GG_CUDA(e, cudaLaunchKernelEx(&lc, decode_fn(e->md), (const GGModelDev*)e->d_md, e->d_st, in_v, in ? 1 : 0,
+                                in ? e->h_st : (GGState*)nullptr));
   return GG_OK;
 }
 
@@ -914,36 +916,13 @@ extern "C" int gg_step(gg_engine* e, int seq, int32_t token, int pos, const gg_s
   s.token = token;
   s.pos = pos;
   set_sampling(s, sp, uniform);
-  if (e->step_graph == 0) {  // capture the per-token sequence once; any failure keeps direct launches
-    e->step_graph = -1;
-    cudaGraph_t g = nullptr;
-    if (cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
-      bool ok = cudaMemcpyAsync(e->d_st, e->h_st, offsetof(GGState, epoch), cudaMemcpyHostToDevice, e->stream) == cudaSuccess;
-      // (external event records: plain records in a capture only order the capture, they record nothing)
-      ok = ok && cudaEventRecordWithFlags(e->ev0, e->stream, cudaEventRecordExternal) == cudaSuccess;
-      ok = ok && launch(e) == GG_OK;
-      ok = ok && cudaEventRecordWithFlags(e->ev1, e->stream, cudaEventRecordExternal) == cudaSuccess;
-      ok = ok && cudaMemcpyAsync(&e->h_st->epoch, &e->d_st->epoch, sizeof(GGState) - offsetof(GGState, epoch),
-                                 cudaMemcpyDeviceToHost, e->stream) == cudaSuccess;
-      const bool ended = cudaStreamEndCapture(e->stream, &g) == cudaSuccess;
-      if (ok && ended && g && cudaGraphInstantiate(&e->step_exec, g, 0) == cudaSuccess) e->step_graph = 1;
-      if (g) cudaGraphDestroy(g);
-    }
-    cudaGetLastError();  // a capture that failed leaves no error behind
-    e->err.clear();
-  }
-  *e->h_st = s;
-  if (e->step_graph == 1) {
-    GG_CUDA(e, cudaGraphLaunch(e->step_exec, e->stream));
-    GG_CUDA(e, cudaStreamSynchronize(e->stream));
-    GG_TRY(finish_synced(e, out_token));
-  } else {
-    GG_TRY(put_inputs(e, s));
-    GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
-    GG_TRY(launch(e));
-    GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
-    GG_TRY(finish(e, out_token));
-  }
+  // inputs as a launch parameter, the result written by the kernel into the mapped pinned state:
+  // the only host <-> device traffic is the launch and those writes
+  GG_CUDA(e, cudaEventRecord(e->ev0, e->stream));
+  GG_TRY(launch(e, &s));
+  GG_CUDA(e, cudaEventRecord(e->ev1, e->stream));
+  GG_CUDA(e, cudaStreamSynchronize(e->stream));
+  GG_TRY(finish_synced(e, out_token));
   e->last_hidden_seq = seq;
   return GG_OK;
 }
@@ -1302,7 +1281,6 @@ extern "C" int gg_destroy(gg_engine* e) {
   if (e->d_unif) cudaFree(e->d_unif);
   if (e->d_ring) cudaFree(e->d_ring);
   if (e->h_ring) cudaFreeHost(e->h_ring);
-  if (e->step_exec) cudaGraphExecDestroy(e->step_exec);
   if (e->h_st) cudaFreeHost(e->h_st);
   if (e->bd_unif) cudaFree(e->bd_unif);
   if (e->bd_out) cudaFree(e->bd_out);

@@ -1202,7 +1202,8 @@ struct Consumer {
 // ---------------------------------------------------------------------------------- kernel
 
 template <bool KV16>
-GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
+GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ st, const GGState& in, int use_in,
+                      GGState* host_st) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ Ctx x;
   const GGModelDev& m = *mp;
@@ -1218,14 +1219,15 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
   if (threadIdx.x == 0) {
   x.m = msm;
   x.st = st;
-  x.mode = st->mode;
-  x.token = st->token;
-  x.pos = st->pos;
-  x.seq = st->seq;
+  // host inputs from the launch's parameters (gg_step) or from the device state (chained launches)
+  x.mode = use_in ? in.mode : st->mode;
+  x.token = use_in ? in.token : st->token;
+  x.pos = use_in ? in.pos : st->pos;
+  x.seq = use_in ? in.seq : st->seq;
   x.tagbase = st->epoch;
   x.par = st->parity & 1u;
   x.sc.err = &st->error;
-  x.sc.timeout_ns = st->timeout_ns;
+  x.sc.timeout_ns = use_in ? in.timeout_ns : st->timeout_ns;
   // carve shared memory (offsets and GGModelDev::smem_bytes computed by the host)
   x.S.ring = smem;
   x.S.full = reinterpret_cast<uint64_t*>(smem + (size_t)NS * GG_STEP_STAGE_BYTES);
@@ -1304,6 +1306,24 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
   __syncthreads();
   if (!*x.S.flag) return;
   __threadfence();
+  if (use_in && threadIdx.x == 0) {  // the launch's inputs become the device state (sampler, chains)
+    st->token = in.token;
+    st->pos = in.pos;
+    st->seq = in.seq;
+    st->mode = in.mode;
+    st->temperature = in.temperature;
+    st->top_p = in.top_p;
+    st->rep_penalty = in.rep_penalty;
+    st->step_index = in.step_index;
+    st->uniform = in.uniform;
+    st->uniforms = in.uniforms;
+    st->timeout_ns = in.timeout_ns;
+    st->prefill_ids = in.prefill_ids;
+    st->prefill_left = in.prefill_left;
+    st->ring_len = in.ring_len;
+    st->token_ring = in.token_ring;
+  }
+  __syncthreads();
   int tok = -1;
   if (x.mode & GG_RUN_SAMPLE) tok = sample_token(m, st, *reinterpret_cast<SampleScratch*>(smem));  // ring is idle
   __syncthreads();
@@ -1333,20 +1353,32 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
       }
       st->pos = x.pos + 1;
     }
+    if (host_st) {  // the device-owned tail straight into the caller's mapped pinned state
+      volatile GGState* h = host_st;
+      h->epoch = st->epoch;
+      h->done = 0;
+      h->error = *(volatile uint32_t*)&st->error;
+      h->out_token = st->out_token;
+      h->seen_count = st->seen_count;
+      h->parity = st->parity;
+      __threadfence_system();
+    }
   }
 }
 
 }  // namespace step
 
 extern "C" __global__ void __launch_bounds__(step::NTH, 1)
-    gg_step_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
-  step::step_body<false>(mp, st);
+    gg_step_kernel(const GGModelDev* __restrict__ mp, GGState* __restrict__ st, const GGState in, int use_in,
+                   GGState* host_st) {
+  step::step_body<false>(mp, st, in, use_in, host_st);
 }
 
 // The same kernel for a bf16 KV cache (GG_FLAG_KV_BF16).
 extern "C" __global__ void __launch_bounds__(step::NTH, 1)
-    gg_step_kernel_kv16(const GGModelDev* __restrict__ mp, GGState* __restrict__ st) {
-  step::step_body<true>(mp, st);
+    gg_step_kernel_kv16(const GGModelDev* __restrict__ mp, GGState* __restrict__ st, const GGState in, int use_in,
+                        GGState* host_st) {
+  step::step_body<true>(mp, st, in, use_in, host_st);
 }
 
 }  // namespace gg

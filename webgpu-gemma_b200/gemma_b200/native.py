@@ -16,11 +16,12 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgemma_b2
 
 GG_OK, GG_E_ARG, GG_E_CUDA, GG_E_STATE, GG_E_DEVICE, GG_E_NOMEM = 0, -1, -2, -3, -4, -5
 
-# Bytes a gg_step call moves: the host-written prefix of GGState (token, pos, sampling options,
-# ... up to `epoch`, csrc/gg_model.h) host->device, and its device-owned tail (out_token,
-# error, ...) device->host.
-STATE_H2D_BYTES = 96
-STATE_D2H_BYTES = 32
+# Bytes a gg_step call moves: host->device, the launch's parameters (a whole GGState of 128 B
+# carrying the token, position and sampling options, a flag and two pointers); device->host, the
+# kernel's writes of GGState's device-owned tail into the mapped pinned state (epoch, ticket,
+# error bits, sampled token, seen count, parity: 24 B).
+STATE_H2D_BYTES = 128 + 4 + 8 + 8
+STATE_D2H_BYTES = 24
 
 # Every symbol the header declares, with (restype, argtypes).
 _P, _I, _D = ctypes.c_void_p, ctypes.c_int, ctypes.c_double
