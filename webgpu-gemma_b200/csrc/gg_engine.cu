@@ -767,9 +767,8 @@ static int batch_step(gg_engine* e, int B, int max_pos, const double* d_unif, in
     int sp = pick_splits(gemm_tiles(B, QKV), m.H / 64, gemm_slots(e, B));
     long long plane = (long long)B * QKV;
     GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, B, e->pf_y, QKV, sp, plane, err, to, s));
-    GG_CUDA(e, bd_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, B, e->bd_pos, e->bd_seq,
-                                m.kv_seq_stride, m.NQH, m.NKH, m.HD, m.eps, e->pf_q, kc, vc, m.kv_es == 2, s));
-    GG_CUDA(e, bd_attention(e->pf_q, kc, vc, m.kv_es == 2, B, e->bd_pos, e->bd_seq, m.kv_seq_stride, max_pos, m.NQH, m.NKH, m.HD,
+    GG_CUDA(e, bd_attention(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, m.eps, kc, vc, m.kv_es == 2, B, e->bd_pos,
+                            e->bd_seq, m.kv_seq_stride, max_pos, m.NQH, m.NKH, m.HD,
                             m.attn_scale, w.window, e->bd_att, thi, tlo, s));
     sp = pick_splits(gemm_tiles(B, m.H), m.Q / 64, gemm_slots(e, B));
     plane = (long long)B * m.H;

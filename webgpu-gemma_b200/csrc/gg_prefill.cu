@@ -618,16 +618,58 @@ GG_DEV void kv_load8(const kv_t<KV16>* p, float* f) {
   }
 }
 
+// The q/k work of pf_qk_kernel for one head of batch row b (warp-wide): the head's elements of
+// every split plane of the q/k/v GEMM summed in plane order, RMSNorm with weights nw, RoPE at pos.
+// Lane l holds elements l + 32 j.
+GG_DEV void bd_head_norm_rope(const float* __restrict__ qkv, int splits, long long plane, long long ob,
+                              const float* __restrict__ nw, const float2* __restrict__ rope, int pos, float eps, float* v) {
+  constexpr int NJ = PF_HD / 32;
+  const int lane = threadIdx.x & 31;
+  float nwv[NJ];
+  float2 cr[NJ / 2];
+#pragma unroll
+  for (int j = 0; j < NJ; j++) nwv[j] = __ldg(nw + lane + 32 * j);
+#pragma unroll
+  for (int j = 0; j < NJ / 2; j++) cr[j] = rope[(size_t)pos * (PF_HD / 2) + lane + 32 * j];
+#pragma unroll
+  for (int j = 0; j < NJ; j++) v[j] = qkv[ob + lane + 32 * j];
+  for (int z = 1; z < splits; z++)
+#pragma unroll
+    for (int j = 0; j < NJ; j++) v[j] += qkv[(long long)z * plane + ob + lane + 32 * j];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NJ; j++) ss += v[j] * v[j];
+  const float rms = sqrtf(warp_sum(ss) / (float)PF_HD + eps);
+#pragma unroll
+  for (int j = 0; j < NJ; j++) v[j] = v[j] * nwv[j] / rms;
+#pragma unroll
+  for (int j = 0; j < NJ / 2; j++) {
+    const float cs = cr[j].x, sn = cr[j].y;
+    const float x0 = v[j], x1 = v[j + NJ / 2];
+    v[j] = x0 * cs - x1 * sn;
+    v[j + NJ / 2] = x0 * sn + x1 * cs;
+  }
+}
+
+// Fused with the q/k step (shaders.ts:420-467, 209-227): every CTA of row b builds the row's
+// normed, rotated q in shared memory from the q/k/v GEMM's split planes, and the CTA whose range
+// holds position pos also computes the new k and v, stores them in the cache and keeps them in
+// shared memory for its own key pos (the cache loads below take the read-only path, which does
+// not see this launch's stores).
 template <bool KV16>
 __global__ void __launch_bounds__(BD_WARPS * 32)
-    bd_attn_part_kernel(const float* __restrict__ q, const kv_t<KV16>* __restrict__ kc,
-                        const kv_t<KV16>* __restrict__ vc, const int32_t* __restrict__ pos_arr,
+    bd_attn_part_kernel(const float* __restrict__ qkv, int splits, long long plane, const float* __restrict__ q_norm,
+                        const float* __restrict__ k_norm, const float2* __restrict__ rope, float eps,
+                        kv_t<KV16>* __restrict__ kc, kv_t<KV16>* __restrict__ vc, const int32_t* __restrict__ pos_arr,
                         const int32_t* __restrict__ seq_arr, size_t seq_stride, float scale, int window, int maxc,
                         float* __restrict__ part) {
   pdl_trigger();
   pdl_wait();  // before touching any buffer shared with the other kernels of the chain
+  static_assert(BD_WARPS == BD_NH, "one warp per query head builds q");
   __shared__ float sm_m[BD_WARPS][BD_NH], sm_l[BD_WARPS][BD_NH];
   __shared__ __align__(16) float sm_o[BD_WARPS][BD_NH][PF_HD];
+  __shared__ __align__(16) float sm_q[BD_NH][PF_HD];
+  __shared__ __align__(16) float sm_kv[2][PF_HD];  // the new position's k and v (as the cache holds them)
   const int c = blockIdx.x, b = blockIdx.y;
   const int pos = pos_arr[b];
   const int k_begin = c * BD_KC;
@@ -635,13 +677,42 @@ __global__ void __launch_bounds__(BD_WARPS * 32)
   const int k_end = min(k_begin + BD_KC, pos + 1);
   const int klo = window > 0 ? max(0, pos + 1 - window) : 0;  // sliding window
   if (k_end <= klo) return;
-  const kv_t<KV16>* kb = kc + (size_t)seq_arr[b] * seq_stride + 8 * (threadIdx.x & 31);
-  const kv_t<KV16>* vb = vc + (size_t)seq_arr[b] * seq_stride + 8 * (threadIdx.x & 31);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int W = BD_NH * PF_HD + 2 * PF_HD;  // one row of the q/k/v GEMM output (NKH = 1)
+  const long long rb = (long long)b * W;
+  const bool owner = k_end == pos + 1;  // this range holds the new position
+  {
+    float v[PF_HD / 32];
+    bd_head_norm_rope(qkv, splits, plane, rb + warp * PF_HD, q_norm, rope, pos, eps, v);
+#pragma unroll
+    for (int j = 0; j < PF_HD / 32; j++) sm_q[warp][lane + 32 * j] = v[j];
+    if (owner) {
+      kv_t<KV16>* krow = kc + (size_t)seq_arr[b] * seq_stride + (size_t)pos * PF_HD;
+      kv_t<KV16>* vrow = vc + (size_t)seq_arr[b] * seq_stride + (size_t)pos * PF_HD;
+      if (warp == 0) {
+        bd_head_norm_rope(qkv, splits, plane, rb + BD_NH * PF_HD, k_norm, rope, pos, eps, v);
+#pragma unroll
+        for (int j = 0; j < PF_HD / 32; j++) {
+          const kv_t<KV16> kk = kv_narrow<KV16>(v[j]);
+          krow[lane + 32 * j] = kk;
+          sm_kv[0][lane + 32 * j] = kv_widen(kk);
+        }
+      } else {
+        for (int i = threadIdx.x - 32; i < PF_HD; i += (BD_WARPS - 1) * 32) {
+          const kv_t<KV16> vv = kv_narrow<KV16>(sum_planes(qkv, splits, plane, rb + BD_NH * PF_HD + PF_HD + i));
+          vrow[i] = vv;
+          sm_kv[1][i] = kv_widen(vv);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const kv_t<KV16>* kb = kc + (size_t)seq_arr[b] * seq_stride + 8 * lane;
+  const kv_t<KV16>* vb = vc + (size_t)seq_arr[b] * seq_stride + 8 * lane;
   float qv[BD_NH][8];
 #pragma unroll
   for (int h = 0; h < BD_NH; h++) {
-    const float4* qp = reinterpret_cast<const float4*>(q + ((size_t)b * BD_NH + h) * PF_HD + 8 * lane);
+    const float4* qp = reinterpret_cast<const float4*>(&sm_q[h][8 * lane]);
     const float4 a = qp[0], bq = qp[1];
     qv[h][0] = a.x; qv[h][1] = a.y; qv[h][2] = a.z; qv[h][3] = a.w;
     qv[h][4] = bq.x; qv[h][5] = bq.y; qv[h][6] = bq.z; qv[h][7] = bq.w;
@@ -659,7 +730,15 @@ __global__ void __launch_bounds__(BD_WARPS * 32)
     float kf[BD_KB][8], vf[BD_KB][8];
 #pragma unroll
     for (int k = 0; k < BD_KB; k++) {
-      if (j0 + k < w1) {
+      if (j0 + k == pos) {  // the new position: from shared memory
+        const float4* kp = reinterpret_cast<const float4*>(&sm_kv[0][8 * lane]);
+        const float4* vp = reinterpret_cast<const float4*>(&sm_kv[1][8 * lane]);
+        const float4 k0 = kp[0], k1 = kp[1], v0 = vp[0], v1 = vp[1];
+        kf[k][0] = k0.x; kf[k][1] = k0.y; kf[k][2] = k0.z; kf[k][3] = k0.w;
+        kf[k][4] = k1.x; kf[k][5] = k1.y; kf[k][6] = k1.z; kf[k][7] = k1.w;
+        vf[k][0] = v0.x; vf[k][1] = v0.y; vf[k][2] = v0.z; vf[k][3] = v0.w;
+        vf[k][4] = v1.x; vf[k][5] = v1.y; vf[k][6] = v1.z; vf[k][7] = v1.w;
+      } else if (j0 + k < w1) {
         kv_load8<KV16>(kb + (size_t)(j0 + k) * PF_HD, kf[k]);
         kv_load8<KV16>(vb + (size_t)(j0 + k) * PF_HD, vf[k]);
       } else {
@@ -868,18 +947,6 @@ cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, con
                     rope, p0, NQH, NKH, eps, q_out, (float*)kc, (float*)vc, nullptr, nullptr, (size_t)0);
 }
 
-cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm, const float* k_norm,
-                             const float2* rope, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
-                             int NKH, int HD, float eps, float* q_out, void* kc, void* vc, bool kv16,
-                             cudaStream_t s) {
-  if (B <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
-  if (kv16)
-    return launch_pdl(pf_qk_kernel<true, true>, dim3(B), dim3(PF_THREADS), 0, s, part, splits, plane, q_norm, k_norm,
-                      rope, 0, NQH, NKH, eps, q_out, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, pos, seqs, seq_stride);
-  return launch_pdl(pf_qk_kernel<true, false>, dim3(B), dim3(PF_THREADS), 0, s, part, splits, plane, q_norm, k_norm,
-                    rope, 0, NQH, NKH, eps, q_out, (float*)kc, (float*)vc, pos, seqs, seq_stride);
-}
-
 size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH) {
   const int G = NQH / NKH, QT = PA_ROWS / G;
   const size_t nb = (size_t)(max_tokens + QT - 1) / QT, maxc = (size_t)(ctx + PA_KC - 1) / PA_KC;
@@ -938,7 +1005,8 @@ size_t bd_attention_part_floats(int max_rows, int ctx) {
   return (size_t)max_rows * ((ctx + BD_KC - 1) / BD_KC) * BD_PART;
 }
 
-cudaError_t bd_attention(const float* q, const void* kc, const void* vc, bool kv16, int B, const int32_t* pos,
+cudaError_t bd_attention(const float* qkv, int splits, long long plane, const float* q_norm, const float* k_norm,
+                         const float2* rope, float eps, void* kc, void* vc, bool kv16, int B, const int32_t* pos,
                          const int32_t* seqs, size_t seq_stride, int max_pos, int NQH, int NKH, int HD, float scale,
                          int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
   if (B <= 0 || HD != PF_HD || NQH != BD_NH || NKH != 1) return cudaErrorInvalidValue;
@@ -946,11 +1014,11 @@ cudaError_t bd_attention(const float* q, const void* kc, const void* vc, bool kv
   if (maxc > 32) return cudaErrorInvalidValue;  // merge weights hold 32 key ranges (2048 positions)
   cudaError_t r;
   if (kv16)
-    r = launch_pdl(bd_attn_part_kernel<true>, dim3(maxc, B), dim3(BD_WARPS * 32), 0, s, q, (const __nv_bfloat16*)kc,
-                   (const __nv_bfloat16*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
+    r = launch_pdl(bd_attn_part_kernel<true>, dim3(maxc, B), dim3(BD_WARPS * 32), 0, s, qkv, splits, plane, q_norm, k_norm,
+                   rope, eps, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
   else
-    r = launch_pdl(bd_attn_part_kernel<false>, dim3(maxc, B), dim3(BD_WARPS * 32), 0, s, q, (const float*)kc,
-                   (const float*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
+    r = launch_pdl(bd_attn_part_kernel<false>, dim3(maxc, B), dim3(BD_WARPS * 32), 0, s, qkv, splits, plane, q_norm,
+                   k_norm, rope, eps, (float*)kc, (float*)vc, pos, seqs, seq_stride, scale, window, maxc, part);
   if (r != cudaSuccess) return r;
   return launch_pdl(bd_attn_merge_kernel, dim3(B), dim3(PF_THREADS), 0, s, (const float*)part, pos, window, maxc, thi,
                     tlo);

@@ -51,17 +51,13 @@ cudaError_t pf_geglu(const float* gu, int splits, long long plane, int T, int I,
 
 // ---- batched decode: row b is one token of the sequence in KV slot seqs[b] at position pos[b]
 
-// As pf_qk_rope_store, per row: kc/vc point at this layer's rows of slot 0, slots seq_stride
-// elements apart.
-cudaError_t bd_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm, const float* k_norm,
-                             const float2* rope, int B, const int32_t* pos, const int32_t* seqs, size_t seq_stride, int NQH,
-                             int NKH, int HD, float eps, float* q_out, void* kc, void* vc, bool kv16,
-                             cudaStream_t s);
-
 // Attention of each row's query over its slot's cache rows 0..pos[b] (4 query heads sharing one
-// KV head), written as activation tiles. max_pos >= every pos[b]; `part` holds
+// KV head), written as activation tiles, with the q/k step fused in: q is normed and rotated from
+// the q/k/v GEMM's split planes (qkv, splits, plane), and the new k and v are stored at pos[b]
+// (kc/vc: this layer's rows of slot 0). max_pos >= every pos[b]; `part` holds
 // bd_attention_part_floats(B, ctx) floats.
 size_t bd_attention_part_floats(int max_rows, int ctx);
-cudaError_t bd_attention(const float* q, const void* kc, const void* vc, bool kv16, int B, const int32_t* pos,
+cudaError_t bd_attention(const float* qkv, int splits, long long plane, const float* q_norm, const float* k_norm,
+                         const float2* rope, float eps, void* kc, void* vc, bool kv16, int B, const int32_t* pos,
                          const int32_t* seqs, size_t seq_stride, int max_pos, int NQH, int NKH, int HD, float scale,
                          int window, float* part, uint8_t* thi, uint8_t* tlo, cudaStream_t s);
