@@ -90,10 +90,11 @@ struct GGModelDev {
   // O / down plane buffer when they fit: none of the three is live while another is.
   int sm_xa, sm_xb, sm_hid, sm_res, sm_tmp, sm_lmv, sm_scal, sm_red, sm_flag, sm_rows;
   // K-split reductions of the step kernel (the O projection: every merge unit adds its 8 columns'
-  // products): per launch parity and layer, acc_stride accumulators in 2^-32 fixed point (u64,
-  // exact and order-independent) and one arrival counter (8 words apart).
+  // products): per launch parity and layer, acc_stride u64 accumulators holding the sum of the
+  // 2^-24 fixed-point partials shifted left by 8 plus, in the low byte, the number of
+  // contributions (exact and order-independent; a reader waits for the full count).
   unsigned long long* acc;  // [2][L][acc_stride]
-  unsigned int* acc_cnt;    // [2][L][8]
+  unsigned int* acc_cnt;    // [2][L][8] (zeroed with the accumulators; unused by the kernel)
   int acc_stride;           // >= H, a multiple of 4
   int wo_rows_per_stage;    // most rows of a Wo column slice (10 bytes each) that one ring stage holds
   // The step kernel keeps a copy of this descriptor up to layers[L - 1] in shared memory at

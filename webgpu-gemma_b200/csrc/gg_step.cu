@@ -260,18 +260,18 @@ GG_DEV void quad_vals(const uint64_t (&w)[4], float* v) {
   for (int j = 0; j < 4; j++) v[j] = __uint_as_float((uint32_t)w[j]);
 }
 
-// K-split reductions: an f32 partial added into a u64 accumulator in 2^-32 fixed point. Integer
-// addition is exact and associative, so the sum is the same whatever order the CTAs arrive in.
+// K-split reductions: an f32 partial added into a u64 accumulator as (round(v * 2^24) << 8) + 1:
+// the high 56 bits sum the 2^-24 fixed-point partials and the low byte counts the contributions
+// (at most 255 adders). Integer addition is exact and associative, so the sum is the same whatever
+// order the CTAs arrive in, and a reader knows a word is complete when its count is full: no
+// fence or separate arrival counter is needed.
 GG_DEV void acc_add(unsigned long long* p, float v) {
-  const long long q = __float2ll_rn(v * 4294967296.0f);
-  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)q) : "memory");
+  const long long q = __float2ll_rn(v * 16777216.0f);
+  const unsigned long long w = ((unsigned long long)q << 8) + 1ull;
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-GG_DEV float acc_value(unsigned long long w) { return (float)(long long)w * 0x1p-32f; }
-GG_DEV uint32_t ld_acquire_u32(const unsigned int* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+GG_DEV float acc_value(unsigned long long w) { return (float)((long long)w >> 8) * 0x1p-24f; }
+GG_DEV uint32_t acc_count(unsigned long long w) { return (uint32_t)(w & 0xffull); }
 
 // ---------------------------------------------------------------------------------- dot products
 
@@ -570,12 +570,11 @@ struct Consumer {
     add_norm_tail(P, v, fa, fb, fbase, out, dbg_out, dbg_x);
   }
 
-  // The same on the fixed-point sums of a K-split reduction: every warp first waits until `cnt`
-  // reaches `target` arrivals (each lane polls with acquire semantics, so its loads that follow
-  // see every arrival's additions). Bounded: after giving up the sums read 0.
-  GG_DEV void add_norm_sums(const XPlanes& P, const unsigned long long* acc, const unsigned int* cnt, uint32_t target,
-                            const float* wa, const float* base, float* out, const float* wb, float* dbg_out,
-                            float* dbg_x) {
+  // The same on the fixed-point sums of a K-split reduction: each warp polls its quads of
+  // accumulators (every pass re-reads the lanes' incomplete words, the warp leaves together) until
+  // every word counts `target` contributions. Bounded: after giving up the sums read 0.
+  GG_DEV void add_norm_sums(const XPlanes& P, const unsigned long long* acc, uint32_t target, const float* wa,
+                            const float* base, float* out, const float* wb, float* dbg_out, float* dbg_x) {
     const GGModelDev& m = *x.m;
     const int nq = m.H >> 2, k = tid;
     const bool ok = k < nq;
@@ -585,21 +584,25 @@ struct Consumer {
       fb = __ldg(reinterpret_cast<const float4*>(wb) + k);
       fbase = reinterpret_cast<const float4*>(base)[k];
     }
-    bool live = true;
+    const uint64_t* p = reinterpret_cast<const uint64_t*>(acc) + 4 * (ok ? k : 0);
+    uint64_t w[4] = {target, target, target, target};  // lanes without a quad: complete
+    if (ok) issue4(p, w);
     {
       SpinClock clk;
 #pragma unroll 1
-      while (ld_acquire_u32(cnt) < target) {
+      for (;;) {
+        const bool done = acc_count(w[0]) == target && acc_count(w[1]) == target && acc_count(w[2]) == target &&
+                          acc_count(w[3]) == target;
+        if (__all_sync(0xffffffffu, done)) break;
+        if (!done) issue4(p, w);
         if (__any_sync(0xffffffffu, clk.expired(x.sc))) {
-          live = false;
+          w[0] = w[1] = w[2] = w[3] = 0ull;
           break;
         }
       }
     }
     float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (ok && live) {
-      uint64_t w[4];
-      issue4(reinterpret_cast<const uint64_t*>(acc) + 4 * k, w);
+    if (ok) {
 #pragma unroll
       for (int j = 0; j < 4; j++) v[j] = acc_value(w[j]);
     }
@@ -1085,10 +1088,6 @@ struct Consumer {
     }
     cbar();
     release_all(nst);
-    if (tid == 0) {
-      __threadfence();
-      atomicAdd(m.acc_cnt + ((size_t)x.par * m.L + l) * 8, 1u);
-    }
   }
 
   GG_DEV void phase_ffn_up(int l) {
@@ -1096,7 +1095,7 @@ struct Consumer {
     const GGLayerW& Lw = m.layers[l];
     // residual = hidden + post_attention_norm(proj) (engine.ts:785), then ffn rmsNorm (786)
     const size_t ai = (size_t)x.par * m.L + l;
-    add_norm_sums(x.S.xa, m.acc + ai * m.acc_stride, m.acc_cnt + ai * 8, (uint32_t)m.ncomb, Lw.post_attn_norm, x.S.hid,
+    add_norm_sums(x.S.xa, m.acc + ai * m.acc_stride, (uint32_t)m.ncomb, Lw.post_attn_norm, x.S.hid,
                   x.S.res, Lw.ffn_norm, blockIdx.x == 0 ? m.dbg_residual : nullptr, nullptr);
     const int n = x.S.rows[RG_I + 1] - x.S.rows[RG_I];
     const int nst = (n + (m.rps_gu >> 1) - 1) / (m.rps_gu >> 1);
