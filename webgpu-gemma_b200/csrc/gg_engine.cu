@@ -72,10 +72,10 @@ __global__ void gg_wo_cols_kernel(const uint8_t* __restrict__ wo, int H, int Q, 
   *reinterpret_cast<uint16_t*>(slice + 8 * (size_t)H + 2 * (size_t)r) = *reinterpret_cast<const uint16_t*>(row + Q + 2 * ((8 * u) / 32));
 }
 
-// Fixed-point accumulators ((2^-24 units << 8) + contribution count, two's complement u64) -> f32.
+// Fixed-point accumulators ((2^-32 units << 8) + contribution count, two's complement u64) -> f32.
 __global__ void gg_fixed_to_f32_kernel(const unsigned long long* __restrict__ src, float* __restrict__ dst, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) dst[i] = (float)((long long)src[i] >> 8) * 0x1p-24f;  // value bits above the 8-bit count
+  if (i < n) dst[i] = (float)((long long)src[i] >> 8) * 0x1p-32f;  // value bits above the 8-bit count
 }
 
 __global__ void gg_init_keys_kernel(unsigned long long* keys) {

@@ -91,7 +91,7 @@ struct GGModelDev {
   int sm_xa, sm_xb, sm_hid, sm_res, sm_tmp, sm_lmv, sm_scal, sm_red, sm_flag, sm_rows;
   // K-split reductions of the step kernel (the O projection: every merge unit adds its 8 columns'
   // products): per launch parity and layer, acc_stride u64 accumulators holding the sum of the
-  // 2^-24 fixed-point partials shifted left by 8 plus, in the low byte, the number of
+  // 2^-32 fixed-point partials shifted left by 8 plus, in the low byte, the number of
   // contributions (exact and order-independent; a reader waits for the full count).
   unsigned long long* acc;  // [2][L][acc_stride]
   unsigned int* acc_cnt;    // [2][L][8] (zeroed with the accumulators; unused by the kernel)

@@ -260,17 +260,17 @@ GG_DEV void quad_vals(const uint64_t (&w)[4], float* v) {
   for (int j = 0; j < 4; j++) v[j] = __uint_as_float((uint32_t)w[j]);
 }
 
-// K-split reductions: an f32 partial added into a u64 accumulator as (round(v * 2^24) << 8) + 1:
-// the high 56 bits sum the 2^-24 fixed-point partials and the low byte counts the contributions
-// (at most 255 adders). Integer addition is exact and associative, so the sum is the same whatever
+// K-split reductions: an f32 partial added into a u64 accumulator as (round(v * 2^32) << 8) + 1:
+// the high 56 bits sum the 2^-32 fixed-point partials (sums up to 2^23 in magnitude) and the low
+// byte counts the contributions (at most 255 adders). Integer addition is exact and associative, so the sum is the same whatever
 // order the CTAs arrive in, and a reader knows a word is complete when its count is full: no
 // fence or separate arrival counter is needed.
 GG_DEV void acc_add(unsigned long long* p, float v) {
-  const long long q = __float2ll_rn(v * 16777216.0f);
+  const long long q = __float2ll_rn(v * 4294967296.0f);
   const unsigned long long w = ((unsigned long long)q << 8) + 1ull;
   asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-GG_DEV float acc_value(unsigned long long w) { return (float)((long long)w >> 8) * 0x1p-24f; }
+GG_DEV float acc_value(unsigned long long w) { return (float)((long long)w >> 8) * 0x1p-32f; }
 GG_DEV uint32_t acc_count(unsigned long long w) { return (uint32_t)(w & 0xffull); }
 
 // ---------------------------------------------------------------------------------- dot products
