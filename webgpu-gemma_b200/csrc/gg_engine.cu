@@ -305,7 +305,6 @@ static int schedule(gg_engine* e) {
   if (m.rs_i > SB || m.rs_q > SB || 2 * m.rs_h > SB) return fail(e, GG_E_ARG, "rows too wide for a %d-byte ring stage", SB);
   m.stage_bytes = SB;
   m.rps_h = SB / m.rs_h;
-  m.rps_q = SB / m.rs_q;
   m.rps_i = SB / m.rs_i;
   m.rps_gu = (SB / m.rs_h) & ~1;
   const auto slot = [&](int nq) { return 4 * ((nq + G - 1) / G); };
@@ -503,9 +502,7 @@ extern "C" int gg_finalize(gg_engine* e) {
     GG_CUDA(e, cudaGetLastError());
   }
   GG_TRY(dalloc(e, &m.acc, 8 * (size_t)2 * c.num_layers * m.acc_stride));
-  GG_TRY(dalloc(e, &m.acc_cnt, 4 * (size_t)2 * c.num_layers * 8));
   GG_CUDA(e, cudaMemsetAsync(m.acc, 0, 8 * (size_t)2 * c.num_layers * m.acc_stride, e->stream));
-  GG_CUDA(e, cudaMemsetAsync(m.acc_cnt, 0, 4 * (size_t)2 * c.num_layers * 8, e->stream));
   for (int l = 0; l < c.num_layers; l++) {
     GGLayerW& w = m.layers[l];
     w.wqkv = e->wqkv[l]; w.wo = e->wo[l]; w.wgu = e->wgu[l]; w.wdown = e->wdown[l];

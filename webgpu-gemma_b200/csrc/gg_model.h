@@ -75,10 +75,10 @@ struct GGModelDev {
   int max_seqs;
   unsigned long long* trace;  // [grid][GG_TRACE_PHASES][4] globaltimer stamps
   int kv_es;  // bytes per KV cache element: 4 (f32), or 2 (bf16)
-  // Step kernel. Rows per ring stage for K = H, Q, I, and for row pairs of K = H (even); words per
+  // Step kernel. Rows per ring stage for K = H, I, and for row pairs of K = H (even); words per
   // CTA slot of the exchange buffers (whole quads: the CTA's outputs start on a 32-byte sector)
   // of the Q+2KV, H and I (pair) outputs; words per attention split (NQH x (HD + 4): o, max, sum).
-  int rps_h, rps_q, rps_i, rps_gu;
+  int rps_h, rps_i, rps_gu;
   int sl_qkv, sl_h, sl_i;
   // ceil(2^40 / nq) for the quad counts of those outputs ((Q + 2KV) / 4, H / 4, I / 4): the owner
   // of quad q is ((q + 1) * G - 1) * mq >> 40 (exact while that product's factors stay below 2^40)
@@ -94,7 +94,6 @@ struct GGModelDev {
   // 2^-32 fixed-point partials shifted left by 8 plus, in the low byte, the number of
   // contributions (exact and order-independent; a reader waits for the full count).
   unsigned long long* acc;  // [2][L][acc_stride]
-  unsigned int* acc_cnt;    // [2][L][8] (zeroed with the accumulators; unused by the kernel)
   int acc_stride;           // >= H, a multiple of 4
   int wo_rows_per_stage;    // most rows of a Wo column slice (10 bytes each) that one ring stage holds
   // The step kernel keeps a copy of this descriptor up to layers[L - 1] in shared memory at

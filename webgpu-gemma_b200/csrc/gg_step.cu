@@ -1280,8 +1280,6 @@ GG_DEV void step_body(const GGModelDev* __restrict__ mp, GGState* __restrict__ s
     unsigned long long* a = m.acc + (size_t)(x.par ^ 1u) * m.L * m.acc_stride;
     const int n = m.L * m.acc_stride, stride = m.grid * (int)blockDim.x;
     for (int i = blockIdx.x * (int)blockDim.x + (int)threadIdx.x; i < n; i += stride) a[i] = 0ull;
-    unsigned int* cn = m.acc_cnt + (size_t)(x.par ^ 1u) * m.L * 8;
-    for (int i = blockIdx.x * (int)blockDim.x + (int)threadIdx.x; i < m.L * 8; i += stride) cn[i] = 0u;
   }
   __syncthreads();
 
