@@ -520,7 +520,12 @@ def main():
                     help="with --profile-batch: context length of the KV slots (smaller = smaller capture)")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="two 512-token batched prefills of the 1B model, for an ncu launch list")
+    ap.add_argument("--gemm-kernel", default="dequant", choices=["dequant", "scaled"],
+                    help="kernel family of the tensor-core products (gg_set_gemm_kernel)")
     args = ap.parse_args()
+    if args.gemm_kernel != "dequant":
+        from gemma_b200.native import set_gemm_kernel, GEMM_SCALED
+        set_gemm_kernel(GEMM_SCALED)
     if args.cfg4:
         return run_cfg4(args)
     if args.cfg0:

@@ -157,6 +157,15 @@ int gg_decode_batch(gg_engine* eng, int n, const int32_t* seqs, const int32_t* t
  * (the GEMM and, when K was split, the sum of the split planes). */
 int gg_linear(gg_engine* eng, int which, int layer, const float* x, int batch, float* y);
 
+/* Kernel family of the tensor-core Q8_0 products (gg_linear, batched prefill, gg_decode_batch),
+ * process-wide: 0 (default) dequantises q * d into bf16 hi + lo operands (in the kernel for up
+ * to 8 rows, else from a dequantised copy made at load: 4 B per weight read); 1 converts the
+ * quants to bf16 exactly and applies each 32-wide block's f16 scale after that block's MMAs
+ * (1.0625 B per weight read, no use of the dequantised copy; slower on B200 today). Returns
+ * the previous value; kind -1 only queries. No counterpart in the reference, which has one
+ * linearQ8 shader (shaders.ts:92-151). */
+int gg_set_gemm_kernel(int kind);
+
 /* Failure-detection self-test: a one-CTA kernel waits on a device flag that nothing sets,
  * with the same bounded wait the step kernel uses. Returns GG_E_DEVICE ("activation wait
  * timed out") after about timeout_ns; the engine stays usable afterwards. No counterpart in

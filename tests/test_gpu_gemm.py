@@ -50,8 +50,17 @@ def mid():
     eng.close()
 
 
-@pytest.mark.parametrize("batch", [1, 8, 64, 65, 200])
-def test_gemm_all_matrices(mid, batch):
+@pytest.fixture(params=[0, 1], ids=["dequant", "scaled"])
+def kernel(request):
+    """Runs the test with each kernel family of the tensor-core products, then restores it."""
+    from gemma_b200.native import set_gemm_kernel
+    prev = set_gemm_kernel(request.param)
+    yield request.param
+    set_gemm_kernel(prev)
+
+
+@pytest.mark.parametrize("batch", [1, 2, 8, 9, 64, 65, 128, 200])
+def test_gemm_all_matrices(mid, batch, kernel):
     cfg, tens, eng = mid
     W = matrices(cfg, tens, 1)
     rng = np.random.default_rng(batch)
@@ -62,7 +71,7 @@ def test_gemm_all_matrices(mid, batch):
         check(y, x, W[which])
 
 
-def test_gemm_prefill_sized_batch_small_model():
+def test_gemm_prefill_sized_batch_small_model(kernel):
     from gemma_b200.native import engine_from_tensors
     cfg, tens = synthetic("small", 5)
     eng = engine_from_tensors(cfg, tens)

@@ -681,9 +681,12 @@ static void set_sampling(GGState& s, const gg_sample* sp, double u) {
 static int pick_splits(int tiles, int KS, int slots);
 
 static int gemm_tiles(int T, int M) { return (T <= 64 ? 1 : (T + 127) / 128) * (M / 128); }
-// CTA slots of the GEMM that gg_gemm_q8 picks for T rows: the Q8 kernel (T <= 8, or no dense
-// copy) fits two CTAs per SM, the dense kernel one.
-static int gemm_slots(const gg_engine* e, int T) { return e->sm_count * (T <= 8 || !e->gemm_ok ? 2 : 1); }
+// CTA slots of the GEMM that gg_gemm_q8 picks for T rows: the block-scaled kernel runs one CTA
+// per SM; of the dequantising kernels the Q8 one (T <= 8, or no dense copy) fits two.
+static int gemm_slots(const gg_engine* e, int T) {
+  if (gg_gemm_path() == GG_GEMM_SCALED) return e->sm_count;
+  return e->sm_count * (T <= 8 || !e->gemm_ok ? 2 : 1);
+}
 
 // Batched prefill of ids already in e->d_ids: chunks of up to GG_PF_CHUNK tokens, each layer
 // as four tensor-core GEMMs over the chunk's rows and the kernels of gg_prefill.cu between them.
@@ -1160,6 +1163,13 @@ extern "C" int gg_read_trace(gg_engine* e, uint64_t* out, int n) {
   GG_CUDA(e, cudaMemcpyAsync(out, e->md.trace, 8 * (size_t)n, cudaMemcpyDeviceToHost, e->stream));
   GG_CUDA(e, cudaStreamSynchronize(e->stream));
   return GG_OK;
+}
+
+extern "C" int gg_set_gemm_kernel(int kind) {
+  const int prev = gg_gemm_path();
+  if (kind == GG_GEMM_SCALED || kind == GG_GEMM_DEQUANT) gg_gemm_set_path(kind);
+  else if (kind != -1) return GG_E_ARG;
+  return prev;
 }
 
 extern "C" int gg_selftest_wait(gg_engine* e, uint64_t timeout_ns) {

@@ -53,7 +53,7 @@ struct GemmArgs {
   const uint8_t* xlo;
   float* y;
   long long ldy, split_stride;
-  int M, K, T, KS, slabs_per_split;
+  int M, K, T, KS, slabs_per_split, splits;
   uint32_t* err;
   uint64_t timeout_ns;
 };
@@ -416,6 +416,381 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const Gemm
   }
 }
 
+// ---------------------------------------------------------------------------- block-scaled path
+// The same product with the Q8_0 scale applied per 32-wide block after the MMAs, as the
+// reference's linearQ8 does (acc += d * sum of q * x per block, shaders.ts:92-151). A
+// persistent kernel: CTA c takes work items c, c + grid, ... (item = 128-row tile x NT-token
+// tile x K split) and every role walks the same sequence of (item, slab) pairs, so the rings
+// run on across item boundaries:
+//   warp 0      bulk copies of the raw Q8_0 slabs (128 x 64 quants + scales, 8704 B) into a
+//               ring (constant data: no wait for the previous kernel);
+//   warp 2      bulk copies of each slab's activation tiles (bf16 hi, lo) into a second ring;
+//   warps 3-6   convert the quants to bf16 (exact: |q| <= 128 has at most 8 significant bits)
+//               into a swizzled operand ring, one weight row per thread, and copy the slab's
+//               block scales (as f32) into a ring of their own;
+//   warp 1      TMEM allocation and the MMAs: the stage's activation tiles are x_hi rows then
+//               x_lo rows, one K-major operand of 2 NT rows, so one MMA of N = 2 NT makes both
+//               products Q*Xhi and Q*Xlo (in adjacent column halves); per Q8_0 block (two K
+//               steps of 16) two MMAs into its own TMEM accumulator, a slab's two blocks in one
+//               of P buffer pairs, then one commit per slab;
+//   warps 7..   per slab, read its two block accumulators (both halves) in TMEM round trips
+//               of CH columns (warp w: TMEM lanes 32*(w%4).., CW of the NT columns) and add
+//               d * (hi + lo) into f32 registers; at the end of an item write its tile.
+// One thread issues a tcgen05.mma about every 80-90 cycles whatever its size, so the product
+// is built from few wide MMAs: 4 per 128 x 64 slab. The MMAs of a slab complete well after
+// they are issued; the 512 TMEM columns hold P = 128 / NT slabs of block accumulators, so that
+// many slabs are in flight between the MMAs and the promotion. Two products per K step
+// instead of three, and 1.0625 bytes per weight read instead of the dequantised copy's four.
+// The products q * x_hi and q * x_lo are exact in f32 and x_hi + x_lo = x to 2^-17 relative.
+constexpr int GS_CONV = 4;
+constexpr int GS_WARP_CONV = 3;  // first converting warp
+constexpr int GS_WARP_EPI = GS_WARP_CONV + GS_CONV;
+
+template <int NT>
+struct ScaledCfg {
+  static constexpr int XROWS = NT < 64 ? NT : 64;               // rows copied from each 64-row tile block
+  static constexpr int XB = NT * 128;                           // one activation operand (hi or lo) of a slab
+  static constexpr int D = NT == 32 ? 6 : (NT == 64 ? 5 : 3);   // operand stages (activations + converted weights)
+  static constexpr int RS = NT == 64 ? 6 : 8;                   // raw weight stages
+  static constexpr int SS = 8;                                  // scale stages
+  static constexpr int P = 128 / NT;                            // TMEM buffer pairs (512 columns: 4 NT each)
+  static constexpr int EPI = NT == 128 ? 8 : NT / 8;            // promoting warps
+  static constexpr int CW = NT * 4 / EPI;                       // columns per promoting warp
+  static constexpr int CH = NT == 128 ? 8 : 16;                 // columns of each block half per TMEM round
+  static constexpr int THREADS = 32 * (GS_WARP_EPI + EPI);
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int A_OFF = D * 2 * XB;                      // after the 1 KB-aligned activation ring
+  static constexpr int RAW_OFF = A_OFF + D * GM_A_BYTES;
+  static constexpr int SC_OFF = RAW_OFF + RS * GG_Q8_TILE_BYTES;
+  static constexpr int BAR_OFF = SC_OFF + SS * 128 * 8;
+  static constexpr int R = P > D ? P : D;                        // slab-done barriers (see the kernel)
+  static constexpr int NBAR = 2 * RS + 2 * D + R + P + 2 * SS + 1;
+  static constexpr int SMEM = 1024 + BAR_OFF + NBAR * 8 + 16;
+  static_assert(CW % CH == 0 && SMEM <= 232448, "fits one CTA per SM");
+};
+
+// 32 consecutive f32 columns of this thread's TMEM lane, without the wait (tmem_ld_wait()).
+GG_DEV void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+GG_DEV void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+GG_DEV void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+template <int N>
+GG_DEV void tmem_ld_nowait(uint32_t taddr, uint32_t* r) {
+  static_assert(N == 8 || N == 16 || N == 32, "x8, x16 or x32");
+  if constexpr (N == 32)
+    tmem_ld32_nowait(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
+  else if constexpr (N == 16)
+    tmem_ld16_nowait(taddr, *reinterpret_cast<uint32_t(*)[16]>(r));
+  else
+    tmem_ld8_nowait(taddr, *reinterpret_cast<uint32_t(*)[8]>(r));
+}
+GG_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Four int8 quants (one word) -> two words of bf16 pairs, exactly.
+GG_DEV uint2 q8x4_to_bf16(uint32_t w) {
+  const uint32_t wx = w ^ 0x80808080u;
+  const uint32_t f0 = __float_as_uint(q8_at(wx, 0)), f1 = __float_as_uint(q8_at(wx, 1));
+  const uint32_t f2 = __float_as_uint(q8_at(wx, 2)), f3 = __float_as_uint(q8_at(wx, 3));
+  return make_uint2(__byte_perm(f0, f1, 0x7632u), __byte_perm(f2, f3, 0x7632u));
+}
+
+// Work item w of a launch: m tile fastest, then token tile, then K split.
+struct ScaledItem {
+  int mt, nt, s0, ns;
+};
+GG_DEV ScaledItem scaled_item(const GemmArgs& a, int w, int m_tiles, int n_tiles) {
+  ScaledItem it;
+  it.mt = w % m_tiles;
+  const int r = w / m_tiles;
+  it.nt = r % n_tiles;
+  it.s0 = (r / n_tiles) * a.slabs_per_split;
+  it.ns = min(a.slabs_per_split, a.KS - it.s0);
+  return it;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(ScaledCfg<NT>::THREADS, 1) gg_gemm_q8s_kernel(const GemmArgs a) {
+  using C = ScaledCfg<NT>;
+  constexpr int D = C::D, RS = C::RS, SS = C::SS, P = C::P, R = C::R;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* xring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* aring = xring + C::A_OFF;
+  uint8_t* rring = xring + C::RAW_OFF;
+  float2* sring = reinterpret_cast<float2*>(xring + C::SC_OFF);  // [SS][128]: a row's two block scales
+  uint64_t* full_r = reinterpret_cast<uint64_t*>(xring + C::BAR_OFF);
+  uint64_t* empty_r = full_r + RS;  // raw slot converted
+  uint64_t* full_x = empty_r + RS;  // activation stage landed
+  uint64_t* full_a = full_x + D;    // weight operand converted (and the activations seen landed)
+  // mdone_s[g % R]: the MMAs of slab g completed, so its block accumulators are complete and its
+  // operand stages free. R >= P and R >= D keep every wait on it within one phase: the MMAs of
+  // slab g + R need operand stage g + R (issued only after the activation producer and the
+  // converters waited for slab g + R - D) and buffer pair g + R (released only after the
+  // promotion consumed slab g + R - P).
+  uint64_t* sdone = full_a + D;
+  uint64_t* tempty = sdone + C::R;  // a slab's block accumulators read
+  uint64_t* sfull = tempty + P;     // scales written
+  uint64_t* sempty = sfull + SS;    // ... and read
+  uint64_t* mdone = sempty + SS;    // every MMA issued has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdone + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = a.M / 128, n_tiles = (a.T + NT - 1) / NT;
+  const int n_items = m_tiles * n_tiles * a.splits;
+  const SpinCtl sc{a.err, a.timeout_ns};
+  pdl_trigger();
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < RS; i++) {
+      mbar_init(&full_r[i], 1);
+      mbar_init(&empty_r[i], GS_CONV);
+    }
+    for (int i = 0; i < D; i++) {
+      mbar_init(&full_x[i], 1);
+      mbar_init(&full_a[i], GS_CONV);
+    }
+    for (int i = 0; i < R; i++) mbar_init(&sdone[i], 1);
+    for (int i = 0; i < P; i++) mbar_init(&tempty[i], C::EPI);
+    for (int i = 0; i < SS; i++) {
+      mbar_init(&sfull[i], GS_CONV);
+      mbar_init(&sempty[i], C::EPI);
+    }
+    mbar_init(mdone, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // raw weight slabs (never written by any kernel: no PDL wait)
+      uint32_t g = 0;
+      bool stop = false;
+      for (int w = blockIdx.x; w < n_items && !stop; w += gridDim.x) {
+        const ScaledItem it = scaled_item(a, w, m_tiles, n_tiles);
+        const uint8_t* src = a.wt + ((size_t)it.mt * a.KS + (size_t)it.s0) * GG_Q8_TILE_BYTES;
+        for (int i = 0; i < it.ns; i++, g++) {
+          const uint32_t o = g % RS;
+          if (*abort_flag || (g >= (uint32_t)RS && !mbar_wait(&empty_r[o], ((g / RS) - 1) & 1, sc))) {
+            *abort_flag = 1;
+            stop = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_r[o], GG_Q8_TILE_BYTES);
+          bulk_g2s_plain(rring + o * GG_Q8_TILE_BYTES, src + (size_t)i * GG_Q8_TILE_BYTES, GG_Q8_TILE_BYTES, &full_r[o]);
+        }
+      }
+      // before exit: every copy issued has landed (none may still write this CTA's memory)
+      for (uint32_t i = g > (uint32_t)RS ? g - RS : 0; i < g; i++) mbar_wait(&full_r[i % RS], (i / RS) & 1, sc);
+    }
+  } else if (warp == 2) {
+    if (lane == 0) {  // activation tiles
+      pdl_wait();
+      uint32_t g = 0;
+      bool stop = false;
+      const size_t KS = (size_t)a.KS;
+      for (int w = blockIdx.x; w < n_items && !stop; w += gridDim.x) {
+        const ScaledItem it = scaled_item(a, w, m_tiles, n_tiles);
+        for (int i = 0; i < it.ns; i++, g++) {
+          const uint32_t o = g % D, u = g - D;  // the stage's previous slab
+          if (*abort_flag || (g >= (uint32_t)D && !mbar_wait(&sdone[u % R], (u / R) & 1, sc))) {
+            *abort_flag = 1;
+            stop = true;
+            break;
+          }
+          uint8_t* dst = xring + o * 2 * C::XB;
+          mbar_arrive_expect_tx(&full_x[o], 2 * C::XB);
+#pragma unroll
+          for (int hh = 0; hh < (NT + 63) / 64; hh++) {
+            // token rows NT*nt + 64*hh.. sit in 64-row tile block (NT*nt)/64 + hh, from row (NT*nt)%64
+            const int tb = (NT * it.nt) / 64 + hh, r0 = (NT * it.nt) % 64;
+            const size_t blk = ((size_t)tb * KS + (size_t)(it.s0 + i)) * 8192u + (size_t)r0 * 128;
+            bulk_g2s_plain(dst + hh * 8192, a.xhi + blk, C::XROWS * 128, &full_x[o]);
+            bulk_g2s_plain(dst + C::XB + hh * 8192, a.xlo + blk, C::XROWS * 128, &full_x[o]);
+          }
+        }
+      }
+      for (uint32_t i = g > (uint32_t)D ? g - D : 0; i < g; i++) mbar_wait(&full_x[i % D], (i / D) & 1, sc);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issue
+      const uint32_t idesc = umma_idesc_bf16_m128(2 * NT);  // x_hi and x_lo rows together
+      // Descriptors of stage 0; a stage, a K step or the lo half only moves the start address
+      // (16-byte units in the low 14 bits, which no sum here carries out of: shared memory < 256 KB).
+      const uint64_t a0 = umma_desc_sw128(smem_u32(aring)), b0 = umma_desc_sw128(smem_u32(xring));
+      uint32_t g = 0;
+      bool stop = false;
+      for (int w = blockIdx.x; w < n_items && !stop; w += gridDim.x) {
+        const ScaledItem it = scaled_item(a, w, m_tiles, n_tiles);
+        for (int i = 0; i < it.ns; i++, g++) {
+          const uint32_t o = g % D, p = g % P, u = g - P;  // u: the pair's previous slab
+          if (!mbar_wait(&full_a[o], (g / D) & 1, sc) || (g >= (uint32_t)P && !mbar_wait(&tempty[p], (u / P) & 1, sc))) {
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = a0 + (uint64_t)(o * (GM_A_BYTES >> 4));
+          const uint64_t bx = b0 + (uint64_t)(o * ((2 * C::XB) >> 4));
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            const uint32_t d = tmem + (uint32_t)((2 * p + h) * 2 * NT);
+#pragma unroll
+            for (int kk = 0; kk < 2; kk++) {
+              const uint64_t off = (uint64_t)(2 * h + kk) * 2;  // 32 bytes per K step of 16
+              umma_bf16(d, ad + off, bx + off, idesc, kk > 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&sdone[g % R]);
+        }
+      }
+      if (stop) *abort_flag = 1;
+      umma_commit(mdone);  // no MMA may still write TMEM when it is freed
+      mbar_wait(mdone, 0, sc);
+    }
+  } else if (warp < GS_WARP_EPI) {  // convert: thread r = weight row r of every slab
+    const int r = (warp - GS_WARP_CONV) * 32 + lane;
+    const uint32_t rowoff = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    uint32_t g = 0;
+    bool stop = false;
+    for (int w = blockIdx.x; w < n_items && !stop; w += gridDim.x) {
+      const ScaledItem it = scaled_item(a, w, m_tiles, n_tiles);
+      for (int i = 0; i < it.ns; i++, g++) {
+        const uint32_t o = g % RS, oa = g % D, os = g % SS, u = g - D;
+        if (*abort_flag || !mbar_wait(&full_r[o], (g / RS) & 1, sc) ||
+            (g >= (uint32_t)D && !mbar_wait(&sdone[u % R], (u / R) & 1, sc)) ||
+            (g >= (uint32_t)SS && !mbar_wait(&sempty[os], ((g / SS) - 1) & 1, sc))) {
+          *abort_flag = 1;
+          stop = true;
+          break;
+        }
+        const uint8_t* raw = rring + o * GG_Q8_TILE_BYTES;
+        const uint32_t s2 = *reinterpret_cast<const uint32_t*>(raw + GM_RAW_Q + r * 4);
+        sring[os * 128 + r] = make_float2(__half2float(__ushort_as_half((unsigned short)(s2 & 0xffffu))),
+                                          __half2float(__ushort_as_half((unsigned short)(s2 >> 16))));
+        uint8_t* dst = aring + oa * GM_A_BYTES;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          // chunk c ^ H[m] for lanes 2m, 2m + 1, with H[m] = 2m in GF(4) = (0, 2, 3, 1): both
+          // H and H ^ m are permutations, so neither the 64-byte-strided loads nor the
+          // swizzled stores of a quarter warp meet a bank twice
+          const int cc = c ^ ((0x78 >> (2 * ((lane >> 1) & 3))) & 3);
+          const uint4 q = *reinterpret_cast<const uint4*>(raw + r * 64 + cc * 16);
+          const uint2 b0 = q8x4_to_bf16(q.x), b1 = q8x4_to_bf16(q.y), b2 = q8x4_to_bf16(q.z), b3 = q8x4_to_bf16(q.w);
+          // weights 16cc..16cc+15 = operand chunks 2cc, 2cc + 1 (8 bf16 each) of row r
+          *reinterpret_cast<uint4*>(dst + rowoff + ((uint32_t)(((2 * cc) ^ (r & 7)) & 7) << 4)) =
+              make_uint4(b0.x, b0.y, b1.x, b1.y);
+          *reinterpret_cast<uint4*>(dst + rowoff + ((uint32_t)(((2 * cc + 1) ^ (r & 7)) & 7) << 4)) =
+              make_uint4(b2.x, b2.y, b3.x, b3.y);
+        }
+        fence_proxy_async_smem();
+        // the stage's activations too have landed before the MMAs are told the stage is ready
+        const bool xin = mbar_wait(&full_x[oa], (g / D) & 1, sc);
+        __syncwarp();
+        if (!xin) {
+          *abort_flag = 1;
+          stop = true;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive(&sfull[os]);
+          mbar_arrive(&full_a[oa]);
+          mbar_arrive(&empty_r[o]);
+        }
+      }
+    }
+  } else {  // block promotion: thread = TMEM lane = weight row, columns cb..cb + CW - 1
+    constexpr int CW = C::CW, CH = C::CH;
+    const int q = warp & 3, rr = q * 32 + lane, cb = ((warp - GS_WARP_EPI) >> 2) * CW;
+    const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cb;
+    uint32_t g = 0;  // slabs consumed, over all items
+    bool ok = true, waited = false;
+    for (int w = blockIdx.x; w < n_items && ok; w += gridDim.x) {
+      const ScaledItem it = scaled_item(a, w, m_tiles, n_tiles);
+      float acc[CW];
+#pragma unroll
+      for (int c = 0; c < CW; c++) acc[c] = 0.f;
+      for (int i = 0; i < it.ns; i++, g++) {
+        const uint32_t p = g % P, os = g % SS;
+        if (*abort_flag || !mbar_wait(&sdone[g % R], (g / R) & 1, sc) || !mbar_wait(&sfull[os], (g / SS) & 1, sc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float2 d = sring[os * 128 + rr];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sempty[os]);
+        const uint32_t t0 = tl + (uint32_t)(4 * p * NT), t1 = t0 + 2 * NT;  // the slab's two block accumulators
+#pragma unroll
+        for (int c0 = 0; c0 < CW; c0 += CH) {  // columns c0..c0 + CH of both halves of both blocks
+          uint32_t v[4 * CH];
+          tmem_ld_nowait<CH>(t0 + (uint32_t)c0, v);
+          tmem_ld_nowait<CH>(t0 + (uint32_t)(NT + c0), v + CH);
+          tmem_ld_nowait<CH>(t1 + (uint32_t)c0, v + 2 * CH);
+          tmem_ld_nowait<CH>(t1 + (uint32_t)(NT + c0), v + 3 * CH);
+          tmem_ld_wait();
+          if (c0 + CH == CW) {  // this warp's columns of both blocks read: release them
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[p]);
+          }
+#pragma unroll
+          for (int c = 0; c < CH; c++) {
+            const float b0v = __uint_as_float(v[c]) + __uint_as_float(v[CH + c]);
+            const float b1v = __uint_as_float(v[2 * CH + c]) + __uint_as_float(v[3 * CH + c]);
+            acc[c0 + c] = fmaf(d.y, b1v, fmaf(d.x, b0v, acc[c0 + c]));
+          }
+        }
+      }
+      if (!ok) break;
+      if (!waited) {  // before the first write to a buffer of the chain
+        pdl_wait();
+        waited = true;
+      }
+      const int z = w / (m_tiles * n_tiles);
+      float* yb = a.y + (long long)z * a.split_stride + (it.mt * 128 + rr);
+#pragma unroll
+      for (int c = 0; c < CW; c++) {
+        const int t = it.nt * NT + cb + c;
+        if (t < a.T) yb[(long long)t * a.ldy] = acc[c];
+      }
+    }
+    if (!ok) *abort_flag = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------------------- one row
 // y[m] = sum_b d[m][b] * (q[m][32b..32b+31] . x[32b..]) for a single activation row: the
 // reference's linearQ8 (shaders.ts:92-151) at batch 1, read straight from the device rows. A
@@ -602,6 +977,35 @@ static cudaError_t launch_dense(const GemmArgs& a, int m_tiles, int splits, cuda
   return cudaGetLastError();
 }
 
+template <int NT>
+static cudaError_t launch_scaled(const GemmArgs& a, int m_tiles, int splits, cudaStream_t s) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t r = cudaGetDevice(&dev);
+  if (r != cudaSuccess) return r;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    r = cudaFuncSetAttribute(gg_gemm_q8s_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, ScaledCfg<NT>::SMEM);
+    if (r != cudaSuccess) return r;
+    attr_set[dev] = true;
+  }
+  // persistent: one CTA per SM at most, each walking work items blockIdx.x, + gridDim.x, ...
+  static int sms[64] = {};
+  if (!sms[dev]) {
+    r = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (r != cudaSuccess) return r;
+  }
+  const long long items = (long long)((a.T + NT - 1) / NT) * m_tiles * splits;
+  dim3 grid((unsigned)std::min<long long>(items, sms[dev]), 1, 1);
+  r = launch_pdl(gg_gemm_q8s_kernel<NT>, grid, dim3(ScaledCfg<NT>::THREADS), ScaledCfg<NT>::SMEM, s, a);
+  if (r != cudaSuccess) return r;
+  return cudaGetLastError();
+}
+
+static int g_gemm_path = GG_GEMM_DEQUANT;
+void gg_gemm_set_path(int path) { g_gemm_path = path; }
+int gg_gemm_path() { return g_gemm_path; }
+
 cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo, int T, float* y, long long ldy,
                        int splits, long long split_stride, uint32_t* err, uint64_t timeout_ns, cudaStream_t s) {
   if (T <= 0 || splits <= 0) return cudaErrorInvalidValue;
@@ -620,6 +1024,11 @@ cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo,
   if ((long long)(splits - 1) * a.slabs_per_split >= a.KS) return cudaErrorInvalidValue;  // an empty split
   a.err = err;
   a.timeout_ns = timeout_ns;
+  a.splits = splits;
+  if (g_gemm_path == GG_GEMM_SCALED) {
+    if (T <= 32) return launch_scaled<32>(a, w.M / 128, splits, s);
+    return T <= 64 ? launch_scaled<64>(a, w.M / 128, splits, s) : launch_scaled<128>(a, w.M / 128, splits, s);
+  }
   if (T > 8 && w.dense) {  // dequantised weights, copies and MMAs only (4 B per weight read)
     a.wt = w.dense;
     if (T <= 64) return launch_dense<64>(a, w.M / 128, splits, s);

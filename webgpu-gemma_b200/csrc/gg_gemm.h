@@ -43,6 +43,15 @@ cudaError_t gg_xtiles_from_f32(const float* x, int T, int K, uint8_t* xhi, uint8
 cudaError_t gg_matvec_q8(const uint8_t* rows, int rs, int M, int K, const float* x, float* y, int sms,
                          cudaStream_t s);
 
+// Kernel family behind gg_gemm_q8: GG_GEMM_DEQUANT (default) dequantises q * d in the kernel
+// for up to 8 rows and reads the dequantised copy (when one was made) for more (three products
+// per K step); GG_GEMM_SCALED converts the quants to bf16 and applies each Q8_0 block's scale
+// after its MMAs (1.0625 B per weight read, two products per K step, one persistent CTA per SM).
+#define GG_GEMM_DEQUANT 0
+#define GG_GEMM_SCALED 1
+void gg_gemm_set_path(int path);
+int gg_gemm_path();
+
 // Y (+ split * split_stride) [t][m] with row stride ldy; K is cut into `splits` slices whose
 // partial results land in consecutive split planes (the caller sums them).
 cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo, int T, float* y, long long ldy,

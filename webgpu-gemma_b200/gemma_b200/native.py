@@ -48,6 +48,7 @@ SIGNATURES = {
     "gg_linear": (_I, [_P, _I, _I, _P, _I, _P]),
     "gg_decode_batch": (_I, [_P, _I, _P, _P, _P, _I, _P, _P, _P]),
     "gg_selftest_wait": (_I, [_P, ctypes.c_uint64]),
+    "gg_set_gemm_kernel": (_I, [_I]),
     "gg_sample_logits_noalloc": (_I, [_P, _I, _P, _P, _D, _P, _P]),
     "gg_set_timeout": (_I, [_P, ctypes.c_uint64]),
     "gg_last_device_ms": (_I, [_P, ctypes.POINTER(ctypes.c_float)]),
@@ -93,6 +94,19 @@ def load(path: str | None = None) -> ctypes.CDLL:
         fn.argtypes = args
     _lib = lib
     return lib
+
+
+GEMM_DEQUANT, GEMM_SCALED = 0, 1
+
+
+def set_gemm_kernel(kind: int) -> int:
+    """Process-wide kernel family of the tensor-core products (gg_set_gemm_kernel); returns the
+    previous one. GEMM_DEQUANT (default) multiplies each Q8_0 block's scale into bf16 hi + lo
+    operands, GEMM_SCALED applies it after the block's MMAs."""
+    rc = load().gg_set_gemm_kernel(int(kind))
+    if rc < 0:
+        raise ValueError(f"unknown GEMM kernel family {kind}")
+    return rc
 
 
 def _i32p(a: np.ndarray):
