@@ -173,7 +173,10 @@ __global__ void __launch_bounds__(GM_THREADS, GemmCfg<NT>::MIN_CTAS) gg_gemm_q8_
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issue
-      const uint32_t idesc = umma_idesc_bf16_m128(NT);
+      // The stage's activation tiles are x_hi rows then x_lo rows: one operand of 2 NT rows, so
+      // one MMA of N = 2 NT makes Whi*Xhi and Whi*Xlo (accumulators 0 and 1) at once. One thread
+      // issues an MMA about every 80 cycles, so two MMAs per K step instead of three.
+      const uint32_t idesc = umma_idesc_bf16_m128(NT), idesc2 = umma_idesc_bf16_m128(2 * NT);
       for (int i = 0; i < ns; i++) {
         const int ia = i % AS, ib = i % BS;
         if (!mbar_wait(&full_b[ib], (i / BS) & 1, sc) || !mbar_wait(&full_a[ia], (i / AS) & 1, sc)) {
@@ -187,8 +190,7 @@ __global__ void __launch_bounds__(GM_THREADS, GemmCfg<NT>::MIN_CTAS) gg_gemm_q8_
         for (int kk = 0; kk < 4; kk++) {
           const uint32_t off = kk * 32;
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          umma_bf16(tmem, umma_desc_sw128(ahi + off), umma_desc_sw128(bhi + off), idesc, acc);
-          umma_bf16(tmem + NT, umma_desc_sw128(ahi + off), umma_desc_sw128(blo + off), idesc, acc);
+          umma_bf16(tmem, umma_desc_sw128(ahi + off), umma_desc_sw128(bhi + off), idesc2, acc);
           umma_bf16(tmem + 2 * NT, umma_desc_sw128(alo + off), umma_desc_sw128(bhi + off), idesc, acc);
         }
         umma_commit(&empty_a[ia]);
@@ -364,7 +366,9 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const Gemm
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16_m128(NT);
+      // x_hi and x_lo rows are one operand of 2 NT rows: for NT <= 128 one MMA of N = 2 NT makes
+      // Whi*Xhi (accumulator 0) and Whi*Xlo (accumulator 1), then Wlo*Xhi adds into accumulator 1.
+      const uint32_t idesc = umma_idesc_bf16_m128(NT), idesc2 = umma_idesc_bf16_m128(NT <= 128 ? 2 * NT : NT);
       for (int i = 0; i < ns; i++) {
         const int o = i % S;
         if (!mbar_wait(&full[o], (i / S) & 1, sc)) {
@@ -378,8 +382,12 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const Gemm
         for (int kk = 0; kk < 4; kk++) {
           const uint32_t off = kk * 32;
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          umma_bf16(tmem, umma_desc_sw128(ahi + off), umma_desc_sw128(bhi + off), idesc, acc);
-          umma_bf16(tmem + NT, umma_desc_sw128(ahi + off), umma_desc_sw128(blo + off), idesc, acc);
+          if constexpr (NT <= 128) {
+            umma_bf16(tmem, umma_desc_sw128(ahi + off), umma_desc_sw128(bhi + off), idesc2, acc);
+          } else {
+            umma_bf16(tmem, umma_desc_sw128(ahi + off), umma_desc_sw128(bhi + off), idesc, acc);
+            umma_bf16(tmem + NT, umma_desc_sw128(ahi + off), umma_desc_sw128(blo + off), idesc, acc);
+          }
           umma_bf16(tmem + NT, umma_desc_sw128(alo + off), umma_desc_sw128(bhi + off), idesc, 1u);
         }
         umma_commit(&empty[o]);
