@@ -157,6 +157,31 @@ GG_DEV float tag_wait(const uint64_t* p, uint32_t tag, const SpinCtl& sc) {
   }
 }
 
+// Bounded wait on an mbarrier phase for a thread that is not on the critical path: each try
+// may suspend the thread (up to 200 ns, woken when the phase completes) instead of spinning, so
+// it takes no issue slots from the warps that work meanwhile. Returns false (and sets err) on
+// timeout.
+GG_DEV bool mbar_wait_suspend(uint64_t* bar, uint32_t parity, const SpinCtl& sc) {
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(200u)
+        : "memory");
+    if (done) return true;
+    const uint64_t dt = global_timer_ns() - t0;
+    if (dt > GG_QUIET_SPIN_NS && *(volatile uint32_t*)sc.err) return false;
+    if (dt > sc.timeout_ns) {
+      atomicOr(sc.err, GG_ERR_WAIT_MBAR);
+      return false;
+    }
+  }
+}
+
 // Bounded wait on an mbarrier phase. Returns false (and sets err) on timeout.
 GG_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const SpinCtl& sc) {
   // Fast path without reading the clock; the timed loop below bounds the wait. Not unrolled:

@@ -75,7 +75,8 @@ __global__ void gg_wo_cols_kernel(const uint8_t* __restrict__ wo, int H, int Q, 
 // Fixed-point accumulators ((2^-32 units << 8) + contribution count, two's complement u64) -> f32.
 __global__ void gg_fixed_to_f32_kernel(const unsigned long long* __restrict__ src, float* __restrict__ dst, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) dst[i] = (float)((long long)src[i] >> 8) * 0x1p-32f;  // value bits above the 8-bit count
+  if (i < n)  // row i's word (padded quads); the value bits sit above the 8-bit count
+    dst[i] = (float)((long long)src[(i >> 2) * GG_ACC_QUAD_WORDS + (i & 3)] >> 8) * 0x1p-32f;
 }
 
 __global__ void gg_init_keys_kernel(unsigned long long* keys) {
@@ -343,7 +344,7 @@ static int schedule(gg_engine* e) {
   m.wo_rows_per_stage = SB / 10;
   if (m.H > m.wo_rows_per_stage || m.H % 8)
     return fail(e, GG_E_ARG, "hidden_size must be a multiple of 8 and at most %d (one ring stage of O columns)", m.wo_rows_per_stage);
-  m.acc_stride = (m.H + 3) / 4 * 4;
+  m.acc_stride = (m.H + 3) / 4 * GG_ACC_QUAD_WORDS;
   m.xs0 = (m.H + 63) / 64 * 64;
   m.xs1 = (std::max(m.Q, m.I) + 63) / 64 * 64;
   m.tmp_floats = m.Q + 2 * m.KV;

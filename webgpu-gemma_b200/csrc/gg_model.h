@@ -42,6 +42,9 @@ struct GGLayerW {
   const uint8_t* wo_cols;
 };
 
+// u64 words from one accumulator quad to the next: one 128-byte L2 line per quad.
+#define GG_ACC_QUAD_WORDS 16
+
 struct GGModelDev {
   int H, Q, KV, NQH, NKH, HD, I, V, L, CTX;
   float eps, attn_scale;
@@ -92,9 +95,11 @@ struct GGModelDev {
   // K-split reductions of the step kernel (the O projection: every merge unit adds its 8 columns'
   // products): per launch parity and layer, acc_stride u64 accumulators holding the sum of the
   // 2^-32 fixed-point partials shifted left by 8 plus, in the low byte, the number of
-  // contributions (exact and order-independent; a reader waits for the full count).
+  // contributions (exact and order-independent; a reader waits for the full count). Each quad
+  // of four rows sits alone in a 128-byte L2 line (GG_ACC_QUAD_WORDS words apart): all CTAs add
+  // into every row, and the atomic updates of one line are applied one after another.
   unsigned long long* acc;  // [2][L][acc_stride]
-  int acc_stride;           // >= H, a multiple of 4
+  int acc_stride;           // (H / 4) * GG_ACC_QUAD_WORDS: row r at word (r / 4) * GG_ACC_QUAD_WORDS + r % 4
   int wo_rows_per_stage;    // most rows of a Wo column slice (10 bytes each) that one ring stage holds
   // The step kernel keeps a copy of this descriptor up to layers[L - 1] in shared memory at
   // sm_model (GG_MODEL_BYTES(L) bytes), so its parameter reads never wait on L2.

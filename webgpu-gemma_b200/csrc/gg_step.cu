@@ -178,7 +178,7 @@ struct Producer {
   GG_DEV void issue(const void* s0, uint32_t b0, const void* s1, uint32_t b1, uint32_t off1) {
     const int slot = idx % NS;
     const uint32_t use = idx / NS;
-    if (use > 0 && ok) ok = mbar_wait(&x.S.empty[slot], (use - 1) & 1, x.sc);
+    if (use > 0 && ok) ok = mbar_wait_suspend(&x.S.empty[slot], (use - 1) & 1, x.sc);
     if (!ok) return;
     uint8_t* dst = x.S.ring + (size_t)slot * GG_STEP_STAGE_BYTES;
     mbar_arrive_expect_tx(&x.S.full[slot], b0 + b1);
@@ -587,7 +587,7 @@ struct Consumer {
       fb = __ldg(reinterpret_cast<const float4*>(wb) + k);
       fbase = reinterpret_cast<const float4*>(base)[k];
     }
-    const uint64_t* p = reinterpret_cast<const uint64_t*>(acc) + 4 * (ok ? k : 0);
+    const uint64_t* p = reinterpret_cast<const uint64_t*>(acc) + GG_ACC_QUAD_WORDS * (ok ? k : 0);
     uint64_t w[4] = {target, target, target, target};  // lanes without a quad: complete
     if (ok) issue4(p, w);
     {
@@ -1087,7 +1087,7 @@ struct Consumer {
       float sum = 0.f;
 #pragma unroll
       for (int j = 0; j < 8; j++) sum = fmaf((float)((int)(q[j >> 2] << (24 - 8 * (j & 3))) >> 24), a[j], sum);
-      acc_add(acc + r, sum * lds_half(slice + 8u * (uint32_t)m.H + 2u * (uint32_t)r));
+      acc_add(acc + ((r >> 2) * GG_ACC_QUAD_WORDS + (r & 3)), sum * lds_half(slice + 8u * (uint32_t)m.H + 2u * (uint32_t)r));
     }
     cbar();
     release_all(nst);
