@@ -350,7 +350,7 @@ GG_DEV float2 dot_pair8(uint32_t ra, int rs, int K, const XPlanes& P) {
   const int gl = threadIdx.x & 7, nch = K >> 4;
   const uint32_t rb = ra + rs;
   float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll 2
+#pragma unroll 1  // (unrolling measured no faster: the loop is bound by shared-memory bandwidth)
   for (int c = gl; c < nch; c += 8) {
     const uint4 a0 = lds128(P.p0 + 16 * c);
     const uint4 a1 = lds128(P.p1 + 16 * c);
