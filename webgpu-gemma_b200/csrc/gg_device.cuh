@@ -109,6 +109,15 @@ GG_DEV void tag_store(uint64_t* p, float v, uint32_t tag) {
   uint64_t w = ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+// Four consecutive tagged words (p 32-byte aligned: one sector) in one 32-byte store. Each 8-byte
+// word still carries its own tag, so a reader that polls word by word sees whole words either
+// way; a quarter of the store instructions and sector writes of four tag_store calls.
+GG_DEV void tag_store4(uint64_t* p, float v0, float v1, float v2, float v3, uint32_t tag) {
+  const uint64_t t = (uint64_t)tag << 32;
+  asm volatile("st.relaxed.gpu.global.v4.b64 [%0], {%1, %2, %3, %4};" ::"l"(p), "l"(t | __float_as_uint(v0)),
+               "l"(t | __float_as_uint(v1)), "l"(t | __float_as_uint(v2)), "l"(t | __float_as_uint(v3))
+               : "memory");
+}
 GG_DEV uint64_t tag_load(const uint64_t* p) {
   uint64_t w;
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");

@@ -980,14 +980,13 @@ struct Consumer {
       for (int jj = 0; jj < 8; jj++) acc[jj] = fmaf(w, vf[jj], acc[jj]);
     }
     uint64_t* o = m.t_o + (size_t)s * m.att_slot + (size_t)h * (HD + 4);
+    // One 32-byte sector per store (att_slot and HD + 4 are multiples of 4 words, so every quad
+    // is sector-aligned). Written as 8-byte stores 64 bytes apart, the split's 2 KB made the step
+    // 0.644 instead of 0.583 ms per token.
+    static_assert((HD + 4) % 4 == 0, "split slots of whole sectors");
 #pragma unroll
-    for (int jj = 0; jj < 8; jj++) tag_store(o + 8 * lane + jj, acc[jj], tag);
-    if (lane == 0) {  // the split's header quad: max, sum of exp, two zero words (one 16-byte pair each)
-      tag_store(o + HD, mx, tag);
-      tag_store(o + HD + 1, sum, tag);
-      tag_store(o + HD + 2, 0.f, tag);
-      tag_store(o + HD + 3, 0.f, tag);
-    }
+    for (int jj = 0; jj < 8; jj += 4) tag_store4(o + 8 * lane + jj, acc[jj], acc[jj + 1], acc[jj + 2], acc[jj + 3], tag);
+    if (lane == 0) tag_store4(o + HD, mx, sum, 0.f, 0.f, tag);  // header quad: max, sum of exp, two zeros
   }
 
   // Merge of the attention splits (online softmax) for 8 output dimensions per unit. The unit's
