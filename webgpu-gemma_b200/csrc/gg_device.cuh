@@ -124,10 +124,13 @@ GG_DEV uint64_t tag_load(const uint64_t* p) {
   return w;
 }
 
-// Two consecutive words (16-byte aligned) with one load at gpu scope (served by L2: always sees
-// the latest store of another SM).
-GG_DEV void ld2_relaxed(const uint64_t* p, uint64_t& a, uint64_t& b) {
-  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+// Four consecutive words (p 32-byte aligned: one sector) with one load at gpu scope (served by
+// L2: always sees the latest store of another SM).
+GG_DEV void ld4_relaxed(const uint64_t* p, uint64_t (&w)[4]) {
+  asm volatile("ld.relaxed.gpu.global.v4.u64 {%0, %1, %2, %3}, [%4];"
+               : "=l"(w[0]), "=l"(w[1]), "=l"(w[2]), "=l"(w[3])
+               : "l"(p)
+               : "memory");
 }
 
 struct SpinCtl {

@@ -465,10 +465,9 @@ struct Consumer {
       }
     }
   }
-  GG_DEV void issue4(const uint64_t* p, uint64_t (&w)[4]) {
-    ld2_relaxed(p, w[0], w[1]);
-    ld2_relaxed(p + 2, w[2], w[3]);
-  }
+  // One tagged quad in one 32-byte load (p is 32-byte aligned at every call site: quads start at
+  // multiples of 4 words of cudaMalloc'd buffers; two 16-byte loads made the step 5 % slower).
+  GG_DEV void issue4(const uint64_t* p, uint64_t (&w)[4]) { ld4_relaxed(p, w); }
 
   // NV sums over the consumer threads with one barrier; warps 0..nw-1 hold data and receive the
   // totals (same summation order everywhere); the other warps only take part in the barrier.
