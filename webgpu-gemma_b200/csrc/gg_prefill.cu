@@ -606,15 +606,17 @@ constexpr int BD_KB = 4;                   // keys per batch (rows in flight per
 constexpr int BD_PART = BD_NH * PF_HD + 2 * BD_NH;
 static_assert(PF_HD == 8 * 32, "a lane holds 8 dims of a 256-wide head");
 
-// Eight consecutive cache elements (16-byte aligned when f32: two loads; bf16: one load) as f32.
+// Eight consecutive cache elements as f32: f32 one 32-byte load (p 32-byte aligned: the cache
+// base, its slot and layer strides and pos * 256 are multiples of 8 floats), bf16 one 16-byte
+// load.
 template <bool KV16>
 GG_DEV void kv_load8(const kv_t<KV16>* p, float* f) {
   if constexpr (KV16) {
     bf16x8_widen(__ldg(reinterpret_cast<const uint4*>(p)), f);
   } else {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    asm volatile("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=f"(f[0]), "=f"(f[1]), "=f"(f[2]), "=f"(f[3]), "=f"(f[4]), "=f"(f[5]), "=f"(f[6]), "=f"(f[7])
+                 : "l"(p));
   }
 }
 
