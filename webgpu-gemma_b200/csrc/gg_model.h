@@ -14,8 +14,7 @@
 #define GG_HEAD_DIM 256                // Gemma 3 head size (compile-time for the attention phase)
 #define GG_POS_PER_SPLIT 8             // KV positions per attention split
 #define GG_TRACE_PHASES 512            // phases traced per CTA by GG_TRACE launches (4 stamps each)
-#define GG_STEP_GRID 128               // step kernel: CTAs (a power of two, one per SM; B200 has 148 SMs)
-#define GG_STEP_LOG2_GRID 7
+#define GG_STEP_GRID 148               // step kernel: CTAs, one per SM of the B200 (a compile-time divisor: / and % by it become a multiply and shift)
 #define GG_STEP_NCW 15                 // step kernel: consumer warps per CTA (+ one producer warp: 4 warps per SM sub-partition, 128 registers a thread)
 #define GG_STEP_STAGES 9               // step kernel: weight ring stages
 #define GG_STEP_STAGE_BYTES 20480      // step kernel: bytes per ring stage (16 rows of 1,152 Q8_0 weights)

@@ -53,7 +53,7 @@ GG_DEV uint32_t make_tag(uint32_t base, int phase) { return 0x80000000u | ((base
 
 // Quad partition: quads [qpart(c), qpart(c + 1)) of nq go to CTA c of G (32-bit: the host checks
 // G * nq < 2^31), and the CTA that owns quad q.
-GG_DEV int qpart(int nq, int c) { return (int)(((uint32_t)c * (uint32_t)nq) >> GG_STEP_LOG2_GRID); }
+GG_DEV int qpart(int nq, int c) { return (int)(((uint32_t)c * (uint32_t)nq) / (uint32_t)GG_STEP_GRID); }
 // (division by nq as a multiply by mq = ceil(2^40 / nq): n * nq < 2^40 here, so it is exact)
 GG_DEV int qowner(unsigned long long mq, int q) {
   return (int)(((unsigned long long)(((uint32_t)q + 1u) * (uint32_t)GG_STEP_GRID - 1u) * mq) >> 40);
@@ -162,8 +162,8 @@ GG_DEV int window_lo(const GGLayerW& Lw, int pos) { return (Lw.window > 0 && pos
 // First split of this CTA in layer l (splits s >= slo with s - slo = (c - rot) mod G).
 GG_DEV int first_split(const GGModelDev& m, int l, int pos, int nsplit, int c) {
   constexpr int G = GG_STEP_GRID;
-  const int rot = (l * nsplit) & (G - 1);
-  return window_lo(m.layers[l], pos) / GG_POS_PER_SPLIT + ((c - rot + G) & (G - 1));
+  const int rot = (l * nsplit) % G;
+  return window_lo(m.layers[l], pos) / GG_POS_PER_SPLIT + (c - rot + G) % G;
 }
 
 // ---------------------------------------------------------------------------------- producer
@@ -793,7 +793,7 @@ struct Consumer {
     const GGLayerW& Lw = m.layers[l];
     constexpr int G = GG_STEP_GRID;
     const int s0 = first_split(m, l, x.pos, x.nsplit, blockIdx.x);
-    const int att_nst = s0 < x.nsplit ? ((x.nsplit - 1 - s0) >> GG_STEP_LOG2_GRID) + 1 : 0;  // this CTA's splits (KV stages)
+    const int att_nst = s0 < x.nsplit ? (x.nsplit - 1 - s0) / G + 1 : 0;  // this CTA's splits (KV stages)
     if (s0 >= x.nsplit) return;
     constexpr int HD = GG_HEAD_DIM;
     const int NQH = m.NQH, NKH = m.NKH, Q = m.Q, KV = m.KV;
@@ -851,7 +851,7 @@ struct Consumer {
     cbar();
     trace(l * PH + 1, 1);
     // the CTA whose splits include the new position stores its k and v
-    if ((((x.pos / GG_POS_PER_SPLIT) - s0) & (G - 1)) == 0 && x.pos / GG_POS_PER_SPLIT >= s0) {
+    if (x.pos / GG_POS_PER_SPLIT >= s0 && (x.pos / GG_POS_PER_SPLIT - s0) % G == 0) {
       using KT = kv_t<KV16>;
       const size_t off = (size_t)x.seq * m.kv_seq_stride + ((size_t)l * m.CTX + x.pos) * KV;
       KT* kc = reinterpret_cast<KT*>(m.kcache);
