@@ -154,6 +154,8 @@ struct gg_engine {
   float* pf_att = nullptr;  // attention partials per key range
   uint8_t* pf_tiles = nullptr;
   size_t pf_tiles_half = 0;
+  uint8_t* pf_gtiles = nullptr;  // GeGLU output tiles written by the gate/up GEMM's epilogue
+  size_t pf_gtiles_half = 0;
   uint8_t* pf_kvsplit = nullptr;  // bf16 hi / lo copies of the K and V rows a chunk attends to
   // batched decode: one token for each of up to bd_max sequences per step
   int bd_max = 0;
@@ -564,6 +566,8 @@ extern "C" int gg_finalize(gg_engine* e) {
     GG_TRY(dalloc(e, &e->pf_y, 4 * yfl));
     GG_TRY(dalloc(e, &e->pf_att, 4 * pf_attention_part_floats((int)TC, m.CTX, m.NQH, m.NKH)));
     GG_TRY(dalloc(e, &e->pf_tiles, 2 * e->pf_tiles_half));
+    e->pf_gtiles_half = gg_xtiles_bytes((int)TC, m.I);
+    GG_TRY(dalloc(e, &e->pf_gtiles, 2 * e->pf_gtiles_half));
     GG_TRY(dalloc(e, &e->pf_kvsplit, pf_kv_split_bytes(m.CTX, m.KV)));
   }
   // exchange buffers of the step kernel (tagged words; one slot per CTA, or per attention split)
@@ -696,6 +700,8 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
   cudaStream_t s = e->stream;
   uint8_t* thi = e->pf_tiles;
   uint8_t* tlo = e->pf_tiles + e->pf_tiles_half;
+  uint8_t* ghi = e->pf_gtiles;
+  uint8_t* glo = e->pf_gtiles + e->pf_gtiles_half;
   uint32_t* err = &e->d_st->error;
   const uint64_t to = e->timeout_ns;
   const int QKV = m.Q + 2 * m.KV;
@@ -725,12 +731,17 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
       GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_attn_norm, e->pf_hidden, e->pf_res, w.ffn_norm, thi, tlo, T,
                             m.H, m.eps, s));
       sp = pick_splits(gemm_tiles(T, 2 * m.I), m.H / 64, gemm_slots(e, T));
-      plane = (long long)T * 2 * m.I;
-      GG_CUDA(e, gg_gemm_q8(mp[2], thi, tlo, T, e->pf_y, 2 * m.I, sp, plane, err, to, s));
-      GG_CUDA(e, pf_geglu(e->pf_y, sp, plane, T, m.I, thi, tlo, s));
+      const bool fuse = gg_gemm_geglu_fusable(mp[2], T, sp);
+      if (fuse) {
+        GG_CUDA(e, gg_gemm_q8_geglu(mp[2], thi, tlo, T, ghi, glo, err, to, s));
+      } else {
+        plane = (long long)T * 2 * m.I;
+        GG_CUDA(e, gg_gemm_q8(mp[2], thi, tlo, T, e->pf_y, 2 * m.I, sp, plane, err, to, s));
+        GG_CUDA(e, pf_geglu(e->pf_y, sp, plane, T, m.I, thi, tlo, s));
+      }
       sp = pick_splits(gemm_tiles(T, m.H), m.I / 64, gemm_slots(e, T));
       plane = (long long)T * m.H;
-      GG_CUDA(e, gg_gemm_q8(mp[3], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));
+      GG_CUDA(e, gg_gemm_q8(mp[3], fuse ? ghi : thi, fuse ? glo : tlo, T, e->pf_y, m.H, sp, plane, err, to, s));
       const float* next_norm = l + 1 < m.L ? m.layers[l + 1].attn_norm : nullptr;
       GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_ffw_norm, e->pf_res, e->pf_hidden, next_norm, thi, tlo, T, m.H,
                             m.eps, s));
@@ -754,6 +765,8 @@ static int batch_step(gg_engine* e, int B, int max_pos, const double* d_unif, in
   cudaStream_t s = e->stream;
   uint8_t* thi = e->pf_tiles;
   uint8_t* tlo = e->pf_tiles + e->pf_tiles_half;
+  uint8_t* ghi = e->pf_gtiles;
+  uint8_t* glo = e->pf_gtiles + e->pf_gtiles_half;
   uint32_t* err = &e->d_st->error;
   const uint64_t to = e->timeout_ns;
   const int QKV = m.Q + 2 * m.KV;
@@ -777,12 +790,17 @@ static int batch_step(gg_engine* e, int B, int max_pos, const double* d_unif, in
     GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_attn_norm, e->pf_hidden, e->pf_res, w.ffn_norm, thi, tlo, B, m.H,
                           m.eps, s));
     sp = pick_splits(gemm_tiles(B, 2 * m.I), m.H / 64, gemm_slots(e, B));
-    plane = (long long)B * 2 * m.I;
-    GG_CUDA(e, gg_gemm_q8(mp[2], thi, tlo, B, e->pf_y, 2 * m.I, sp, plane, err, to, s));
-    GG_CUDA(e, pf_geglu(e->pf_y, sp, plane, B, m.I, thi, tlo, s));
+    const bool fuse = gg_gemm_geglu_fusable(mp[2], B, sp);
+    if (fuse) {
+      GG_CUDA(e, gg_gemm_q8_geglu(mp[2], thi, tlo, B, ghi, glo, err, to, s));
+    } else {
+      plane = (long long)B * 2 * m.I;
+      GG_CUDA(e, gg_gemm_q8(mp[2], thi, tlo, B, e->pf_y, 2 * m.I, sp, plane, err, to, s));
+      GG_CUDA(e, pf_geglu(e->pf_y, sp, plane, B, m.I, thi, tlo, s));
+    }
     sp = pick_splits(gemm_tiles(B, m.H), m.I / 64, gemm_slots(e, B));
     plane = (long long)B * m.H;
-    GG_CUDA(e, gg_gemm_q8(mp[3], thi, tlo, B, e->pf_y, m.H, sp, plane, err, to, s));
+    GG_CUDA(e, gg_gemm_q8(mp[3], fuse ? ghi : thi, fuse ? glo : tlo, B, e->pf_y, m.H, sp, plane, err, to, s));
     // the last layer's output goes through the final norm (output_norm) into the LM-head tiles
     const float* next_norm = l + 1 < m.L ? m.layers[l + 1].attn_norm : m.out_norm;
     GG_CUDA(e, pf_addnorm(e->pf_y, sp, plane, w.post_ffw_norm, e->pf_res, e->pf_hidden, next_norm, thi, tlo, B, m.H,

@@ -52,6 +52,8 @@ struct GemmArgs {
   const uint8_t* xhi;
   const uint8_t* xlo;
   float* y;
+  uint8_t* ghi;  // dense kernel only: when set, gelu(gate) * up of row pairs (2j, 2j + 1) goes
+  uint8_t* glo;  // to these activation tiles (M / 2 columns) instead of y
   long long ldy, split_stride;
   int M, K, T, KS, slabs_per_split, splits;
   uint32_t* err;
@@ -297,6 +299,57 @@ struct DenseCfg {
   static constexpr int TMEM_COLS = NT == 256 ? 512 : 256;  // two accumulators of NT columns
 };
 
+constexpr int GD_EPI_FLOATS = 16 * 36;  // per epilogue warp: 16 tokens x 32 rows, rows padded to 36 floats
+
+// Epilogue of one 128-row x NT-token tile whose two accumulators sit in TMEM columns
+// [tacc, tacc + NT) and [tacc + NT, tacc + 2 NT) (warp q: TMEM lanes 32q..32q+31, so lane = row
+// 32q + lane of the tile): their sum goes to y (+ split z's plane) as f32, or, with a.ghi set,
+// through GeGLU (geluMul, shaders.ts:153-170) to activation tiles. For GeGLU the matrix
+// interleaves gate (row 2j) and up (row 2j + 1), so a warp's 32 rows are output columns
+// 16q'..16q'+15 (q' = 4 m_tile + q) as gate/up lane pairs; a block of 16 tokens x 32 rows goes
+// through shared memory st (GD_EPI_FLOATS; rows of 36 floats keep the float4 reads
+// conflict-free) and each lane turns one token's 8 pairs into one 8-column hi/lo chunk.
+template <int NT>
+GG_DEV void dense_epilogue(const GemmArgs& a, uint32_t tacc, int q, int lane, int n_tile, int m_tile, int z, float* st) {
+  const uint32_t tl = tacc + ((uint32_t)(q * 32) << 16);
+  if (a.ghi) {
+    const int j0 = m_tile * 64 + q * 16, tt = lane & 15, hf = lane >> 4;
+    const int KSo = a.M / 128;  // 64-column blocks of the M / 2 output columns
+#pragma unroll 1
+    for (int c = 0; c < NT; c += 16) {
+      float v[16], u[16];
+      tmem_ld16(tl + (uint32_t)c, v);
+      tmem_ld16(tl + (uint32_t)(NT + c), u);
+#pragma unroll
+      for (int j = 0; j < 16; j++) st[j * 36 + lane] = v[j] + u[j];
+      __syncwarp();
+      const float4* r = reinterpret_cast<const float4*>(st + tt * 36 + 16 * hf);
+      const float4 p0 = r[0], p1 = r[1], p2 = r[2], p3 = r[3];
+      __syncwarp();
+      const int t = n_tile * NT + c + tt;
+      if (t < a.T) {
+        const float o[8] = {gelu_tanh(p0.x) * p0.y, gelu_tanh(p0.z) * p0.w, gelu_tanh(p1.x) * p1.y,
+                            gelu_tanh(p1.z) * p1.w, gelu_tanh(p2.x) * p2.y, gelu_tanh(p2.z) * p2.w,
+                            gelu_tanh(p3.x) * p3.y, gelu_tanh(p3.z) * p3.w};
+        xtile_put8(a.ghi, a.glo, KSo, t, j0 + 8 * hf, o);
+      }
+    }
+  } else {
+    float* yb = a.y + (long long)z * a.split_stride + m_tile * 128 + q * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < NT; c += 16) {
+      float v[16], u[16];
+      tmem_ld16(tl + (uint32_t)c, v);
+      tmem_ld16(tl + (uint32_t)(NT + c), u);
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const int t = n_tile * NT + c + j;
+        if (t < a.T) yb[(long long)t * a.ldy] = v[j] + u[j];
+      }
+    }
+  }
+}
+
 template <int NT>
 __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const GemmArgs a) {
   using C = DenseCfg<NT>;
@@ -400,20 +453,193 @@ __global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_kernel(const Gemm
     const bool ok = mbar_wait(acc_bar, 0, sc);
     tc_fence_after();
     const int go = __shfl_sync(0xffffffffu, (ok && !*abort_flag) ? 1 : 0, 0);
+    // the ring is idle once the accumulator is complete: its first bytes stage the GeGLU blocks
     if (go) {
-      const int m = m_tile * 128 + q * 32 + lane;
-      float* yb = a.y + (long long)blockIdx.z * a.split_stride + m;
-#pragma unroll 1
-      for (int c = 0; c < NT; c += 16) {
-        float v[16], u[16];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(NT + c), u);
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const int t = n_tile * NT + c + j;
-          if (t < a.T) yb[(long long)t * a.ldy] = v[j] + u[j];
+      float* st = reinterpret_cast<float*>(ring) + q * GD_EPI_FLOATS;
+      dense_epilogue<NT>(a, tmem, q, lane, n_tile, m_tile, blockIdx.z, st);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// The same GEMM as a persistent tile loop (NT = 64, 128): CTA c takes work items c, c + grid, ...
+// (item = 128-row tile x NT-token tile x K split, token tiles fastest so the CTAs running at once
+// share weight tiles in L2). The copy ring runs on across items, and TMEM holds two accumulator
+// sets of 2 NT columns: while the epilogue warps drain item k from one set, the MMAs of item
+// k + 1 fill the other, so the epilogue (and a GeGLU in it) is off the tensor pipe's path.
+// Hand-offs: full / empty per ring stage (copies -> MMAs -> copies), accf[b] (the MMAs of an
+// item in set b complete; one commit) and acce[b] (the four epilogue warps have read set b).
+template <int NT>
+struct DensePCfg {
+  static constexpr int B_BYTES = NT * 128;
+  static constexpr int STAGE = GD_A_STAGE + 2 * B_BYTES;
+  static constexpr int S = NT == 64 ? 4 : 3;
+  static constexpr int EPI = 4 * GD_EPI_FLOATS * 4;
+  static constexpr int SMEM = 1024 + S * STAGE + EPI + 256;
+  static constexpr int TMEM_COLS = 4 * NT;
+};
+
+struct DenseItem {
+  int n_tile, m_tile, z, s0, ns;
+};
+GG_DEV DenseItem dense_item(const GemmArgs& a, int w, int ntt, int mt) {
+  DenseItem d;
+  d.n_tile = w % ntt;
+  const int r = w / ntt;
+  d.m_tile = r % mt;
+  d.z = r / mt;
+  d.s0 = d.z * a.slabs_per_split;
+  d.ns = min(a.slabs_per_split, a.KS - d.s0);
+  return d;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(GD_THREADS, 1) gg_gemm_dense_pk_kernel(const GemmArgs a) {
+  static_assert(NT == 64 || NT == 128, "two accumulator sets of 2 NT columns in TMEM's 512");
+  using C = DensePCfg<NT>;
+  constexpr int S = C::S;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* epi = reinterpret_cast<float*>(ring + S * C::STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + S * C::STAGE + C::EPI);
+  uint64_t* empty = full + S;
+  uint64_t* accf = empty + S;  // [2]
+  uint64_t* acce = accf + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntt = (a.T + NT - 1) / NT, mt = a.M / 128;
+  const int items = ntt * mt * a.splits;
+  const SpinCtl sc{a.err, a.timeout_ns};
+  pdl_trigger();  // weight tiles of the first stages load before pdl_wait(), activations after
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0) {
+    if (lane == 0) {
+      const size_t KS = (size_t)a.KS;
+      int pre = 0;  // stages of the first item whose weight tile is issued before the wait
+      if ((int)blockIdx.x < items) {
+        const DenseItem d = dense_item(a, blockIdx.x, ntt, mt);
+        pre = min(d.ns, S);
+        for (int i = 0; i < pre; i++) {
+          mbar_arrive_expect_tx(&full[i], C::STAGE);
+          bulk_g2s_plain(ring + i * C::STAGE, a.wt + ((size_t)d.m_tile * KS + (size_t)(d.s0 + i)) * GD_A_STAGE,
+                         GD_A_STAGE, &full[i]);
         }
       }
+      pdl_wait();
+      int g = 0;  // stages issued (over all items)
+      bool run = true;
+      for (int w = blockIdx.x; w < items && run; w += gridDim.x) {
+        const DenseItem d = dense_item(a, w, ntt, mt);
+        for (int i = 0; i < d.ns; i++) {
+          const int o = g % S;
+          if (*abort_flag) {
+            run = false;
+            break;
+          }
+          if (g >= S && !mbar_wait(&empty[o], ((g / S) - 1) & 1, sc)) {
+            *abort_flag = 1;
+            run = false;
+            break;
+          }
+          uint8_t* dst = ring + o * C::STAGE;
+          if (g >= pre) {
+            mbar_arrive_expect_tx(&full[o], C::STAGE);
+            bulk_g2s_plain(dst, a.wt + ((size_t)d.m_tile * KS + (size_t)(d.s0 + i)) * GD_A_STAGE, GD_A_STAGE, &full[o]);
+          }
+#pragma unroll
+          for (int hh = 0; hh < NT / 64; hh++) {
+            const size_t blk = ((size_t)(d.n_tile * (NT / 64) + hh) * KS + (size_t)(d.s0 + i)) * 8192u;
+            bulk_g2s_plain(dst + GD_A_STAGE + hh * 8192, a.xhi + blk, 8192, &full[o]);
+            bulk_g2s_plain(dst + GD_A_STAGE + C::B_BYTES + hh * 8192, a.xlo + blk, 8192, &full[o]);
+          }
+          g++;
+        }
+      }
+      for (int i = g > S ? g - S : 0; i < g; i++) mbar_wait(&full[i % S], (i / S) & 1, sc);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // x_hi and x_lo rows are one operand of 2 NT rows: one MMA of N = 2 NT makes Whi*Xhi
+      // (columns 0..NT-1 of the set) and Whi*Xlo (NT..2NT-1), then Wlo*Xhi adds into the latter.
+      const uint32_t idesc = umma_idesc_bf16_m128(NT), idesc2 = umma_idesc_bf16_m128(2 * NT);
+      int g = 0, k = 0;
+      for (int w = blockIdx.x; w < items; w += gridDim.x, k++) {
+        if (*abort_flag) break;
+        const DenseItem d = dense_item(a, w, ntt, mt);
+        const int b = k & 1;
+        if (k >= 2 && !mbar_wait(&acce[b], ((k >> 1) - 1) & 1, sc)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc0 = tmem + (uint32_t)(b * 2 * NT);
+        bool run = true;
+        for (int i = 0; i < d.ns; i++, g++) {
+          const int o = g % S;
+          if (!mbar_wait(&full[o], (g / S) & 1, sc)) {
+            *abort_flag = 1;
+            run = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ahi = smem_u32(ring + o * C::STAGE), alo = ahi + GM_A_BYTES;
+          const uint32_t bhi = ahi + GD_A_STAGE;
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++) {
+            const uint32_t off = kk * 32;
+            umma_bf16(acc0, umma_desc_sw128(ahi + off), umma_desc_sw128(bhi + off), idesc2, (i > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16(acc0 + NT, umma_desc_sw128(alo + off), umma_desc_sw128(bhi + off), idesc, 1u);
+          }
+          umma_commit(&empty[o]);
+        }
+        if (!run) break;
+        umma_commit(&accf[b]);
+      }
+    }
+  } else {  // warps 2..5: epilogue (warp w reads TMEM lanes 32*(w%4)..)
+    const int q = warp & 3;
+    float* st = epi + q * GD_EPI_FLOATS;
+    pdl_wait();
+    int k = 0;
+    for (int w = blockIdx.x; w < items; w += gridDim.x, k++) {
+      const int b = k & 1;
+      const bool ok = mbar_wait(&accf[b], (k >> 1) & 1, sc);
+      tc_fence_after();
+      const int go = __shfl_sync(0xffffffffu, (ok && !*abort_flag) ? 1 : 0, 0);
+      if (!go) {
+        if (lane == 0) *abort_flag = 1;
+        break;
+      }
+      const DenseItem d = dense_item(a, w, ntt, mt);
+      dense_epilogue<NT>(a, tmem + (uint32_t)(b * 2 * NT), q, lane, d.n_tile, d.m_tile, d.z, st);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[b]);
     }
   }
   tc_fence_before();
@@ -985,6 +1211,37 @@ static cudaError_t launch_dense(const GemmArgs& a, int m_tiles, int splits, cuda
   return cudaGetLastError();
 }
 
+static cudaError_t device_sms(int dev, int* out) {
+  static int sms[64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!sms[dev]) {
+    cudaError_t r = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (r != cudaSuccess) return r;
+  }
+  *out = sms[dev];
+  return cudaSuccess;
+}
+
+// Persistent dense kernel: one CTA per SM at most, each walking work items blockIdx.x, + gridDim.x, ...
+template <int NT>
+static cudaError_t launch_dense_pk(const GemmArgs& a, int m_tiles, int splits, cudaStream_t s) {
+  static bool attr_set[64] = {};
+  int dev = 0, sms = 0;
+  cudaError_t r = cudaGetDevice(&dev);
+  if (r == cudaSuccess) r = device_sms(dev, &sms);
+  if (r != cudaSuccess) return r;
+  if (!attr_set[dev]) {
+    r = cudaFuncSetAttribute(gg_gemm_dense_pk_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DensePCfg<NT>::SMEM);
+    if (r != cudaSuccess) return r;
+    attr_set[dev] = true;
+  }
+  const long long items = (long long)((a.T + NT - 1) / NT) * m_tiles * splits;
+  dim3 grid((unsigned)std::min<long long>(items, sms), 1, 1);
+  r = launch_pdl(gg_gemm_dense_pk_kernel<NT>, grid, dim3(GD_THREADS), DensePCfg<NT>::SMEM, s, a);
+  if (r != cudaSuccess) return r;
+  return cudaGetLastError();
+}
+
 template <int NT>
 static cudaError_t launch_scaled(const GemmArgs& a, int m_tiles, int splits, cudaStream_t s) {
   static bool attr_set[64] = {};
@@ -1014,6 +1271,16 @@ static int g_gemm_path = GG_GEMM_DEQUANT;
 void gg_gemm_set_path(int path) { g_gemm_path = path; }
 int gg_gemm_path() { return g_gemm_path; }
 
+// The dense (dequantised copy) kernel for T > 8 rows: the row tile width by T.
+static cudaError_t dispatch_dense(const GGQ8Map& w, GemmArgs a, int splits, cudaStream_t s) {
+  a.wt = w.dense;
+  if (a.T <= 64) return launch_dense_pk<64>(a, w.M / 128, splits, s);
+  // 256-row tiles halve the weight-tile reads, but only matrices wide enough to fill two waves
+  // of 256-row tiles have tiles to spare (one and a half waves lose more than the reads save)
+  const bool wide = a.T > 128 && (long long)((a.T + 255) / 256) * (w.M / 128) * splits >= 2 * 148;
+  return wide ? launch_dense<256>(a, w.M / 128, splits, s) : launch_dense_pk<128>(a, w.M / 128, splits, s);
+}
+
 cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo, int T, float* y, long long ldy,
                        int splits, long long split_stride, uint32_t* err, uint64_t timeout_ns, cudaStream_t s) {
   if (T <= 0 || splits <= 0) return cudaErrorInvalidValue;
@@ -1037,15 +1304,31 @@ cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo,
     if (T <= 32) return launch_scaled<32>(a, w.M / 128, splits, s);
     return T <= 64 ? launch_scaled<64>(a, w.M / 128, splits, s) : launch_scaled<128>(a, w.M / 128, splits, s);
   }
-  if (T > 8 && w.dense) {  // dequantised weights, copies and MMAs only (4 B per weight read)
-    a.wt = w.dense;
-    if (T <= 64) return launch_dense<64>(a, w.M / 128, splits, s);
-    // 256-row tiles halve the weight-tile reads, but only matrices wide enough to fill two waves
-    // of 256-row tiles have tiles to spare (one and a half waves lose more than the reads save)
-    const bool wide = T > 128 && (long long)((T + 255) / 256) * (w.M / 128) * splits >= 2 * 148;
-    return wide ? launch_dense<256>(a, w.M / 128, splits, s) : launch_dense<128>(a, w.M / 128, splits, s);
-  }
+  if (T > 8 && w.dense) return dispatch_dense(w, a, splits, s);  // dequantised copy: 4 B per weight read
   return T <= 64 ? launch_nt<64>(w, a, splits, s) : launch_nt<128>(w, a, splits, s);
+}
+
+bool gg_gemm_geglu_fusable(const GGQ8Map& w, int T, int splits) {
+  return g_gemm_path == GG_GEMM_DEQUANT && T > 8 && w.dense != nullptr && splits == 1 && w.M % 128 == 0;
+}
+
+cudaError_t gg_gemm_q8_geglu(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo, int T, uint8_t* ghi,
+                             uint8_t* glo, uint32_t* err, uint64_t timeout_ns, cudaStream_t s) {
+  if (T <= 0 || !ghi || !glo || !gg_gemm_geglu_fusable(w, T, 1)) return cudaErrorInvalidValue;
+  GemmArgs a{};
+  a.xhi = xhi;
+  a.xlo = xlo;
+  a.ghi = ghi;
+  a.glo = glo;
+  a.M = w.M;
+  a.K = w.K;
+  a.T = T;
+  a.KS = w.K / 64;
+  a.slabs_per_split = a.KS;
+  a.err = err;
+  a.timeout_ns = timeout_ns;
+  a.splits = 1;
+  return dispatch_dense(w, a, 1, s);
 }
 
 cudaError_t gg_matvec_q8(const uint8_t* rows, int rs, int M, int K, const float* x, float* y, int sms,

@@ -56,3 +56,11 @@ int gg_gemm_path();
 // partial results land in consecutive split planes (the caller sums them).
 cudaError_t gg_gemm_q8(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo, int T, float* y, long long ldy,
                        int splits, long long split_stride, uint32_t* err, uint64_t timeout_ns, cudaStream_t s);
+
+// The gate/up projection with GeGLU in the GEMM's epilogue: w's rows interleave gate (2j) and
+// up (2j + 1); gelu(gate) * up for the T rows goes straight to activation tiles (ghi, glo) of
+// K = M / 2 columns, which must not alias xhi / xlo. Only the dense single-split kernel has
+// this epilogue: gg_gemm_geglu_fusable says whether gg_gemm_q8 with `splits` would take it.
+bool gg_gemm_geglu_fusable(const GGQ8Map& w, int T, int splits);
+cudaError_t gg_gemm_q8_geglu(const GGQ8Map& w, const uint8_t* xhi, const uint8_t* xlo, int T, uint8_t* ghi,
+                             uint8_t* glo, uint32_t* err, uint64_t timeout_ns, cudaStream_t s);
