@@ -722,9 +722,9 @@ static int prefill_batched(gg_engine* e, int seq, int n, int start_pos) {
       long long plane = (long long)T * QKV;
       GG_CUDA(e, gg_gemm_q8(mp[0], thi, tlo, T, e->pf_y, QKV, sp, plane, err, to, s));
       GG_CUDA(e, pf_qk_rope_store(e->pf_y, sp, plane, w.q_norm, w.k_norm, w.rope, T, p0, m.NQH, m.NKH, m.HD, m.eps,
-                                  e->pf_q, kc, vc, m.kv_es == 2, s));
+                                  e->pf_q, kc, vc, m.kv_es == 2, e->pf_kvsplit, m.CTX, s));
       GG_CUDA(e, pf_attention(e->pf_q, kc, vc, m.kv_es == 2, T, p0, m.NQH, m.NKH, m.HD, m.attn_scale, w.window,
-                              e->pf_att, e->pf_kvsplit, m.CTX, thi, tlo, s));
+                              e->pf_att, e->pf_kvsplit, m.CTX, true, thi, tlo, s));
       sp = pick_splits(gemm_tiles(T, m.H), m.Q / 64, gemm_slots(e, T));
       plane = (long long)T * m.H;
       GG_CUDA(e, gg_gemm_q8(mp[1], thi, tlo, T, e->pf_y, m.H, sp, plane, err, to, s));

@@ -147,12 +147,21 @@ __global__ void __launch_bounds__(1024)
 
 // BATCH: row t is a different sequence, in KV slot seq_arr[t] (slot stride seq_stride floats)
 // at position pos_arr[t]; otherwise row t is prompt position p0 + t of one slot.
+// Element i of a bf16 hi / lo pair of planes (lo n elements after hi) from the value the cache
+// holds: hi = f rounded to bf16, lo = (f - hi) rounded, as pf_kv_split_kernel makes them.
+GG_DEV void split_put(uint16_t* hi, long long n, long long i, float f) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(f);
+  hi[i] = __bfloat16_as_ushort(h);
+  hi[n + i] = __bfloat16_as_ushort(__float2bfloat16_rn(f - __bfloat162float(h)));
+}
+
 template <bool BATCH, bool KV16>
 __global__ void __launch_bounds__(PF_THREADS)
     pf_qk_kernel(const float* __restrict__ part, int splits, long long plane, const float* __restrict__ q_norm,
                  const float* __restrict__ k_norm, const float2* __restrict__ rope, int p0, int NQH, int NKH, float eps,
                  float* __restrict__ q_out, kv_t<KV16>* __restrict__ kc, kv_t<KV16>* __restrict__ vc,
-                 const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride) {
+                 const int32_t* __restrict__ pos_arr, const int32_t* __restrict__ seq_arr, size_t seq_stride,
+                 uint16_t* __restrict__ ksplit, int ctx) {
   pdl_trigger();
   constexpr int NJ = PF_HD / 32;
   const int t = blockIdx.x;
@@ -219,11 +228,19 @@ __global__ void __launch_bounds__(PF_THREADS)
           qs[(long long)gridDim.x * QD + qi] = __bfloat16_as_ushort(__float2bfloat16_rn(v[j] - __bfloat162float(hi)));
         }
       }
-      else kc[(long long)pos * KVD + (h - NQH) * PF_HD + i] = kv_narrow<KV16>(v[j]);
+      else {
+        const long long ki = (long long)pos * KVD + (h - NQH) * PF_HD + i;
+        const kv_t<KV16> kk = kv_narrow<KV16>(v[j]);
+        kc[ki] = kk;
+        if (!BATCH && ksplit) split_put(ksplit, (long long)ctx * KVD, ki, kv_widen(kk));
+      }
     }
   }
   for (int i = threadIdx.x; i < KVD; i += PF_THREADS) {
-    vc[(long long)pos * KVD + i] = kv_narrow<KV16>(sum_planes(part, splits, plane, base + QD + KVD + i));
+    const long long vi = (long long)pos * KVD + i;
+    const kv_t<KV16> vv = kv_narrow<KV16>(sum_planes(part, splits, plane, base + QD + KVD + i));
+    vc[vi] = vv;
+    if (!BATCH && ksplit) split_put(ksplit + 2 * (size_t)ctx * KVD, (long long)ctx * KVD, vi, kv_widen(vv));
   }
 }
 
@@ -939,14 +956,15 @@ cudaError_t pf_addnorm(const float* part, int splits, long long plane, const flo
 
 cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm,
                              const float* k_norm, const float2* rope, int T, int p0, int NQH, int NKH, int HD, float eps,
-                             float* q_out, void* kc, void* vc, bool kv16, cudaStream_t s) {
-  if (T <= 0 || HD != PF_HD) return cudaErrorInvalidValue;
+                             float* q_out, void* kc, void* vc, bool kv16, uint8_t* split, int ctx, cudaStream_t s) {
+  if (T <= 0 || HD != PF_HD || (split && p0 + T > ctx)) return cudaErrorInvalidValue;
+  uint16_t* ks = reinterpret_cast<uint16_t*>(split);
   if (kv16)
     return launch_pdl(pf_qk_kernel<false, true>, dim3(T), dim3(PF_THREADS), 0, s, part, splits, plane, q_norm, k_norm,
                       rope, p0, NQH, NKH, eps, q_out, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, nullptr, nullptr,
-                      (size_t)0);
+                      (size_t)0, ks, ctx);
   return launch_pdl(pf_qk_kernel<false, false>, dim3(T), dim3(PF_THREADS), 0, s, part, splits, plane, q_norm, k_norm,
-                    rope, p0, NQH, NKH, eps, q_out, (float*)kc, (float*)vc, nullptr, nullptr, (size_t)0);
+                    rope, p0, NQH, NKH, eps, q_out, (float*)kc, (float*)vc, nullptr, nullptr, (size_t)0, ks, ctx);
 }
 
 size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH) {
@@ -958,8 +976,8 @@ size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH) {
 size_t pf_kv_split_bytes(int ctx, int KVD) { return (size_t)4 * ctx * KVD * sizeof(uint16_t); }
 
 cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv16, int T, int p0, int NQH, int NKH,
-                         int HD, float scale, int window, float* part, uint8_t* split, int ctx, uint8_t* thi,
-                         uint8_t* tlo, cudaStream_t s) {
+                         int HD, float scale, int window, float* part, uint8_t* split, int ctx, bool rows_split,
+                         uint8_t* thi, uint8_t* tlo, cudaStream_t s) {
   if (T <= 0 || HD != PF_HD || NKH <= 0 || NQH % NKH || !split || p0 + T > ctx) return cudaErrorInvalidValue;
   const int G = NQH / NKH;
   if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) return cudaErrorInvalidValue;
@@ -979,20 +997,23 @@ cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv
   if (maxc > 32) return cudaErrorInvalidValue;  // merge weights hold 32 key ranges (2048 positions)
   // bf16 hi / lo copies of the rows the chunk can see: [klo, p0 + T)
   const int KVD = NKH * PF_HD;
-  const int r0 = window > 0 ? max(0, p0 + 1 - window) / PA_KC * PA_KC : 0, r1 = p0 + T;
+  // (rows p0.. when pf_qk_rope_store made their copies already)
+  const int r0 = window > 0 ? max(0, p0 + 1 - window) / PA_KC * PA_KC : 0, r1 = rows_split ? p0 : p0 + T;
   uint16_t* khi = reinterpret_cast<uint16_t*>(split);
   uint16_t* klo = khi + (size_t)ctx * KVD;
   uint16_t* vhi = klo + (size_t)ctx * KVD;
   uint16_t* vlo = vhi + (size_t)ctx * KVD;
   const long long n8 = (long long)(r1 - r0) * (KVD / 8);
   const int sblocks = (int)std::min<long long>((n8 + 255) / 256, 148 * 8);
-  if (kv16)
-    r = launch_pdl(pf_kv_split_kernel<true>, dim3(sblocks), dim3(256), 0, s, (const __nv_bfloat16*)kc,
-                   (const __nv_bfloat16*)vc, r0, r1, KVD, khi, klo, vhi, vlo);
-  else
-    r = launch_pdl(pf_kv_split_kernel<false>, dim3(sblocks), dim3(256), 0, s, (const float*)kc, (const float*)vc, r0, r1,
-                   KVD, khi, klo, vhi, vlo);
-  if (r != cudaSuccess) return r;
+  if (n8 > 0) {  // none for a chunk at the start of the window whose own rows were split
+    if (kv16)
+      r = launch_pdl(pf_kv_split_kernel<true>, dim3(sblocks), dim3(256), 0, s, (const __nv_bfloat16*)kc,
+                     (const __nv_bfloat16*)vc, r0, r1, KVD, khi, klo, vhi, vlo);
+    else
+      r = launch_pdl(pf_kv_split_kernel<false>, dim3(sblocks), dim3(256), 0, s, (const float*)kc, (const float*)vc, r0,
+                     r1, KVD, khi, klo, vhi, vlo);
+    if (r != cudaSuccess) return r;
+  }
   const uint16_t* qhi = reinterpret_cast<const uint16_t*>(q);  // hi / lo halves from pf_qk_rope_store
   const uint16_t* qlo = qhi + (size_t)T * NQH * PF_HD;
   r = launch_pdl(pf_attn_tc_kernel, dim3(maxc, nb, NKH), dim3(TA_THREADS), TA_SMEM, s, qhi, qlo, (const uint16_t*)khi,

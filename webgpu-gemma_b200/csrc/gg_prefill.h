@@ -26,10 +26,12 @@ cudaError_t pf_addnorm(const float* part, int splits, long long plane, const flo
 // Per token: sum the QKV planes, q/k per-head rmsNorm + RoPE at position p0 + t
 // (shaders.ts:420-467), q -> q_out as bf16 hi / lo halves ([T][NQH*HD] hi, then [T][NQH*HD] lo,
 // the operand form pf_attention reads), k and v -> rows p0.. of this layer's cache (f32
-// elements, or bf16 rounded to nearest even when kv16).
+// elements, or bf16 rounded to nearest even when kv16). With `split` (pf_attention's scratch
+// for a cache of ctx rows) the new rows' bf16 hi / lo copies are written there too, so
+// pf_attention with rows_split = true splits only the rows before p0.
 cudaError_t pf_qk_rope_store(const float* part, int splits, long long plane, const float* q_norm,
                              const float* k_norm, const float2* rope, int T, int p0, int NQH, int NKH, int HD, float eps,
-                             float* q_out, void* kc, void* vc, bool kv16, cudaStream_t s);
+                             float* q_out, void* kc, void* vc, bool kv16, uint8_t* split, int ctx, cudaStream_t s);
 
 // Causal attention of the T queries (q as written by pf_qk_rope_store) at positions
 // p0..p0+T-1 over cache rows 0..p0+t
@@ -41,8 +43,8 @@ size_t pf_attention_part_floats(int max_tokens, int ctx, int NQH, int NKH);
 // the chunk attends to, made once per call and read by every attention CTA.
 size_t pf_kv_split_bytes(int ctx, int KVD);
 cudaError_t pf_attention(const float* q, const void* kc, const void* vc, bool kv16, int T, int p0, int NQH, int NKH,
-                         int HD, float scale, int window, float* part, uint8_t* split, int ctx, uint8_t* thi,
-                         uint8_t* tlo, cudaStream_t s);
+                         int HD, float scale, int window, float* part, uint8_t* split, int ctx, bool rows_split,
+                         uint8_t* thi, uint8_t* tlo, cudaStream_t s);
 
 // act[t][i] = gelu_tanh(gu[t][2i]) * gu[t][2i+1] (shaders.ts:153-170, gu = sum of planes) as
 // activation tiles of width I.
