@@ -66,7 +66,7 @@ def measured_peaks() -> tuple[float, str]:
 # ncu capture of the step kernel on this workload (summary under profiles/): dram bytes read +
 # written by one launch at position NCU_TRAFFIC_POS. The line reports it moved to the mean timed
 # position by the KV bytes per position (the weights are the same every token).
-NCU_TRAFFIC_PER_LAUNCH = 1109342208 + 5203200
+NCU_TRAFFIC_PER_LAUNCH = 1109333504 + 4751104
 NCU_TRAFFIC_POS = 641
 
 
