@@ -75,8 +75,7 @@ __global__ void __launch_bounds__(1024)
                       const float* rin, float* rout, const float* __restrict__ w_norm, uint8_t* thi, uint8_t* tlo,
                       int H, float eps) {
   pdl_trigger();
-  __shared__ float red[32];
-  __shared__ float tot[2];
+  __shared__ float red[2][32];
   const int t = blockIdx.x, k = threadIdx.x, nq = H >> 2;
   const bool ok = k < nq;
   const long long base = (long long)t * H + 4 * k;
@@ -89,17 +88,15 @@ __global__ void __launch_bounds__(1024)
     const float4 ri = *reinterpret_cast<const float4*>(rin + base);
     r[0] = ri.x; r[1] = ri.y; r[2] = ri.z; r[3] = ri.w;
   }
+  // block sum with one barrier: every warp adds the per-warp partials itself (in lane order, so
+  // all warps get the same bits); the two sums use their own slots, so no second barrier guards
+  // the slots' reuse
   auto bsum = [&](float v, int slot) {
     v = warp_sum(v);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    if ((threadIdx.x & 31) == 0) red[slot][threadIdx.x >> 5] = v;
     __syncthreads();
-    if (threadIdx.x < 32) {
-      float x = threadIdx.x < (int)(blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-      x = warp_sum(x);
-      if (threadIdx.x == 0) tot[slot] = x;
-    }
-    __syncthreads();
-    return tot[slot];
+    const int ln = threadIdx.x & 31;
+    return warp_sum(ln < (int)(blockDim.x >> 5) ? red[slot][ln] : 0.f);
   };
   if (part) {
     float v[4] = {0.f, 0.f, 0.f, 0.f};
