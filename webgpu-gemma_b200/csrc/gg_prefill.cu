@@ -579,7 +579,7 @@ __global__ void __launch_bounds__(PF_THREADS)
   float M = -1e30f;
   for (int i = 0; i < nc; i++) M = fmaxf(M, wm[i][r]);
   float L = 0.f, v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  constexpr int MB = 4;  // key ranges whose outputs are loaded together
+  constexpr int MB = 8;  // key ranges whose outputs are loaded together (one round for 512 keys)
   for (int i0 = 0; i0 < nc; i0 += MB) {
     float4 va[MB], vb[MB];
 #pragma unroll
